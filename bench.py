@@ -1,0 +1,546 @@
+#!/usr/bin/env python
+"""Headline benchmark: int8 split-KV decode attention at S=32K, plus quantize-on-write.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...      (one rank per GPU)
+
+Workload (decode-attention length sweep at S = 32768, B=1, Hq=16, Hkv=8, D=128):
+bf16 q, int8 K/V with float32 scales, codes made by the product's own
+quantize-on-write kernels from K ~ N(0,1) with 4 outlier channels per head x20
+and V ~ N(0,1) (synthetic, seeded).  A step decodes one token through 28
+layers, each with its own cache (28 x 68 MB = 1.9 GB > L2, read round-robin,
+so no layer's cache is still in L2 when it is read again); the 28 launches are
+one CUDA graph.  At N > 1 GPUs each rank holds a 32768-token chunk of every
+layer of an N x 32768-token sequence (weak scaling): per layer it computes its
+softmax partials, all-gathers them (NCCL) and combines on the device.
+
+metric / value: algorithmic HBM GB/s of the decode kernel (K+V codes, scales,
+q and output bytes) over the whole job; ``us_per_layer`` and the fraction of
+the measured HBM peak ride along.  ``e2e`` is the same metric through the
+public API (``QuantizedKVCache.update`` + ``quantized_attention_forward``)
+with each step's q / new K / new V copied from pinned host memory and the
+outputs read back.  The extra keys report the int8 / bf16-twin speedup, the S
+sweep and the bulk quantize-on-write GB/s (B=8, Hkv=8, S=32768, bf16).
+
+``--impl reference`` times the reference's CPU path (the numpy restatement in
+``oracle/``) on the host cores instead.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+B, HQ, HKV, D, S_HEAD, LAYERS = 1, 16, 8, 128, 32768, 28
+METRIC = "int8 decode-attn HBM GB/s at S=32K (B=1, Hq=16, Hkv=8, D=128)"
+FALLBACK_HBM = 6650.0
+L2_BYTES = 126 * 2 ** 20
+
+
+def decode_bytes(b, hq, hkv, s, d, kv_bytes=1, scale_bytes=4):
+    """Algorithmic bytes of one decode launch: K+V, scales, q in and out (bf16)."""
+    kv = 2 * b * hkv * s * d * kv_bytes
+    sc = (b * hkv * s * scale_bytes + b * hkv * d * scale_bytes) if kv_bytes == 1 else 0
+    return kv + sc + 2 * b * hq * d * 2
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-extras", action="store_true", help="skip sweep / twin / quant extras")
+    return ap.parse_args()
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM, "fallback"
+
+
+def profile_traffic():
+    """Per-launch DRAM bytes of the decode kernel from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", "decode_int8_s32k_ncu.txt")
+    try:
+        for line in open(path):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return int(float(line.split(":", 1)[1]))
+    except OSError:
+        pass
+    return None
+
+
+# ---------------------------------------------------------------- clocks
+class Clocks:
+    """nvidia-smi sampling of SM clocks and throttle reasons during a timed region."""
+
+    Q = ("clocks.sm,clocks.max.sm,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index):
+        import torch
+        try:
+            self.index = "GPU-" + str(torch.cuda.get_device_properties(device_index).uuid)
+        except Exception:
+            self.index = str(device_index)
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "50"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        self.out = ""
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out, _ = self.proc.communicate()
+        return False
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in (self.out or "").splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 7:
+                continue
+            try:
+                sm.append(float(f[0]))
+                mx.append(float(f[1]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[3:7]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        loaded = sorted(sm)[len(sm) // 4:] or sm   # drop the idle head of the window
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": max(mx),
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------- workload
+def make_layer_caches(torch, kernels, n_layers, S, device, gen, kv="int8"):
+    """n_layers caches [B, Hkv, S, D]: int8 codes + fp32 scales (made by the
+    product's quantizers) or bf16 K/V for the twin."""
+    caches = []
+    for _ in range(n_layers):
+        k = torch.randn((B, HKV, S, D), generator=gen, device=device)
+        ch = torch.stack([torch.randperm(D, generator=gen, device=device)[:4] for _ in range(B * HKV)])
+        gain = torch.ones((B * HKV, D), device=device).scatter_(1, ch, 20.0).view(B, HKV, 1, D)
+        k = (k * gain).to(torch.bfloat16)
+        v = torch.randn((B, HKV, S, D), generator=gen, device=device).to(torch.bfloat16)
+        if kv == "int8":
+            k8, ks = kernels.quant_k_perchannel(k, scale_dtype=torch.float32)
+            v8, vs = kernels.quant_v_pertoken(v, scale_dtype=torch.float32)
+            caches.append((k8, ks, v8, vs))
+        else:
+            caches.append((k, v))
+        del k, v
+    return caches
+
+
+def time_graph(torch, fn, steps, warmup, stream, clocks_index=None):
+    """Capture fn() in a CUDA graph, replay warmup + steps; returns (ms/step, clocks)."""
+    fn()  # first call outside capture: kernel attributes, workspaces
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        fn()
+    for _ in range(warmup):
+        g.replay()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clk = Clocks(clocks_index) if clocks_index is not None else None
+    if clk:
+        clk.__enter__()
+    with torch.cuda.stream(stream):
+        ev0.record(stream)
+        for _ in range(steps):
+            g.replay()
+        ev1.record(stream)
+    torch.cuda.synchronize()
+    if clk:
+        clk.__exit__()
+    del g
+    return ev0.elapsed_time(ev1) / steps, (clk.summary() if clk else None)
+
+
+# ---------------------------------------------------------------- CPU baseline
+def cpu_decode_gbs(seconds=10.0, max_layers=None):
+    """The oracle (numpy restatement of the reference CPU path) on all host
+    cores: decode attention of S=32768 layers, one (layer, kv head) per task."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    import numpy as np
+
+    from oracle import attention as oa
+    from oracle import inputs as oin
+    cores = len(os.sched_getaffinity(0))
+    c = oin.decode_case(0, 1, HQ, HKV, S_HEAD, D, kv_dtype="bf16", q_dtype="bf16")
+    n_rep = HQ // HKV
+
+    def one_head(h):
+        sl = slice(h, h + 1)
+        qs = slice(h * n_rep, (h + 1) * n_rep)
+        return oa.decode_int8(c["q"][:, qs], c["k_i8"][:, sl], c["k_sc"][:, sl], c["v_i8"][:, sl],
+                              c["v_sc"][:, sl], n_rep)
+
+    per_round = max(1, cores // HKV)          # layers decoded concurrently
+    if max_layers:
+        per_round = min(per_round, max_layers)
+    tasks = list(range(HKV)) * per_round
+    layers = 0
+    t0 = time.perf_counter()
+    with ThreadPoolExecutor(max_workers=cores) as ex:
+        while True:
+            list(ex.map(one_head, tasks))
+            layers += per_round
+            el = time.perf_counter() - t0
+            if el >= seconds or (max_layers and layers >= max_layers):
+                break
+    gbs = layers * decode_bytes(B, HQ, HKV, S_HEAD, D) / el / 1e9
+    return gbs, cores, layers, el
+
+
+# ---------------------------------------------------------------- reference arm
+def reference_arm(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    per = []
+    for i in range(args.warmup + args.steps):
+        # one step = one round of (layer, kv head) tasks filling every host core
+        gbs, cores, layers, el = cpu_decode_gbs(seconds=0.0)
+        if i >= args.warmup:
+            per.append(el)
+        if sum(per) > 150:   # keep the whole run within a few minutes
+            break
+    t = sum(per) / len(per)
+    per_step_bytes = layers * decode_bytes(B, HQ, HKV, S_HEAD, D)
+    value = per_step_bytes / t / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": len(per), "warmup": args.warmup,
+        "ms_per_step": round(t * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"decode attention, S={S_HEAD}, B={B}, Hq={HQ}, Hkv={HKV}, D={D}, "
+                               f"int8 K/V + fp32 scales; {layers} layer(s) per step on CPU",
+                   "l2": "n/a (CPU)"},
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": cores, "kind": "port",
+                         "sample": f"{layers} layer(s) of S={S_HEAD} per step, numpy oracle, "
+                                   f"(layer, kv head) tasks on {cores} threads"},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------- our arm
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return reference_arm(args)
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local),
+                                timeout=datetime.timedelta(seconds=120))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    from halftone_quantizedkvcache_b200 import kernels, sharding
+    from halftone_quantizedkvcache_b200.integration import QuantizedKVCache
+    from halftone_quantizedkvcache_b200.integration.quantized_attention import (
+        quantized_attention_forward)
+
+    peak, peak_kind = load_peaks()
+    gen = torch.Generator(device=device).manual_seed(1234 + rank)
+    stream = torch.cuda.Stream(device)
+    caches = make_layer_caches(torch, kernels, LAYERS, S_HEAD, device, gen)
+    q = torch.randn((LAYERS, B, HQ, D), generator=gen, device=device).to(torch.bfloat16)
+    out = torch.empty((LAYERS, B, HQ, D), dtype=torch.bfloat16, device=device)
+    sm_scale = 1.0 / math.sqrt(D)
+    seq = sharding.SequenceShardedDecode(B, HQ, D, device) if world > 1 else None
+
+    def step():
+        for l, (k8, ks, v8, vs) in enumerate(caches):
+            if seq is None:
+                kernels.int8_decode_attn(q[l], k8, ks, v8, vs, HQ // HKV, sm_scale=sm_scale,
+                                         out=out[l])
+            else:
+                seq(q[l], k8, ks, v8, vs, sm_scale=sm_scale, out=out[l])
+
+    with torch.cuda.stream(stream):
+        ms, clocks = time_graph(torch, step, args.steps, args.warmup, stream,
+                                clocks_index=torch.cuda.current_device() if rank == 0 else None)
+    if world > 1:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    per_layer = decode_bytes(B, HQ, HKV, S_HEAD, D)
+    value = world * LAYERS * per_layer / (ms * 1e-3) / 1e9
+    us_layer = ms * 1e3 / LAYERS
+    achieved = per_layer / (us_layer * 1e-6) / 1e9
+
+    # ---- e2e through the public API (cache + patched attention), host buffers
+    e2e = run_e2e(torch, kernels, QuantizedKVCache, quantized_attention_forward, caches, device,
+                  stream, min(args.steps, 100), min(args.warmup, 5), world, dist, seq)
+
+    extras = {}
+    if world == 1 and not args.no_extras:
+        extras = run_extras(torch, kernels, device, gen, stream, us_layer, peak)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic",
+            "config": {"workload": f"decode attention over {LAYERS} layer caches, S={S_HEAD} per "
+                                   f"rank, B={B}, Hq={HQ}, Hkv={HKV}, D={D}, bf16 q, int8 K/V, "
+                                   "fp32 scales",
+                       "l2": f"inputs larger than L2: {LAYERS} caches x "
+                             f"{per_layer / 1e6:.1f} MB read round-robin",
+                       "parallelism": f"sequence-sharded x{world}" if world > 1 else "single GPU",
+                       "graph": "28 launches per step in one CUDA graph"},
+            "us_per_layer": round(us_layer, 3),
+            "frac_of_peak": round(achieved / peak, 4),
+            "frac_of_8tbs": round(achieved / 8000.0, 4),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "traffic": profile_traffic(), "peak_kind": peak_kind,
+                         "kernel": "hq::dec::decode_kernel<2, int8, f32 scales, bf16 q>",
+                         "algorithmic_bytes_per_launch": per_layer},
+            "clocks": clocks or {},
+            "e2e": e2e,
+            "gpu_launches": args.steps * LAYERS * (1 if world == 1 else 2),
+        }
+        line.update(extras)
+        if world == 1:
+            gbs, cores, layers, el = cpu_decode_gbs(seconds=10.0)
+            line["cpu_baseline"] = {
+                "value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": "port",
+                "sample": f"{layers} layers of S={S_HEAD} decode in {el:.1f} s, numpy oracle, "
+                          f"(layer, kv head) tasks on {cores} threads"}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+class _Attn:
+    """The attributes ``quantized_attention_forward`` reads from Qwen3Attention."""
+
+    def __init__(self, n_rep, head_dim):
+        self.num_key_value_groups = n_rep
+        self.head_dim = head_dim
+        self.training = False
+
+
+def run_e2e(torch, kernels, QuantizedKVCache, attn_fwd, caches, device, stream, steps, warmup,
+            world, dist, seq=None):
+    """Public-API decode: per step, per layer ``cache.update`` (append one token)
+    and ``quantized_attention_forward`` (split-KV decode); inputs copied from
+    pinned host memory, outputs copied back, inside the timed region.  With
+    several ranks each rank appends to its own chunk and the attention is the
+    sequence-sharded decode (partials, all_gather, combine)."""
+    import transformers.models.qwen3.modeling_qwen3 as qwen3_mod  # noqa: F401
+    from halftone_quantizedkvcache_b200.integration import quantized_attention as qa
+    module = _Attn(HQ // HKV, D)
+    cache = QuantizedKVCache(mode="fused", capacity=S_HEAD + 2 * (steps + warmup) + 512)
+    # prefill through the public API: dequantize our codes back to bf16 and update()
+    with torch.cuda.stream(stream):
+        for l, (k8, ks, v8, vs) in enumerate(caches):
+            kd = kernels.dequant(k8, ks, torch.bfloat16, per_channel=True)
+            vd = kernels.dequant(v8, vs, torch.bfloat16, per_channel=False)
+            cache.update(kd, vd, l)
+            del kd, vd
+    torch.cuda.synchronize()
+    per_layer_in = (B * HQ * D + 2 * B * HKV * D) * 2
+    h_in = torch.randn((LAYERS, per_layer_in // 2), dtype=torch.float32).to(torch.bfloat16).pin_memory()
+    h_out = torch.empty((LAYERS, B, 1, HQ, D), dtype=torch.bfloat16).pin_memory()
+    d_in = torch.empty_like(h_in, device=device)
+    d_out = torch.empty((LAYERS, B, 1, HQ, D), dtype=torch.bfloat16, device=device)
+    nq, nk = B * HQ * D, B * HKV * D
+
+    def one_step():
+        d_in.copy_(h_in, non_blocking=True)
+        for l in range(LAYERS):
+            qv = d_in[l, :nq].view(B, 1, HQ, D).transpose(1, 2)
+            kn = d_in[l, nq:nq + nk].view(B, 1, HKV, D).transpose(1, 2)
+            vn = d_in[l, nq + nk:].view(B, 1, HKV, D).transpose(1, 2)
+            k, v = cache.update(kn, vn, l)
+            if seq is None:
+                o, _ = attn_fwd(module, qv, k, v, None, scaling=1.0 / math.sqrt(D))
+                d_out[l].copy_(o)
+            else:
+                k8, v8, ks, vs = cache._store[l].codes()
+                seq(qv[:, :, 0, :], k8, ks, v8, vs, sm_scale=1.0 / math.sqrt(D),
+                    q_quant=True, out=d_out[l, :, 0])
+        h_out.copy_(d_out, non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        for _ in range(warmup):
+            one_step()
+        torch.cuda.synchronize()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record(stream)
+        for _ in range(steps):
+            one_step()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1) / steps
+    if world > 1:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    S_mid = S_HEAD + warmup + steps // 2
+    gbs = world * LAYERS * decode_bytes(B, HQ, HKV, S_mid, D, scale_bytes=2) / (ms * 1e-3) / 1e9
+    del cache
+    return {"value": round(gbs, 2), "unit": "GB/s", "h2d_bytes_per_step": LAYERS * per_layer_in,
+            "d2h_bytes_per_step": LAYERS * B * HQ * D * 2, "ms_per_step": round(ms, 4),
+            "path": "QuantizedKVCache.update + quantized_attention_forward per layer, eager "
+                    "(no graph), fp16 cache scales"}
+
+
+def run_extras(torch, kernels, device, gen, stream, us_int8, peak):
+    """bf16-twin speedup at S=32K, the S sweep, bulk quantize-on-write GB/s."""
+    res = {}
+    sm_scale = 1.0 / math.sqrt(D)
+    # -- twin at S=32K (28 bf16 layers: 3.8 GB)
+    twin = make_layer_caches(torch, kernels, LAYERS, S_HEAD, device, gen, kv="bf16")
+    q = torch.randn((LAYERS, B, HQ, D), generator=gen, device=device).to(torch.bfloat16)
+    o = torch.empty_like(q)
+
+    def tstep():
+        for l, (k, v) in enumerate(twin):
+            kernels.fp16_decode_attn(q[l], k, v, HQ // HKV, sm_scale=sm_scale, out=o[l])
+    with torch.cuda.stream(stream):
+        ms, _ = time_graph(torch, tstep, 200, 10, stream)
+    us_bf16 = ms * 1e3 / LAYERS
+    res["bf16_twin_us_per_layer"] = round(us_bf16, 3)
+    res["int8_vs_bf16_speedup"] = round(us_bf16 / us_int8, 3)
+    del twin
+    torch.cuda.empty_cache()
+    # -- sweep
+    sweep = []
+    for S in (64, 512, 4096, 32768, 131072):
+        per8 = decode_bytes(B, HQ, HKV, S, D)
+        n = max(4, min(2048, math.ceil(3 * L2_BYTES / per8)))
+        c8 = make_sweep_caches(torch, n, S, device, gen, "int8")
+        c16 = make_sweep_caches(torch, max(4, min(2048, math.ceil(3 * L2_BYTES / (2 * per8)))),
+                                S, device, gen, "bf16")
+        qq = torch.randn((B, HQ, D), generator=gen, device=device).to(torch.bfloat16)
+        oo = torch.empty_like(qq)
+
+        def s8():
+            for (k8, ks, v8, vs) in c8:
+                kernels.int8_decode_attn(qq, k8, ks, v8, vs, HQ // HKV, sm_scale=sm_scale, out=oo)
+
+        def s16():
+            for (k, v) in c16:
+                kernels.fp16_decode_attn(qq, k, v, HQ // HKV, sm_scale=sm_scale, out=oo)
+        reps = max(3, min(200, int(2e5 / (n * max(1.0, S / 4096)))))
+        with torch.cuda.stream(stream):
+            m8, _ = time_graph(torch, s8, reps, 3, stream)
+            m16, _ = time_graph(torch, s16, reps, 3, stream)
+        u8, u16 = m8 * 1e3 / len(c8), m16 * 1e3 / len(c16)
+        sweep.append({"S": S, "us_int8": round(u8, 3), "us_bf16": round(u16, 3),
+                      "speedup": round(u16 / u8, 3), "gbs_int8": round(per8 / u8 / 1e3, 1),
+                      "layers": len(c8)})
+        del c8, c16
+        torch.cuda.empty_cache()
+    res["decode_sweep"] = sweep
+    # -- bulk quantize-on-write, config B=8, Hkv=8, S=32768, D=128 bf16
+    Bq, Hq_, Sq = 8, 8, 32768
+    k = torch.randn((Bq, Hq_, Sq, D), generator=gen, device=device).to(torch.bfloat16)
+    v = torch.randn((Bq, Hq_, Sq, D), generator=gen, device=device).to(torch.bfloat16)
+    k8 = torch.empty((Bq, Hq_, Sq, D), dtype=torch.int8, device=device)
+    v8 = torch.empty_like(k8)
+    ks = torch.empty((Bq, Hq_, 1, D), dtype=torch.float32, device=device)
+    vs = torch.empty((Bq, Hq_, Sq, 1), dtype=torch.float32, device=device)
+    n = Bq * Hq_ * Sq * D
+    kb = 3 * n + Bq * Hq_ * D * 4
+    vb = 3 * n + Bq * Hq_ * Sq * 4
+    with torch.cuda.stream(stream):
+        mk, _ = time_graph(torch, lambda: kernels.quant_k_perchannel(
+            k, out=k8, scale_dtype=None, scale_f32_out=ks), 20, 3, stream)
+        mv, _ = time_graph(torch, lambda: kernels.quant_v_pertoken(
+            v, out=v8, scale_dtype=None, scale_f32_out=vs), 20, 3, stream)
+    res["quant_write"] = {
+        "workload": "B=8, Hkv=8, S=32768, D=128 bf16 -> int8 + fp32 scales (1.07 GB input, > L2)",
+        "k_gbs": round(kb / (mk * 1e-3) / 1e9, 1), "k_us": round(mk * 1e3, 2),
+        "k_frac_of_peak": round(kb / (mk * 1e-3) / 1e9 / peak, 4),
+        "v_gbs": round(vb / (mv * 1e-3) / 1e9, 1), "v_us": round(mv * 1e3, 2),
+        "v_frac_of_peak": round(vb / (mv * 1e-3) / 1e9 / peak, 4)}
+    # -- 1024 single-token appends (B=8, Hkv=8): fused append kernel latency
+    kn = torch.randn((Bq, Hq_, 1, D), generator=gen, device=device).to(torch.bfloat16)
+    vn = torch.randn((Bq, Hq_, 1, D), generator=gen, device=device).to(torch.bfloat16)
+    vs16 = torch.empty((Bq, Hq_, Sq, 1), dtype=torch.float16, device=device)
+
+    def app():
+        for i in range(1024):
+            p = Sq - 1024 + i
+            kernels.append_kv(kn, vn, k8[:, :, p:p + 1], v8[:, :, p:p + 1],
+                              v_scale_dst=vs16[:, :, p:p + 1])
+    with torch.cuda.stream(stream):
+        ma, _ = time_graph(torch, app, 5, 2, stream)
+    res["quant_write"]["append_us"] = round(ma * 1e3 / 1024, 3)
+    del k, v, k8, v8
+    torch.cuda.empty_cache()
+    return res
+
+
+def make_sweep_caches(torch, n, S, device, gen, kind):
+    out = []
+    for _ in range(n):
+        if kind == "int8":
+            k8 = torch.randint(-127, 128, (B, HKV, S, D), generator=gen, device=device,
+                               dtype=torch.int8)
+            v8 = torch.randint(-127, 128, (B, HKV, S, D), generator=gen, device=device,
+                               dtype=torch.int8)
+            ks = torch.rand((B, HKV, 1, D), generator=gen, device=device) * 0.1
+            vs = torch.rand((B, HKV, S, 1), generator=gen, device=device) * 0.02
+            out.append((k8, ks, v8, vs))
+        else:
+            k = torch.randn((B, HKV, S, D), generator=gen, device=device).to(torch.bfloat16)
+            v = torch.randn((B, HKV, S, D), generator=gen, device=device).to(torch.bfloat16)
+            out.append((k, v))
+    return out
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,236 @@
+// Shared device helpers for the Halftone int8 KV-cache kernels (sm_100a).
+//
+// Contents:
+//   * element-type traits (bf16 / f16 / f32 inputs, int8 codes);
+//   * the guarded symmetric-int8 quantizer used by every quantize-on-write
+//     kernel (bit-exact with the float32 IEEE reference rule
+//     scale = max(amax, 1e-8) / 127, code = clamp(rint(x / scale), -127, 127));
+//   * int8 -> float conversion by byte permute (Kim et al., "Who Says
+//     Elephants Can't Run", 2022: place the biased byte under the exponent of
+//     2^23 and subtract);
+//   * packed f32x2 arithmetic (sm_100 `fma.rn.f32x2` / `add.rn.f32x2`);
+//   * mbarrier + cp.async.bulk (1-D TMA) helpers with bounded waits.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/halftone_b200.h"
+
+namespace hq {
+
+// ---------------------------------------------------------------- element types
+template <int DT> struct Elem;
+template <> struct Elem<HQ_DTYPE_F32> {
+  using T = float;
+  static constexpr int kBytes = 4;
+  __device__ __forceinline__ static float to_f32(T v) { return v; }
+  __device__ __forceinline__ static T from_f32(float v) { return v; }
+};
+template <> struct Elem<HQ_DTYPE_BF16> {
+  using T = __nv_bfloat16;
+  static constexpr int kBytes = 2;
+  __device__ __forceinline__ static float to_f32(T v) { return __bfloat162float(v); }
+  __device__ __forceinline__ static T from_f32(float v) { return __float2bfloat16_rn(v); }
+};
+template <> struct Elem<HQ_DTYPE_F16> {
+  using T = __half;
+  static constexpr int kBytes = 2;
+  __device__ __forceinline__ static float to_f32(T v) { return __half2float(v); }
+  __device__ __forceinline__ static T from_f32(float v) { return __float2half_rn(v); }
+};
+
+// Unpack one 16-byte vector of DT elements into floats (8 for 16-bit types, 4 for f32).
+template <int DT> struct Vec16;
+template <> struct Vec16<HQ_DTYPE_BF16> {
+  static constexpr int N = 8;
+  __device__ __forceinline__ static void unpack(const uint4& v, float* f) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      f[2 * i] = __uint_as_float(w[i] << 16);
+      f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+    }
+  }
+};
+template <> struct Vec16<HQ_DTYPE_F16> {
+  static constexpr int N = 8;
+  __device__ __forceinline__ static void unpack(const uint4& v, float* f) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      __half2 h = *reinterpret_cast<const __half2*>(&w[i]);
+      float2 p = __half22float2(h);
+      f[2 * i] = p.x;
+      f[2 * i + 1] = p.y;
+    }
+  }
+};
+template <> struct Vec16<HQ_DTYPE_F32> {
+  static constexpr int N = 4;
+  __device__ __forceinline__ static void unpack(const uint4& v, float* f) {
+    f[0] = __uint_as_float(v.x);
+    f[1] = __uint_as_float(v.y);
+    f[2] = __uint_as_float(v.z);
+    f[3] = __uint_as_float(v.w);
+  }
+};
+
+// ---------------------------------------------------------------- quantizer
+// Reference rule (float32 IEEE):  scale = max(amax, 1e-8f) / 127  (true divide)
+//                                 code  = clamp(rint_even(RN(x / scale)), -127, 127)
+//
+// Fast path: r = RN(1 / scale) once per row / column; per element one FFMA
+// y = x * r + 1.5 * 2^23 rounds the exact product x * r to an integer k
+// (ties to even), and d = fma(x, r, -k) is its exact-product residual.
+// |x * r - RN(x / scale)| <= 127.5 * 2^-24 + 2^-18 < 2^-15 for |x| <= amax,
+// so k can differ from the reference code only when |d| > 0.5 - 2^-15; those
+// elements (about 1e-3 of bf16 inputs) redo the true IEEE divide.  The
+// equivalence is checked exhaustively for every bf16 and fp16 (x, amax) pair by
+// tests/test_quant_rounding_model.py and on the GPU by the parity tests.
+struct Quantizer {
+  float scale;  // RN(amax / 127)
+  float rcp;    // RN(1 / scale)
+  __device__ __forceinline__ static Quantizer from_amax(float amax) {
+    Quantizer q;
+    q.scale = __fdiv_rn(fmaxf(amax, 1e-8f), 127.0f);
+    q.rcp = __frcp_rn(q.scale);
+    return q;
+  }
+  // Returns the code as an int in [-127, 127].
+  __device__ __forceinline__ int code(float x) const {
+    const float kMagic = 12582912.0f;  // 1.5 * 2^23
+    float y = __fmaf_rn(x, rcp, kMagic);
+    float k = y - kMagic;
+    float d = __fmaf_rn(x, rcp, -k);
+    int c = static_cast<int>(__float_as_uint(y) - 0x4B400000u);
+    if (fabsf(d) > 0.499969482421875f) {  // 0.5 - 2^-15: redo with the IEEE divide
+      float e = rintf(__fdiv_rn(x, scale));
+      e = fminf(fmaxf(e, -127.0f), 127.0f);
+      c = static_cast<int>(e);
+    }
+    return c;
+  }
+};
+
+__device__ __forceinline__ uint32_t pack4_s8(int a, int b, int c, int d) {
+  return (static_cast<uint32_t>(a) & 0xffu) | ((static_cast<uint32_t>(b) & 0xffu) << 8) |
+         ((static_cast<uint32_t>(c) & 0xffu) << 16) | (static_cast<uint32_t>(d) << 24);
+}
+
+// ---------------------------------------------------------------- int8 -> f32
+// Byte i of w (a signed int8) becomes float exactly: flip the sign bit
+// (b + 128 as an unsigned byte), place it in the low mantissa byte of 2^23,
+// and subtract 2^23 + 128.
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+  return d;
+}
+
+// Converts 4 int8 in w to 4 floats, returned as two packed f32x2 (lo pair, hi pair).
+struct F2 {
+  unsigned long long v;
+};
+__device__ __forceinline__ F2 f2_make(float a, float b) {
+  F2 r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r.v) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2_split(F2 x, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(x.v));
+}
+__device__ __forceinline__ F2 f2_fma(F2 a, F2 b, F2 c) {
+  F2 d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d.v) : "l"(a.v), "l"(b.v), "l"(c.v));
+  return d;
+}
+__device__ __forceinline__ F2 f2_add(F2 a, F2 b) {
+  F2 d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d.v) : "l"(a.v), "l"(b.v));
+  return d;
+}
+__device__ __forceinline__ F2 f2_mul(F2 a, F2 b) {
+  F2 d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d.v) : "l"(a.v), "l"(b.v));
+  return d;
+}
+
+__device__ __forceinline__ void s8x4_to_f2x2(uint32_t w, F2& lo, F2& hi) {
+  const uint32_t kExp = 0x4B000000u;
+  const uint32_t u = w ^ 0x80808080u;
+  F2 a, b;
+  a.v = (static_cast<unsigned long long>(prmt(u, kExp, 0x7651u)) << 32) | prmt(u, kExp, 0x7650u);
+  b.v = (static_cast<unsigned long long>(prmt(u, kExp, 0x7653u)) << 32) | prmt(u, kExp, 0x7652u);
+  const F2 bias = f2_make(-8388736.0f, -8388736.0f);  // -(2^23 + 128)
+  lo = f2_add(a, bias);
+  hi = f2_add(b, bias);
+}
+
+// bf16 pair word -> packed f32x2 (exact)
+__device__ __forceinline__ F2 bf16x2_to_f2(uint32_t w) {
+  F2 r;
+  r.v = (static_cast<unsigned long long>(w & 0xffff0000u) << 32) | (w << 16);
+  return r;
+}
+__device__ __forceinline__ F2 f16x2_to_f2(uint32_t w) {
+  __half2 h = *reinterpret_cast<const __half2*>(&w);
+  float2 p = __half22float2(h);
+  return f2_make(p.x, p.y);
+}
+
+// ---------------------------------------------------------------- mbarrier / bulk copy
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait: returns false after kSpinLimit polls (each try_wait itself
+// suspends for a hardware-defined interval), never hangs.
+constexpr uint32_t kSpinLimit = 1u << 22;
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kSpinLimit; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  return false;
+}
+// 1-D bulk copy global -> shared (no tensor map, no multicast); `bytes` and
+// both addresses must be multiples of 16.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,
+                                         uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Records a device-side error in the caller's status word (first error wins).
+__device__ __forceinline__ void report_error(int* status, int code) {
+  if (status) atomicCAS(status, 0, code);
+}
+
+}  // namespace hq

@@ -1,0 +1,275 @@
+"""Drop-in surface of the reference: an int8 HF cache and the patched Qwen3 attention.
+
+* ``QuantizedKVCache`` keeps the API of the reference class
+  (tests/qwen_kvcache_full.py:27-89): no-argument constructor,
+  ``update(key_states, value_states, layer_idx, cache_kwargs=None)``,
+  ``get_seq_length``, ``__len__``, ``storage_bytes``, ``fp16_equiv_bytes`` and
+  the per-layer dicts ``_k_i8 / _v_i8 / _k_sc / _v_sc / _lens`` (int8
+  ``[B,H,S,D]`` codes, fp16 scales ``[B,H,1,D]`` and ``[B,H,S,1]``).
+  Storage is a preallocated capacity buffer per layer (no ``torch.cat``);
+  the prefill is quantized by the CUDA K-per-channel / V-per-token kernels and
+  every later update by the fused append kernel, with the reference's rule
+  (the first K scale is kept, tests/qwen_kvcache_full.py:54).
+* ``quantized_attention_forward`` has the signature of the reference's patch
+  (tests/qwen_kvcache_full.py:95-113).  For a decode step over this cache it
+  runs the split-KV int8 CUDA kernel directly on the codes (with the
+  per-token q fake quantization of ``Q_DIMS = (3,)`` fused into its
+  prologue); for a prefill it dequantizes the cache with the CUDA dequant
+  kernel and evaluates the reference's attention math.
+
+What ``update`` returns follows ``mode``:
+  ``"dequant"`` - the whole cache dequantized to the model dtype, exactly the
+                  reference's return value (lines 64-66); works with any
+                  attention implementation;
+  ``"fused"``   - int8 code views tagged with the layer's storage, consumed by
+                  ``quantized_attention_forward`` without any dequantization;
+  ``"auto"``    - ``"fused"`` while ``quantized_attention_forward`` is installed
+                  as Qwen3's eager attention, else ``"dequant"``.
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+from transformers.cache_utils import DynamicCache
+
+from .. import kernels
+
+Q_DIMS = (3,)  # per-token q fake quantization, as the reference default (line 93)
+_ALIGN = 256   # token capacity granularity
+
+
+def _round_up(n: int, m: int) -> int:
+    return (n + m - 1) // m * m
+
+
+class _LayerStore:
+    """Capacity buffers of one layer: codes ``[B,H,cap,D]``, fp16 scales."""
+
+    __slots__ = ("k", "v", "k_sc", "v_sc", "length")
+
+    def __init__(self, B, H, D, cap, device):
+        self.k = torch.empty((B, H, cap, D), dtype=torch.int8, device=device)
+        self.v = torch.empty((B, H, cap, D), dtype=torch.int8, device=device)
+        self.k_sc = torch.empty((B, H, 1, D), dtype=torch.float16, device=device)
+        self.v_sc = torch.empty((B, H, cap, 1), dtype=torch.float16, device=device)
+        self.length = 0
+
+    @property
+    def capacity(self) -> int:
+        return self.k.shape[2]
+
+    def reserve(self, n: int) -> None:
+        if n <= self.capacity:
+            return
+        B, H, cap, D = self.k.shape
+        new = _LayerStore(B, H, D, _round_up(max(2 * cap, n), _ALIGN), self.k.device)
+        L = self.length
+        new.k[:, :, :L].copy_(self.k[:, :, :L])
+        new.v[:, :, :L].copy_(self.v[:, :, :L])
+        new.v_sc[:, :, :L].copy_(self.v_sc[:, :, :L])
+        new.k_sc.copy_(self.k_sc)
+        self.k, self.v, self.k_sc, self.v_sc = new.k, new.v, new.k_sc, new.v_sc
+
+    def codes(self):
+        L = self.length
+        return self.k[:, :, :L], self.v[:, :, :L], self.k_sc, self.v_sc[:, :, :L]
+
+
+def _tag(t: torch.Tensor, store: _LayerStore) -> torch.Tensor:
+    t._hq_store = store
+    return t
+
+
+class QuantizedKVCache(DynamicCache):
+    """int8 KV cache, drop-in for the reference's ``QuantizedKVCache``."""
+
+    def __init__(self, mode: str = "auto", capacity: int | None = None):
+        super().__init__()
+        if mode not in ("auto", "fused", "dequant"):
+            raise ValueError(f"mode must be auto, fused or dequant, not {mode!r}")
+        self.mode = mode
+        self.capacity = capacity
+        self._store: dict[int, _LayerStore] = {}
+
+    # -- reference-compatible views (tests/qwen_kvcache_full.py:34-36)
+    @property
+    def _k_i8(self):
+        return {i: s.k[:, :, : s.length] for i, s in self._store.items()}
+
+    @property
+    def _v_i8(self):
+        return {i: s.v[:, :, : s.length] for i, s in self._store.items()}
+
+    @property
+    def _k_sc(self):
+        return {i: s.k_sc for i, s in self._store.items()}
+
+    @property
+    def _v_sc(self):
+        return {i: s.v_sc[:, :, : s.length] for i, s in self._store.items()}
+
+    @property
+    def _lens(self):
+        return {i: s.length for i, s in self._store.items()}
+
+    def _fused(self) -> bool:
+        return self.mode == "fused" or (self.mode == "auto" and is_installed())
+
+    def update(self, key_states, value_states, layer_idx, cache_kwargs=None):
+        """Quantize the new K/V into the layer's int8 storage (tests/qwen_kvcache_full.py:38-66)."""
+        if key_states.shape != value_states.shape:
+            raise ValueError("QuantizedKVCache.update: key and value shapes differ")
+        B, H, S_new, D = key_states.shape
+        st = self._store.get(layer_idx)
+        if st is None:
+            cap = _round_up(max(S_new + _ALIGN, self.capacity or 0), _ALIGN)
+            st = _LayerStore(B, H, D, cap, key_states.device)
+            kernels.quant_k_perchannel(key_states, out=st.k[:, :, :S_new], scale_out=st.k_sc)
+            kernels.quant_v_pertoken(value_states, out=st.v[:, :, :S_new],
+                                     scale_out=st.v_sc[:, :, :S_new])
+            st.length = S_new
+            self._store[layer_idx] = st
+        else:
+            if st.k.shape[0] != B or st.k.shape[1] != H or st.k.shape[3] != D:
+                raise ValueError("QuantizedKVCache.update: batch/head shape changed for this layer")
+            L = st.length
+            st.reserve(L + S_new)
+            kdst, vdst = st.k[:, :, L:L + S_new], st.v[:, :, L:L + S_new]
+            vsc = st.v_sc[:, :, L:L + S_new]
+            if S_new <= 64:
+                kernels.append_kv(key_states, value_states, kdst, vdst, v_scale_dst=vsc)
+            else:
+                # codes with the new tokens' own per-channel scale; that scale is not kept
+                kernels.quant_k_perchannel(key_states, out=kdst, scale_dtype=None)
+                kernels.quant_v_pertoken(value_states, out=vdst, scale_out=vsc)
+            st.length = L + S_new
+        k, v, k_sc, v_sc = st.codes()
+        if self._fused():
+            return _tag(k.view(k.shape), st), _tag(v.view(v.shape), st)
+        return (kernels.dequant(k, k_sc, key_states.dtype, per_channel=True),
+                kernels.dequant(v, v_sc, value_states.dtype, per_channel=False))
+
+    def get_seq_length(self, layer_idx=0, cache_position=None):
+        st = self._store.get(layer_idx)
+        return st.length if st is not None else 0
+
+    def __len__(self):
+        return len(self._store)
+
+    def storage_bytes(self):
+        """int8 codes at 1 B, fp16 scales at 2 B (tests/qwen_kvcache_full.py:75-82)."""
+        b = 0
+        for s in self._store.values():
+            b += 2 * s.k[:, :, : s.length].numel()
+            b += 2 * (s.k_sc.numel() + s.v_sc[:, :, : s.length].numel())
+        return b
+
+    def fp16_equiv_bytes(self):
+        """Same K/V held in fp16 (tests/qwen_kvcache_full.py:84-89)."""
+        return sum(4 * s.k[:, :, : s.length].numel() for s in self._store.values())
+
+
+# ---------------------------------------------------------------- attention patch
+def _fake_quant(x: torch.Tensor, dims) -> torch.Tensor:
+    """tests/qwen_kvcache_full.py:19-23, with IEEE true divisions on the GPU."""
+    xf = x.float()
+    amax = xf.abs().amax(dim=dims, keepdim=True).clamp(min=1e-8)
+    scale = amax / torch.full((), 127.0, device=x.device)
+    codes = torch.clamp(torch.round(xf / scale), -127, 127)
+    return (codes * scale).to(x.dtype)
+
+
+def _reference_math(module, q, key, value, attention_mask, scaling, dropout):
+    """The reference's attention math (tests/qwen_kvcache_full.py:104-113)."""
+    n_rep = module.num_key_value_groups
+    k = key if n_rep == 1 else key.repeat_interleave(n_rep, dim=1)
+    v = value if n_rep == 1 else value.repeat_interleave(n_rep, dim=1)
+    scores = torch.matmul(q, k.transpose(2, 3)) * scaling
+    if attention_mask is not None:
+        m = attention_mask[:, :, :, : k.shape[-2]]
+        if m.shape[-1] != k.shape[-2] and m.shape[-1] != 1:
+            # an append of several tokens onto a cache: causal over the whole cache
+            Sq, Sk = q.shape[2], k.shape[2]
+            pos_q = torch.arange(Sk - Sq, Sk, device=q.device)[:, None]
+            allowed = torch.arange(Sk, device=q.device)[None, :] <= pos_q
+            m = torch.zeros((Sq, Sk), dtype=scores.dtype, device=q.device).masked_fill(
+                ~allowed, torch.finfo(scores.dtype).min)
+        scores = scores + m
+    attn = F.softmax(scores, dim=-1, dtype=torch.float32).to(q.dtype)
+    attn = F.dropout(attn, p=dropout, training=module.training)
+    return torch.matmul(attn, v).transpose(1, 2).contiguous()
+
+
+def quantized_attention_forward(module, query, key, value, attention_mask, scaling=None,
+                                dropout=0.0, **kwargs):
+    """Replacement for Qwen3's ``eager_attention_forward`` (tests/qwen_kvcache_full.py:95-113).
+
+    Returns ``(attn_output [B, Sq, Hq, D], None)``.
+    """
+    if scaling is None:
+        scaling = module.head_dim ** -0.5
+    st = getattr(key, "_hq_store", None)
+    B, Hq, Sq, D = query.shape
+    if st is not None and Sq == 1 and not (module.training and dropout > 0.0):
+        if attention_mask is not None and attention_mask.shape[-1] not in (1, st.length):
+            raise ValueError("quantized_attention_forward: unexpected decode mask width")
+        q_quant = Q_DIMS is not None and tuple(Q_DIMS) == (3,)
+        q = query if (Q_DIMS is None or q_quant) else _fake_quant(query, Q_DIMS)
+        k, v, k_sc, v_sc = st.codes()
+        out = torch.empty((B, 1, Hq, D), dtype=query.dtype, device=query.device)
+        if attention_mask is not None and attention_mask.shape[-1] == st.length and st.length > 1:
+            if bool((attention_mask != 0).any()):
+                raise NotImplementedError("padded decode masks are not supported by the int8 kernel")
+        kernels.int8_decode_attn(q[:, :, 0, :], k, k_sc, v, v_sc, module.num_key_value_groups,
+                                 sm_scale=scaling, q_quant=q_quant, out=out[:, 0])
+        return out, None
+    if st is not None:
+        k, v, k_sc, v_sc = st.codes()
+        key = kernels.dequant(k, k_sc, query.dtype, per_channel=True)
+        value = kernels.dequant(v, v_sc, query.dtype, per_channel=False)
+    q = _fake_quant(query, Q_DIMS) if Q_DIMS is not None else query
+    return _reference_math(module, q, key, value, attention_mask, scaling, dropout), None
+
+
+# ---------------------------------------------------------------- installation
+_saved = {}
+
+
+def install(module=None) -> None:
+    """Install ``quantized_attention_forward`` as Qwen3's eager attention
+    (the reference assigns the module global, tests/qwen_kvcache_full.py:161)."""
+    if module is None:
+        import transformers.models.qwen3.modeling_qwen3 as module
+    if module.eager_attention_forward is not quantized_attention_forward:
+        _saved[module.__name__] = module.eager_attention_forward
+        module.eager_attention_forward = quantized_attention_forward
+
+
+def uninstall(module=None) -> None:
+    """Restore the original eager attention (tests/qwen_kvcache_full.py:186)."""
+    if module is None:
+        import transformers.models.qwen3.modeling_qwen3 as module
+    orig = _saved.pop(module.__name__, None)
+    if orig is not None:
+        module.eager_attention_forward = orig
+
+
+def is_installed(module=None) -> bool:
+    if module is None:
+        import transformers.models.qwen3.modeling_qwen3 as module
+    return module.eager_attention_forward is quantized_attention_forward
+
+
+class installed:
+    """Context manager around ``install`` / ``uninstall``."""
+
+    def __init__(self, module=None):
+        self.module = module
+
+    def __enter__(self):
+        install(self.module)
+        return self
+
+    def __exit__(self, *exc):
+        uninstall(self.module)
+        return False

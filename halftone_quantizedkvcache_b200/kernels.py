@@ -1,0 +1,362 @@
+"""torch-facing ops over the C ABI (device memory and streams from PyTorch).
+
+Mirrors the reference's kernel API (src/kernels/quant_kv_triton.py:90-117,
+src/kernels/int8_decode_attn_triton.py:101-127) with the same names minus the
+``_triton`` suffix, the same argument meaning and the same output shapes and
+dtypes:
+
+* ``quant_k_perchannel(x)`` -> (int8 ``[B,H,S,D]``, fp16 scale ``[B,H,1,D]``)
+* ``quant_v_pertoken(x)``   -> (int8 ``[B,H,S,D]``, fp16 scale ``[B,H,S,1]``)
+* ``int8_decode_attn(q, k_i8, k_sc, v_i8, v_sc, n_rep)`` -> ``[H_q,1,D]`` (or batched)
+* ``fp16_decode_attn(q, k, v, n_rep)`` -> the dense twin (fp16 or bf16 K/V)
+
+plus what the cache and the sharded decode need (``append_kv``, ``dequant``,
+``decode_partials``, ``decode_combine``).  Every op runs on the current CUDA
+stream of the input's device and raises on bad input; there is no CPU path.
+"""
+from __future__ import annotations
+
+import math
+import threading
+
+import torch
+
+from . import _lib
+from ._lib import DTYPE_BF16, DTYPE_F16, DTYPE_F32, check
+
+_DT = {torch.float32: DTYPE_F32, torch.bfloat16: DTYPE_BF16, torch.float16: DTYPE_F16}
+
+
+def _dtype_code(t: torch.Tensor, what: str) -> int:
+    try:
+        return _DT[t.dtype]
+    except KeyError:
+        raise TypeError(f"{what}: unsupported dtype {t.dtype} (float32, bfloat16, float16)") from None
+
+
+def _cuda(t: torch.Tensor, what: str) -> None:
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise ValueError(f"{what}: expected a CUDA tensor (there is no CPU path)")
+
+
+def _stream(dev: torch.device) -> int:
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _rows_ok(t: torch.Tensor) -> bool:
+    """[..., D] with unit inner stride and 16-byte aligned rows."""
+    es = t.element_size()
+    return (t.stride(-1) == 1 and t.data_ptr() % 16 == 0 and
+            all((s * es) % 16 == 0 for s in t.stride()[:-1]))
+
+
+def _rowmajor(t: torch.Tensor) -> torch.Tensor:
+    return t if _rows_ok(t) else t.contiguous()
+
+
+# ---------------------------------------------------------------- workspaces
+class _Workspaces:
+    """Per (device, stream, kind) scratch buffers, grown on demand.
+
+    Decode workspaces must be zero when first used (arrival tickets); the
+    kernel leaves them zero again, so they are zero-filled only when allocated.
+    """
+
+    def __init__(self):
+        self._bufs: dict = {}
+        self._lock = threading.Lock()
+
+    def get(self, dev: torch.device, kind: str, nbytes: int) -> torch.Tensor:
+        key = (dev.index, _stream(dev), kind)
+        with self._lock:
+            buf = self._bufs.get(key)
+            if buf is None or buf.numel() < nbytes:
+                buf = torch.zeros(max(nbytes, 4096), dtype=torch.uint8, device=dev)
+                self._bufs[key] = buf
+            return buf
+
+
+WORKSPACES = _Workspaces()
+
+
+# ---------------------------------------------------------------- quantize-on-write
+def _check_bhsd(x: torch.Tensor, what: str) -> None:
+    _cuda(x, what)
+    if x.dim() != 4:
+        raise ValueError(f"{what}: expected [B, H, S, D], got {tuple(x.shape)}")
+    if x.shape[2] < 1:
+        raise ValueError(f"{what}: S must be >= 1 (the reference's amax over an empty axis raises)")
+
+
+def quant_k_perchannel(x: torch.Tensor, *, out: torch.Tensor | None = None,
+                       scale_dtype: torch.dtype | None = torch.float16,
+                       scale_out: torch.Tensor | None = None,
+                       scale_f32_out: torch.Tensor | None = None):
+    """K per channel: absmax over S of ``x [B,H,S,D]`` -> (int8 codes, scale ``[B,H,1,D]``).
+
+    Same contract as ``quant_k_perchannel_triton`` (src/kernels/quant_kv_triton.py:90-102):
+    scale returned as float16 by default; ``scale_dtype=torch.float32`` returns
+    the float32 scale of ``quantize_int8`` (reference/page_attention_int8_pytorch.py:23-30);
+    ``scale_dtype=None`` writes no scale.  ``out`` / ``scale_out`` /
+    ``scale_f32_out`` write into caller buffers (``out`` may be a strided view).
+    """
+    _check_bhsd(x, "quant_k_perchannel")
+    B, H, S, D = x.shape
+    x = _rowmajor(x)
+    q = out if out is not None else torch.empty((B, H, S, D), dtype=torch.int8, device=x.device)
+    if q.shape != x.shape or q.dtype != torch.int8 or q.device != x.device:
+        raise ValueError("quant_k_perchannel: out must be int8 with x's shape and device")
+    s16 = scale_out
+    s32 = scale_f32_out
+    if s16 is None and scale_dtype == torch.float16:
+        s16 = torch.empty((B, H, 1, D), dtype=torch.float16, device=x.device)
+    if s32 is None and scale_dtype == torch.float32:
+        s32 = torch.empty((B, H, 1, D), dtype=torch.float32, device=x.device)
+    for t, dt in ((s16, torch.float16), (s32, torch.float32)):
+        if t is not None and (t.dtype != dt or not t.is_contiguous() or t.numel() != B * H * D):
+            raise ValueError("quant_k_perchannel: scale buffers must be contiguous [B,H,1,D]")
+    wsb = _lib.lib().hq_quant_k_workspace_bytes(B, H, D)
+    ws = WORKSPACES.get(x.device, "quant_k", wsb)
+    rc = _lib.lib().hq_quant_k_perchannel(
+        x.data_ptr(), _dtype_code(x, "quant_k_perchannel"), _lib.strides(x.stride(), 4), B, H, S,
+        D, q.data_ptr(), _lib.strides(q.stride(), 4), s32.data_ptr() if s32 is not None else None,
+        s16.data_ptr() if s16 is not None else None, ws.data_ptr(), ws.numel(),
+        _stream(x.device))
+    check(rc, "hq_quant_k_perchannel")
+    if scale_dtype == torch.float32:
+        return q, s32
+    return q, s16
+
+
+def quant_v_pertoken(x: torch.Tensor, *, out: torch.Tensor | None = None,
+                     scale_dtype: torch.dtype | None = torch.float16,
+                     scale_out: torch.Tensor | None = None,
+                     scale_f32_out: torch.Tensor | None = None):
+    """V per token: absmax over D of ``x [B,H,S,D]`` -> (int8 codes, scale ``[B,H,S,1]``).
+
+    Same contract as ``quant_v_pertoken_triton`` (src/kernels/quant_kv_triton.py:105-117);
+    options as ``quant_k_perchannel``.  Scale buffers may be strided ``[B,H,S,1]`` views.
+    """
+    _check_bhsd(x, "quant_v_pertoken")
+    B, H, S, D = x.shape
+    x = _rowmajor(x)
+    q = out if out is not None else torch.empty((B, H, S, D), dtype=torch.int8, device=x.device)
+    if q.shape != x.shape or q.dtype != torch.int8 or q.device != x.device:
+        raise ValueError("quant_v_pertoken: out must be int8 with x's shape and device")
+    s16 = scale_out
+    s32 = scale_f32_out
+    if s16 is None and scale_dtype == torch.float16:
+        s16 = torch.empty((B, H, S, 1), dtype=torch.float16, device=x.device)
+    if s32 is None and scale_dtype == torch.float32:
+        s32 = torch.empty((B, H, S, 1), dtype=torch.float32, device=x.device)
+    ref = s16 if s16 is not None else s32
+    if s16 is not None and s32 is not None and s16.stride() != s32.stride():
+        raise ValueError("quant_v_pertoken: both scale buffers must share strides")
+    for t, dt in ((s16, torch.float16), (s32, torch.float32)):
+        if t is not None and (t.dtype != dt or tuple(t.shape) != (B, H, S, 1)):
+            raise ValueError("quant_v_pertoken: scale buffers must be [B,H,S,1]")
+    sst = _lib.strides(ref.stride()[:3], 3) if ref is not None else None
+    rc = _lib.lib().hq_quant_v_pertoken(
+        x.data_ptr(), _dtype_code(x, "quant_v_pertoken"), _lib.strides(x.stride(), 4), B, H, S, D,
+        q.data_ptr(), _lib.strides(q.stride(), 4), s32.data_ptr() if s32 is not None else None,
+        s16.data_ptr() if s16 is not None else None, sst, _stream(x.device))
+    check(rc, "hq_quant_v_pertoken")
+    if scale_dtype == torch.float32:
+        return q, s32
+    return q, s16
+
+
+def append_kv(k_new: torch.Tensor, v_new: torch.Tensor, k_dst: torch.Tensor, v_dst: torch.Tensor,
+              v_scale_dst: torch.Tensor | None = None,
+              v_scale_f32_dst: torch.Tensor | None = None) -> None:
+    """Append ``S_new <= 64`` tokens with the reference update rule in one launch.
+
+    New K codes use the per-channel scale of the new tokens (not stored: the
+    cache keeps its first K scale, tests/qwen_kvcache_full.py:54); V codes use
+    per-token scales written to ``v_scale_dst`` (fp16 ``[B,H,S_new,1]`` view)
+    and/or ``v_scale_f32_dst``.  ``k_dst`` / ``v_dst`` are int8 views of the
+    cache rows at the append position.
+    """
+    _check_bhsd(k_new, "append_kv")
+    _check_bhsd(v_new, "append_kv")
+    if k_new.shape != v_new.shape or k_new.dtype != v_new.dtype:
+        raise ValueError("append_kv: key and value must match in shape and dtype")
+    B, H, S_new, D = k_new.shape
+    if S_new > 64:
+        raise ValueError("append_kv: at most 64 new tokens per call")
+    for t in (k_dst, v_dst):
+        if tuple(t.shape) != (B, H, S_new, D) or t.dtype != torch.int8 or t.stride(-1) != 1:
+            raise ValueError("append_kv: destinations must be int8 [B,H,S_new,D] views")
+    k_new = k_new if k_new.stride(-1) == 1 else k_new.contiguous()
+    v_new = v_new if v_new.stride(-1) == 1 else v_new.contiguous()
+    ref = v_scale_dst if v_scale_dst is not None else v_scale_f32_dst
+    sst = _lib.strides(ref.stride()[:3], 3) if ref is not None else None
+    rc = _lib.lib().hq_append_kv(
+        k_new.data_ptr(), v_new.data_ptr(), _dtype_code(k_new, "append_kv"),
+        _lib.strides(k_new.stride(), 4), _lib.strides(v_new.stride(), 4), B, H, S_new, D,
+        k_dst.data_ptr(), _lib.strides(k_dst.stride(), 4), v_dst.data_ptr(),
+        _lib.strides(v_dst.stride(), 4),
+        v_scale_f32_dst.data_ptr() if v_scale_f32_dst is not None else None,
+        v_scale_dst.data_ptr() if v_scale_dst is not None else None, sst, _stream(k_new.device))
+    check(rc, "hq_append_kv")
+
+
+def dequant(q: torch.Tensor, scale: torch.Tensor, dtype: torch.dtype, per_channel: bool,
+            out: torch.Tensor | None = None) -> torch.Tensor:
+    """``dtype(float(q) * float(scale))`` for an int8 cache tensor ``[B,H,S,D]``.
+
+    tests/qwen_kvcache_full.py:64-65; ``scale`` is ``[B,H,1,D]`` (K, per channel)
+    or ``[B,H,S,1]`` (V, per token), float16 or float32.
+    """
+    _cuda(q, "dequant")
+    B, H, S, D = q.shape
+    if out is None:
+        out = torch.empty((B, H, S, D), dtype=dtype, device=q.device)
+    if per_channel:
+        sst = (scale.stride(0), scale.stride(1), scale.stride(3))
+    else:
+        sst = (scale.stride(0), scale.stride(1), scale.stride(2))
+    rc = _lib.lib().hq_dequant(
+        q.data_ptr(), _lib.strides(q.stride(), 4), B, H, S, D, scale.data_ptr(),
+        _dtype_code(scale, "dequant scale"), _lib.strides(sst, 3), int(per_channel),
+        out.data_ptr(), _dtype_code(out, "dequant out"), _lib.strides(out.stride(), 4),
+        _stream(q.device))
+    check(rc, "hq_dequant")
+    return out
+
+
+# ---------------------------------------------------------------- decode attention
+def _as_bhd(q: torch.Tensor):
+    """q ``[Hq,1,D]`` / ``[B,Hq,1,D]`` / ``[B,Hq,D]`` -> (view ``[B,Hq,D]``, restore fn)."""
+    if q.dim() == 3 and q.shape[1] == 1:          # reference layout [H_q, 1, D]
+        return q[:, 0, :].unsqueeze(0), lambda o: o[0].unsqueeze(1)
+    if q.dim() == 4 and q.shape[2] == 1:          # [B, H_q, 1, D]
+        return q[:, :, 0, :], lambda o: o.unsqueeze(2)
+    if q.dim() == 3:                              # [B, H_q, D]
+        return q, lambda o: o
+    raise ValueError(f"decode: q must be [Hq,1,D], [B,Hq,1,D] or [B,Hq,D], got {tuple(q.shape)}")
+
+
+def _as_bhsd(t: torch.Tensor):
+    return t.unsqueeze(0) if t.dim() == 3 else t
+
+
+def _decode_ws(dev, B, Hq, Hkv, S, D):
+    nb = _lib.lib().hq_decode_workspace_bytes(B, Hq, Hkv, S, D)
+    if nb == 0:
+        raise ValueError(f"decode: unsupported shape B={B} Hq={Hq} Hkv={Hkv} S={S} D={D}")
+    return WORKSPACES.get(dev, "decode", nb)
+
+
+def _kv_strides(k, v):
+    if k.stride() != v.stride():
+        raise ValueError("decode: K and V must share strides")
+    if k.stride(3) != 1 or k.stride(2) != k.shape[3]:
+        raise ValueError("decode: K/V token rows must be contiguous (stride(2) == D)")
+    return _lib.strides((k.stride(0), k.stride(1), k.stride(2)), 3)
+
+
+def int8_decode_attn(q, k_i8, k_sc, v_i8, v_sc, n_rep=None, *, sm_scale=None, q_quant=False,
+                     out=None, partial_out=None):
+    """Int8 decode attention (split-KV), the contract of ``int8_decode_attn``
+    (src/kernels/int8_decode_attn_triton.py:101-113), batched.
+
+    q ``[Hq,1,D]`` | ``[B,Hq,1,D]`` | ``[B,Hq,D]`` (bf16/f16/f32); k_i8, v_i8
+    int8 ``[Hkv,S,D]`` | ``[B,Hkv,S,D]``; k_sc ``[.., Hkv,1,D]``; v_sc
+    ``[.., Hkv,S,1]`` (f16 or f32).  Returns the output in q's layout and dtype,
+    or writes the float32 (m, l, o) partials to ``partial_out [B,Hq,D+2]`` and
+    returns it.  ``q_quant`` applies the per-token fake quantization of the
+    reference's patched attention (tests/qwen_kvcache_full.py:103).
+    """
+    for t, n in ((q, "q"), (k_i8, "k_i8"), (k_sc, "k_sc"), (v_i8, "v_i8"), (v_sc, "v_sc")):
+        _cuda(t, f"int8_decode_attn {n}")
+    qb, restore = _as_bhd(q)
+    k4, v4, ks4, vs4 = _as_bhsd(k_i8), _as_bhsd(v_i8), _as_bhsd(k_sc), _as_bhsd(v_sc)
+    B, Hq, D = qb.shape
+    _, Hkv, S, _ = k4.shape
+    if k4.dtype != torch.int8 or v4.dtype != torch.int8:
+        raise TypeError("int8_decode_attn: K/V must be int8")
+    if ks4.dtype != vs4.dtype or ks4.dtype not in (torch.float16, torch.float32):
+        raise TypeError("int8_decode_attn: scales must both be float16 or float32")
+    if n_rep is not None and n_rep * Hkv != Hq:
+        raise ValueError("int8_decode_attn: n_rep * H_kv != H_q")
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(D)
+    res = None
+    if partial_out is None:
+        res = out if out is not None else torch.empty((B, Hq, D), dtype=qb.dtype, device=qb.device)
+    ws = _decode_ws(qb.device, B, Hq, Hkv, S, D)
+    ost = _lib.strides(res.stride(), 3) if res is not None else None
+    rc = _lib.lib().hq_decode_int8(
+        qb.data_ptr(), _dtype_code(qb, "int8_decode_attn q"), _lib.strides(qb.stride(), 3),
+        k4.data_ptr(), v4.data_ptr(), _kv_strides(k4, v4), ks4.data_ptr(), vs4.data_ptr(),
+        _dtype_code(ks4, "scale"), _lib.strides((ks4.stride(0), ks4.stride(1), ks4.stride(3)), 3),
+        _lib.strides((vs4.stride(0), vs4.stride(1), vs4.stride(2)), 3), B, Hq, Hkv, S, D,
+        float(sm_scale), int(bool(q_quant)), res.data_ptr() if res is not None else None, ost,
+        partial_out.data_ptr() if partial_out is not None else None, ws.data_ptr(), ws.numel(),
+        _stream(qb.device))
+    check(rc, "hq_decode_int8")
+    if partial_out is not None:
+        return partial_out
+    return restore(res) if out is None else res
+
+
+def fp16_decode_attn(q, k, v, n_rep=None, *, sm_scale=None, q_quant=False, out=None,
+                     partial_out=None):
+    """Dense twin with the same tiling (src/kernels/int8_decode_attn_triton.py:116-127);
+    K/V float16 or bfloat16 (q must match)."""
+    for t, n in ((q, "q"), (k, "k"), (v, "v")):
+        _cuda(t, f"fp16_decode_attn {n}")
+    qb, restore = _as_bhd(q)
+    k4, v4 = _as_bhsd(k), _as_bhsd(v)
+    B, Hq, D = qb.shape
+    _, Hkv, S, _ = k4.shape
+    if not (k4.dtype == v4.dtype == qb.dtype) or k4.dtype not in (torch.float16, torch.bfloat16):
+        raise TypeError("fp16_decode_attn: q, K, V must all be float16 or all bfloat16")
+    if n_rep is not None and n_rep * Hkv != Hq:
+        raise ValueError("fp16_decode_attn: n_rep * H_kv != H_q")
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(D)
+    res = None
+    if partial_out is None:
+        res = out if out is not None else torch.empty((B, Hq, D), dtype=qb.dtype, device=qb.device)
+    ws = _decode_ws(qb.device, B, Hq, Hkv, S, D)
+    ost = _lib.strides(res.stride(), 3) if res is not None else None
+    rc = _lib.lib().hq_decode_dense(
+        qb.data_ptr(), _lib.strides(qb.stride(), 3), k4.data_ptr(), v4.data_ptr(),
+        _dtype_code(k4, "fp16_decode_attn kv"), _kv_strides(k4, v4), B, Hq, Hkv, S, D,
+        float(sm_scale), int(bool(q_quant)), res.data_ptr() if res is not None else None, ost,
+        partial_out.data_ptr() if partial_out is not None else None, ws.data_ptr(), ws.numel(),
+        _stream(qb.device))
+    check(rc, "hq_decode_dense")
+    if partial_out is not None:
+        return partial_out
+    return restore(res) if out is None else res
+
+
+dense_decode_attn = fp16_decode_attn
+
+
+def decode_combine(parts: torch.Tensor, out_dtype: torch.dtype = torch.bfloat16,
+                   out: torch.Tensor | None = None) -> torch.Tensor:
+    """Merge ``parts [P, B, Hq, D+2]`` float32 (m, l, o) partials -> ``[B, Hq, D]``."""
+    _cuda(parts, "decode_combine")
+    if parts.dtype != torch.float32 or parts.dim() != 4 or not parts.is_contiguous():
+        raise ValueError("decode_combine: parts must be contiguous float32 [P, B, Hq, D+2]")
+    P, B, Hq, D2 = parts.shape
+    D = D2 - 2
+    if out is None:
+        out = torch.empty((B, Hq, D), dtype=out_dtype, device=parts.device)
+    rc = _lib.lib().hq_decode_combine(
+        parts.data_ptr(), P, B * Hq * D2, B, Hq, D, out.data_ptr(),
+        _dtype_code(out, "decode_combine out"), _lib.strides(out.stride(), 3),
+        _stream(parts.device))
+    check(rc, "hq_decode_combine")
+    return out
+
+
+def read_status(kind: str = "decode", device=None) -> int:
+    """Device status word of this stream's ``kind`` workspace (0 = ok)."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    ws = WORKSPACES.get(dev, kind, 4096)
+    return _lib.lib().hq_read_status(ws.data_ptr(), _stream(dev))

@@ -1,0 +1,201 @@
+/*
+ * halftone_b200.h — C ABI of the B200 (sm_100a) int8 KV-cache kernels.
+ *
+ * Two hot paths of the Halftone int8 KV cache, as plain C entry points:
+ *   1. quantize-on-write: symmetric int8, K per channel (absmax over tokens),
+ *      V per token (absmax over head_dim), round half to even;
+ *   2. split-KV (flash-decoding) decode attention over int8 K/V with register
+ *      dequantization and a float32 online softmax, plus a same-design dense
+ *      (bf16/f16) twin and the log-sum-exp combine of partial results.
+ *
+ * Conventions (every entry point):
+ *   - Pointers are device pointers; sizes and strides are in ELEMENTS of the
+ *     pointed-to type.  The innermost (head_dim) stride is always 1.
+ *   - Tensors are 4-D [B, H, S, D] (batch, head, token, head_dim) unless noted.
+ *   - Nothing allocates.  Kernels that need scratch take a caller-owned
+ *     `workspace`; its size comes from the matching *_workspace_bytes query.
+ *   - Work is enqueued on `stream` (a cudaStream_t; NULL = legacy default)
+ *     without any host synchronisation.
+ *   - The return value is HQ_OK (0), a negative hq_status for argument errors
+ *     (nothing is launched), or a positive cudaError_t from the launch.
+ *   - No C++ exception crosses this boundary; entry points are reentrant and
+ *     keep no global mutable state besides a per-device SM-count cache.
+ */
+#ifndef HALFTONE_B200_H_
+#define HALFTONE_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define HQ_API __attribute__((visibility("default")))
+#else
+#define HQ_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* hq_stream_t; /* == cudaStream_t */
+
+/* Element types. */
+enum {
+  HQ_DTYPE_F32 = 0,
+  HQ_DTYPE_BF16 = 1,
+  HQ_DTYPE_F16 = 2,
+  HQ_DTYPE_I8 = 3
+};
+
+/* Negative status codes (positive values are cudaError_t). */
+enum {
+  HQ_OK = 0,
+  HQ_ERR_INVALID_ARGUMENT = -1, /* null pointer, bad shape, stride or alignment */
+  HQ_ERR_UNSUPPORTED = -2,      /* dtype / head_dim / group size not compiled in */
+  HQ_ERR_WORKSPACE = -3,        /* workspace missing, too small or misaligned */
+  HQ_ERR_DEVICE_TIMEOUT = -4    /* a bounded device-side wait gave up (see hq_read_status) */
+};
+
+/* Human-readable text for any return value of this library (static storage). */
+HQ_API const char* hq_status_string(int status);
+/* Library version, "major.minor.patch". */
+HQ_API const char* hq_version(void);
+
+/* ------------------------------------------------------------------------
+ * Quantize-on-write, K per channel.
+ * Replaces quant_k_perchannel_triton (src/kernels/quant_kv_triton.py:90-102,
+ * kernel :16-50) and the K half of QuantizedKVCache.update
+ * (tests/qwen_kvcache_full.py:41-43); math of quantize_int8(x, (2,))
+ * (reference/page_attention_int8_pytorch.py:23-30).
+ *
+ * x        [B, H, S, D] of x_dtype (F32/BF16/F16), strides x_strides[4].
+ * q        [B, H, S, D] int8 codes, strides q_strides[4].
+ * scale_f32, scale_f16 : optional (may be NULL) per-channel scales [B, H, D]
+ *          contiguous, float32 and float16 (round to nearest even).
+ * Requires S >= 1, D in {64, 128, 256}, 16-byte aligned rows.
+ * workspace: >= hq_quant_k_workspace_bytes(B, H, D) bytes, 256-byte aligned;
+ *          cleared by this call on `stream`.  The kernel is a cooperative
+ *          persistent grid whose blocks exchange per-channel maxima through
+ *          the workspace; a bounded wait reports HQ_ERR_DEVICE_TIMEOUT in the
+ *          workspace status word (hq_read_status) instead of hanging.
+ */
+HQ_API size_t hq_quant_k_workspace_bytes(int B, int H, int D);
+HQ_API int hq_quant_k_perchannel(const void* x, int x_dtype, const int64_t x_strides[4], int B, int H,
+                          int S, int D, int8_t* q, const int64_t q_strides[4], float* scale_f32,
+                          uint16_t* scale_f16, void* workspace, size_t workspace_bytes,
+                          hq_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Quantize-on-write, V per token.
+ * Replaces quant_v_pertoken_triton (src/kernels/quant_kv_triton.py:105-117,
+ * kernel :55-87) and the V half of QuantizedKVCache.update
+ * (tests/qwen_kvcache_full.py:45-47); math of quantize_int8(x, (3,)).
+ *
+ * scale_f32 / scale_f16: optional [B, H, S] per-token scales with strides
+ * scale_strides[3] (shared by both outputs).  No workspace.
+ */
+HQ_API int hq_quant_v_pertoken(const void* x, int x_dtype, const int64_t x_strides[4], int B, int H,
+                        int S, int D, int8_t* q, const int64_t q_strides[4], float* scale_f32,
+                        uint16_t* scale_f16, const int64_t scale_strides[3], hq_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Fused append of S_new tokens to an int8 cache, following the reference
+ * storage rule of QuantizedKVCache.update on a non-empty layer
+ * (tests/qwen_kvcache_full.py:38-54): the new K codes use the per-channel
+ * scale of THESE S_new tokens, which is not stored (the cache keeps its first
+ * K scale, line 54); the new V codes use per-token scales, which are stored.
+ *
+ * k_new, v_new  [B, H, S_new, D] of x_dtype with strides k_strides / v_strides.
+ * k_dst, v_dst  int8 cache rows for the new tokens ([B, H, S_new, D] views at
+ *               the append position) with strides kq_strides / vq_strides.
+ * v_scale_f32 / v_scale_f16: optional [B, H, S_new] views, strides vs_strides[3].
+ * Requires 1 <= S_new <= 64, D in {64, 128, 256}.  One launch, no workspace.
+ */
+HQ_API int hq_append_kv(const void* k_new, const void* v_new, int x_dtype, const int64_t k_strides[4],
+                 const int64_t v_strides[4], int B, int H, int S_new, int D, int8_t* k_dst,
+                 const int64_t kq_strides[4], int8_t* v_dst, const int64_t vq_strides[4],
+                 float* v_scale_f32, uint16_t* v_scale_f16, const int64_t vs_strides[3],
+                 hq_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Dequantize an int8 cache tensor: out = dtype(float(code) * float(scale)).
+ * Replaces the read path of QuantizedKVCache.update
+ * (tests/qwen_kvcache_full.py:64-65) and dequantize_int8
+ * (reference/page_attention_int8_pytorch.py:33-34).
+ *
+ * per_channel != 0: scale is [B, H, D] (K); else [B, H, S] (V).
+ * scale_strides[3] are the scale's (b, h, d-or-s) strides; scale_dtype F32 or F16.
+ */
+HQ_API int hq_dequant(const int8_t* q, const int64_t q_strides[4], int B, int H, int S, int D,
+               const void* scale, int scale_dtype, const int64_t scale_strides[3],
+               int per_channel, void* out, int out_dtype, const int64_t out_strides[4],
+               hq_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Split-KV int8 decode attention (one query token per sequence).
+ * Replaces int8_decode_attn (src/kernels/int8_decode_attn_triton.py:101-113,
+ * kernel :15-63) and the decode step of quantized_attention_forward
+ * (tests/qwen_kvcache_full.py:95-113): out[b, h] = softmax(q K^T * sm_scale) V
+ * over the dequantized cache, GQA q head h reading kv head h / (Hq / Hkv).
+ *
+ * q        [B, Hq, D] of q_dtype (F32/BF16/F16), strides q_strides[3].
+ * k, v     int8 [B, Hkv, S, D], strides kv_strides[3] = (b, h, s) shared by K
+ *          and V (token rows contiguous: kv_strides[2] == D).
+ * k_scale  per-channel [B, Hkv, D], strides ksc_strides[3]; v_scale per-token
+ *          [B, Hkv, S], strides vsc_strides[3]; scale_dtype F32 or F16.
+ * q_quant  0: use q as given; 1: per-token symmetric int8 fake quantization
+ *          of q first, rounded back to q_dtype (tests/qwen_kvcache_full.py:19-23,103).
+ * out      [B, Hq, D] of q_dtype, strides out_strides[3]; or, when
+ *          partial_out != NULL, out is ignored and the unnormalised partial
+ *          (m, l, o[D]) per (b, h) is written as float32 to
+ *          partial_out[(b * Hq + h) * (D + 2)], with m the base-2 running max
+ *          of s * sm_scale * log2(e), l = sum 2^(s-m), o = sum 2^(s-m) v.
+ * Requires D == 128, Hq / Hkv in {1, 2, 4}, S >= 0 (S == 0 gives zeros).
+ * workspace: >= hq_decode_workspace_bytes(B, Hq, Hkv, S, D) bytes, 256-byte
+ *          aligned, zero-filled once when allocated; the kernel leaves it
+ *          zero-filled again (its arrival counters reset themselves).
+ */
+HQ_API size_t hq_decode_workspace_bytes(int B, int Hq, int Hkv, int S, int D);
+HQ_API int hq_decode_int8(const void* q, int q_dtype, const int64_t q_strides[3], const int8_t* k,
+                   const int8_t* v, const int64_t kv_strides[3], const void* k_scale,
+                   const void* v_scale, int scale_dtype, const int64_t ksc_strides[3],
+                   const int64_t vsc_strides[3], int B, int Hq, int Hkv, int S, int D,
+                   float sm_scale, int q_quant, void* out, const int64_t out_strides[3],
+                   float* partial_out, void* workspace, size_t workspace_bytes,
+                   hq_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Same-design dense twin: identical tiling over bf16/f16 K/V (kv_dtype), no
+ * scales.  Replaces fp16_decode_attn (src/kernels/int8_decode_attn_triton.py:116-127,
+ * kernel :67-97).  Arguments as hq_decode_int8; q_dtype must equal kv_dtype.
+ */
+HQ_API int hq_decode_dense(const void* q, const int64_t q_strides[3], const void* k, const void* v,
+                    int kv_dtype, const int64_t kv_strides[3], int B, int Hq, int Hkv, int S,
+                    int D, float sm_scale, int q_quant, void* out, const int64_t out_strides[3],
+                    float* partial_out, void* workspace, size_t workspace_bytes,
+                    hq_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Log-sum-exp combine of n_parts partials in the hq_decode_int8 partial
+ * format (e.g. one per GPU of a sequence-sharded cache, gathered into one
+ * buffer): parts[p * part_stride + (b * Hq + h) * (D + 2) + {0: m, 1: l, 2..: o}].
+ * out [B, Hq, D] of out_dtype with strides out_strides[3].
+ * No counterpart in the reference (it has no split); the combine restates the
+ * flash-decoding rule  out = sum_p 2^(m_p - M) o_p / sum_p 2^(m_p - M) l_p.
+ */
+HQ_API int hq_decode_combine(const float* parts, int n_parts, int64_t part_stride, int B, int Hq,
+                      int D, void* out, int out_dtype, const int64_t out_strides[3],
+                      hq_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Reads (and synchronises `stream` for) the device status word at the start
+ * of a quantize-K or decode workspace: HQ_OK, or HQ_ERR_DEVICE_TIMEOUT if a
+ * bounded device wait gave up during an earlier call on that workspace.
+ */
+HQ_API int hq_read_status(const void* workspace, hq_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HALFTONE_B200_H_ */

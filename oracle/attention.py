@@ -50,13 +50,14 @@ def page_attention_reference(q, k, v, n_rep=None, sm_scale=None, acc="f32"):
         n_rep = hq // hkv
     if sm_scale is None:
         sm_scale = 1.0 / math.sqrt(d)
-    K = repeat_kv(k.astype(dt), n_rep)
-    V = repeat_kv(v.astype(dt), n_rep)
-    scores = np.matmul(q.astype(dt), np.swapaxes(K, -1, -2)) * dt(sm_scale)
+    # grouped GQA without materialising repeat_kv: q head h = g * n_rep + r reads kv head g
+    B, _, Sq, _ = q.shape
+    qg = q.astype(dt).reshape(B, hkv, n_rep, Sq, d)
+    scores = np.matmul(qg, np.swapaxes(k.astype(dt), -1, -2)[:, :, None]) * dt(sm_scale)
     scores = scores - scores.max(axis=-1, keepdims=True)
     p = np.exp(scores)
     p = p / p.sum(axis=-1, keepdims=True)
-    out = np.matmul(p, V)
+    out = np.matmul(p, v.astype(dt)[:, :, None]).reshape(B, hq, Sq, d)
     return out if batched else out[0]
 
 
