@@ -59,6 +59,12 @@ def parse():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-extras", action="store_true", help="skip sweep / twin / quant extras")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the public-API end-to-end leg")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--layers", type=int, default=LAYERS,
+                    help="layer caches per step (profiling runs use a few; default 28)")
+    ap.add_argument("--only", choices=["all", "decode", "twin", "quant"], default="all",
+                    help="profiling: run one kernel family on a small case and exit")
     return ap.parse_args()
 
 
@@ -288,9 +294,12 @@ def main():
     peak, peak_kind = load_peaks()
     gen = torch.Generator(device=device).manual_seed(1234 + rank)
     stream = torch.cuda.Stream(device)
-    caches = make_layer_caches(torch, kernels, LAYERS, S_HEAD, device, gen)
-    q = torch.randn((LAYERS, B, HQ, D), generator=gen, device=device).to(torch.bfloat16)
-    out = torch.empty((LAYERS, B, HQ, D), dtype=torch.bfloat16, device=device)
+    nl = args.layers
+    if args.only != "all":
+        return profile_only(args, torch, kernels, device, gen, stream)
+    caches = make_layer_caches(torch, kernels, nl, S_HEAD, device, gen)
+    q = torch.randn((nl, B, HQ, D), generator=gen, device=device).to(torch.bfloat16)
+    out = torch.empty((nl, B, HQ, D), dtype=torch.bfloat16, device=device)
     sm_scale = 1.0 / math.sqrt(D)
     seq = sharding.SequenceShardedDecode(B, HQ, D, device) if world > 1 else None
 
@@ -310,13 +319,15 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     per_layer = decode_bytes(B, HQ, HKV, S_HEAD, D)
-    value = world * LAYERS * per_layer / (ms * 1e-3) / 1e9
-    us_layer = ms * 1e3 / LAYERS
+    value = world * nl * per_layer / (ms * 1e-3) / 1e9
+    us_layer = ms * 1e3 / nl
     achieved = per_layer / (us_layer * 1e-6) / 1e9
 
     # ---- e2e through the public API (cache + patched attention), host buffers
-    e2e = run_e2e(torch, kernels, QuantizedKVCache, quantized_attention_forward, caches, device,
-                  stream, min(args.steps, 100), min(args.warmup, 5), world, dist, seq)
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(torch, kernels, QuantizedKVCache, quantized_attention_forward, caches,
+                      device, stream, min(args.steps, 100), min(args.warmup, 5), world, dist, seq)
 
     extras = {}
     if world == 1 and not args.no_extras:
@@ -328,13 +339,13 @@ def main():
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
             "data": "synthetic",
-            "config": {"workload": f"decode attention over {LAYERS} layer caches, S={S_HEAD} per "
+            "config": {"workload": f"decode attention over {nl} layer caches, S={S_HEAD} per "
                                    f"rank, B={B}, Hq={HQ}, Hkv={HKV}, D={D}, bf16 q, int8 K/V, "
                                    "fp32 scales",
-                       "l2": f"inputs larger than L2: {LAYERS} caches x "
+                       "l2": f"inputs larger than L2: {nl} caches x "
                              f"{per_layer / 1e6:.1f} MB read round-robin",
                        "parallelism": f"sequence-sharded x{world}" if world > 1 else "single GPU",
-                       "graph": "28 launches per step in one CUDA graph"},
+                       "graph": f"{nl} launches per step in one CUDA graph"},
             "us_per_layer": round(us_layer, 3),
             "frac_of_peak": round(achieved / peak, 4),
             "frac_of_8tbs": round(achieved / 8000.0, 4),
@@ -345,10 +356,10 @@ def main():
                          "algorithmic_bytes_per_launch": per_layer},
             "clocks": clocks or {},
             "e2e": e2e,
-            "gpu_launches": args.steps * LAYERS * (1 if world == 1 else 2),
+            "gpu_launches": args.steps * nl * (1 if world == 1 else 2),
         }
         line.update(extras)
-        if world == 1:
+        if world == 1 and not args.no_cpu:
             gbs, cores, layers, el = cpu_decode_gbs(seconds=10.0)
             line["cpu_baseline"] = {
                 "value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": "port",
@@ -380,6 +391,7 @@ def run_e2e(torch, kernels, QuantizedKVCache, attn_fwd, caches, device, stream, 
     import transformers.models.qwen3.modeling_qwen3 as qwen3_mod  # noqa: F401
     from halftone_quantizedkvcache_b200.integration import quantized_attention as qa
     module = _Attn(HQ // HKV, D)
+    nl = len(caches)
     cache = QuantizedKVCache(mode="fused", capacity=S_HEAD + 2 * (steps + warmup) + 512)
     # prefill through the public API: dequantize our codes back to bf16 and update()
     with torch.cuda.stream(stream):
@@ -390,15 +402,15 @@ def run_e2e(torch, kernels, QuantizedKVCache, attn_fwd, caches, device, stream, 
             del kd, vd
     torch.cuda.synchronize()
     per_layer_in = (B * HQ * D + 2 * B * HKV * D) * 2
-    h_in = torch.randn((LAYERS, per_layer_in // 2), dtype=torch.float32).to(torch.bfloat16).pin_memory()
-    h_out = torch.empty((LAYERS, B, 1, HQ, D), dtype=torch.bfloat16).pin_memory()
+    h_in = torch.randn((nl, per_layer_in // 2), dtype=torch.float32).to(torch.bfloat16).pin_memory()
+    h_out = torch.empty((nl, B, 1, HQ, D), dtype=torch.bfloat16).pin_memory()
     d_in = torch.empty_like(h_in, device=device)
-    d_out = torch.empty((LAYERS, B, 1, HQ, D), dtype=torch.bfloat16, device=device)
+    d_out = torch.empty((nl, B, 1, HQ, D), dtype=torch.bfloat16, device=device)
     nq, nk = B * HQ * D, B * HKV * D
 
     def one_step():
         d_in.copy_(h_in, non_blocking=True)
-        for l in range(LAYERS):
+        for l in range(nl):
             qv = d_in[l, :nq].view(B, 1, HQ, D).transpose(1, 2)
             kn = d_in[l, nq:nq + nk].view(B, 1, HKV, D).transpose(1, 2)
             vn = d_in[l, nq + nk:].view(B, 1, HKV, D).transpose(1, 2)
@@ -428,10 +440,10 @@ def run_e2e(torch, kernels, QuantizedKVCache, attn_fwd, caches, device, stream, 
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     S_mid = S_HEAD + warmup + steps // 2
-    gbs = world * LAYERS * decode_bytes(B, HQ, HKV, S_mid, D, scale_bytes=2) / (ms * 1e-3) / 1e9
+    gbs = world * nl * decode_bytes(B, HQ, HKV, S_mid, D, scale_bytes=2) / (ms * 1e-3) / 1e9
     del cache
-    return {"value": round(gbs, 2), "unit": "GB/s", "h2d_bytes_per_step": LAYERS * per_layer_in,
-            "d2h_bytes_per_step": LAYERS * B * HQ * D * 2, "ms_per_step": round(ms, 4),
+    return {"value": round(gbs, 2), "unit": "GB/s", "h2d_bytes_per_step": nl * per_layer_in,
+            "d2h_bytes_per_step": nl * B * HQ * D * 2, "ms_per_step": round(ms, 4),
             "path": "QuantizedKVCache.update + quantized_attention_forward per layer, eager "
                     "(no graph), fp16 cache scales"}
 
@@ -522,6 +534,36 @@ def run_extras(torch, kernels, device, gen, stream, us_int8, peak):
     del k, v, k8, v8
     torch.cuda.empty_cache()
     return res
+
+
+def profile_only(args, torch, kernels, device, gen, stream):
+    """A few launches of one kernel family on a small case, for ncu captures."""
+    sm_scale = 1.0 / math.sqrt(D)
+    with torch.cuda.stream(stream):
+        if args.only in ("decode", "twin"):
+            kind = "int8" if args.only == "decode" else "bf16"
+            caches = make_layer_caches(torch, kernels, args.layers, S_HEAD, device, gen, kv=kind)
+            q = torch.randn((B, HQ, D), generator=gen, device=device).to(torch.bfloat16)
+            o = torch.empty_like(q)
+            torch.cuda.synchronize()
+            for _ in range(args.warmup + args.steps):
+                for c in caches:
+                    if kind == "int8":
+                        kernels.int8_decode_attn(q, *c, HQ // HKV, sm_scale=sm_scale, out=o)
+                    else:
+                        kernels.fp16_decode_attn(q, *c, HQ // HKV, sm_scale=sm_scale, out=o)
+        else:
+            x = torch.randn((8, 8, 32768, D), generator=gen, device=device).to(torch.bfloat16)
+            y = torch.empty(x.shape, dtype=torch.int8, device=device)
+            s32k = torch.empty((8, 8, 1, D), dtype=torch.float32, device=device)
+            s32v = torch.empty((8, 8, 32768, 1), dtype=torch.float32, device=device)
+            torch.cuda.synchronize()
+            for _ in range(args.warmup + args.steps):
+                kernels.quant_k_perchannel(x, out=y, scale_dtype=None, scale_f32_out=s32k)
+                kernels.quant_v_pertoken(x, out=y, scale_dtype=None, scale_f32_out=s32v)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_only": args.only, "steps": args.steps, "layers": args.layers}))
+    return 0
 
 
 def make_sweep_caches(torch, n, S, device, gen, kind):

@@ -30,9 +30,16 @@ Q_DIMS = (3,)
 
 
 def sym_int8(x: torch.Tensor, dims):
-    """Symmetric int8 of ``x`` reduced over ``dims``: float32 (codes, scale)."""
+    """Symmetric int8 of ``x`` reduced over ``dims``: float32 (codes, scale).
+
+    ``amax / 127`` is an IEEE true division on every device.  On the CPU this
+    is what the reference computes (bit-identical, pinned by the golden
+    logits); on a GPU torch would turn a division by the Python scalar 127.0
+    into a multiply by its reciprocal, so the divisor is a tensor here.
+    """
     xf = x.float()
-    scale = xf.abs().amax(dim=dims, keepdim=True).clamp(min=1e-8) / 127.0
+    amax = xf.abs().amax(dim=dims, keepdim=True).clamp(min=1e-8)
+    scale = amax / torch.full((), 127.0, dtype=torch.float32, device=x.device)
     return torch.clamp(torch.round(xf / scale), -127, 127), scale
 
 
@@ -75,8 +82,18 @@ class OracleQuantizedKVCache(DynamicCache):
 
 
 def oracle_attention_forward(module, query, key, value, attention_mask, scaling=None,
-                             dropout=0.0, **kwargs):
-    """Restatement of tests/qwen_kvcache_full.py:95-113."""
+                             dropout=0.0, fp32_math=False, **kwargs):
+    """Restatement of tests/qwen_kvcache_full.py:95-113.
+
+    ``fp32_math=True`` evaluates the same attention in float32 (then casts
+    back): the reference's sensitivity to its own bf16 arithmetic, used as
+    the noise floor of whole-model comparisons.
+    """
+    if fp32_math:
+        out, _ = oracle_attention_forward(
+            module, query.float(), key.float(), value.float(),
+            None if attention_mask is None else attention_mask.float(), scaling, dropout)
+        return out.to(query.dtype), None
     if scaling is None:
         scaling = module.head_dim ** -0.5
     n_rep = module.num_key_value_groups
