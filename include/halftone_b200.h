@@ -188,6 +188,29 @@ HQ_API int hq_decode_combine(const float* parts, int n_parts, int64_t part_strid
                       hq_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * hq_decode_int8 for callers that cannot allocate device memory (no
+ * counterpart in the reference).  A runtime that owns all device memory - a
+ * plugin inside another engine's decode loop, a binding whose language
+ * runtime manages the GPU heap - can hand over its tensors but cannot call
+ * cudaMalloc for a workspace.  This entry point takes the same arguments as
+ * hq_decode_int8 minus the workspace and keeps its scratch in a static
+ * 8 MiB (8,388,608-byte) device array of the library, present on every GPU
+ * that loads it until the process exits.  Returns HQ_ERR_WORKSPACE without
+ * launching when hq_decode_workspace_bytes(B, Hq, Hkv, S, D) exceeds 8 MiB.
+ * It allocates nothing; its first call on a device looks up the array's
+ * device address (make that first call before any stream capture).  All
+ * calls share the array and each clears its tickets first: calls that
+ * overlap on the GPU race and must be ordered by the caller.
+ */
+HQ_API int hq_decode_int8_noalloc(const void* q, int q_dtype, const int64_t q_strides[3],
+                                  const int8_t* k, const int8_t* v, const int64_t kv_strides[3],
+                                  const void* k_scale, const void* v_scale, int scale_dtype,
+                                  const int64_t ksc_strides[3], const int64_t vsc_strides[3],
+                                  int B, int Hq, int Hkv, int S, int D, float sm_scale,
+                                  int q_quant, void* out, const int64_t out_strides[3],
+                                  float* partial_out, hq_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * Reads (and synchronises `stream` for) the device status word at the start
  * of a quantize-K or decode workspace: HQ_OK, or HQ_ERR_DEVICE_TIMEOUT if a
  * bounded device wait gave up during an earlier call on that workspace.
