@@ -24,6 +24,9 @@
 //   * combines splits in the same launch: each block writes (m, l, o) for its
 //     split, and the last block of a (batch, kv head) to arrive - an atomic
 //     ticket, no waiting - merges them and resets the ticket.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include <atomic>
 #include <cmath>
 
@@ -142,6 +145,92 @@ __device__ __forceinline__ void emit(const Params& p, int b, int hq, int d, floa
     auto* o = reinterpret_cast<typename QE::T*>(p.out);
     o[b * p.osb + hq * p.osh + d] = QE::from_f32(L > 0.0f ? O / L : 0.0f);
   }
+}
+
+// Workspace rows of the split partials: m, l, two pad words, o[kD] (o 16-byte aligned).
+constexpr int kPartRow = kD + 4;
+
+// Publishes one split's (m, l, o) for q head hq; thread d writes o[d].
+__device__ __forceinline__ void publish_split(const Params& p, int b, int hq, int split, int d,
+                                              float M, float L, float O) {
+  float* dst = p.ws_part + ((static_cast<int64_t>(b) * p.Hq + hq) * p.n_split + split) * kPartRow;
+  if (d == 0) {
+    dst[0] = M;
+    dst[1] = L;
+  }
+  dst[4 + d] = O;
+}
+
+// Run by the last block of (b, kvh) to arrive: merges the n_split partials of
+// its NREP q heads and emits them.  Latency-oriented: one parallel pass over
+// the (m, l) pairs, then every warp streams a quarter of the o rows with
+// independent 16-byte loads.  scratch (16-byte aligned): >= 2 * n_split + 3 +
+// kWarps * kD floats.
+template <int NREP, int QDT>
+__device__ __forceinline__ void merge_splits(const Params& p, int b, int kvh, float* scratch) {
+  __shared__ float sred[kWarps];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int n = p.n_split;
+  float* wgt = scratch;
+  float* lv = scratch + n;
+  float* red4 = scratch + ((2 * n + 3) & ~3);  // 16-byte aligned for float4 stores
+  for (int r = 0; r < NREP; ++r) {
+    const float* base =
+        p.ws_part + (static_cast<int64_t>(b) * p.Hq + kvh * NREP + r) * n * kPartRow;
+    float M = -INFINITY;
+    for (int s = tid; s < n; s += kThreads) {
+      const float2 ml = __ldcg(reinterpret_cast<const float2*>(base + static_cast<int64_t>(s) * kPartRow));
+      wgt[s] = ml.x;
+      lv[s] = ml.y;
+      M = fmaxf(M, ml.x);
+    }
+    M = warp_max(M, 1);
+    if (lane == 0) sred[warp] = M;
+    __syncthreads();
+    M = fmaxf(fmaxf(sred[0], sred[1]), fmaxf(sred[2], sred[3]));
+    float L = 0.0f;
+    for (int s = tid; s < n; s += kThreads) {
+      const float m = wgt[s];
+      const float w = m == -INFINITY ? 0.0f : exp2f(m - M);
+      wgt[s] = w;
+      L += w * lv[s];
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+    __syncthreads();  // sred (M) read by everyone; wgt complete
+    if (lane == 0) sred[warp] = L;
+    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    const float4* o4 = reinterpret_cast<const float4*>(base + 4) + lane;
+    int s = warp;
+    for (; s + 3 * kWarps < n; s += 4 * kWarps) {
+      float4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) v[u] = __ldcg(o4 + static_cast<int64_t>(s + u * kWarps) * (kPartRow / 4));
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float w = wgt[s + u * kWarps];
+        acc.x += w * v[u].x;
+        acc.y += w * v[u].y;
+        acc.z += w * v[u].z;
+        acc.w += w * v[u].w;
+      }
+    }
+    for (; s < n; s += kWarps) {
+      const float4 v = __ldcg(o4 + static_cast<int64_t>(s) * (kPartRow / 4));
+      const float w = wgt[s];
+      acc.x += w * v.x;
+      acc.y += w * v.y;
+      acc.z += w * v.z;
+      acc.w += w * v.w;
+    }
+    reinterpret_cast<float4*>(red4 + warp * kD)[lane] = acc;
+    __syncthreads();
+    L = sred[0] + sred[1] + sred[2] + sred[3];
+    const float O = red4[tid] + red4[kD + tid] + red4[2 * kD + tid] + red4[3 * kD + tid];
+    emit<QDT>(p, b, kvh * NREP + r, tid, M, L, O);
+    __syncthreads();  // scratch and sred are reused by the next head
+  }
+  if (tid == 0) p.ws_count[b * p.Hkv + kvh] = 0;  // ready for the next launch
 }
 
 template <int NREP, int KVDT, int SDT, int QDT>
@@ -418,14 +507,7 @@ __global__ void __launch_bounds__(kThreads, 3) decode_kernel(const Params p) {
 
   // ---- publish this split, then the last block of (b, kvh) merges all splits
 #pragma unroll
-  for (int r = 0; r < NREP; ++r) {
-    float* dst = p.ws_part + ((static_cast<int64_t>(b) * p.Hq + kvh * NREP + r) * p.n_split + split) * (kD + 2);
-    if (d == 0) {
-      dst[0] = Ms[r];
-      dst[1] = Ls[r];
-    }
-    dst[2 + d] = Os[r];
-  }
+  for (int r = 0; r < NREP; ++r) publish_split(p, b, kvh * NREP + r, split, d, Ms[r], Ls[r], Os[r]);
   __syncthreads();
   if (tid == 0) {
     __threadfence();
@@ -436,39 +518,483 @@ __global__ void __launch_bounds__(kThreads, 3) decode_kernel(const Params p) {
   if (!s_last) return;
   __threadfence();
 
-  float* wsc = reinterpret_cast<float*>(ring);  // [n_split] weights (ring is free now)
-  for (int r = 0; r < NREP; ++r) {
-    const float* src = p.ws_part + (static_cast<int64_t>(b) * p.Hq + kvh * NREP + r) * p.n_split * (kD + 2);
-    float M = -INFINITY;
-    for (int s = tid; s < p.n_split; s += kThreads) M = fmaxf(M, __ldcg(src + s * (kD + 2)));
-    M = warp_max(M, 1);
-    if (lane == 0) red[warp][0] = M;
-    __syncthreads();
-    M = fmaxf(fmaxf(red[0][0], red[1][0]), fmaxf(red[2][0], red[3][0]));
-    float L = 0.0f;
-    for (int s = tid; s < p.n_split; s += kThreads) {
-      const float ms = __ldcg(src + s * (kD + 2));
-      const float w = ms == -INFINITY ? 0.0f : exp2f(ms - M);
-      wsc[s] = w;
-      L += w * __ldcg(src + s * (kD + 2) + 1);
+  merge_splits<NREP, QDT>(p, b, kvh, reinterpret_cast<float*>(ring));
+}
+
+// ------------------------------------------------------------------ int8 tensor-core kernel
+// The int8 decode kernel proper.  Same grid, split plan, partial format and
+// last-block combine as the CUDA-core kernel above (which remains the dense
+// bf16/f16 twin), but the two dot products run on the int8 tensor cores with
+// exact integer accumulation:
+//
+//   scores  S[t, c] = sum_d K[t, d] * Qlimb[d, c]        mma.m16n8k32 s8 x s8 -> s32
+//   output  O[d, c] = sum_t V[t, d] * Plimb[t, c]        (A = V^T via ldmatrix.trans)
+//
+// q' = q * k_scale * sm_scale * log2(e) and p' = p * v_scale are real-valued,
+// so each is written as three balanced int8 limbs of a 24-bit fixed-point value
+// (x24 = 65536 a + 256 b + c, |x24| <= 127 * 65793) with one float scale
+// per head; the 8 n-columns of an MMA hold (a, b) and (c, 0) of two q heads.
+// Scores are rebuilt exactly as sa * Sa + sb * Sb + sc * Sc in float32.  The
+// PV products accumulate in int32 across tiles and are flushed into float32
+// only when the running max or the limb scale of a head changes.
+//
+// K / V tiles of 128 tokens x 128 bytes arrive by tensor-map TMA with 128-byte
+// swizzle (16-byte chunk c of row r stored at chunk c ^ (r % 8)), which makes
+// every ldmatrix phase conflict-free.  4 warps per block, 32 tokens per warp
+// per tile; each warp keeps its own online-softmax state.
+namespace mmak {
+
+constexpr int kTileT = 128;                // tokens per tile
+constexpr int kTileB = kTileT * kD;        // 16 KB per K or V tile
+constexpr int kStagesM = 3;
+constexpr float kLimbMax = 8355711.0f;     // 127 * (65536 + 256 + 1): largest |x| of 3 int8 digits
+
+template <int NREP>
+struct MCfg {
+  static constexpr int NT = (NREP + 1) / 2;               // n8 tiles, 2 heads each
+  static constexpr int RING = kStagesM * 2 * kTileB;      // 96 KB
+  static constexpr int LIMB = kWarps * NT * 8 * 32;       // p' limb staging
+  static constexpr int SMEM = 1024 + RING + NREP * kD * 4 + LIMB + 2 * kStagesM * 8;
+  static_assert(kWarps * NREP * kD * 4 + kWarps * NREP * 8 <= RING, "epilogue scratch");
+};
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr));
+}
+__device__ __forceinline__ void mma_s8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                       uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+      "{%8, %9}, {%0, %1, %2, %3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, int x, int y,
+                                            int z, int w, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// balanced base-256 digits of x in [-kLimbMax, kLimbMax]: x = 65536 a + 256 b + c,
+// each digit in [-128, 127] (a in [-127, 127])
+__device__ __forceinline__ void limbs24(int x, int& a, int& b, int& c) {
+  c = ((x + 128) & 255) - 128;
+  const int x1 = (x - c) >> 8;
+  b = ((x1 + 128) & 255) - 128;
+  a = (x1 - b) >> 8;
+}
+__device__ __forceinline__ uint32_t limb_byte(int x, int which) {
+  int a, b, c;
+  limbs24(x, a, b, c);
+  return static_cast<uint32_t>(which == 0 ? a : which == 1 ? b : c) & 0xffu;
+}
+// byte offset of (row, 16-byte chunk) in a 128-byte-row tile stored with 128B swizzle
+__device__ __forceinline__ uint32_t swz(int row, int chunk) {
+  return static_cast<uint32_t>(row * 128 + ((chunk ^ (row & 7)) << 4));
+}
+// logical MMA k index (0..31) of the warp-local token p (0..31) in the PV product
+__device__ __forceinline__ int pv_k(int p) {
+  const int th = p >> 4, w = p & 15;
+  return 16 * th + 4 * ((w & 7) >> 1) + (w & 1) + 2 * (w >> 3);
+}
+
+template <int NREP, int SDT, int QDT>
+__global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(
+    const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
+    const Params p) {
+  using C = MCfg<NREP>;
+  using QE = Elem<QDT>;
+  using SE = Elem<SDT>;
+  constexpr int NT = C::NT;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* ring = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float* qs = reinterpret_cast<float*>(ring + C::RING);
+  unsigned char* plimb = reinterpret_cast<unsigned char*>(qs + NREP * kD);
+  uint64_t* full = reinterpret_cast<uint64_t*>(plimb + C::LIMB);
+  uint64_t* empty = full + kStagesM;
+  __shared__ float red[kWarps][NREP];
+  __shared__ float qmax_s[NREP];
+  __shared__ float cM[NREP], cL[NREP];
+  __shared__ int s_last;
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, t4 = lane & 3;
+  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int s_begin = split * p.tiles_per_split * kTileT;
+  const int s_end = min(p.S, s_begin + p.tiles_per_split * kTileT);
+  const int ntok = max(0, s_end - s_begin);
+  const int ntiles = (ntok + kTileT - 1) / kTileT;
+
+  int issued = 0;
+  auto issue = [&](int t) {
+    const int st = t % kStagesM;
+    unsigned char* dst = ring + st * 2 * kTileB;
+    mbar_arrive_expect_tx(&full[st], 2 * kTileB);
+    tma_load_4d(dst, &tmk, 0, s_begin + t * kTileT, kvh, b, &full[st]);
+    tma_load_4d(dst + kTileB, &tmv, 0, s_begin + t * kTileT, kvh, b, &full[st]);
+    issued = t + 1;
+  };
+  if (tid == 0) {
+    for (int s = 0; s < kStagesM; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kWarps);
+    }
+    fence_mbar_init();
+  }
+  // zero the p' staging (columns 3 and 7 stay zero)
+  for (int i = tid; i < C::LIMB / 4; i += kThreads) reinterpret_cast<uint32_t*>(plimb)[i] = 0;
+  __syncthreads();
+  if (tid == 0)
+    for (int t = 0; t < min(kStagesM, ntiles); ++t) issue(t);
+
+  // ---- q prologue: q' = q_in * k_scale * sm_scale * log2(e), thread owns channel d
+  {
+    const int d = tid;
+    const auto* qp = reinterpret_cast<const typename QE::T*>(p.q);
+    const auto* kp = reinterpret_cast<const typename SE::T*>(p.ksc);
+    const float ks = SE::to_f32(kp[b * p.kscb + kvh * p.ksch + d * p.kscd]);
+    float qv[NREP];
+#pragma unroll
+    for (int r = 0; r < NREP; ++r) qv[r] = QE::to_f32(qp[b * p.qsb + (kvh * NREP + r) * p.qsh + d]);
+    if (p.q_quant) {
+#pragma unroll
+      for (int r = 0; r < NREP; ++r) {
+        const float m = warp_max(fabsf(qv[r]), 1);
+        if (lane == 0) red[warp][r] = m;
+      }
+      __syncthreads();
+#pragma unroll
+      for (int r = 0; r < NREP; ++r) {
+        float m = red[0][r];
+#pragma unroll
+        for (int w = 1; w < kWarps; ++w) m = fmaxf(m, red[w][r]);
+        const Quantizer qz = Quantizer::from_amax(m);
+        qv[r] = QE::to_f32(QE::from_f32(static_cast<float>(qz.code(qv[r])) * qz.scale));
+      }
+      __syncthreads();
     }
 #pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
-    __syncthreads();  // red[] reads above are done; wsc[] complete
-    if (lane == 0) red[warp][0] = L;
-    __syncthreads();
-    if (tid == 0) {
-      cM[r] = M;
-      cL[r] = red[0][0] + red[1][0] + red[2][0] + red[3][0];
+    for (int r = 0; r < NREP; ++r) {
+      const float v = qv[r] * ks * p.qk_scale;
+      qs[r * kD + d] = v;
+      const float m = warp_max(fabsf(v), 1);
+      if (lane == 0) red[warp][r] = m;
     }
-    float O = 0.0f;
-    for (int s = 0; s < p.n_split; ++s) O += wsc[s] * __ldcg(src + s * (kD + 2) + 2 + d);
     __syncthreads();
-    emit<QDT>(p, b, kvh * NREP + r, d, cM[r], cL[r], O);
+    if (tid < NREP) {
+      float m = red[0][tid];
+#pragma unroll
+      for (int w = 1; w < kWarps; ++w) m = fmaxf(m, red[w][tid]);
+      qmax_s[tid] = m;
+    }
     __syncthreads();
   }
-  if (tid == 0) p.ws_count[b * p.Hkv + kvh] = 0;  // ready for the next launch
+
+  // per lane: q' limb B-fragments, per n-tile and k-step; score factors
+  uint32_t bq[NT][4][2];
+  float f0[NT], f1[NT];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const int col_head = 2 * nt + (g >> 2), col_limb = g & 3;
+    const bool live = col_head < NREP && col_limb < 3;
+    const float qm = live ? qmax_s[col_head] : 0.0f;
+    const float inv = qm > 0.0f ? kLimbMax / qm : 0.0f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        uint32_t w = 0;
+        if (live)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int d = 32 * j + 16 * hh + 4 * t4 + e;
+            const int x = max(-static_cast<int>(kLimbMax),
+                              min(static_cast<int>(kLimbMax), __float2int_rn(qs[col_head * kD + d] * inv)));
+            w |= limb_byte(x, col_limb) << (8 * e);
+          }
+        bq[nt][j][hh] = w;
+      }
+    const int my_head = 2 * nt + (t4 >> 1);
+    const float qsc = my_head < NREP && qmax_s[my_head] > 0.0f ? qmax_s[my_head] / kLimbMax : 0.0f;
+    f0[nt] = (t4 & 1) ? qsc : qsc * 65536.0f;
+    f1[nt] = (t4 & 1) ? 0.0f : qsc * 256.0f;
+  }
+
+  // running state per n-tile (this lane's head 2*nt + t4/2)
+  float m_run[NT], l_run[NT], pmax[NT], o_acc[NT][4][2][2];
+  int acc[NT][4][2][4];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    m_run[nt] = -INFINITY;
+    l_run[nt] = 0.0f;
+    pmax[nt] = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int pi = 0; pi < 2; ++pi) {
+        o_acc[nt][j][pi][0] = o_acc[nt][j][pi][1] = 0.0f;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[nt][j][pi][e] = 0;
+      }
+  }
+  // flush the int32 PV sums of n-tile nt into float (lanes where do_flush)
+  auto flush = [&](int nt, bool do_flush) {
+    const float ps = pmax[nt] / kLimbMax;
+    const float F0 = (t4 & 1) ? ps : ps * 65536.0f;
+    const float F1 = (t4 & 1) ? 0.0f : ps * 256.0f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int pi = 0; pi < 2; ++pi) {
+        float lo = F0 * static_cast<float>(acc[nt][j][pi][0]) + F1 * static_cast<float>(acc[nt][j][pi][1]);
+        float hi = F0 * static_cast<float>(acc[nt][j][pi][2]) + F1 * static_cast<float>(acc[nt][j][pi][3]);
+        lo += __shfl_xor_sync(0xffffffffu, lo, 1);
+        hi += __shfl_xor_sync(0xffffffffu, hi, 1);
+        if (do_flush) {
+          o_acc[nt][j][pi][0] += lo;
+          o_acc[nt][j][pi][1] += hi;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) acc[nt][j][pi][e] = 0;
+        }
+      }
+  };
+
+  const auto* vscp = reinterpret_cast<const typename SE::T*>(p.vsc);
+  const int64_t vsc_row = b * p.vscb + kvh * p.vsch;
+  unsigned char* my_limb = plimb + warp * NT * 256;
+  bool ok = true;
+  int consumed = 0;
+  for (int t = 0; t < ntiles; ++t) {
+    const int st = t % kStagesM;
+    const uint32_t par = (t / kStagesM) & 1;
+    const int base_tok = t * kTileT + warp * 32;  // first token of this warp (within split)
+    // this lane's own tokens: row g (even t4) or g + 8 (odd t4) of both 16-row blocks
+    float vsf[2];
+    bool own_ok[2];
+#pragma unroll
+    for (int rb = 0; rb < 2; ++rb) {
+      const int tok = base_tok + rb * 16 + g + 8 * (t4 & 1);
+      own_ok[rb] = tok < ntok;
+      vsf[rb] = own_ok[rb] ? SE::to_f32(vscp[vsc_row + static_cast<int64_t>(s_begin + tok) * p.vscs]) : 0.0f;
+    }
+    if (!mbar_wait(&full[st], par)) {
+      ok = false;
+      break;
+    }
+    consumed = t + 1;
+    const uint32_t kt = smem_u32(ring + st * 2 * kTileB);
+    const uint32_t vt = kt + kTileB;
+
+    // ---- scores: 2 row blocks of 16 tokens x 4 k-steps of 32 channels
+    float sc[NT][2][2];  // [nt][rb][lo=row g, hi=row g+8]
+#pragma unroll
+    for (int rb = 0; rb < 2; ++rb) {
+      int sacc[NT][4];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) sacc[nt][e] = 0;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int mat = lane >> 3;
+        const int row = warp * 32 + rb * 16 + (mat & 1) * 8 + (lane & 7);
+        uint32_t a[4];
+        ldsm_x4(kt + swz(row, 2 * j + (mat >> 1)), a);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) mma_s8(sacc[nt], a, bq[nt][j][0], bq[nt][j][1]);
+      }
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        float lo = f0[nt] * static_cast<float>(sacc[nt][0]) + f1[nt] * static_cast<float>(sacc[nt][1]);
+        float hi = f0[nt] * static_cast<float>(sacc[nt][2]) + f1[nt] * static_cast<float>(sacc[nt][3]);
+        lo += __shfl_xor_sync(0xffffffffu, lo, 1);
+        hi += __shfl_xor_sync(0xffffffffu, hi, 1);
+        const int tok = base_tok + rb * 16 + g;
+        sc[nt][rb][0] = tok < ntok ? lo : -INFINITY;
+        sc[nt][rb][1] = tok + 8 < ntok ? hi : -INFINITY;
+      }
+    }
+    // ---- online softmax per head; p' limbs of this lane's own two tokens
+    __syncwarp();  // the previous tile's limb reads are done
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      float mt = fmaxf(fmaxf(sc[nt][0][0], sc[nt][0][1]), fmaxf(sc[nt][1][0], sc[nt][1][1]));
+      mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 4));
+      mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 8));
+      mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 16));
+      const float m_new = fmaxf(m_run[nt], mt);
+      float pr[2], pv[2];
+      float pm = 0.0f;
+#pragma unroll
+      for (int rb = 0; rb < 2; ++rb) {
+        const float sown = (t4 & 1) ? sc[nt][rb][1] : sc[nt][rb][0];
+        pr[rb] = own_ok[rb] ? exp2f(sown - m_new) : 0.0f;
+        pv[rb] = pr[rb] * vsf[rb];
+        pm = fmaxf(pm, pv[rb]);
+      }
+      pm = fmaxf(pm, __shfl_xor_sync(0xffffffffu, pm, 1));
+      pm = fmaxf(pm, __shfl_xor_sync(0xffffffffu, pm, 4));
+      pm = fmaxf(pm, __shfl_xor_sync(0xffffffffu, pm, 8));
+      pm = fmaxf(pm, __shfl_xor_sync(0xffffffffu, pm, 16));
+      const bool rescale = m_new > m_run[nt];
+      const bool grow = pm > pmax[nt];
+      if (__any_sync(0xffffffffu, rescale || grow)) {
+        flush(nt, rescale || grow);
+        if (rescale) {
+          const float alpha = exp2f(m_run[nt] - m_new);  // 0 on the first tile
+          l_run[nt] *= alpha;
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+#pragma unroll
+            for (int pi = 0; pi < 2; ++pi) {
+              o_acc[nt][j][pi][0] *= alpha;
+              o_acc[nt][j][pi][1] *= alpha;
+            }
+        }
+        if (grow) pmax[nt] = 2.0f * pm;
+      }
+      m_run[nt] = m_new;
+      l_run[nt] += pr[0] + pr[1];
+      const float inv_ps = pmax[nt] > 0.0f ? kLimbMax / pmax[nt] : 0.0f;
+      const int hh = t4 >> 1;
+      unsigned char* dst = my_limb + nt * 256;
+#pragma unroll
+      for (int rb = 0; rb < 2; ++rb) {
+        const int x = min(__float2int_rn(pv[rb] * inv_ps), static_cast<int>(kLimbMax));
+        int la, lb, lc;
+        limbs24(x, la, lb, lc);
+        const int k = pv_k(rb * 16 + g + 8 * (t4 & 1));
+        dst[(4 * hh + 0) * 32 + k] = static_cast<unsigned char>(la);
+        dst[(4 * hh + 1) * 32 + k] = static_cast<unsigned char>(lb);
+        dst[(4 * hh + 2) * 32 + k] = static_cast<unsigned char>(lc);
+      }
+    }
+    __syncwarp();
+    // ---- PV: A = V^T (ldmatrix.trans + byte permute), B = p' limbs
+    uint32_t bp[NT][2];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      const unsigned char* src = my_limb + nt * 256 + g * 32;
+      bp[nt][0] = *reinterpret_cast<const uint32_t*>(src + 4 * t4);
+      bp[nt][1] = *reinterpret_cast<const uint32_t*>(src + 16 + 4 * t4);
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint32_t ae[4], ao[4];
+#pragma unroll
+      for (int th = 0; th < 2; ++th) {
+        const int mat = lane >> 3;
+        const int row = warp * 32 + th * 16 + (mat & 1) * 8 + (lane & 7);
+        uint32_t r[4];
+        ldsm_x4_t(vt + swz(row, 2 * j + (mat >> 1)), r);
+        ae[2 * th + 0] = prmt(r[0], r[1], 0x6420u);
+        ao[2 * th + 0] = prmt(r[0], r[1], 0x7531u);
+        ae[2 * th + 1] = prmt(r[2], r[3], 0x6420u);
+        ao[2 * th + 1] = prmt(r[2], r[3], 0x7531u);
+      }
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        mma_s8(acc[nt][j][0], ae, bp[nt][0], bp[nt][1]);
+        mma_s8(acc[nt][j][1], ao, bp[nt][0], bp[nt][1]);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[st]);
+    if (tid == 0 && t + kStagesM < ntiles) {
+      if (!mbar_wait(&empty[st], par)) {
+        ok = false;
+        break;
+      }
+      issue(t + kStagesM);
+    }
+  }
+  if (!ok) {
+    report_error(p.ws_status, HQ_ERR_DEVICE_TIMEOUT);
+    if (tid == 0)
+      for (int t = consumed; t < issued; ++t) mbar_wait(&full[t % kStagesM], (t / kStagesM) & 1);
+  }
+  __syncthreads();
+  if (__syncthreads_or(!ok)) return;
+
+  // ---- block epilogue: flush, then merge the 4 warps
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) flush(nt, true);
+  float* wo = reinterpret_cast<float*>(ring);                 // [kWarps][NREP][kD]
+  float* wl = wo + kWarps * NREP * kD;                        // [kWarps][NREP]
+  float* wm = wl + kWarps * NREP;                             // [kWarps][NREP]
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const int h = 2 * nt + (t4 >> 1);
+    float l = l_run[nt];
+    l += __shfl_xor_sync(0xffffffffu, l, 1);
+    l += __shfl_xor_sync(0xffffffffu, l, 4);
+    l += __shfl_xor_sync(0xffffffffu, l, 8);
+    l += __shfl_xor_sync(0xffffffffu, l, 16);
+    if (h < NREP) {
+      float* dst = wo + (warp * NREP + h) * kD;
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int pi = 0; pi < 2; ++pi) {
+          // even lane writes the row-g channel, odd lane the row-g+8 channel
+          const int d = 32 * j + 2 * g + pi + 16 * (t4 & 1);
+          dst[d] = (t4 & 1) ? o_acc[nt][j][pi][1] : o_acc[nt][j][pi][0];
+        }
+      if (g == 0 && (t4 & 1) == 0) {
+        wl[warp * NREP + h] = l;
+        wm[warp * NREP + h] = m_run[nt];
+      }
+    }
+  }
+  __syncthreads();
+  const int d = tid;
+  float Ms[NREP], Ls[NREP], Os[NREP];
+#pragma unroll
+  for (int r = 0; r < NREP; ++r) {
+    float M = wm[r];
+#pragma unroll
+    for (int w = 1; w < kWarps; ++w) M = fmaxf(M, wm[w * NREP + r]);
+    float L = 0.0f, O = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      const float mw = wm[w * NREP + r];
+      const float f = mw == -INFINITY ? 0.0f : exp2f(mw - M);
+      L += wl[w * NREP + r] * f;
+      O += wo[(w * NREP + r) * kD + d] * f;
+    }
+    Ms[r] = M;
+    Ls[r] = L;
+    Os[r] = O;
+  }
+  if (p.n_split == 1) {
+#pragma unroll
+    for (int r = 0; r < NREP; ++r) emit<QDT>(p, b, kvh * NREP + r, d, Ms[r], Ls[r], Os[r]);
+    return;
+  }
+#pragma unroll
+  for (int r = 0; r < NREP; ++r) publish_split(p, b, kvh * NREP + r, split, d, Ms[r], Ls[r], Os[r]);
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    const int ticket = atomicAdd(p.ws_count + b * p.Hkv + kvh, 1);
+    s_last = ticket == p.n_split - 1;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  merge_splits<NREP, QDT>(p, b, kvh, reinterpret_cast<float*>(ring));
 }
+
+}  // namespace mmak
 
 // ------------------------------------------------------------------ cross-part combine
 template <int ODT>
@@ -510,8 +1036,8 @@ inline int max_splits(int units, int tiles, int sms) {
 }
 
 // Picks the tile count per split that minimises (waves x tiles per block).
-inline Plan make_plan(int units, int S, int slots, int sms) {
-  const int tiles = (S + kTile - 1) / kTile;
+inline Plan make_plan(int units, int S, int slots, int sms, int tile = kTile) {
+  const int tiles = (S + tile - 1) / tile;
   if (tiles <= 0) return {1, 1};
   const int cap = max_splits(units, tiles, sms);
   Plan best{1, tiles};
@@ -539,7 +1065,7 @@ inline size_t workspace_bytes(int B, int Hq, int Hkv, int S, int sms) {
   const int tiles = (S + kTile - 1) / kTile;
   const int ms = max_splits(units > 0 ? units : 1, tiles, sms);
   return 256 + align256(sizeof(int) * static_cast<size_t>(B) * Hkv) +
-         sizeof(float) * static_cast<size_t>(B) * Hq * ms * (kD + 2);
+         sizeof(float) * static_cast<size_t>(B) * Hq * ms * kPartRow;
 }
 
 template <int NREP, int KVDT, int SDT, int QDT>
@@ -572,6 +1098,85 @@ int launch(Params p, int B, void* ws, size_t ws_bytes, cudaStream_t st) {
   kern<<<grid, kThreads, C::SMEM, st>>>(p);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? HQ_OK : static_cast<int>(e);
+}
+
+// ---- tensor maps for the int8 kernel (driver entry point, no libcuda link)
+inline PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static std::atomic<void*> cached{nullptr};
+  void* f = cached.load(std::memory_order_acquire);
+  if (!f) {
+    cudaDriverEntryPointQueryResult qr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &qr) !=
+            cudaSuccess ||
+        qr != cudaDriverEntryPointSuccess || !f)
+      return nullptr;
+    cached.store(f, std::memory_order_release);
+  }
+  return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+}
+
+// int8 [B, Hkv, S, 128] with byte strides (sb, sh, 128): boxes of 128 tokens x 128 bytes,
+// 128-byte swizzle, zero fill past S.
+inline int encode_kv_map(CUtensorMap* m, const void* base, int64_t sb, int64_t sh, int S, int Hkv,
+                         int B) {
+  auto enc = encode_fn();
+  if (!enc) return HQ_ERR_UNSUPPORTED;
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(kD), static_cast<cuuint64_t>(S > 0 ? S : 1),
+                        static_cast<cuuint64_t>(Hkv), static_cast<cuuint64_t>(B)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(kD), static_cast<cuuint64_t>(sh),
+                           static_cast<cuuint64_t>(sb)};
+  cuuint32_t box[4] = {static_cast<cuuint32_t>(kD), static_cast<cuuint32_t>(mmak::kTileT), 1, 1};
+  cuuint32_t es[4] = {1, 1, 1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void*>(base), dims, strides,
+                   box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? HQ_OK : HQ_ERR_INVALID_ARGUMENT;
+}
+
+template <int NREP, int SDT, int QDT>
+int launch_mma(Params p, int B, void* ws, size_t ws_bytes, cudaStream_t st) {
+  using C = mmak::MCfg<NREP>;
+  auto kern = mmak::decode_mma_kernel<NREP, SDT, QDT>;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static std::atomic<int> occ[64];
+  int per_sm = (dev >= 0 && dev < 64) ? occ[dev].load(std::memory_order_relaxed) : 0;
+  if (per_sm <= 0) {
+    cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(kern),
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, C::SMEM);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    if (per_sm <= 0) return HQ_ERR_UNSUPPORTED;
+    if (dev >= 0 && dev < 64) occ[dev].store(per_sm, std::memory_order_relaxed);
+  }
+  const int sms = sm_count(dev);
+  const Plan pl = make_plan(B * p.Hkv, p.S, per_sm * sms, sms, mmak::kTileT);
+  if (ws_bytes < workspace_bytes(B, p.Hq, p.Hkv, p.S, sms)) return HQ_ERR_WORKSPACE;
+  CUtensorMap tmk, tmv;
+  int rc = encode_kv_map(&tmk, p.k, p.kvsb, p.kvsh, p.S, p.Hkv, B);
+  if (rc == HQ_OK) rc = encode_kv_map(&tmv, p.v, p.kvsb, p.kvsh, p.S, p.Hkv, B);
+  if (rc != HQ_OK) return rc;
+  char* w = static_cast<char*>(ws);
+  p.ws_status = reinterpret_cast<int*>(w);
+  p.ws_count = reinterpret_cast<int*>(w + 256);
+  p.ws_part = reinterpret_cast<float*>(w + 256 + align256(sizeof(int) * static_cast<size_t>(B) * p.Hkv));
+  p.n_split = pl.n_split;
+  p.tiles_per_split = pl.tiles_per_split;
+  dim3 grid(pl.n_split, p.Hkv, B);
+  kern<<<grid, kThreads, C::SMEM, st>>>(tmk, tmv, p);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? HQ_OK : static_cast<int>(e);
+}
+
+template <int SDT, int QDT>
+int dispatch_mma(int nrep, const Params& p, int B, void* ws, size_t wsb, cudaStream_t st) {
+  switch (nrep) {
+    case 1: return launch_mma<1, SDT, QDT>(p, B, ws, wsb, st);
+    case 2: return launch_mma<2, SDT, QDT>(p, B, ws, wsb, st);
+    case 4: return launch_mma<4, SDT, QDT>(p, B, ws, wsb, st);
+    default: return HQ_ERR_UNSUPPORTED;
+  }
 }
 
 template <int KVDT, int SDT, int QDT>
@@ -656,9 +1261,9 @@ extern "C" int hq_decode_int8(const void* q, int q_dtype, const int64_t q_stride
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
 #define HQ_Q(SDT)                                                                                \
   switch (q_dtype) {                                                                             \
-    case HQ_DTYPE_BF16: return dispatch_nrep<HQ_DTYPE_I8, SDT, HQ_DTYPE_BF16>(nrep, p, B, workspace, workspace_bytes, st); \
-    case HQ_DTYPE_F16: return dispatch_nrep<HQ_DTYPE_I8, SDT, HQ_DTYPE_F16>(nrep, p, B, workspace, workspace_bytes, st);   \
-    case HQ_DTYPE_F32: return dispatch_nrep<HQ_DTYPE_I8, SDT, HQ_DTYPE_F32>(nrep, p, B, workspace, workspace_bytes, st);   \
+    case HQ_DTYPE_BF16: return dispatch_mma<SDT, HQ_DTYPE_BF16>(nrep, p, B, workspace, workspace_bytes, st); \
+    case HQ_DTYPE_F16: return dispatch_mma<SDT, HQ_DTYPE_F16>(nrep, p, B, workspace, workspace_bytes, st);   \
+    case HQ_DTYPE_F32: return dispatch_mma<SDT, HQ_DTYPE_F32>(nrep, p, B, workspace, workspace_bytes, st);   \
     default: return HQ_ERR_UNSUPPORTED;                                                          \
   }
   if (scale_dtype == HQ_DTYPE_F16) {

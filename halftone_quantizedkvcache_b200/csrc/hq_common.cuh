@@ -90,12 +90,37 @@ template <> struct Vec16<HQ_DTYPE_F32> {
 // elements (about 1e-3 of bf16 inputs) redo the true IEEE divide.  The
 // equivalence is checked exhaustively for every bf16 and fp16 (x, amax) pair by
 // tests/test_quant_rounding_model.py and on the GPU by the parity tests.
+//
+// For 16-bit inputs the kernels skip the guard altogether: with the exact
+// reciprocal y = RN(1/scale), Markstein's division with two correction steps
+//   q0 = x*y, r0 = fma(-q0, s, x), q1 = fma(r0, y, q0), r1 = fma(-q1, s, x),
+//   q2 = fma(r1, y, q1)
+// returns the IEEE quotient RN(x/s) for every bf16 and fp16 x with |x| <= amax
+// (checked exhaustively by the model test), so the code is rint(q2) with no
+// branch.  amax itself has 8 (bf16) or 11 (fp16) significant bits, and
+// scale = RN(amax / 127) needs no divide either: q = amax * RN(1/127), then one
+// FMA correction q + fma(-q, 127, amax) * RN(1/127), exact for every such
+// mantissa; the clamp value 1e-8 (not 16-bit representable) takes the divide.
+constexpr float kInv127 = 0.007874015718698502f;  // RN(1/127), 0x3c010204
+
 struct Quantizer {
   float scale;  // RN(amax / 127)
   float rcp;    // RN(1 / scale)
   __device__ __forceinline__ static Quantizer from_amax(float amax) {
     Quantizer q;
     q.scale = __fdiv_rn(fmaxf(amax, 1e-8f), 127.0f);
+    q.rcp = __frcp_rn(q.scale);
+    return q;
+  }
+  // amax must be a bf16 or fp16 value (or below 1e-8)
+  __device__ __forceinline__ static Quantizer from_amax16(float amax) {
+    Quantizer q;
+    if (amax >= 1e-8f) {
+      const float s0 = amax * kInv127;
+      q.scale = __fmaf_rn(__fmaf_rn(-s0, 127.0f, amax), kInv127, s0);
+    } else {
+      q.scale = __fdiv_rn(1e-8f, 127.0f);
+    }
     q.rcp = __frcp_rn(q.scale);
     return q;
   }
@@ -156,6 +181,75 @@ __device__ __forceinline__ F2 f2_mul(F2 a, F2 b) {
   F2 d;
   asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d.v) : "l"(a.v), "l"(b.v));
   return d;
+}
+
+__device__ __forceinline__ F2 f2_sub(F2 a, F2 b) {
+  F2 d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d.v) : "l"(a.v), "l"(b.v));
+  return d;
+}
+__device__ __forceinline__ uint32_t f2_lo_bits(F2 x) { return static_cast<uint32_t>(x.v); }
+__device__ __forceinline__ uint32_t f2_hi_bits(F2 x) { return static_cast<uint32_t>(x.v >> 32); }
+
+// Packed form of Quantizer::code for two elements with reciprocals r.  The low
+// byte of each float of y is the code (y = 1.5 * 2^23 + k, |k| <= 127); dev
+// accumulates the largest |residual| so the caller can take the exact path
+// for the whole vector when any element lies within 2^-15 of a tie.
+__device__ __forceinline__ F2 quant_pair(F2 x, F2 r, float& dev) {
+  const F2 m2 = f2_make(12582912.0f, 12582912.0f);
+  const F2 y = f2_fma(x, r, m2);
+  const F2 d = f2_fma(x, r, f2_sub(m2, y));  // x*r - k, exact product, one rounding
+  float d0, d1;
+  f2_split(d, d0, d1);
+  dev = fmaxf(dev, fmaxf(fabsf(d0), fabsf(d1)));
+  return y;
+}
+constexpr float kTieGuard = 0.499969482421875f;  // 0.5 - 2^-15
+
+// Low bytes of four floats -> one word of int8 codes.
+__device__ __forceinline__ uint32_t pack_low_bytes(F2 a, F2 b) {
+  const uint32_t t0 = prmt(f2_lo_bits(a), f2_hi_bits(a), 0x0040u);
+  const uint32_t t1 = prmt(f2_lo_bits(b), f2_hi_bits(b), 0x0040u);
+  return prmt(t0, t1, 0x5410u);
+}
+
+// Exact RN(x / s) for a pair (16-bit inputs, see Quantizer): ns = -s, y = RN(1/s).
+__device__ __forceinline__ F2 quot_pair(F2 x, F2 ns, F2 y) {
+  const F2 q0 = f2_mul(x, y);
+  const F2 q1 = f2_fma(f2_fma(q0, ns, x), y, q0);
+  return f2_fma(f2_fma(q1, ns, x), y, q1);
+}
+// rint(q) (half to even) as the low byte of q + 1.5 * 2^23
+__device__ __forceinline__ F2 round_magic(F2 q) {
+  return f2_add(q, f2_make(12582912.0f, 12582912.0f));
+}
+
+// max(|acc|, |w|) per 16-bit lane (the sign bit of the result is meaningless)
+template <int DT>
+__device__ __forceinline__ uint32_t absmax_x2(uint32_t acc, uint32_t w);
+template <>
+__device__ __forceinline__ uint32_t absmax_x2<HQ_DTYPE_BF16>(uint32_t acc, uint32_t w) {
+  uint32_t d;
+  asm("max.xorsign.abs.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(acc), "r"(w));
+  return d;
+}
+template <>
+__device__ __forceinline__ uint32_t absmax_x2<HQ_DTYPE_F16>(uint32_t acc, uint32_t w) {
+  uint32_t d;
+  asm("max.xorsign.abs.f16x2 %0, %1, %2;" : "=r"(d) : "r"(acc), "r"(w));
+  return d;
+}
+// the larger magnitude of the two halves, as float
+template <int DT>
+__device__ __forceinline__ float absmax_of_x2(uint32_t w);
+template <>
+__device__ __forceinline__ float absmax_of_x2<HQ_DTYPE_BF16>(uint32_t w) {
+  return fmaxf(fabsf(__uint_as_float(w << 16)), fabsf(__uint_as_float(w & 0xffff0000u)));
+}
+template <>
+__device__ __forceinline__ float absmax_of_x2<HQ_DTYPE_F16>(uint32_t w) {
+  const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w));
+  return fmaxf(fabsf(f.x), fabsf(f.y));
 }
 
 __device__ __forceinline__ void s8x4_to_f2x2(uint32_t w, F2& lo, F2& hi) {

@@ -9,12 +9,10 @@
 //   * V per token: each row of D elements is read once with 16-byte vector
 //     loads by D*esize/16 lanes, reduced with warp shuffles, and written as
 //     packed int8 (8 codes per 16-byte input vector).
-//   * K per channel: a cooperative persistent grid.  A (b, h) slab of S x D is
-//     cut into 32 KB chunks of whole rows; each block loads its chunk once
-//     into registers (row-contiguous, coalesced), reduces its column maxima,
-//     publishes them with atomicMax, waits (bounded) until every chunk of the
-//     slab has published, then quantizes the chunk still held in registers.
-//     HBM traffic is the algorithmic minimum: 1 read + 1 int8 write per element.
+//   * K per channel: an ordered work queue over 32 KB chunks of whole rows.
+//     For each group of slabs (<= 24 MB of input) one pass publishes the
+//     column maxima and a second pass, one group later, re-reads the chunks
+//     from L2 and writes codes, so HBM sees 1 read + 1 int8 write per element.
 //   * Append: one block per (b, h) quantizes the few new tokens of K (per
 //     channel over the new tokens; scale not stored) and V (per token; scale
 //     stored), exactly as the reference's update() does on a non-empty layer.
@@ -59,64 +57,161 @@ __device__ __forceinline__ uint4 ldg_stream(const void* p) {
   return v;
 }
 
+// Unpacks a 16-byte vector into packed float pairs (4 pairs for 16-bit types, 2 for f32).
+template <int DT>
+__device__ __forceinline__ void vec_to_f2(const uint4& v, F2* f);
+template <>
+__device__ __forceinline__ void vec_to_f2<HQ_DTYPE_BF16>(const uint4& v, F2* f) {
+  f[0] = bf16x2_to_f2(v.x);
+  f[1] = bf16x2_to_f2(v.y);
+  f[2] = bf16x2_to_f2(v.z);
+  f[3] = bf16x2_to_f2(v.w);
+}
+template <>
+__device__ __forceinline__ void vec_to_f2<HQ_DTYPE_F16>(const uint4& v, F2* f) {
+  f[0] = f16x2_to_f2(v.x);
+  f[1] = f16x2_to_f2(v.y);
+  f[2] = f16x2_to_f2(v.z);
+  f[3] = f16x2_to_f2(v.w);
+}
+template <>
+__device__ __forceinline__ void vec_to_f2<HQ_DTYPE_F32>(const uint4& v, F2* f) {
+  f[0].v = (static_cast<unsigned long long>(v.y) << 32) | v.x;
+  f[1].v = (static_cast<unsigned long long>(v.w) << 32) | v.z;
+}
+
+// Quantizes one 16-byte vector (VE elements) with per-element quantizers qz
+// (pairs: ns2 = -scale, rcp2 = RN(1/scale)) and stores its VE codes at dst.
+// 16-bit inputs: exact quotient, no branch.  f32 inputs: one-FFMA fast path
+// guarded by the tie check, exact divide for the (rare) flagged vector.
+template <int DT>
+__device__ __forceinline__ void quant_vec_store(const uint4& v, const F2* ns2, const F2* rcp2,
+                                                const Quantizer* qz, int8_t* dst) {
+  constexpr int VE = Vec16<DT>::N;
+  F2 x[VE / 2];
+  vec_to_f2<DT>(v, x);
+  F2 y[VE / 2];
+  if constexpr (DT != HQ_DTYPE_F32) {
+#pragma unroll
+    for (int p = 0; p < VE / 2; ++p) y[p] = round_magic(quot_pair(x[p], ns2[p], rcp2[p]));
+  } else {
+    float dev = 0.0f;
+#pragma unroll
+    for (int p = 0; p < VE / 2; ++p) y[p] = quant_pair(x[p], rcp2[p], dev);
+    if (dev > kTieGuard) {  // rare: some element sits next to a rounding tie
+      float f[VE];
+      Vec16<DT>::unpack(v, f);
+      int c[VE];
+#pragma unroll
+      for (int e = 0; e < VE; ++e) c[e] = qz[e].code(f[e]);
+      store_codes<VE>(dst, c);
+      return;
+    }
+  }
+  if constexpr (VE == 8) {
+    uint2 w;
+    w.x = pack_low_bytes(y[0], y[1]);
+    w.y = pack_low_bytes(y[2], y[3]);
+    *reinterpret_cast<uint2*>(dst) = w;
+  } else {
+    *reinterpret_cast<uint32_t*>(dst) = pack_low_bytes(y[0], y[1]);
+  }
+}
+
+template <int DT>
+__device__ __forceinline__ Quantizer quantizer_for(float amax) {
+  return DT == HQ_DTYPE_F32 ? Quantizer::from_amax(amax) : Quantizer::from_amax16(amax);
+}
+
+// |x| maximum over one 16-byte vector, folded into a running float maximum
+template <int DT>
+__device__ __forceinline__ float vec_absmax(const uint4& v, float m) {
+  if constexpr (DT == HQ_DTYPE_F32) {
+    float f[4];
+    Vec16<DT>::unpack(v, f);
+    return fmaxf(fmaxf(m, fmaxf(fabsf(f[0]), fabsf(f[1]))), fmaxf(fabsf(f[2]), fabsf(f[3])));
+  } else {
+    const uint32_t a = absmax_x2<DT>(absmax_x2<DT>(v.x, v.y), absmax_x2<DT>(v.z, v.w));
+    return fmaxf(m, absmax_of_x2<DT>(a));
+  }
+}
+
+// grid = (token blocks, slabs); each warp quantizes kIters groups of
+// kRowsPerWarp rows, all of whose loads are issued before any compute.
 template <int DT, int D>
 __global__ void __launch_bounds__(kThreads) quant_v_kernel(
-    const char* __restrict__ x, int64_t xsb, int64_t xsh, int64_t xss, int H, int S,
-    int64_t n_rows, int8_t* __restrict__ q, int64_t qsb, int64_t qsh, int64_t qss,
-    float* __restrict__ sc32, __half* __restrict__ sc16, int64_t ssb, int64_t ssh, int64_t sss) {
+    const char* __restrict__ x, int64_t xsb, int64_t xsh, int64_t xss, int H, int S, int n_slabs,
+    int8_t* __restrict__ q, int64_t qsb, int64_t qsh, int64_t qss, float* __restrict__ sc32,
+    __half* __restrict__ sc16, int64_t ssb, int64_t ssh, int64_t sss) {
   using Sh = VShape<DT, D>;
   constexpr int EB = Elem<DT>::kBytes;
-  const int lane = threadIdx.x & 31;
+  constexpr int VE = Sh::kVecElems;
+  constexpr int IT = Sh::kVecPerLane >= 4 ? 1 : 4 / Sh::kVecPerLane;
+  constexpr int kRowsPerWarp = Sh::kRowsPerWarp * IT;
+  constexpr int kRowsPerBlock = (kThreads / 32) * kRowsPerWarp;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int sub = lane % Sh::kLanesPerRow;
-  const int64_t warp0 = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) >> 5;
-  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * kThreads) >> 5;
-  for (int64_t w = warp0; w * Sh::kRowsPerWarp < n_rows; w += nwarps) {
-    const int64_t r = w * Sh::kRowsPerWarp + lane / Sh::kLanesPerRow;
-    const bool valid = r < n_rows;
-    int64_t s = 0, h = 0, b = 0;
-    if (valid) {
-      s = r % S;
-      const int64_t bh = r / S;
-      h = bh % H;
-      b = bh / H;
-    }
-    uint4 vec[Sh::kVecPerLane];
-    float amax = 0.0f;
-    const char* row = x + (b * xsb + h * xsh + s * xss) * EB;
+  for (int slab = blockIdx.y; slab < n_slabs; slab += gridDim.y) {
+    const int b = slab / H, h = slab - (slab / H) * H;
+    const char* base = x + (static_cast<int64_t>(b) * xsb + static_cast<int64_t>(h) * xsh) * EB;
+    int8_t* qbase = q + static_cast<int64_t>(b) * qsb + static_cast<int64_t>(h) * qsh;
+    const int s0 = blockIdx.x * kRowsPerBlock + warp * kRowsPerWarp + lane / Sh::kLanesPerRow;
+    uint4 vec[IT][Sh::kVecPerLane];
 #pragma unroll
-    for (int i = 0; i < Sh::kVecPerLane; ++i) {
-      vec[i] = valid ? ldg_stream(row + (sub + i * Sh::kLanesPerRow) * 16) : make_uint4(0, 0, 0, 0);
-      float f[Vec16<DT>::N];
-      Vec16<DT>::unpack(vec[i], f);
+    for (int it = 0; it < IT; ++it) {
+      const int s = s0 + it * Sh::kRowsPerWarp;
 #pragma unroll
-      for (int e = 0; e < Vec16<DT>::N; ++e) amax = fmaxf(amax, fabsf(f[e]));
+      for (int i = 0; i < Sh::kVecPerLane; ++i)
+        vec[it][i] = s < S ? ldg_stream(base + static_cast<int64_t>(s) * xss * EB +
+                                        (sub + i * Sh::kLanesPerRow) * 16)
+                           : make_uint4(0, 0, 0, 0);
     }
 #pragma unroll
-    for (int off = Sh::kLanesPerRow / 2; off > 0; off >>= 1)
-      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
-    if (!valid) continue;
-    const Quantizer qz = Quantizer::from_amax(amax);
-    int8_t* qrow = q + b * qsb + h * qsh + s * qss;
+    for (int it = 0; it < IT; ++it) {
+      const int s = s0 + it * Sh::kRowsPerWarp;
+      float amax = 0.0f;
 #pragma unroll
-    for (int i = 0; i < Sh::kVecPerLane; ++i) {
-      float f[Vec16<DT>::N];
-      Vec16<DT>::unpack(vec[i], f);
-      int c[Vec16<DT>::N];
+      for (int i = 0; i < Sh::kVecPerLane; ++i) amax = vec_absmax<DT>(vec[it][i], amax);
 #pragma unroll
-      for (int e = 0; e < Vec16<DT>::N; ++e) c[e] = qz.code(f[e]);
-      store_codes<Vec16<DT>::N>(qrow + (sub + i * Sh::kLanesPerRow) * Sh::kVecElems, c);
-    }
-    if (sub == 0) {
-      const int64_t so = b * ssb + h * ssh + s * sss;
-      if (sc32) sc32[so] = qz.scale;
-      if (sc16) sc16[so] = __float2half_rn(qz.scale);
+      for (int off = Sh::kLanesPerRow / 2; off > 0; off >>= 1)
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+      if (s >= S) continue;
+      const Quantizer qz = quantizer_for<DT>(amax);
+      Quantizer qzv[VE];
+      F2 rcp2[VE / 2], ns2[VE / 2];
+#pragma unroll
+      for (int e = 0; e < VE; ++e) qzv[e] = qz;
+#pragma unroll
+      for (int p = 0; p < VE / 2; ++p) {
+        rcp2[p] = f2_make(qz.rcp, qz.rcp);
+        ns2[p] = f2_make(-qz.scale, -qz.scale);
+      }
+#pragma unroll
+      for (int i = 0; i < Sh::kVecPerLane; ++i)
+        quant_vec_store<DT>(vec[it][i], ns2, rcp2, qzv,
+                            qbase + static_cast<int64_t>(s) * qss + (sub + i * Sh::kLanesPerRow) * VE);
+      if (sub == 0) {
+        const int64_t so = static_cast<int64_t>(b) * ssb + static_cast<int64_t>(h) * ssh +
+                           static_cast<int64_t>(s) * sss;
+        if (sc32) sc32[so] = qz.scale;
+        if (sc16) sc16[so] = __float2half_rn(qz.scale);
+      }
     }
   }
 }
 
 // ------------------------------------------------------------------ K per channel
-// Chunk = kPasses x (kThreads / kVecPerRow) rows; every thread keeps kPasses
-// 16-byte vectors of one fixed column group in registers.
+// A (b, h) slab of S x D is cut into chunks of kRowsPerChunk whole rows (32 KB
+// of input); every thread keeps kPasses 16-byte vectors of one fixed column
+// group of a chunk in registers.
+//
+// Work is an ordered queue of items (one chunk each), dequeued with an atomic
+// counter.  Slabs form groups of at most kGroupBytes of input; for group g,
+// A(g) items publish column maxima (atomicMax) and B(g) items re-read their
+// chunk - from L2, since the group was read moments before - and write codes.
+// Queue order A0, A1, B0, A2, B1, ..., A(n-1), B(n-2), B(n-1): a B(g) item only
+// waits (bounded) for A(g) items, which were dequeued earlier by running blocks
+// and never wait themselves, so no block depends on a block that is not running.
 template <int DT, int D>
 struct KShape {
   static constexpr int kVecElems = 16 / Elem<DT>::kBytes;
@@ -130,57 +225,160 @@ struct KShape {
   static constexpr int kRedRows = kVecPerRow <= 32 ? kWarps : kRowSlots;
 };
 
+constexpr size_t kGroupBytes = size_t(24) << 20;
+
 struct KWorkspace {
   int* status;        // [1]
-  int* count;         // [B*H] chunks that published their maxima
+  int* next;          // [1] queue head
+  int* done;          // [groups] A items finished
+  int* ready;         // [groups] quantizer table of the group written
   unsigned* amax;     // [B*H*D] column absmax as float bits (all >= 0)
+  float2* qtab;       // [B*H*D] (scale, reciprocal) per column
+};
+
+struct KPlan {
+  int n_slabs, n_chunks, spg, n_groups;
+  int total;          // queue length (fused: one item per slab)
+  int fused;          // a slab is one chunk: no queue phases
 };
 
 __host__ __device__ inline size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
 
-// mode 0: fused (publish maxima, wait for the slab, write codes; cooperative launch)
-// mode 1: publish maxima only          mode 2: write codes from published maxima
+// L2 policies: A items keep their chunk in L2 for the B re-read, B items mark
+// it as last use.
+__device__ __forceinline__ uint64_t l2_policy_keep() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t l2_policy_drop() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint4 ldg_hint(const void* p, uint64_t pol) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0, %1, %2, %3}, [%4], %5;"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p), "l"(pol));
+  return v;
+}
+
 template <int DT, int D>
 __global__ void __launch_bounds__(kThreads, 3) quant_k_kernel(
-    const char* __restrict__ x, int64_t xsb, int64_t xsh, int64_t xss, int H, int S,
-    int n_chunks, int64_t n_tasks, int8_t* __restrict__ q, int64_t qsb, int64_t qsh, int64_t qss,
-    float* __restrict__ sc32, __half* __restrict__ sc16, KWorkspace ws, int mode) {
+    const char* __restrict__ x, int64_t xsb, int64_t xsh, int64_t xss, int H, int S, KPlan pl,
+    int8_t* __restrict__ q, int64_t qsb, int64_t qsh, int64_t qss, float* __restrict__ sc32,
+    __half* __restrict__ sc16, KWorkspace ws) {
   using Sh = KShape<DT, D>;
   constexpr int EB = Elem<DT>::kBytes;
   constexpr int VE = Sh::kVecElems;
   __shared__ float red[Sh::kRedRows][D];
-  __shared__ int s_ok;
+  // decoded current item: index, slab, chunk, group, is_a, b, h
+  __shared__ int s_info[7];
+  __shared__ int s_next, s_ok, s_last;
   const int tid = threadIdx.x;
   const int cg = tid % Sh::kVecPerRow;      // column group: columns cg*VE .. +VE
   const int rs = tid / Sh::kVecPerRow;      // row slot
   const int warp = tid >> 5;
   const int red_row = Sh::kVecPerRow <= 32 ? warp : rs;
   const bool red_writer = Sh::kVecPerRow <= 32 ? (tid & 31) < Sh::kVecPerRow : true;
+  const uint64_t pol_keep = l2_policy_keep(), pol_drop = l2_policy_drop();
 
-  for (int64_t task = blockIdx.x; task < n_tasks; task += gridDim.x) {
-    const int64_t slab = task / n_chunks;
-    const int chunk = static_cast<int>(task % n_chunks);
-    const int64_t h = slab % H, b = slab / H;
-    const int row0 = chunk * Sh::kRowsPerChunk;
-    const char* base = x + (b * xsb + h * xsh) * EB + cg * 16;
-
-    uint4 data[Sh::kPasses];
-#pragma unroll
-    for (int p = 0; p < Sh::kPasses; ++p) {
-      const int s = row0 + p * Sh::kRowSlots + rs;
-      data[p] = s < S ? ldg_stream(base + static_cast<int64_t>(s) * xss * EB)
-                      : make_uint4(0, 0, 0, 0);
+  // thread 0 only: item index -> (slab, chunk, group, phase kind, b, h)
+  auto decode = [&](int item) {
+    int slab, chunk, g = 0, is_a = 1;
+    if (pl.fused) {
+      slab = item;
+      chunk = 0;
+    } else {
+      const int per_phase = pl.spg * pl.n_chunks;
+      const int phase = item / per_phase;
+      const int r = item - phase * per_phase;
+      if (phase == 0) {
+        g = 0;
+      } else if (phase == 2 * pl.n_groups - 1) {
+        g = pl.n_groups - 1;
+        is_a = 0;
+      } else if (phase & 1) {
+        g = (phase + 1) >> 1;
+      } else {
+        g = (phase >> 1) - 1;
+        is_a = 0;
+      }
+      slab = g * pl.spg + r / pl.n_chunks;
+      chunk = r % pl.n_chunks;
     }
-    if (mode != 2) {
-      float cmax[VE];
-#pragma unroll
-      for (int e = 0; e < VE; ++e) cmax[e] = 0.0f;
+    s_info[0] = item;
+    s_info[1] = slab;
+    s_info[2] = chunk;
+    s_info[3] = g;
+    s_info[4] = is_a;
+    s_info[5] = slab / H;
+    s_info[6] = slab % H;
+  };
+
+  if (tid == 0) decode(atomicAdd(ws.next, 1));
+  __syncthreads();
+  while (s_info[0] < pl.total) {
+    if (tid == 0) s_next = atomicAdd(ws.next, 1);  // overlaps this item's work
+    const int slab = s_info[1], chunk = s_info[2], g = s_info[3];
+    const bool is_a = s_info[4] != 0;
+    const int b = s_info[5], h = s_info[6];
+    bool valid = slab < pl.n_slabs;  // padding items of the last group do nothing
+    const int row0 = chunk * Sh::kRowsPerChunk;
+    const char* base = x + (static_cast<int64_t>(b) * xsb + static_cast<int64_t>(h) * xsh) * EB + cg * 16;
+
+    if (valid && !is_a) {  // wait until the group's quantizer table is written (bounded)
+      if (tid == 0) {
+        int ok = 0;
+        for (uint32_t it = 0; it < kSpinLimit; ++it) {
+          if (*reinterpret_cast<volatile int*>(ws.ready + g) != 0) {
+            ok = 1;
+            break;
+          }
+          __nanosleep(64);
+        }
+        __threadfence();
+        if (!ok) report_error(ws.status, HQ_ERR_DEVICE_TIMEOUT);
+        s_ok = ok;
+      }
+      __syncthreads();
+      valid = s_ok != 0;  // gave up: status word set, this chunk's codes are not written
+    }
+    uint4 data[Sh::kPasses];
+    if (valid) {
 #pragma unroll
       for (int p = 0; p < Sh::kPasses; ++p) {
-        float f[VE];
-        Vec16<DT>::unpack(data[p], f);
+        const int s = row0 + p * Sh::kRowSlots + rs;
+        const char* src = base + static_cast<int64_t>(s) * xss * EB;
+        data[p] = s < S ? ldg_hint(src, is_a ? pol_keep : pol_drop) : make_uint4(0, 0, 0, 0);
+      }
+    }
+    if (valid && is_a) {
+      float cmax[VE];
+      if constexpr (DT == HQ_DTYPE_F32) {
 #pragma unroll
-        for (int e = 0; e < VE; ++e) cmax[e] = fmaxf(cmax[e], fabsf(f[e]));
+        for (int e = 0; e < VE; ++e) cmax[e] = 0.0f;
+#pragma unroll
+        for (int p = 0; p < Sh::kPasses; ++p) {
+          float f[VE];
+          Vec16<DT>::unpack(data[p], f);
+#pragma unroll
+          for (int e = 0; e < VE; ++e) cmax[e] = fmaxf(cmax[e], fabsf(f[e]));
+        }
+      } else {
+        uint4 m = data[0];
+#pragma unroll
+        for (int p = 1; p < Sh::kPasses; ++p) {
+          m.x = absmax_x2<DT>(m.x, data[p].x);
+          m.y = absmax_x2<DT>(m.y, data[p].y);
+          m.z = absmax_x2<DT>(m.z, data[p].z);
+          m.w = absmax_x2<DT>(m.w, data[p].w);
+        }
+        float f[VE];
+        Vec16<DT>::unpack(m, f);
+#pragma unroll
+        for (int e = 0; e < VE; ++e) cmax[e] = fabsf(f[e]);
       }
       // lanes of one warp that share a column group differ in bits >= log2(kVecPerRow)
 #pragma unroll
@@ -197,62 +395,78 @@ __global__ void __launch_bounds__(kThreads, 3) quant_k_kernel(
         float m = red[0][c];
 #pragma unroll
         for (int w = 1; w < Sh::kRedRows; ++w) m = fmaxf(m, red[w][c]);
-        if (n_chunks == 1 && mode == 0)
+        if (pl.fused)
           red[0][c] = m;  // whole slab in this block: the block maximum is final
         else
-          atomicMax(ws.amax + slab * D + c, __float_as_uint(m));
+          atomicMax(ws.amax + static_cast<int64_t>(slab) * D + c, __float_as_uint(m));
       }
       __syncthreads();
-      if (mode == 1) continue;
-    }
-    if (mode == 0 && n_chunks > 1) {
-      if (tid == 0) {
-        __threadfence();
-        atomicAdd(ws.count + slab, 1);
-        int ok = 0;
-        for (uint32_t it = 0; it < kSpinLimit; ++it) {
-          if (*reinterpret_cast<volatile int*>(ws.count + slab) >= n_chunks) {
-            ok = 1;
-            break;
-          }
-          __nanosleep(128);
+      if (!pl.fused) {
+        if (tid == 0) {
+          __threadfence();
+          const int need = min(pl.spg, pl.n_slabs - g * pl.spg) * pl.n_chunks;
+          s_last = atomicAdd(ws.done + g, 1) == need - 1;
         }
-        __threadfence();
-        if (!ok) report_error(ws.status, HQ_ERR_DEVICE_TIMEOUT);
-        s_ok = ok;
+        __syncthreads();
+        if (s_last) {  // the group's last A item: quantizers + scale outputs, once per column
+          __threadfence();
+          const int g_slabs = min(pl.spg, pl.n_slabs - g * pl.spg);
+          for (int i = tid; i < g_slabs * D; i += kThreads) {
+            const int64_t col = static_cast<int64_t>(g * pl.spg) * D + i;
+            const Quantizer qz = quantizer_for<DT>(__uint_as_float(__ldcg(ws.amax + col)));
+            ws.qtab[col] = make_float2(qz.scale, qz.rcp);
+            if (sc32) sc32[col] = qz.scale;
+            if (sc16) sc16[col] = __float2half_rn(qz.scale);
+          }
+          __threadfence();
+          __syncthreads();
+          if (tid == 0) atomicExch(ws.ready + g, 1);
+        }
       }
+    } else {
       __syncthreads();
-      if (!s_ok) continue;  // status word set; codes of this chunk are left unwritten
     }
-    if (mode == 2 || n_chunks > 1) {
-      for (int c = tid; c < D; c += kThreads) red[0][c] = __uint_as_float(__ldcg(ws.amax + slab * D + c));
-      __syncthreads();
-    }
-    Quantizer qz[VE];
+    if (valid && (!is_a || pl.fused)) {
+      Quantizer qz[VE];
+      F2 rcp2[VE / 2];
+      if (pl.fused) {
 #pragma unroll
-    for (int e = 0; e < VE; ++e) qz[e] = Quantizer::from_amax(red[0][cg * VE + e]);
-    if (chunk == 0 && rs == 0) {
+        for (int e = 0; e < VE; ++e) qz[e] = quantizer_for<DT>(red[0][cg * VE + e]);
+        if (rs == 0) {
 #pragma unroll
-      for (int e = 0; e < VE; ++e) {
-        const int64_t so = slab * D + cg * VE + e;
-        if (sc32) sc32[so] = qz[e].scale;
-        if (sc16) sc16[so] = __float2half_rn(qz[e].scale);
+          for (int e = 0; e < VE; ++e) {
+            const int64_t so = static_cast<int64_t>(slab) * D + cg * VE + e;
+            if (sc32) sc32[so] = qz[e].scale;
+            if (sc16) sc16[so] = __float2half_rn(qz[e].scale);
+          }
+        }
+      } else {
+        const float4* qt = reinterpret_cast<const float4*>(ws.qtab + static_cast<int64_t>(slab) * D + cg * VE);
+#pragma unroll
+        for (int e = 0; e < VE / 2; ++e) {
+          const float4 t = __ldcg(qt + e);
+          qz[2 * e].scale = t.x;
+          qz[2 * e].rcp = t.y;
+          qz[2 * e + 1].scale = t.z;
+          qz[2 * e + 1].rcp = t.w;
+        }
+      }
+      F2 ns2[VE / 2];
+#pragma unroll
+      for (int p = 0; p < VE / 2; ++p) {
+        rcp2[p] = f2_make(qz[2 * p].rcp, qz[2 * p + 1].rcp);
+        ns2[p] = f2_make(-qz[2 * p].scale, -qz[2 * p + 1].scale);
+      }
+      int8_t* qbase = q + static_cast<int64_t>(b) * qsb + static_cast<int64_t>(h) * qsh + cg * VE;
+#pragma unroll
+      for (int p = 0; p < Sh::kPasses; ++p) {
+        const int s = row0 + p * Sh::kRowSlots + rs;
+        if (s < S) quant_vec_store<DT>(data[p], ns2, rcp2, qz, qbase + static_cast<int64_t>(s) * qss);
       }
     }
-    int8_t* qbase = q + b * qsb + h * qsh + cg * VE;
-#pragma unroll
-    for (int p = 0; p < Sh::kPasses; ++p) {
-      const int s = row0 + p * Sh::kRowSlots + rs;
-      if (s < S) {
-        float f[VE];
-        Vec16<DT>::unpack(data[p], f);
-        int c[VE];
-#pragma unroll
-        for (int e = 0; e < VE; ++e) c[e] = qz[e].code(f[e]);
-        store_codes<VE>(qbase + static_cast<int64_t>(s) * qss, c);
-      }
-    }
-    __syncthreads();  // red[] is reused by the next task
+    __syncthreads();  // red[] and s_info are reused by the next item; s_next is written
+    if (tid == 0) decode(s_next);
+    __syncthreads();
   }
 }
 
@@ -353,32 +567,51 @@ static int launch_quant_v(const void* x, const int64_t* xs, int B, int H, int S,
                           const int64_t* qs, float* s32, uint16_t* s16, const int64_t* ss,
                           cudaStream_t st) {
   using Sh = VShape<DT, D>;
-  const int64_t n_rows = static_cast<int64_t>(B) * H * S;
-  const int64_t warps = (n_rows + Sh::kRowsPerWarp - 1) / Sh::kRowsPerWarp;
-  int64_t blocks = (warps + kThreads / 32 - 1) / (kThreads / 32);
-  const int64_t cap = static_cast<int64_t>(current_sm_count()) * 8;
-  if (blocks > cap) blocks = cap;
+  constexpr int IT = Sh::kVecPerLane >= 4 ? 1 : 4 / Sh::kVecPerLane;
+  constexpr int kRowsPerBlock = (kThreads / 32) * Sh::kRowsPerWarp * IT;
+  const int n_slabs = B * H;
   const int64_t z[3] = {0, 0, 0};
   if (!ss) ss = z;
-  quant_v_kernel<DT, D><<<static_cast<unsigned>(blocks), kThreads, 0, st>>>(
-      static_cast<const char*>(x), xs[0], xs[1], xs[2], H, S, n_rows, q, qs[0], qs[1], qs[2], s32,
+  dim3 grid((S + kRowsPerBlock - 1) / kRowsPerBlock, n_slabs < 65535 ? n_slabs : 65535);
+  quant_v_kernel<DT, D><<<grid, kThreads, 0, st>>>(
+      static_cast<const char*>(x), xs[0], xs[1], xs[2], H, S, n_slabs, q, qs[0], qs[1], qs[2], s32,
       reinterpret_cast<__half*>(s16), ss[0], ss[1], ss[2]);
   return finish_launch();
+}
+
+template <int DT, int D>
+static KPlan plan_quant_k(int B, int H, int S) {
+  using Sh = KShape<DT, D>;
+  KPlan pl;
+  pl.n_slabs = B * H;
+  pl.n_chunks = (S + Sh::kRowsPerChunk - 1) / Sh::kRowsPerChunk;
+  const size_t slab_bytes = static_cast<size_t>(S) * D * Elem<DT>::kBytes;
+  pl.spg = static_cast<int>(kGroupBytes / (slab_bytes ? slab_bytes : 1));
+  if (pl.spg < 1) pl.spg = 1;
+  if (pl.spg > pl.n_slabs) pl.spg = pl.n_slabs;
+  pl.n_groups = (pl.n_slabs + pl.spg - 1) / pl.spg;
+  pl.fused = pl.n_chunks == 1;
+  pl.total = pl.fused ? pl.n_slabs : 2 * pl.n_groups * pl.spg * pl.n_chunks;
+  return pl;
 }
 
 template <int DT, int D>
 static int launch_quant_k(const void* x, const int64_t* xs, int B, int H, int S, int8_t* q,
                           const int64_t* qs, float* s32, uint16_t* s16, void* wsp,
                           cudaStream_t st) {
-  using Sh = KShape<DT, D>;
-  const int n_chunks = (S + Sh::kRowsPerChunk - 1) / Sh::kRowsPerChunk;
-  const int64_t n_tasks = static_cast<int64_t>(B) * H * n_chunks;
+  const KPlan pl = plan_quant_k<DT, D>(B, H, S);
   char* w = static_cast<char*>(wsp);
+  const size_t nbh = static_cast<size_t>(B) * H;
   KWorkspace ws;
   ws.status = reinterpret_cast<int*>(w);
-  ws.count = reinterpret_cast<int*>(w + 256);
-  ws.amax = reinterpret_cast<unsigned*>(w + 256 + align256(sizeof(int) * B * H));
-  const size_t clear = 256 + align256(sizeof(int) * B * H) + sizeof(unsigned) * B * H * D;
+  ws.next = reinterpret_cast<int*>(w + 4);
+  ws.done = reinterpret_cast<int*>(w + 256);
+  ws.ready = reinterpret_cast<int*>(w + 256 + align256(sizeof(int) * nbh));
+  ws.amax = reinterpret_cast<unsigned*>(w + 256 + 2 * align256(sizeof(int) * nbh));
+  ws.qtab = reinterpret_cast<float2*>(w + 256 + 2 * align256(sizeof(int) * nbh) +
+                                      align256(sizeof(unsigned) * nbh * D));
+  // status, queue head, counters, flags and maxima start at zero (the table need not)
+  const size_t clear = 256 + 2 * align256(sizeof(int) * nbh) + sizeof(unsigned) * nbh * D;
   cudaError_t e = cudaMemsetAsync(wsp, 0, clear, st);
   if (e != cudaSuccess) return static_cast<int>(e);
   auto kern = quant_k_kernel<DT, D>;
@@ -392,32 +625,14 @@ static int launch_quant_k(const void* x, const int64_t* xs, int B, int H, int S,
     if (per_sm <= 0) return HQ_ERR_UNSUPPORTED;
     if (dev >= 0 && dev < 64) occ_cache[dev].store(per_sm, std::memory_order_relaxed);
   }
-  const int64_t resident = static_cast<int64_t>(per_sm) * sm_count(dev);
-  int64_t grid = resident < n_tasks ? resident : n_tasks;
-  const char* xp = static_cast<const char*>(x);
-  int64_t xsb = xs[0], xsh = xs[1], xss = xs[2];
-  int64_t qsb = qs[0], qsh = qs[1], qss = qs[2];
-  __half* s16h = reinterpret_cast<__half*>(s16);
-  if (n_chunks <= resident) {
-    // every chunk of a slab can be resident at once: fused single pass
-    int mode = 0;
-    void* args[] = {&xp, &xsb, &xsh, &xss, &H, &S, (void*)&n_chunks, (void*)&n_tasks, &q, &qsb,
-                    &qsh, &qss, &s32, &s16h, &ws, &mode};
-    e = cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(kern),
-                                    dim3(static_cast<unsigned>(grid)), dim3(kThreads), args, 0,
-                                    st);
-    if (e != cudaSuccess) return static_cast<int>(e);
-    return finish_launch();
-  }
-  // a slab larger than the resident grid: maxima pass, then code pass
-  for (int mode = 1; mode <= 2; ++mode) {
-    kern<<<static_cast<unsigned>(grid), kThreads, 0, st>>>(xp, xsb, xsh, xss, H, S, n_chunks,
-                                                            n_tasks, q, qsb, qsh, qss, s32, s16h,
-                                                            ws, mode);
-    const int r = finish_launch();
-    if (r != HQ_OK) return r;
-  }
-  return HQ_OK;
+  int64_t grid = static_cast<int64_t>(per_sm) * sm_count(dev);
+  if (grid > pl.total) grid = pl.total;
+  if (static_cast<int64_t>(2) * pl.n_groups * pl.spg * pl.n_chunks >= (int64_t(1) << 31))
+    return HQ_ERR_UNSUPPORTED;
+  kern<<<static_cast<unsigned>(grid), kThreads, 0, st>>>(
+      static_cast<const char*>(x), xs[0], xs[1], xs[2], H, S, pl, q, qs[0], qs[1], qs[2], s32,
+      reinterpret_cast<__half*>(s16), ws);
+  return finish_launch();
 }
 
 template <int DT, int D>
@@ -467,7 +682,9 @@ using namespace hq;
 
 extern "C" size_t hq_quant_k_workspace_bytes(int B, int H, int D) {
   if (B < 0 || H < 0 || D < 0) return 0;
-  return 256 + align256(sizeof(int) * B * H) + align256(sizeof(unsigned) * B * H * D);
+  const size_t nbh = static_cast<size_t>(B) * H;
+  return 256 + 2 * align256(sizeof(int) * nbh) + align256(sizeof(unsigned) * nbh * D) +
+         align256(sizeof(float2) * nbh * D);
 }
 
 extern "C" int hq_quant_k_perchannel(const void* x, int x_dtype, const int64_t x_strides[4], int B,

@@ -15,6 +15,7 @@ float32 occurs for bf16/fp16 data once amax >= 1e-8), so one binade of amax
 covers all of them; the clamped case amax < 1e-8 is enumerated separately.
 """
 import numpy as np
+import pytest
 
 THR = np.float32(0.5 - 2.0 ** -15)
 
@@ -23,12 +24,14 @@ def _binade(mbits, e):
     return (1.0 + np.arange(2 ** mbits) / 2.0 ** mbits) * 2.0 ** e
 
 
-def _check(amaxs, xs_of):
+def _check(amaxs, xs_of, rcp_ulps=0):
     flagged = total = 0
     for a in amaxs:
         a32 = np.maximum(np.float32(a), np.float32(1e-8))
         s = np.float32(a32 / np.float32(127.0))
         r = np.float32(np.float32(1.0) / s)
+        for _ in range(abs(rcp_ulps)):  # a reciprocal approximation up to one ulp off
+            r = np.nextafter(r, np.float32(np.inf if rcp_ulps > 0 else -np.inf))
         xs = xs_of(a)
         xs = np.concatenate([xs, -xs]).astype(np.float32)
         ref = np.clip(np.rint(xs / s), -127, 127)
@@ -44,11 +47,12 @@ def _check(amaxs, xs_of):
     return flagged / total
 
 
-def test_bf16_all_pairs():
+@pytest.mark.parametrize("ulps", [0, -1, 1])
+def test_bf16_all_pairs(ulps):
     def xs_of(a):
         v = np.concatenate([_binade(7, e) for e in range(-16, 1)] + [np.zeros(1)])
         return v[v <= a]
-    rate = _check(_binade(7, 0), xs_of)
+    rate = _check(_binade(7, 0), xs_of, ulps)
     assert rate < 5e-3  # the slow path stays rare
 
 
@@ -59,12 +63,51 @@ def test_bf16_clamped_amax():
     _check([0.0, 5e-9], xs_of)
 
 
-def test_fp16_all_pairs():
+@pytest.mark.parametrize("ulps", [0, -1, 1])
+def test_fp16_all_pairs(ulps):
     def xs_of(a):
         v = np.concatenate([_binade(10, e) for e in range(-16, 1)] + [np.zeros(1)])
         return v[v <= a]
-    rate = _check(_binade(10, 0), xs_of)
+    rate = _check(_binade(10, 0), xs_of, ulps)
     assert rate < 1e-3
+
+
+@pytest.mark.parametrize("bits", [7, 10])
+def test_scale_without_divide_for_16bit_amax(bits):
+    """scale = q + fma(-q, 127, amax) * c with q = amax * c, c = RN(1/127), equals
+    RN(amax / 127) for every bf16 (7-bit) and fp16 (10-bit) mantissa; exponents
+    scale both sides exactly.  The FMA is modelled exactly with fractions."""
+    from fractions import Fraction
+
+    def rn32(fr):
+        f = np.float32(float(fr))
+        cands = [np.nextafter(f, np.float32(-np.inf)), f, np.nextafter(f, np.float32(np.inf))]
+        return min(cands, key=lambda v: (abs(Fraction(float(v)) - fr),
+                                         int(np.float32(v).view(np.uint32)) & 1))
+    c = np.float32(1) / np.float32(127)
+    assert int(c.view(np.uint32)) == 0x3C010204
+    for m in range(2 ** bits):
+        a = np.float32(1 + m / 2 ** bits)
+        q = np.float32(a * c)
+        r = rn32(Fraction(float(a)) - 127 * Fraction(float(q)))
+        s = rn32(Fraction(float(q)) + Fraction(float(r)) * Fraction(float(c)))
+        assert s == np.float32(a / np.float32(127)), m
+
+
+def test_balanced_limb_digits():
+    """The decode kernel writes q * k_scale and p * v_scale as x = 65536 a + 256 b + c
+    with int8 digits; every |x| <= 127 * 65793 must split without overflow."""
+    KL = 127 * 65793
+    xs = np.concatenate([np.arange(-KL, -KL + 70000), np.arange(-70000, 70000),
+                         np.arange(KL - 70000, KL + 1),
+                         np.random.default_rng(0).integers(-KL, KL + 1, 1_000_000)]).astype(np.int64)
+    c = ((xs + 128) & 255) - 128
+    x1 = (xs - c) >> 8
+    b = ((x1 + 128) & 255) - 128
+    a = (x1 - b) >> 8
+    assert np.array_equal(65536 * a + 256 * b + c, xs)
+    for d in (a, b, c):
+        assert d.min() >= -128 and d.max() <= 127
 
 
 def test_plain_reciprocal_would_not_be_exact():
@@ -77,3 +120,63 @@ def test_plain_reciprocal_would_not_be_exact():
         v = v[v <= a]
         mism += int(np.count_nonzero(np.rint(v / s) != np.rint(v.astype(np.float64) * np.float64(r))))
     assert mism > 0
+
+
+def _fma32(a, b, c):
+    """RN32(a * b + c) elementwise for float32 arrays.  a * b is exact in float64;
+    when the float64 sum lands next to a float32 rounding boundary the value is
+    recomputed exactly with fractions, so the model is exact."""
+    from fractions import Fraction
+    t = a.astype(np.float64) * b.astype(np.float64) + c.astype(np.float64)
+    r = t.astype(np.float32)
+    rr = r.astype(np.float64)
+    lo = np.nextafter(r, np.float32(-np.inf)).astype(np.float64)
+    hi = np.nextafter(r, np.float32(np.inf)).astype(np.float64)
+    near = ((np.abs(t - (rr + lo) / 2) <= np.abs(rr) * 2.0 ** -50) |
+            (np.abs(t - (rr + hi) / 2) <= np.abs(rr) * 2.0 ** -50))
+    for i in np.nonzero(near)[0]:
+        fr = Fraction(float(a[i])) * Fraction(float(b[i])) + Fraction(float(c[i]))
+        f = np.float32(float(fr))
+        cands = [np.nextafter(f, np.float32(-np.inf)), f, np.nextafter(f, np.float32(np.inf))]
+        r[i] = min(cands, key=lambda v: (abs(Fraction(float(v)) - fr),
+                                         int(np.float32(v).view(np.uint32)) & 1))
+    return r
+
+
+def _markstein_check(amaxs, xs_of, codes_only=False):
+    for a in amaxs:
+        s = np.float32(np.maximum(np.float32(a), np.float32(1e-8)) / np.float32(127))
+        y = np.float32(np.float32(1) / s)
+        xs = xs_of(a)
+        xs = np.concatenate([xs, -xs]).astype(np.float32)
+        S = np.full(xs.size, s, np.float32)
+        Y = np.full(xs.size, y, np.float32)
+        q0 = (xs.astype(np.float64) * np.float64(y)).astype(np.float32)
+        q1 = _fma32(_fma32(-q0, S, xs), Y, q0)
+        q2 = _fma32(_fma32(-q1, S, xs), Y, q1)
+        if codes_only:
+            np.testing.assert_array_equal(np.rint(q2), np.rint(xs / s))
+        else:
+            np.testing.assert_array_equal(q2, xs / s)
+
+
+@pytest.mark.parametrize("bits", [7, 10])
+def test_branch_free_quotient_16bit(bits):
+    """The 16-bit quantize kernels compute RN(x / s) as q0 = x * y,
+    q1 = fma(fma(-q0, s, x), y, q0), q2 = fma(fma(-q1, s, x), y, q1) with
+    y = RN(1 / s): for every bf16 / fp16 pair (x, amax), |x| <= amax, q2 is the
+    IEEE quotient, so rint(q2) is the reference code."""
+    def xs_of(a):
+        v = np.concatenate([_binade(bits, e) for e in range(-16, 1)] + [np.zeros(1)])
+        return v[v <= a]
+    _markstein_check(_binade(bits, 0), xs_of)
+
+
+def test_branch_free_quotient_clamped_amax():
+    """amax < 1e-8 (scale from the clamp): codes match for every bf16 |x| < 1e-8.
+    Quotients of x below ~4e-37 lose their last bit to subnormal intermediates;
+    they are < 1e-26, far from any rounding boundary of the code."""
+    def xs_of(a):
+        v = np.concatenate([_binade(7, e) for e in range(-133, -26)] + [np.zeros(1)])
+        return v[v < 1e-8]
+    _markstein_check([0.0], xs_of, codes_only=True)
