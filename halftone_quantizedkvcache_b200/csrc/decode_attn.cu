@@ -162,74 +162,104 @@ __device__ __forceinline__ void publish_split(const Params& p, int b, int hq, in
 }
 
 // Run by the last block of (b, kvh) to arrive: merges the n_split partials of
-// its NREP q heads and emits them.  Latency-oriented: one parallel pass over
-// the (m, l) pairs, then every warp streams a quarter of the o rows with
-// independent 16-byte loads.  scratch (16-byte aligned): >= 2 * n_split + 3 +
-// kWarps * kD floats.
+// its NREP q heads and emits them.  The rows of one head are contiguous, so the
+// block copies them into shared memory with 16-byte cp.async - one round trip
+// to L2 - then reduces the row maxima, writes one weight per row, and folds the
+// rows with warp w taking rows w, w + 4, ... and lane l channels 4 l .. 4 l + 3
+// (16-byte shared loads); a last pass adds the 4 warps.  Rows beyond the scratch
+// capacity are merged in further chunks (online rescaling).  scratch: 16-byte
+// aligned, scratch_floats floats.
 template <int NREP, int QDT>
-__device__ __forceinline__ void merge_splits(const Params& p, int b, int kvh, float* scratch) {
-  __shared__ float sred[kWarps];
+__device__ __forceinline__ void merge_splits(const Params& p, int b, int kvh, float* scratch,
+                                             int scratch_floats) {
+  constexpr int kRowVec = kPartRow / 4;  // 16-byte pieces per partial row
+  __shared__ float s_red[kWarps][NREP];
+  __shared__ float s_l[kWarps][NREP];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int n = p.n_split;
-  float* wgt = scratch;
-  float* lv = scratch + n;
-  float* red4 = scratch + ((2 * n + 3) & ~3);  // 16-byte aligned for float4 stores
+  const float* src = p.ws_part + (static_cast<int64_t>(b) * p.Hq + kvh * NREP) * n * kPartRow;
+  float* wsum = scratch;                          // [kWarps][NREP][kD] per-warp sums
+  float* rows_base = scratch + kWarps * NREP * kD;
+  const int per_chunk = max(1, (scratch_floats - kWarps * NREP * kD) / (NREP * (kPartRow + 1)));
+  float M[NREP], L[NREP], O[NREP];
+#pragma unroll
   for (int r = 0; r < NREP; ++r) {
-    const float* base =
-        p.ws_part + (static_cast<int64_t>(b) * p.Hq + kvh * NREP + r) * n * kPartRow;
-    float M = -INFINITY;
-    for (int s = tid; s < n; s += kThreads) {
-      const float2 ml = __ldcg(reinterpret_cast<const float2*>(base + static_cast<int64_t>(s) * kPartRow));
-      wgt[s] = ml.x;
-      lv[s] = ml.y;
-      M = fmaxf(M, ml.x);
+    M[r] = -INFINITY;
+    L[r] = 0.0f;
+    O[r] = 0.0f;
+  }
+  for (int s0 = 0; s0 < n; s0 += per_chunk) {
+    const int cs = min(per_chunk, n - s0);
+    float* wbuf = rows_base + NREP * cs * kPartRow;  // [NREP][cs] row weights
+#pragma unroll
+    for (int r = 0; r < NREP; ++r) {
+      float* dst = rows_base + r * cs * kPartRow;
+      const float* from = src + (static_cast<int64_t>(r) * n + s0) * kPartRow;
+      for (int i = tid; i < cs * kRowVec; i += kThreads) cp_async16(dst + 4 * i, from + 4 * i);
     }
-    M = warp_max(M, 1);
-    if (lane == 0) sred[warp] = M;
+    cp_async_commit();
+    cp_async_wait<0>();
     __syncthreads();
-    M = fmaxf(fmaxf(sred[0], sred[1]), fmaxf(sred[2], sred[3]));
-    float L = 0.0f;
-    for (int s = tid; s < n; s += kThreads) {
-      const float m = wgt[s];
-      const float w = m == -INFINITY ? 0.0f : exp2f(m - M);
-      wgt[s] = w;
-      L += w * lv[s];
+    float Mn[NREP];
+#pragma unroll
+    for (int r = 0; r < NREP; ++r) {
+      const float* rows = rows_base + r * cs * kPartRow;
+      float m = -INFINITY;
+      for (int s = tid; s < cs; s += kThreads) m = fmaxf(m, rows[s * kPartRow]);
+      m = warp_max(m, 1);
+      if (lane == 0) s_red[warp][r] = m;
     }
+    __syncthreads();
 #pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
-    __syncthreads();  // sred (M) read by everyone; wgt complete
-    if (lane == 0) sred[warp] = L;
-    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    const float4* o4 = reinterpret_cast<const float4*>(base + 4) + lane;
-    int s = warp;
-    for (; s + 3 * kWarps < n; s += 4 * kWarps) {
-      float4 v[4];
+    for (int r = 0; r < NREP; ++r) {
+      float m = s_red[0][r];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) v[u] = __ldcg(o4 + static_cast<int64_t>(s + u * kWarps) * (kPartRow / 4));
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const float w = wgt[s + u * kWarps];
-        acc.x += w * v[u].x;
-        acc.y += w * v[u].y;
-        acc.z += w * v[u].z;
-        acc.w += w * v[u].w;
+      for (int w = 1; w < kWarps; ++w) m = fmaxf(m, s_red[w][r]);
+      Mn[r] = fmaxf(M[r], m);
+      const float* rows = rows_base + r * cs * kPartRow;
+      for (int s = tid; s < cs; s += kThreads) {
+        const float ms = rows[s * kPartRow];
+        wbuf[r * cs + s] = ms == -INFINITY ? 0.0f : exp2f(ms - Mn[r]);
       }
     }
-    for (; s < n; s += kWarps) {
-      const float4 v = __ldcg(o4 + static_cast<int64_t>(s) * (kPartRow / 4));
-      const float w = wgt[s];
-      acc.x += w * v.x;
-      acc.y += w * v.y;
-      acc.z += w * v.z;
-      acc.w += w * v.w;
-    }
-    reinterpret_cast<float4*>(red4 + warp * kD)[lane] = acc;
     __syncthreads();
-    L = sred[0] + sred[1] + sred[2] + sred[3];
-    const float O = red4[tid] + red4[kD + tid] + red4[2 * kD + tid] + red4[3 * kD + tid];
-    emit<QDT>(p, b, kvh * NREP + r, tid, M, L, O);
-    __syncthreads();  // scratch and sred are reused by the next head
+#pragma unroll
+    for (int r = 0; r < NREP; ++r) {
+      const float* rows = rows_base + r * cs * kPartRow;
+      const float* w = wbuf + r * cs;
+      float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      float l = 0.0f;
+      for (int s = warp; s < cs; s += kWarps) {
+        const float ws = w[s];
+        const float4 v = reinterpret_cast<const float4*>(rows + s * kPartRow + 4)[lane];
+        acc.x += ws * v.x;
+        acc.y += ws * v.y;
+        acc.z += ws * v.z;
+        acc.w += ws * v.w;
+        l += ws * rows[s * kPartRow + 1];
+      }
+      reinterpret_cast<float4*>(wsum + (warp * NREP + r) * kD)[lane] = acc;
+      if (lane == 0) s_l[warp][r] = l;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < NREP; ++r) {
+      if (Mn[r] == -INFINITY) continue;  // no token seen yet
+      float o = 0.0f, l = 0.0f;
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) {
+        o += wsum[(w * NREP + r) * kD + tid];
+        l += s_l[w][r];
+      }
+      const float a = M[r] == -INFINITY ? 0.0f : exp2f(M[r] - Mn[r]);
+      L[r] = L[r] * a + l;
+      O[r] = O[r] * a + o;
+      M[r] = Mn[r];
+    }
+    __syncthreads();  // scratch, s_red and s_l are reused by the next chunk
   }
+#pragma unroll
+  for (int r = 0; r < NREP; ++r) emit<QDT>(p, b, kvh * NREP + r, tid, M[r], L[r], O[r]);
   if (tid == 0) p.ws_count[b * p.Hkv + kvh] = 0;  // ready for the next launch
 }
 
@@ -518,7 +548,7 @@ __global__ void __launch_bounds__(kThreads, 3) decode_kernel(const Params p) {
   if (!s_last) return;
   __threadfence();
 
-  merge_splits<NREP, QDT>(p, b, kvh, reinterpret_cast<float*>(ring));
+  merge_splits<NREP, QDT>(p, b, kvh, reinterpret_cast<float*>(ring), C::SMEM_STAGES / 4);
 }
 
 // ------------------------------------------------------------------ int8 tensor-core kernel
@@ -554,7 +584,8 @@ struct MCfg {
   static constexpr int NT = (NREP + 1) / 2;               // n8 tiles, 2 heads each
   static constexpr int RING = kStagesM * 2 * kTileB;      // 96 KB
   static constexpr int LIMB = kWarps * NT * 8 * 32;       // p' limb staging
-  static constexpr int SMEM = 1024 + RING + NREP * kD * 4 + LIMB + 2 * kStagesM * 8;
+  static constexpr int QTAB = NT * 256 * 4;                // q' limb B-fragment words
+  static constexpr int SMEM = 1024 + RING + NREP * kD * 4 + LIMB + 2 * kStagesM * 8 + QTAB;
   static_assert(kWarps * NREP * kD * 4 + kWarps * NREP * 8 <= RING, "epilogue scratch");
 };
 
@@ -574,13 +605,22 @@ __device__ __forceinline__ void mma_s8(int (&d)[4], const uint32_t (&a)[4], uint
       : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
+// K / V tiles are read once per decode step: they go through L2 as evict-first
+// so that they do not push out what every launch reuses (code, q, scales,
+// split partials).
 __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, int x, int y,
-                                            int z, int w, uint64_t* bar) {
+                                            int z, int w, uint64_t* bar, uint64_t pol) {
   asm volatile(
-      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_u32(bar))
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_u32(bar)),
+      "l"(pol)
       : "memory");
+}
+__device__ __forceinline__ uint64_t l2_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
 }
 
 // balanced base-256 digits of x in [-kLimbMax, kLimbMax]: x = 65536 a + 256 b + c,
@@ -621,6 +661,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(
   unsigned char* plimb = reinterpret_cast<unsigned char*>(qs + NREP * kD);
   uint64_t* full = reinterpret_cast<uint64_t*>(plimb + C::LIMB);
   uint64_t* empty = full + kStagesM;
+  uint32_t* qtab = reinterpret_cast<uint32_t*>(empty + kStagesM);
   __shared__ float red[kWarps][NREP];
   __shared__ float qmax_s[NREP];
   __shared__ float cM[NREP], cL[NREP];
@@ -635,14 +676,42 @@ __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(
   const int ntiles = (ntok + kTileT - 1) / kTileT;
 
   int issued = 0;
+  const uint64_t pol_stream = l2_evict_first();
   auto issue = [&](int t) {
     const int st = t % kStagesM;
     unsigned char* dst = ring + st * 2 * kTileB;
     mbar_arrive_expect_tx(&full[st], 2 * kTileB);
-    tma_load_4d(dst, &tmk, 0, s_begin + t * kTileT, kvh, b, &full[st]);
-    tma_load_4d(dst + kTileB, &tmv, 0, s_begin + t * kTileT, kvh, b, &full[st]);
+    tma_load_4d(dst, &tmk, 0, s_begin + t * kTileT, kvh, b, &full[st], pol_stream);
+    tma_load_4d(dst + kTileB, &tmv, 0, s_begin + t * kTileT, kvh, b, &full[st], pol_stream);
     issued = t + 1;
   };
+  // V scales of this lane's own tokens (row g for even t4, g + 8 for odd t4, of
+  // both 16-row blocks), loaded two tiles ahead so their latency stays hidden
+  const auto* vscp = reinterpret_cast<const typename SE::T*>(p.vsc);
+  const int64_t vsc_row = b * p.vscb + kvh * p.vsch;
+  auto load_vs = [&](int t, float (&v)[2]) {
+#pragma unroll
+    for (int rb = 0; rb < 2; ++rb) {
+      const int tok = t * kTileT + warp * 32 + rb * 16 + g + 8 * (t4 & 1);
+      v[rb] = tok < ntok ? SE::to_f32(vscp[vsc_row + static_cast<int64_t>(s_begin + tok) * p.vscs]) : 0.0f;
+    }
+  };
+  // The small loads (q, K scales, first V scales) go out before this block's
+  // first TMA copy and only one stage is requested until q' is ready: the
+  // grid's opening burst of tile copies would otherwise queue ahead of them.
+  const int d = tid;
+  typename SE::T ks_raw;
+  typename QE::T q_raw[NREP];
+  {
+    const auto* qp = reinterpret_cast<const typename QE::T*>(p.q);
+    const auto* kp = reinterpret_cast<const typename SE::T*>(p.ksc);
+    ks_raw = kp[b * p.kscb + kvh * p.ksch + d * p.kscd];
+#pragma unroll
+    for (int r = 0; r < NREP; ++r) q_raw[r] = qp[b * p.qsb + (kvh * NREP + r) * p.qsh + d];
+  }
+  float vs_a[2], vs_b[2];
+  load_vs(0, vs_a);
+  load_vs(1, vs_b);
   if (tid == 0) {
     for (int s = 0; s < kStagesM; ++s) {
       mbar_init(&full[s], 1);
@@ -653,18 +722,14 @@ __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(
   // zero the p' staging (columns 3 and 7 stay zero)
   for (int i = tid; i < C::LIMB / 4; i += kThreads) reinterpret_cast<uint32_t*>(plimb)[i] = 0;
   __syncthreads();
-  if (tid == 0)
-    for (int t = 0; t < min(kStagesM, ntiles); ++t) issue(t);
+  if (tid == 0 && ntiles > 0) issue(0);
 
   // ---- q prologue: q' = q_in * k_scale * sm_scale * log2(e), thread owns channel d
   {
-    const int d = tid;
-    const auto* qp = reinterpret_cast<const typename QE::T*>(p.q);
-    const auto* kp = reinterpret_cast<const typename SE::T*>(p.ksc);
-    const float ks = SE::to_f32(kp[b * p.kscb + kvh * p.ksch + d * p.kscd]);
+    const float ks = SE::to_f32(ks_raw);
     float qv[NREP];
 #pragma unroll
-    for (int r = 0; r < NREP; ++r) qv[r] = QE::to_f32(qp[b * p.qsb + (kvh * NREP + r) * p.qsh + d]);
+    for (int r = 0; r < NREP; ++r) qv[r] = QE::to_f32(q_raw[r]);
     if (p.q_quant) {
 #pragma unroll
       for (int r = 0; r < NREP; ++r) {
@@ -698,31 +763,40 @@ __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(
     }
     __syncthreads();
   }
+  if (tid == 0)
+    for (int t = 1; t < min(kStagesM, ntiles); ++t) issue(t);
 
-  // per lane: q' limb B-fragments, per n-tile and k-step; score factors
+  // q' limb B-fragments, built by the whole block into qtab: word
+  // (nt, j, hh, lane g * 4 + t4) packs limb g % 4 of head 2 nt + g / 4 at the four
+  // channels 32 j + 16 hh + 4 t4 + e (a compact loop: this code runs once per block)
+#pragma unroll 1
+  for (int i = tid; i < NT * 256; i += kThreads) {
+    const int nt = i >> 8, j = (i >> 6) & 3, hh = (i >> 5) & 1, gg = (i >> 2) & 7, tt = i & 3;
+    const int col_head = 2 * nt + (gg >> 2), col_limb = gg & 3;
+    uint32_t w = 0;
+    if (col_head < NREP && col_limb < 3) {
+      const float qm = qmax_s[col_head];
+      const float inv = qm > 0.0f ? kLimbMax / qm : 0.0f;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int dd = 32 * j + 16 * hh + 4 * tt + e;
+        const int x = max(-static_cast<int>(kLimbMax),
+                          min(static_cast<int>(kLimbMax), __float2int_rn(qs[col_head * kD + dd] * inv)));
+        w |= limb_byte(x, col_limb) << (8 * e);
+      }
+    }
+    qtab[i] = w;
+  }
+  __syncthreads();
+  // per lane: its B-fragments, per n-tile and k-step; score factors
   uint32_t bq[NT][4][2];
   float f0[NT], f1[NT];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
-    const int col_head = 2 * nt + (g >> 2), col_limb = g & 3;
-    const bool live = col_head < NREP && col_limb < 3;
-    const float qm = live ? qmax_s[col_head] : 0.0f;
-    const float inv = qm > 0.0f ? kLimbMax / qm : 0.0f;
 #pragma unroll
     for (int j = 0; j < 4; ++j)
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        uint32_t w = 0;
-        if (live)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int d = 32 * j + 16 * hh + 4 * t4 + e;
-            const int x = max(-static_cast<int>(kLimbMax),
-                              min(static_cast<int>(kLimbMax), __float2int_rn(qs[col_head * kD + d] * inv)));
-            w |= limb_byte(x, col_limb) << (8 * e);
-          }
-        bq[nt][j][hh] = w;
-      }
+      for (int hh = 0; hh < 2; ++hh) bq[nt][j][hh] = qtab[(nt << 8) | (j << 6) | (hh << 5) | lane];
     const int my_head = 2 * nt + (t4 >> 1);
     const float qsc = my_head < NREP && qmax_s[my_head] > 0.0f ? qmax_s[my_head] / kLimbMax : 0.0f;
     f0[nt] = (t4 & 1) ? qsc : qsc * 65536.0f;
@@ -768,8 +842,6 @@ __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(
       }
   };
 
-  const auto* vscp = reinterpret_cast<const typename SE::T*>(p.vsc);
-  const int64_t vsc_row = b * p.vscb + kvh * p.vsch;
   unsigned char* my_limb = plimb + warp * NT * 256;
   bool ok = true;
   int consumed = 0;
@@ -777,15 +849,15 @@ __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(
     const int st = t % kStagesM;
     const uint32_t par = (t / kStagesM) & 1;
     const int base_tok = t * kTileT + warp * 32;  // first token of this warp (within split)
-    // this lane's own tokens: row g (even t4) or g + 8 (odd t4) of both 16-row blocks
     float vsf[2];
     bool own_ok[2];
 #pragma unroll
     for (int rb = 0; rb < 2; ++rb) {
-      const int tok = base_tok + rb * 16 + g + 8 * (t4 & 1);
-      own_ok[rb] = tok < ntok;
-      vsf[rb] = own_ok[rb] ? SE::to_f32(vscp[vsc_row + static_cast<int64_t>(s_begin + tok) * p.vscs]) : 0.0f;
+      own_ok[rb] = base_tok + rb * 16 + g + 8 * (t4 & 1) < ntok;
+      vsf[rb] = vs_a[rb];
+      vs_a[rb] = vs_b[rb];
     }
+    load_vs(t + 2, vs_b);
     if (!mbar_wait(&full[st], par)) {
       ok = false;
       break;
@@ -956,7 +1028,6 @@ __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(
     }
   }
   __syncthreads();
-  const int d = tid;
   float Ms[NREP], Ls[NREP], Os[NREP];
 #pragma unroll
   for (int r = 0; r < NREP; ++r) {
@@ -991,7 +1062,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-  merge_splits<NREP, QDT>(p, b, kvh, reinterpret_cast<float*>(ring));
+  merge_splits<NREP, QDT>(p, b, kvh, reinterpret_cast<float*>(ring), C::RING / 4);
 }
 
 }  // namespace mmak

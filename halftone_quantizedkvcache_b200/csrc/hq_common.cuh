@@ -305,6 +305,27 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 // Bounded wait: returns false after kSpinLimit polls (each try_wait itself
 // suspends for a hardware-defined interval), never hangs.
+// 16-byte global -> shared copy; src_bytes 0 fills the slot with zeros
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, int src_bytes,
+                                           uint64_t pol) {
+  asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2, %3;" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(src_bytes), "l"(pol)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+// 16-byte global -> shared copy (L2 only)
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
+               : "memory");
+}
+
 constexpr uint32_t kSpinLimit = 1u << 22;
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   for (uint32_t i = 0; i < kSpinLimit; ++i)

@@ -166,17 +166,39 @@ __global__ void __launch_bounds__(kThreads) quant_v_kernel(
                                         (sub + i * Sh::kLanesPerRow) * 16)
                            : make_uint4(0, 0, 0, 0);
     }
+    // row maxima of the IT row groups, then one quantizer per row computed by
+    // lane sub == it of the row's lanes and broadcast to them
+    float amax[IT];
+#pragma unroll
+    for (int it = 0; it < IT; ++it) {
+      float m = 0.0f;
+#pragma unroll
+      for (int i = 0; i < Sh::kVecPerLane; ++i) m = vec_absmax<DT>(vec[it][i], m);
+#pragma unroll
+      for (int off = Sh::kLanesPerRow / 2; off > 0; off >>= 1)
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+      amax[it] = m;
+    }
+    const int my_it = sub % IT;
+    float my_amax = amax[0];
+#pragma unroll
+    for (int it = 1; it < IT; ++it) my_amax = my_it == it ? amax[it] : my_amax;
+    const Quantizer mine = quantizer_for<DT>(my_amax);
+    const int my_s = s0 + my_it * Sh::kRowsPerWarp;
+    if (sub < IT && my_s < S) {
+      const int64_t so = static_cast<int64_t>(b) * ssb + static_cast<int64_t>(h) * ssh +
+                         static_cast<int64_t>(my_s) * sss;
+      if (sc32) sc32[so] = mine.scale;
+      if (sc16) sc16[so] = __float2half_rn(mine.scale);
+    }
+    const int group_base = lane - sub;
 #pragma unroll
     for (int it = 0; it < IT; ++it) {
       const int s = s0 + it * Sh::kRowsPerWarp;
-      float amax = 0.0f;
-#pragma unroll
-      for (int i = 0; i < Sh::kVecPerLane; ++i) amax = vec_absmax<DT>(vec[it][i], amax);
-#pragma unroll
-      for (int off = Sh::kLanesPerRow / 2; off > 0; off >>= 1)
-        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+      Quantizer qz;
+      qz.scale = __shfl_sync(0xffffffffu, mine.scale, group_base + it);
+      qz.rcp = __shfl_sync(0xffffffffu, mine.rcp, group_base + it);
       if (s >= S) continue;
-      const Quantizer qz = quantizer_for<DT>(amax);
       Quantizer qzv[VE];
       F2 rcp2[VE / 2], ns2[VE / 2];
 #pragma unroll
@@ -190,39 +212,49 @@ __global__ void __launch_bounds__(kThreads) quant_v_kernel(
       for (int i = 0; i < Sh::kVecPerLane; ++i)
         quant_vec_store<DT>(vec[it][i], ns2, rcp2, qzv,
                             qbase + static_cast<int64_t>(s) * qss + (sub + i * Sh::kLanesPerRow) * VE);
-      if (sub == 0) {
-        const int64_t so = static_cast<int64_t>(b) * ssb + static_cast<int64_t>(h) * ssh +
-                           static_cast<int64_t>(s) * sss;
-        if (sc32) sc32[so] = qz.scale;
-        if (sc16) sc16[so] = __float2half_rn(qz.scale);
-      }
     }
   }
 }
 
 // ------------------------------------------------------------------ K per channel
 // A (b, h) slab of S x D is cut into chunks of kRowsPerChunk whole rows (32 KB
-// of input); every thread keeps kPasses 16-byte vectors of one fixed column
-// group of a chunk in registers.
+// of input).
 //
 // Work is an ordered queue of items (one chunk each), dequeued with an atomic
 // counter.  Slabs form groups of at most kGroupBytes of input; for group g,
 // A(g) items publish column maxima (atomicMax) and B(g) items re-read their
 // chunk - from L2, since the group was read moments before - and write codes.
-// Queue order A0, A1, B0, A2, B1, ..., A(n-1), B(n-2), B(n-1): a B(g) item only
-// waits (bounded) for A(g) items, which were dequeued earlier by running blocks
-// and never wait themselves, so no block depends on a block that is not running.
+// Queue order A0, A1, B0, A2, B1, ..., A(n-1), B(n-2), B(n-1): every A(g) item
+// precedes every B(g) item, and a block works through its items in queue
+// order, so the lowest unfinished item can always proceed (an A item never
+// waits; a B item waits, bounded, only for lower A items).
+//
+// A block is 8 compute warps and one control warp.  Compute warps stream
+// chunks through a kKStages-deep shared-memory ring with cp.async (each thread
+// reads back only the 16-byte slots it copied, so the ring needs no barrier);
+// the control warp dequeues items, counts finished A items per group, builds
+// the group's quantizer table when the last one lands, and does the bounded
+// wait of B items - so compute warps never fence or spin.  One barrier per
+// A item, two per B item.
+constexpr int kKCompute = 256;               // compute threads
+constexpr int kKThreads = kKCompute + 32;    // + control warp
+constexpr int kKStages = 3;
+
 template <int DT, int D>
 struct KShape {
   static constexpr int kVecElems = 16 / Elem<DT>::kBytes;
   static constexpr int kVecPerRow = D / kVecElems;             // column groups
-  static constexpr int kRowSlots = kThreads / kVecPerRow;      // rows per pass
+  static constexpr int kRowSlots = kKCompute / kVecPerRow;     // rows per pass
   static constexpr int kPasses = 8;
   static constexpr int kRowsPerChunk = kRowSlots * kPasses;    // 32 KB of input
-  static constexpr int kWarps = kThreads / 32;
+  static constexpr int kWarps = kKCompute / 32;
   // rows of the block-level max table: one per warp when a warp spans whole
   // rows, else one per row slot
   static constexpr int kRedRows = kVecPerRow <= 32 ? kWarps : kRowSlots;
+  static constexpr int kStageVecs = kKCompute * kPasses;       // 16-byte slots per stage
+  static constexpr size_t kTableOff = size_t(kKStages) * kStageVecs * 16;
+  static constexpr size_t kQsOff = kTableOff + size_t(2) * kRedRows * D * 4;
+  static constexpr size_t kSmem = kQsOff + size_t(D) * 8;
 };
 
 constexpr size_t kGroupBytes = size_t(24) << 20;
@@ -244,8 +276,8 @@ struct KPlan {
 
 __host__ __device__ inline size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
 
-// L2 policies: A items keep their chunk in L2 for the B re-read, B items mark
-// it as last use.
+// L2 policies: A items keep their chunk in L2 for the B re-read, B items (and
+// single-pass items) mark it as last use.
 __device__ __forceinline__ uint64_t l2_policy_keep() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
@@ -256,218 +288,274 @@ __device__ __forceinline__ uint64_t l2_policy_drop() {
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
   return p;
 }
-__device__ __forceinline__ uint4 ldg_hint(const void* p, uint64_t pol) {
-  uint4 v;
-  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0, %1, %2, %3}, [%4], %5;"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p), "l"(pol));
-  return v;
-}
+enum KKind : int { kItemA = 0, kItemB = 1, kItemFused = 2 };
 
 template <int DT, int D>
-__global__ void __launch_bounds__(kThreads, 3) quant_k_kernel(
+__global__ void __launch_bounds__(kKThreads, 2) quant_k_kernel(
     const char* __restrict__ x, int64_t xsb, int64_t xsh, int64_t xss, int H, int S, KPlan pl,
     int8_t* __restrict__ q, int64_t qsb, int64_t qsh, int64_t qss, float* __restrict__ sc32,
     __half* __restrict__ sc16, KWorkspace ws) {
   using Sh = KShape<DT, D>;
   constexpr int EB = Elem<DT>::kBytes;
   constexpr int VE = Sh::kVecElems;
-  __shared__ float red[Sh::kRedRows][D];
-  // decoded current item: index, slab, chunk, group, is_a, b, h
-  __shared__ int s_info[7];
-  __shared__ int s_next, s_ok, s_last;
+  constexpr int NS = kKStages;
+  constexpr int R = NS + 1;  // decoded items in flight: current + NS ahead
+  extern __shared__ __align__(128) unsigned char smem[];
+  uint4* stages = reinterpret_cast<uint4*>(smem);
+  float* table = reinterpret_cast<float*>(smem + Sh::kTableOff);  // [2][kRedRows][D]
+  float2* qs = reinterpret_cast<float2*>(smem + Sh::kQsOff);      // [D] (scale, rcp)
+  // decoded items: index, slab, chunk, group, kind, b, h, valid
+  __shared__ int s_info[R][8];
+  __shared__ int s_ok;
   const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const bool control = tid >= kKCompute;
   const int cg = tid % Sh::kVecPerRow;      // column group: columns cg*VE .. +VE
   const int rs = tid / Sh::kVecPerRow;      // row slot
   const int warp = tid >> 5;
   const int red_row = Sh::kVecPerRow <= 32 ? warp : rs;
-  const bool red_writer = Sh::kVecPerRow <= 32 ? (tid & 31) < Sh::kVecPerRow : true;
-  const uint64_t pol_keep = l2_policy_keep(), pol_drop = l2_policy_drop();
+  const bool red_writer = Sh::kVecPerRow <= 32 ? lane < Sh::kVecPerRow : true;
 
-  // thread 0 only: item index -> (slab, chunk, group, phase kind, b, h)
-  auto decode = [&](int item) {
-    int slab, chunk, g = 0, is_a = 1;
-    if (pl.fused) {
-      slab = item;
-      chunk = 0;
-    } else {
-      const int per_phase = pl.spg * pl.n_chunks;
-      const int phase = item / per_phase;
-      const int r = item - phase * per_phase;
-      if (phase == 0) {
-        g = 0;
-      } else if (phase == 2 * pl.n_groups - 1) {
-        g = pl.n_groups - 1;
-        is_a = 0;
-      } else if (phase & 1) {
-        g = (phase + 1) >> 1;
+  // control lane 0 only: item index -> slot
+  auto decode = [&](int item, int slot) {
+    int slab = 0, chunk = 0, g = 0, kind = kItemFused;
+    if (item < pl.total) {
+      if (pl.fused) {
+        slab = item;
       } else {
-        g = (phase >> 1) - 1;
-        is_a = 0;
+        const int per_phase = pl.spg * pl.n_chunks;
+        const int phase = item / per_phase;
+        const int r = item - phase * per_phase;
+        kind = kItemA;
+        if (phase == 0) {
+          g = 0;
+        } else if (phase == 2 * pl.n_groups - 1) {
+          g = pl.n_groups - 1;
+          kind = kItemB;
+        } else if (phase & 1) {
+          g = (phase + 1) >> 1;
+        } else {
+          g = (phase >> 1) - 1;
+          kind = kItemB;
+        }
+        slab = g * pl.spg + r / pl.n_chunks;
+        chunk = r % pl.n_chunks;
       }
-      slab = g * pl.spg + r / pl.n_chunks;
-      chunk = r % pl.n_chunks;
     }
-    s_info[0] = item;
-    s_info[1] = slab;
-    s_info[2] = chunk;
-    s_info[3] = g;
-    s_info[4] = is_a;
-    s_info[5] = slab / H;
-    s_info[6] = slab % H;
+    int* o = s_info[slot];
+    o[0] = item;
+    o[1] = slab;
+    o[2] = chunk;
+    o[3] = g;
+    o[4] = kind;
+    o[5] = slab / H;
+    o[6] = slab % H;
+    o[7] = item < pl.total && slab < pl.n_slabs;  // padding items of the last group do nothing
   };
 
-  if (tid == 0) decode(atomicAdd(ws.next, 1));
-  __syncthreads();
-  while (s_info[0] < pl.total) {
-    if (tid == 0) s_next = atomicAdd(ws.next, 1);  // overlaps this item's work
-    const int slab = s_info[1], chunk = s_info[2], g = s_info[3];
-    const bool is_a = s_info[4] != 0;
-    const int b = s_info[5], h = s_info[6];
-    bool valid = slab < pl.n_slabs;  // padding items of the last group do nothing
-    const int row0 = chunk * Sh::kRowsPerChunk;
-    const char* base = x + (static_cast<int64_t>(b) * xsb + static_cast<int64_t>(h) * xsh) * EB + cg * 16;
-
-    if (valid && !is_a) {  // wait until the group's quantizer table is written (bounded)
-      if (tid == 0) {
-        int ok = 0;
-        for (uint32_t it = 0; it < kSpinLimit; ++it) {
-          if (*reinterpret_cast<volatile int*>(ws.ready + g) != 0) {
-            ok = 1;
-            break;
-          }
-          __nanosleep(64);
-        }
-        __threadfence();
-        if (!ok) report_error(ws.status, HQ_ERR_DEVICE_TIMEOUT);
-        s_ok = ok;
-      }
-      __syncthreads();
-      valid = s_ok != 0;  // gave up: status word set, this chunk's codes are not written
-    }
-    uint4 data[Sh::kPasses];
-    if (valid) {
+  // compute threads: copy the chunk of the item in `slot` into ring stage `stage`
+  auto issue = [&](int slot, int stage) {
+    const int* in = s_info[slot];
+    if (in[7]) {
+      const uint64_t pol = in[4] == kItemA ? l2_policy_keep() : l2_policy_drop();
+      const char* base = x + (static_cast<int64_t>(in[5]) * xsb + static_cast<int64_t>(in[6]) * xsh) * EB +
+                         cg * 16;
+      const int row0 = in[2] * Sh::kRowsPerChunk;
+      uint4* dst = stages + stage * Sh::kStageVecs + tid;
 #pragma unroll
       for (int p = 0; p < Sh::kPasses; ++p) {
         const int s = row0 + p * Sh::kRowSlots + rs;
-        const char* src = base + static_cast<int64_t>(s) * xss * EB;
-        data[p] = s < S ? ldg_hint(src, is_a ? pol_keep : pol_drop) : make_uint4(0, 0, 0, 0);
+        const char* src = s < S ? base + static_cast<int64_t>(s) * xss * EB : base;
+        cp_async16(dst + p * kKCompute, src, s < S ? 16 : 0, pol);
       }
     }
-    if (valid && is_a) {
-      float cmax[VE];
-      if constexpr (DT == HQ_DTYPE_F32) {
+    cp_async_commit();
+  };
+
+  // control warp: count one finished A item of group g; the last one builds the
+  // group's quantizer table and scale outputs, then publishes ready[g]
+  auto signal = [&](int g) {
+    int last = 0;
+    if (lane == 0) {
+      __threadfence();  // the block's column maxima (ordered by the barrier) before the count
+      const int need = min(pl.spg, pl.n_slabs - g * pl.spg) * pl.n_chunks;
+      last = atomicAdd(ws.done + g, 1) == need - 1;
+    }
+    last = __shfl_sync(0xffffffffu, last, 0);
+    if (!last) return;
+    __threadfence();
+    const int64_t col0 = static_cast<int64_t>(g) * pl.spg * D;
+    const int n4 = min(pl.spg, pl.n_slabs - g * pl.spg) * (D / 4);
+    const float4* a4 = reinterpret_cast<const float4*>(ws.amax + col0);
+    float4* t4 = reinterpret_cast<float4*>(ws.qtab + col0);
+    for (int j0 = 0; j0 < n4; j0 += 4 * 32) {
+      float4 a[4];
 #pragma unroll
-        for (int e = 0; e < VE; ++e) cmax[e] = 0.0f;
-#pragma unroll
-        for (int p = 0; p < Sh::kPasses; ++p) {
-          float f[VE];
-          Vec16<DT>::unpack(data[p], f);
-#pragma unroll
-          for (int e = 0; e < VE; ++e) cmax[e] = fmaxf(cmax[e], fabsf(f[e]));
-        }
-      } else {
-        uint4 m = data[0];
-#pragma unroll
-        for (int p = 1; p < Sh::kPasses; ++p) {
-          m.x = absmax_x2<DT>(m.x, data[p].x);
-          m.y = absmax_x2<DT>(m.y, data[p].y);
-          m.z = absmax_x2<DT>(m.z, data[p].z);
-          m.w = absmax_x2<DT>(m.w, data[p].w);
-        }
-        float f[VE];
-        Vec16<DT>::unpack(m, f);
-#pragma unroll
-        for (int e = 0; e < VE; ++e) cmax[e] = fabsf(f[e]);
+      for (int u = 0; u < 4; ++u) {
+        const int j = j0 + u * 32 + lane;
+        a[u] = j < n4 ? __ldcg(a4 + j) : make_float4(0.f, 0.f, 0.f, 0.f);
       }
-      // lanes of one warp that share a column group differ in bits >= log2(kVecPerRow)
 #pragma unroll
-      for (int off = Sh::kVecPerRow; off < 32; off <<= 1)
-#pragma unroll
-        for (int e = 0; e < VE; ++e)
-          cmax[e] = fmaxf(cmax[e], __shfl_xor_sync(0xffffffffu, cmax[e], off));
-      if (red_writer) {
-#pragma unroll
-        for (int e = 0; e < VE; ++e) red[red_row][cg * VE + e] = cmax[e];
-      }
-      __syncthreads();
-      for (int c = tid; c < D; c += kThreads) {
-        float m = red[0][c];
-#pragma unroll
-        for (int w = 1; w < Sh::kRedRows; ++w) m = fmaxf(m, red[w][c]);
-        if (pl.fused)
-          red[0][c] = m;  // whole slab in this block: the block maximum is final
-        else
-          atomicMax(ws.amax + static_cast<int64_t>(slab) * D + c, __float_as_uint(m));
-      }
-      __syncthreads();
-      if (!pl.fused) {
-        if (tid == 0) {
-          __threadfence();
-          const int need = min(pl.spg, pl.n_slabs - g * pl.spg) * pl.n_chunks;
-          s_last = atomicAdd(ws.done + g, 1) == need - 1;
+      for (int u = 0; u < 4; ++u) {
+        const int j = j0 + u * 32 + lane;
+        if (j >= n4) continue;
+        const Quantizer q0 = quantizer_for<DT>(a[u].x), q1 = quantizer_for<DT>(a[u].y);
+        const Quantizer q2 = quantizer_for<DT>(a[u].z), q3 = quantizer_for<DT>(a[u].w);
+        t4[2 * j] = make_float4(q0.scale, q0.rcp, q1.scale, q1.rcp);
+        t4[2 * j + 1] = make_float4(q2.scale, q2.rcp, q3.scale, q3.rcp);
+        const int64_t c = col0 + 4 * static_cast<int64_t>(j);
+        if (sc32) {
+          sc32[c] = q0.scale;
+          sc32[c + 1] = q1.scale;
+          sc32[c + 2] = q2.scale;
+          sc32[c + 3] = q3.scale;
         }
-        __syncthreads();
-        if (s_last) {  // the group's last A item: quantizers + scale outputs, once per column
-          __threadfence();
-          const int g_slabs = min(pl.spg, pl.n_slabs - g * pl.spg);
-          for (int i = tid; i < g_slabs * D; i += kThreads) {
-            const int64_t col = static_cast<int64_t>(g * pl.spg) * D + i;
-            const Quantizer qz = quantizer_for<DT>(__uint_as_float(__ldcg(ws.amax + col)));
-            ws.qtab[col] = make_float2(qz.scale, qz.rcp);
-            if (sc32) sc32[col] = qz.scale;
-            if (sc16) sc16[col] = __float2half_rn(qz.scale);
+        if (sc16) {
+          sc16[c] = __float2half_rn(q0.scale);
+          sc16[c + 1] = __float2half_rn(q1.scale);
+          sc16[c + 2] = __float2half_rn(q2.scale);
+          sc16[c + 3] = __float2half_rn(q3.scale);
+        }
+      }
+    }
+    __threadfence();
+    __syncwarp();
+    if (lane == 0) atomicExch(ws.ready + g, 1);
+  };
+
+  if (control && lane == 0) {
+    for (int k = 0; k < NS; ++k) decode(atomicAdd(ws.next, 1), k);
+  }
+  __syncthreads();
+  if (!control) {
+    for (int k = 0; k < NS - 1; ++k) issue(k, k);
+  }
+  int pend_g = -1;  // control warp: group of this block's last A item, not yet counted
+  for (int i = 0;; ++i) {
+    const int* in = s_info[i % R];
+    if (in[0] >= pl.total) break;
+    const int slab = in[1], chunk = in[2], g = in[3], kind = in[4], b = in[5], h = in[6];
+    const bool valid = in[7] != 0;
+    const uint4* st = stages + (i % NS) * Sh::kStageVecs + tid;
+    if (!control) {
+      issue((i + NS - 1) % R, (i + NS - 1) % NS);
+      cp_async_wait<NS - 1>();  // this thread's copies of item i have landed
+      if (kind != kItemB && valid) {
+        float cmax[VE];
+        if constexpr (DT == HQ_DTYPE_F32) {
+#pragma unroll
+          for (int e = 0; e < VE; ++e) cmax[e] = 0.0f;
+#pragma unroll
+          for (int p = 0; p < Sh::kPasses; ++p) {
+            float f[VE];
+            Vec16<DT>::unpack(st[p * kKCompute], f);
+#pragma unroll
+            for (int e = 0; e < VE; ++e) cmax[e] = fmaxf(cmax[e], fabsf(f[e]));
           }
-          __threadfence();
-          __syncthreads();
-          if (tid == 0) atomicExch(ws.ready + g, 1);
+        } else {
+          uint4 m = st[0];
+#pragma unroll
+          for (int p = 1; p < Sh::kPasses; ++p) {
+            const uint4 d = st[p * kKCompute];
+            m.x = absmax_x2<DT>(m.x, d.x);
+            m.y = absmax_x2<DT>(m.y, d.y);
+            m.z = absmax_x2<DT>(m.z, d.z);
+            m.w = absmax_x2<DT>(m.w, d.w);
+          }
+          float f[VE];
+          Vec16<DT>::unpack(m, f);
+#pragma unroll
+          for (int e = 0; e < VE; ++e) cmax[e] = fabsf(f[e]);
+        }
+        // lanes of one warp that share a column group differ in bits >= log2(kVecPerRow)
+#pragma unroll
+        for (int off = Sh::kVecPerRow; off < 32; off <<= 1)
+#pragma unroll
+          for (int e = 0; e < VE; ++e)
+            cmax[e] = fmaxf(cmax[e], __shfl_xor_sync(0xffffffffu, cmax[e], off));
+        if (red_writer) {
+          float* row = table + ((i & 1) * Sh::kRedRows + red_row) * D + cg * VE;
+#pragma unroll
+          for (int e = 0; e < VE; e += 4)
+            *reinterpret_cast<float4*>(row + e) = make_float4(cmax[e], cmax[e + 1], cmax[e + 2], cmax[e + 3]);
+        }
+      }
+    } else if (lane == 0) {
+      decode(atomicAdd(ws.next, 1), (i + NS) % R);
+    }
+    __syncthreads();  // table rows, decoded item i+NS
+    if (!control) {
+      if (kind != kItemB && valid && tid < D) {
+        const float* col = table + (i & 1) * Sh::kRedRows * D + tid;
+        float m = col[0];
+#pragma unroll
+        for (int w = 1; w < Sh::kRedRows; ++w) m = fmaxf(m, col[w * D]);
+        if (kind == kItemFused) {  // whole slab in this item: the maximum is final
+          const Quantizer qz = quantizer_for<DT>(m);
+          qs[tid] = make_float2(qz.scale, qz.rcp);
+          const int64_t so = static_cast<int64_t>(slab) * D + tid;
+          if (sc32) sc32[so] = qz.scale;
+          if (sc16) sc16[so] = __float2half_rn(qz.scale);
+        } else {
+          atomicMax(ws.amax + static_cast<int64_t>(slab) * D + tid, __float_as_uint(m));
         }
       }
     } else {
-      __syncthreads();
-    }
-    if (valid && (!is_a || pl.fused)) {
-      Quantizer qz[VE];
-      F2 rcp2[VE / 2];
-      if (pl.fused) {
-#pragma unroll
-        for (int e = 0; e < VE; ++e) qz[e] = quantizer_for<DT>(red[0][cg * VE + e]);
-        if (rs == 0) {
-#pragma unroll
-          for (int e = 0; e < VE; ++e) {
-            const int64_t so = static_cast<int64_t>(slab) * D + cg * VE + e;
-            if (sc32) sc32[so] = qz[e].scale;
-            if (sc16) sc16[so] = __float2half_rn(qz[e].scale);
+      if (pend_g >= 0) signal(pend_g);  // the previous item's maxima are ordered by the barrier
+      pend_g = kind == kItemA && valid ? g : -1;
+      if (kind == kItemB) {
+        int ok = 0;
+        if (valid) {
+          if (lane == 0) {
+            for (uint32_t it = 0; it < kSpinLimit; ++it) {
+              if (*reinterpret_cast<volatile int*>(ws.ready + g) != 0) {
+                ok = 1;
+                break;
+              }
+              __nanosleep(64);
+            }
+            __threadfence();
+            if (!ok) report_error(ws.status, HQ_ERR_DEVICE_TIMEOUT);
+          }
+          ok = __shfl_sync(0xffffffffu, ok, 0);
+          if (ok) {
+            const float4* t4 = reinterpret_cast<const float4*>(ws.qtab + static_cast<int64_t>(slab) * D);
+            float4* d4 = reinterpret_cast<float4*>(qs);
+            for (int j = lane; j < D / 2; j += 32) d4[j] = __ldcg(t4 + j);
           }
         }
-      } else {
-        const float4* qt = reinterpret_cast<const float4*>(ws.qtab + static_cast<int64_t>(slab) * D + cg * VE);
+        if (lane == 0) s_ok = ok;  // gave up: status word set, this chunk's codes are not written
+      }
+    }
+    if (kind != kItemA) {
+      __syncthreads();  // quantizer row qs[] of the slab
+      if (!control && valid && (kind == kItemFused || s_ok)) {
+        Quantizer qz[VE];
+        F2 rcp2[VE / 2], ns2[VE / 2];
+        const float4* q4 = reinterpret_cast<const float4*>(qs + cg * VE);
 #pragma unroll
         for (int e = 0; e < VE / 2; ++e) {
-          const float4 t = __ldcg(qt + e);
+          const float4 t = q4[e];
           qz[2 * e].scale = t.x;
           qz[2 * e].rcp = t.y;
           qz[2 * e + 1].scale = t.z;
           qz[2 * e + 1].rcp = t.w;
+          rcp2[e] = f2_make(t.y, t.w);
+          ns2[e] = f2_make(-t.x, -t.z);
+        }
+        int8_t* qbase = q + static_cast<int64_t>(b) * qsb + static_cast<int64_t>(h) * qsh + cg * VE;
+        const int row0 = chunk * Sh::kRowsPerChunk;
+#pragma unroll
+        for (int p = 0; p < Sh::kPasses; ++p) {
+          const int s = row0 + p * Sh::kRowSlots + rs;
+          if (s < S) quant_vec_store<DT>(st[p * kKCompute], ns2, rcp2, qz, qbase + static_cast<int64_t>(s) * qss);
         }
       }
-      F2 ns2[VE / 2];
-#pragma unroll
-      for (int p = 0; p < VE / 2; ++p) {
-        rcp2[p] = f2_make(qz[2 * p].rcp, qz[2 * p + 1].rcp);
-        ns2[p] = f2_make(-qz[2 * p].scale, -qz[2 * p + 1].scale);
-      }
-      int8_t* qbase = q + static_cast<int64_t>(b) * qsb + static_cast<int64_t>(h) * qsh + cg * VE;
-#pragma unroll
-      for (int p = 0; p < Sh::kPasses; ++p) {
-        const int s = row0 + p * Sh::kRowSlots + rs;
-        if (s < S) quant_vec_store<DT>(data[p], ns2, rcp2, qz, qbase + static_cast<int64_t>(s) * qss);
-      }
     }
-    __syncthreads();  // red[] and s_info are reused by the next item; s_next is written
-    if (tid == 0) decode(s_next);
-    __syncthreads();
   }
+  __syncthreads();  // maxima of the block's last item
+  if (control && pend_g >= 0) signal(pend_g);
+  if (!control) cp_async_wait<0>();
 }
 
 // ------------------------------------------------------------------ append
@@ -615,12 +703,15 @@ static int launch_quant_k(const void* x, const int64_t* xs, int B, int H, int S,
   cudaError_t e = cudaMemsetAsync(wsp, 0, clear, st);
   if (e != cudaSuccess) return static_cast<int>(e);
   auto kern = quant_k_kernel<DT, D>;
+  constexpr size_t smem = KShape<DT, D>::kSmem;
   int dev = 0;
   cudaGetDevice(&dev);
   static std::atomic<int> occ_cache[64];
   int per_sm = (dev >= 0 && dev < 64) ? occ_cache[dev].load(std::memory_order_relaxed) : 0;
   if (per_sm <= 0) {
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, 0);
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return static_cast<int>(e);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kKThreads, smem);
     if (e != cudaSuccess) return static_cast<int>(e);
     if (per_sm <= 0) return HQ_ERR_UNSUPPORTED;
     if (dev >= 0 && dev < 64) occ_cache[dev].store(per_sm, std::memory_order_relaxed);
@@ -629,7 +720,7 @@ static int launch_quant_k(const void* x, const int64_t* xs, int B, int H, int S,
   if (grid > pl.total) grid = pl.total;
   if (static_cast<int64_t>(2) * pl.n_groups * pl.spg * pl.n_chunks >= (int64_t(1) << 31))
     return HQ_ERR_UNSUPPORTED;
-  kern<<<static_cast<unsigned>(grid), kThreads, 0, st>>>(
+  kern<<<static_cast<unsigned>(grid), kKThreads, smem, st>>>(
       static_cast<const char*>(x), xs[0], xs[1], xs[2], H, S, pl, q, qs[0], qs[1], qs[2], s32,
       reinterpret_cast<__half*>(s16), ws);
   return finish_launch();
