@@ -171,8 +171,9 @@ def make_layer_caches(torch, kernels, n_layers, S, device, gen, kv="int8"):
     return caches
 
 
-def time_graph(torch, fn, steps, warmup, stream, clocks_index=None):
-    """Capture fn() in a CUDA graph, replay warmup + steps; returns (ms/step, clocks)."""
+def time_graph(torch, fn, steps, warmup, stream, clocks_index=None, label=None):
+    """Capture fn() in a CUDA graph, replay warmup + steps; returns (ms/step, clocks).
+    ``label`` names an NVTX range around the timed replays (for ncu --nvtx-include)."""
     fn()  # first call outside capture: kernel attributes, workspaces
     torch.cuda.synchronize()
     g = torch.cuda.CUDAGraph()
@@ -185,12 +186,16 @@ def time_graph(torch, fn, steps, warmup, stream, clocks_index=None):
     clk = Clocks(clocks_index) if clocks_index is not None else None
     if clk:
         clk.__enter__()
+    if label:
+        torch.cuda.nvtx.range_push(label)
     with torch.cuda.stream(stream):
         ev0.record(stream)
         for _ in range(steps):
             g.replay()
         ev1.record(stream)
     torch.cuda.synchronize()
+    if label:
+        torch.cuda.nvtx.range_pop()
     if clk:
         clk.__exit__()
     del g
@@ -313,7 +318,8 @@ def main():
 
     with torch.cuda.stream(stream):
         ms, clocks = time_graph(torch, step, args.steps, args.warmup, stream,
-                                clocks_index=torch.cuda.current_device() if rank == 0 else None)
+                                clocks_index=torch.cuda.current_device() if rank == 0 else None,
+                                label="decode_step")
     if world > 1:
         t = torch.tensor([ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -352,7 +358,7 @@ def main():
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "traffic": profile_traffic(), "peak_kind": peak_kind,
-                         "kernel": "hq::dec::decode_kernel<2, int8, f32 scales, bf16 q>",
+                         "kernel": "hq::dec::mmak::decode_mma_kernel<2, f32 scales, bf16 q>",
                          "algorithmic_bytes_per_launch": per_layer},
             "clocks": clocks or {},
             "e2e": e2e,

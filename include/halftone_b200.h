@@ -74,10 +74,11 @@ HQ_API const char* hq_version(void);
  *          contiguous, float32 and float16 (round to nearest even).
  * Requires S >= 1, D in {64, 128, 256}, 16-byte aligned rows.
  * workspace: >= hq_quant_k_workspace_bytes(B, H, D) bytes, 256-byte aligned;
- *          cleared by this call on `stream`.  The kernel is a cooperative
- *          persistent grid whose blocks exchange per-channel maxima through
- *          the workspace; a bounded wait reports HQ_ERR_DEVICE_TIMEOUT in the
- *          workspace status word (hq_read_status) instead of hanging.
+ *          cleared by this call on `stream`.  The kernel is a persistent
+ *          grid working through an ordered queue of chunks; blocks exchange
+ *          per-channel maxima and per-group counts through the workspace; a
+ *          bounded wait reports HQ_ERR_DEVICE_TIMEOUT in the workspace status
+ *          word (hq_read_status) instead of hanging.
  */
 HQ_API size_t hq_quant_k_workspace_bytes(int B, int H, int D);
 HQ_API int hq_quant_k_perchannel(const void* x, int x_dtype, const int64_t x_strides[4], int B, int H,

@@ -77,9 +77,12 @@ def test_golden_edge_cases(golden):
     ((1, 2, 33, 256), "bf16"),
     ((3, 2, 129, 128), "f16"),
     ((1, 2, 65, 128), "f32"),
-    ((2, 4, 8192, 128), "bf16"),     # 64 chunks per slab: cooperative exchange
-    ((1, 1, 131072, 128), "bf16"),   # 1024 chunks: more than the resident grid (two-pass)
+    ((2, 4, 8192, 128), "bf16"),     # 64 chunks per slab, one group
+    ((1, 1, 131072, 128), "bf16"),   # 1024 chunks of one slab: every block shares it
     ((1, 1, 40000, 256), "f32"),
+    ((32, 8, 256, 128), "bf16"),     # 256 slabs of 2 chunks: one block range spans slabs
+    ((16, 8, 300, 64), "f16"),       # ragged 3-chunk slabs
+    ((4, 8, 16384, 128), "bf16"),    # 4 MB slabs: several groups, A / B phases interleave
 ])
 def test_random_vs_oracle(shape, dt):
     rng = np.random.default_rng(hash(shape) % 2**32)
