@@ -306,15 +306,13 @@ def main():
     q = torch.randn((nl, B, HQ, D), generator=gen, device=device).to(torch.bfloat16)
     out = torch.empty((nl, B, HQ, D), dtype=torch.bfloat16, device=device)
     sm_scale = 1.0 / math.sqrt(D)
-    seq = sharding.SequenceShardedDecode(B, HQ, D, device) if world > 1 else None
-
+    # One sequence per GPU (batch sharding): every rank decodes its own caches,
+    # no collective on the data path.  The sequence-sharded mode (one long
+    # sequence split across ranks, partials exchanged) is measured separately.
     def step():
         for l, (k8, ks, v8, vs) in enumerate(caches):
-            if seq is None:
-                kernels.int8_decode_attn(q[l], k8, ks, v8, vs, HQ // HKV, sm_scale=sm_scale,
-                                         out=out[l])
-            else:
-                seq(q[l], k8, ks, v8, vs, sm_scale=sm_scale, out=out[l])
+            kernels.int8_decode_attn(q[l], k8, ks, v8, vs, HQ // HKV, sm_scale=sm_scale,
+                                     out=out[l])
 
     with torch.cuda.stream(stream):
         ms, clocks = time_graph(torch, step, args.steps, args.warmup, stream,
@@ -324,6 +322,33 @@ def main():
         t = torch.tensor([ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
+
+    batched = None
+    if not args.no_extras:
+        batched = run_batched(torch, kernels, device, stream, world, dist, peak)
+
+    seq_sharded = None
+    if world > 1 and not args.no_extras:
+        seq = sharding.SequenceShardedDecode(B, HQ, D, device)
+
+        def seq_step():
+            for l, (k8, ks, v8, vs) in enumerate(caches):
+                seq(q[l], k8, ks, v8, vs, sm_scale=sm_scale, out=out[l])
+
+        with torch.cuda.stream(stream):
+            ms_seq, _ = time_graph(torch, seq_step, min(args.steps, 100), min(args.warmup, 5),
+                                   stream, label="seq_sharded_step")
+        t = torch.tensor([ms_seq], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_seq = float(t.item())
+        seq_sharded = {
+            "workload": f"one sequence of S={S_HEAD * world} split across {world} ranks "
+                        f"({S_HEAD} tokens each), {nl} layers",
+            "us_per_layer": round(ms_seq * 1e3 / nl, 3),
+            "gbs": round(world * nl * decode_bytes(B, HQ, HKV, S_HEAD, D) / (ms_seq * 1e-3) / 1e9, 1),
+            "exchange": "per layer: split kernel writes (m, l, o) partials, NCCL all_gather, "
+                        "combine kernel"}
+        del seq
     per_layer = decode_bytes(B, HQ, HKV, S_HEAD, D)
     value = world * nl * per_layer / (ms * 1e-3) / 1e9
     us_layer = ms * 1e3 / nl
@@ -333,7 +358,7 @@ def main():
     e2e = None
     if not args.no_e2e:
         e2e = run_e2e(torch, kernels, QuantizedKVCache, quantized_attention_forward, caches,
-                      device, stream, min(args.steps, 100), min(args.warmup, 5), world, dist, seq)
+                      device, stream, min(args.steps, 100), min(args.warmup, 5), world, dist)
 
     extras = {}
     if world == 1 and not args.no_extras:
@@ -350,7 +375,8 @@ def main():
                                    "fp32 scales",
                        "l2": f"inputs larger than L2: {nl} caches x "
                              f"{per_layer / 1e6:.1f} MB read round-robin",
-                       "parallelism": f"sequence-sharded x{world}" if world > 1 else "single GPU",
+                       "parallelism": (f"batch-sharded x{world}: one sequence per GPU, no "
+                                       "collective" if world > 1 else "single GPU"),
                        "graph": f"{nl} launches per step in one CUDA graph"},
             "us_per_layer": round(us_layer, 3),
             "frac_of_peak": round(achieved / peak, 4),
@@ -362,8 +388,12 @@ def main():
                          "algorithmic_bytes_per_launch": per_layer},
             "clocks": clocks or {},
             "e2e": e2e,
-            "gpu_launches": args.steps * nl * (1 if world == 1 else 2),
+            "gpu_launches": args.steps * nl,
         }
+        if batched:
+            line["batched_decode"] = batched
+        if seq_sharded:
+            line["seq_sharded"] = seq_sharded
         line.update(extras)
         if world == 1 and not args.no_cpu:
             gbs, cores, layers, el = cpu_decode_gbs(seconds=10.0)
@@ -388,12 +418,11 @@ class _Attn:
 
 
 def run_e2e(torch, kernels, QuantizedKVCache, attn_fwd, caches, device, stream, steps, warmup,
-            world, dist, seq=None):
+            world, dist):
     """Public-API decode: per step, per layer ``cache.update`` (append one token)
     and ``quantized_attention_forward`` (split-KV decode); inputs copied from
     pinned host memory, outputs copied back, inside the timed region.  With
-    several ranks each rank appends to its own chunk and the attention is the
-    sequence-sharded decode (partials, all_gather, combine)."""
+    several ranks every rank runs its own sequence (batch sharding)."""
     import transformers.models.qwen3.modeling_qwen3 as qwen3_mod  # noqa: F401
     from halftone_quantizedkvcache_b200.integration import quantized_attention as qa
     module = _Attn(HQ // HKV, D)
@@ -421,13 +450,8 @@ def run_e2e(torch, kernels, QuantizedKVCache, attn_fwd, caches, device, stream, 
             kn = d_in[l, nq:nq + nk].view(B, 1, HKV, D).transpose(1, 2)
             vn = d_in[l, nq + nk:].view(B, 1, HKV, D).transpose(1, 2)
             k, v = cache.update(kn, vn, l)
-            if seq is None:
-                o, _ = attn_fwd(module, qv, k, v, None, scaling=1.0 / math.sqrt(D))
-                d_out[l].copy_(o)
-            else:
-                k8, v8, ks, vs = cache._store[l].codes()
-                seq(qv[:, :, 0, :], k8, ks, v8, vs, sm_scale=1.0 / math.sqrt(D),
-                    q_quant=True, out=d_out[l, :, 0])
+            o, _ = attn_fwd(module, qv, k, v, None, scaling=1.0 / math.sqrt(D))
+            d_out[l].copy_(o)
         h_out.copy_(d_out, non_blocking=True)
 
     with torch.cuda.stream(stream):
@@ -452,6 +476,44 @@ def run_e2e(torch, kernels, QuantizedKVCache, attn_fwd, caches, device, stream, 
             "d2h_bytes_per_step": nl * B * HQ * D * 2, "ms_per_step": round(ms, 4),
             "path": "QuantizedKVCache.update + quantized_attention_forward per layer, eager "
                     "(no graph), fp16 cache scales"}
+
+
+def run_batched(torch, kernels, device, stream, world, dist, peak, B_all=64, S=8192, nl=LAYERS):
+    """Batched decode (B=64 sequences of S=8192, 28 layers): the batch is split
+    across ranks (B/N per GPU, no collective); one CUDA graph per 28-layer step."""
+    if B_all % world:
+        return None
+    b = B_all // world
+    gen = torch.Generator(device=device).manual_seed(77 + (dist.get_rank() if world > 1 else 0))
+    caches = []
+    for _ in range(nl):
+        k8 = torch.randint(-127, 128, (b, HKV, S, D), generator=gen, device=device, dtype=torch.int8)
+        v8 = torch.randint(-127, 128, (b, HKV, S, D), generator=gen, device=device, dtype=torch.int8)
+        ks = torch.rand((b, HKV, 1, D), generator=gen, device=device) * 0.1
+        vs = torch.rand((b, HKV, S, 1), generator=gen, device=device) * 0.02
+        caches.append((k8, ks, v8, vs))
+    q = torch.randn((nl, b, HQ, D), generator=gen, device=device).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    sm_scale = 1.0 / math.sqrt(D)
+
+    def step():
+        for l, (k8, ks, v8, vs) in enumerate(caches):
+            kernels.int8_decode_attn(q[l], k8, ks, v8, vs, HQ // HKV, sm_scale=sm_scale, out=out[l])
+
+    with torch.cuda.stream(stream):
+        ms, _ = time_graph(torch, step, 20, 3, stream, label="batched_step")
+    if world > 1:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    per_layer = decode_bytes(b, HQ, HKV, S, D)
+    del caches, q, out
+    torch.cuda.empty_cache()
+    return {"workload": f"B={B_all} sequences ({b} per GPU), S={S}, Hq={HQ}, Hkv={HKV}, D={D}, "
+                        f"{nl} layers, int8 K/V + fp32 scales; one CUDA graph per step",
+            "ms_per_step": round(ms, 4), "us_per_layer": round(ms * 1e3 / nl, 2),
+            "gbs": round(world * nl * per_layer / (ms * 1e-3) / 1e9, 1),
+            "frac_of_peak_per_gpu": round(nl * per_layer / (ms * 1e-3) / 1e9 / peak, 4)}
 
 
 def run_extras(torch, kernels, device, gen, stream, us_int8, peak):

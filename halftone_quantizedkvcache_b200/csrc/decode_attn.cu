@@ -2,28 +2,25 @@
 // (bf16 / f16) twin and the log-sum-exp combine.
 //
 // Reference semantics: int8_decode_attn (src/kernels/int8_decode_attn_triton.py:15-63,
-// 101-113) - dequantize K per channel and V per token in registers, online
-// float32 softmax, one query token - and the decode step of
-// quantized_attention_forward (tests/qwen_kvcache_full.py:95-113), including its
-// optional per-token fake quantization of q.  The reference launches one
-// program per q head (16 programs for the whole GPU).  This kernel:
+// 101-113) - dequantize K per channel and V per token, online float32 softmax,
+// one query token - and the decode step of quantized_attention_forward
+// (tests/qwen_kvcache_full.py:95-113), including its optional per-token fake
+// quantization of q.  The reference launches one program per q head (16
+// programs for the whole GPU).  Here, common to both kernels:
 //
-//   * splits the sequence: grid = (split, kv head, batch), split count chosen
+//   * the sequence is split: grid = (split, kv head, batch), split count chosen
 //     on the host so that the grid fills every SM (batch 1 included);
-//   * serves all n_rep = Hq / Hkv q heads of a kv head from one K/V tile;
-//   * streams K/V tiles (64 tokens) through a 4-stage shared-memory ring filled
-//     by 1-D bulk copies (cp.async.bulk, completion on mbarriers, no tensor
-//     map, no multicast); every barrier wait is bounded;
-//   * gives each token to LPT lanes (LPT = 2 * n_rep), each owning D / LPT
-//     channels; a lane keeps q * k_scale * sm_scale * log2(e) for its channels
-//     in registers, so K dequantization costs nothing per element beyond the
-//     int8 -> float conversion (byte permute + packed subtract) and the packed
-//     f32x2 FMA; V scales are folded into the softmax weight p;
-//   * rotates each lane's chunk order by its token parity so the 16-byte
-//     shared-memory reads of a quarter warp hit 8 distinct bank groups;
-//   * combines splits in the same launch: each block writes (m, l, o) for its
-//     split, and the last block of a (batch, kv head) to arrive - an atomic
+//   * all n_rep = Hq / Hkv q heads of a kv head are served from one K/V tile;
+//   * K/V tiles stream through a shared-memory ring filled by asynchronous
+//     copies completing on mbarriers; every barrier wait is bounded;
+//   * splits are combined in the same launch: each block writes (m, l, o) for
+//     its split, and the last block of a (batch, kv head) to arrive - an atomic
 //     ticket, no waiting - merges them and resets the ticket.
+//
+// decode_mma_kernel (int8 K/V, the hq_decode_int8 path) runs both dot products
+// on the int8 tensor cores; decode_kernel (the dense twin, hq_decode_dense) uses
+// CUDA-core packed f32x2 FMAs on 64-token tiles copied with 1-D bulk copies,
+// each token owned by LPT = 2 * n_rep lanes.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 

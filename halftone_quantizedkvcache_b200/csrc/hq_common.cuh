@@ -332,7 +332,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
     if (mbar_try_wait(bar, parity)) return true;
   return false;
 }
-// 1-D bulk copy global -> shared (no tensor map, no multicast); `bytes` and
+// 1-D bulk copy global -> this CTA's shared memory (no tensor map); `bytes` and
 // both addresses must be multiples of 16.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,
                                          uint64_t* bar) {
