@@ -16,6 +16,7 @@
 //   * Append: one block per (b, h) quantizes the few new tokens of K (per
 //     channel over the new tokens; scale not stored) and V (per token; scale
 //     stored), exactly as the reference's update() does on a non-empty layer.
+#include <algorithm>
 #include <atomic>
 #include <cstdio>
 
@@ -218,66 +219,51 @@ __global__ void __launch_bounds__(kThreads) quant_v_kernel(
 
 // ------------------------------------------------------------------ K per channel
 // A (b, h) slab of S x D is cut into chunks of kRowsPerChunk whole rows (32 KB
-// of input).
-//
-// Work is an ordered queue of items (one chunk each), dequeued with an atomic
-// counter.  Slabs form groups of at most kGroupBytes of input; for group g,
-// A(g) items publish column maxima (atomicMax) and B(g) items re-read their
-// chunk - from L2, since the group was read moments before - and write codes.
-// Queue order A0, A1, B0, A2, B1, ..., A(n-1), B(n-2), B(n-1): every A(g) item
-// precedes every B(g) item, and a block works through its items in queue
-// order, so the lowest unfinished item can always proceed (an A item never
-// waits; a B item waits, bounded, only for lower A items).
-//
-// A block is 8 compute warps and one control warp.  Compute warps stream
-// chunks through a kKStages-deep shared-memory ring with cp.async (each thread
-// reads back only the 16-byte slots it copied, so the ring needs no barrier);
-// the control warp dequeues items, counts finished A items per group, builds
-// the group's quantizer table when the last one lands, and does the bounded
-// wait of B items - so compute warps never fence or spin.  One barrier per
-// A item, two per B item.
-constexpr int kKCompute = 256;               // compute threads
-constexpr int kKThreads = kKCompute + 32;    // + control warp
+// of input).  The persistent grid (every block resident) is split into teams;
+// team t handles slabs t, t + T, t + 2T, ..., one at a time, every block of the
+// team taking one contiguous run of the slab's chunks:
+//   A  stream the run, fold column maxima in registers; reduce over the block;
+//      publish to the slab's global maxima (one atomicMax per column, waited
+//      for), count the block, and wait (bounded) until the whole team counted;
+//   B  re-read the run - from L2: the team read the slab moments before, and T
+//      is chosen so that T slabs fit in kTeamBytes - and write codes.
+// Chunks stream through a kKStages-deep shared-memory ring with cp.async; the
+// ring runs ahead across the A / B / next-slab boundaries, so HBM stays busy
+// while a block waits for its team.  A team of one block needs no exchange.
 constexpr int kKStages = 3;
+constexpr size_t kTeamBytes = size_t(64) << 20;  // input of the slabs in flight
 
 template <int DT, int D>
 struct KShape {
   static constexpr int kVecElems = 16 / Elem<DT>::kBytes;
   static constexpr int kVecPerRow = D / kVecElems;             // column groups
-  static constexpr int kRowSlots = kKCompute / kVecPerRow;     // rows per pass
+  static constexpr int kRowSlots = kThreads / kVecPerRow;      // rows per pass
   static constexpr int kPasses = 8;
   static constexpr int kRowsPerChunk = kRowSlots * kPasses;    // 32 KB of input
-  static constexpr int kWarps = kKCompute / 32;
+  static constexpr int kWarps = kThreads / 32;
   // rows of the block-level max table: one per warp when a warp spans whole
   // rows, else one per row slot
   static constexpr int kRedRows = kVecPerRow <= 32 ? kWarps : kRowSlots;
-  static constexpr int kStageVecs = kKCompute * kPasses;       // 16-byte slots per stage
+  static constexpr int kStageVecs = kThreads * kPasses;        // 16-byte slots per stage
   static constexpr size_t kTableOff = size_t(kKStages) * kStageVecs * 16;
-  static constexpr size_t kQsOff = kTableOff + size_t(2) * kRedRows * D * 4;
+  static constexpr size_t kQsOff = kTableOff + size_t(kRedRows) * D * 4;
   static constexpr size_t kSmem = kQsOff + size_t(D) * 8;
 };
 
-constexpr size_t kGroupBytes = size_t(24) << 20;
-
 struct KWorkspace {
   int* status;        // [1]
-  int* next;          // [1] queue head
-  int* done;          // [groups] A items finished
-  int* ready;         // [groups] quantizer table of the group written
+  int* done;          // [B*H] blocks of the team that published the slab's maxima
   unsigned* amax;     // [B*H*D] column absmax as float bits (all >= 0)
-  float2* qtab;       // [B*H*D] (scale, reciprocal) per column
 };
 
 struct KPlan {
-  int n_slabs, n_chunks, spg, n_groups;
-  int total;          // queue length (fused: one item per slab)
-  int fused;          // a slab is one chunk: no queue phases
+  int n_slabs, n_chunks, teams;
 };
 
 __host__ __device__ inline size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
 
-// L2 policies: A items keep their chunk in L2 for the B re-read, B items (and
-// single-pass items) mark it as last use.
+// L2 policies: A reads keep their chunk in L2 for the B re-read, B reads mark it
+// as last use.
 __device__ __forceinline__ uint64_t l2_policy_keep() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
@@ -288,10 +274,9 @@ __device__ __forceinline__ uint64_t l2_policy_drop() {
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
   return p;
 }
-enum KKind : int { kItemA = 0, kItemB = 1, kItemFused = 2 };
 
 template <int DT, int D>
-__global__ void __launch_bounds__(kKThreads, 2) quant_k_kernel(
+__global__ void __launch_bounds__(kThreads, 2) quant_k_kernel(
     const char* __restrict__ x, int64_t xsb, int64_t xsh, int64_t xss, int H, int S, KPlan pl,
     int8_t* __restrict__ q, int64_t qsb, int64_t qsh, int64_t qss, float* __restrict__ sc32,
     __half* __restrict__ sc16, KWorkspace ws) {
@@ -299,263 +284,177 @@ __global__ void __launch_bounds__(kKThreads, 2) quant_k_kernel(
   constexpr int EB = Elem<DT>::kBytes;
   constexpr int VE = Sh::kVecElems;
   constexpr int NS = kKStages;
-  constexpr int R = NS + 1;  // decoded items in flight: current + NS ahead
   extern __shared__ __align__(128) unsigned char smem[];
   uint4* stages = reinterpret_cast<uint4*>(smem);
-  float* table = reinterpret_cast<float*>(smem + Sh::kTableOff);  // [2][kRedRows][D]
+  float* table = reinterpret_cast<float*>(smem + Sh::kTableOff);  // [kRedRows][D]
   float2* qs = reinterpret_cast<float2*>(smem + Sh::kQsOff);      // [D] (scale, rcp)
-  // decoded items: index, slab, chunk, group, kind, b, h, valid
-  __shared__ int s_info[R][8];
   __shared__ int s_ok;
   const int tid = threadIdx.x;
-  const int lane = tid & 31;
-  const bool control = tid >= kKCompute;
+  const int lane = tid & 31, warp = tid >> 5;
   const int cg = tid % Sh::kVecPerRow;      // column group: columns cg*VE .. +VE
   const int rs = tid / Sh::kVecPerRow;      // row slot
-  const int warp = tid >> 5;
   const int red_row = Sh::kVecPerRow <= 32 ? warp : rs;
   const bool red_writer = Sh::kVecPerRow <= 32 ? lane < Sh::kVecPerRow : true;
+  const int G = gridDim.x, T = pl.teams;
+  const int team = blockIdx.x % T, rank = blockIdx.x / T;
+  const int members = (G - team + T - 1) / T;   // blocks b < G with b % T == team
+  const int lo = static_cast<int>(static_cast<int64_t>(pl.n_chunks) * rank / members);
+  const int hi = static_cast<int>(static_cast<int64_t>(pl.n_chunks) * (rank + 1) / members);
+  const uint64_t pol_keep = l2_policy_keep(), pol_drop = l2_policy_drop();
 
-  // control lane 0 only: item index -> slot
-  auto decode = [&](int item, int slot) {
-    int slab = 0, chunk = 0, g = 0, kind = kItemFused;
-    if (item < pl.total) {
-      if (pl.fused) {
-        slab = item;
-      } else {
-        const int per_phase = pl.spg * pl.n_chunks;
-        const int phase = item / per_phase;
-        const int r = item - phase * per_phase;
-        kind = kItemA;
-        if (phase == 0) {
-          g = 0;
-        } else if (phase == 2 * pl.n_groups - 1) {
-          g = pl.n_groups - 1;
-          kind = kItemB;
-        } else if (phase & 1) {
-          g = (phase + 1) >> 1;
-        } else {
-          g = (phase >> 1) - 1;
-          kind = kItemB;
-        }
-        slab = g * pl.spg + r / pl.n_chunks;
-        chunk = r % pl.n_chunks;
-      }
-    }
-    int* o = s_info[slot];
-    o[0] = item;
-    o[1] = slab;
-    o[2] = chunk;
-    o[3] = g;
-    o[4] = kind;
-    o[5] = slab / H;
-    o[6] = slab % H;
-    o[7] = item < pl.total && slab < pl.n_slabs;  // padding items of the last group do nothing
-  };
-
-  // compute threads: copy the chunk of the item in `slot` into ring stage `stage`
-  auto issue = [&](int slot, int stage) {
-    const int* in = s_info[slot];
-    if (in[7]) {
-      const uint64_t pol = in[4] == kItemA ? l2_policy_keep() : l2_policy_drop();
-      const char* base = x + (static_cast<int64_t>(in[5]) * xsb + static_cast<int64_t>(in[6]) * xsh) * EB +
-                         cg * 16;
-      const int row0 = in[2] * Sh::kRowsPerChunk;
+  // prefetch cursor over (slab k of the team, pass, chunk r)
+  int pf_k = 0, pf_pass = 0, pf_r = lo;
+  const bool empty = lo >= hi;
+  auto issue = [&](int stage) {
+    const int slab = team + pf_k * T;
+    if (!empty && slab < pl.n_slabs) {
+      const int b = slab / H, h = slab - (slab / H) * H;
+      const char* base = x + (static_cast<int64_t>(b) * xsb + static_cast<int64_t>(h) * xsh) * EB + cg * 16;
+      const int row0 = pf_r * Sh::kRowsPerChunk;
+      const uint64_t pol = pf_pass == 0 ? pol_keep : pol_drop;
       uint4* dst = stages + stage * Sh::kStageVecs + tid;
 #pragma unroll
       for (int p = 0; p < Sh::kPasses; ++p) {
         const int s = row0 + p * Sh::kRowSlots + rs;
         const char* src = s < S ? base + static_cast<int64_t>(s) * xss * EB : base;
-        cp_async16(dst + p * kKCompute, src, s < S ? 16 : 0, pol);
+        cp_async16(dst + p * kThreads, src, s < S ? 16 : 0, pol);
+      }
+      if (++pf_r >= hi) {
+        pf_r = lo;
+        if (++pf_pass == 2) {
+          pf_pass = 0;
+          ++pf_k;
+        }
       }
     }
     cp_async_commit();
   };
 
-  // control warp: count one finished A item of group g; the last one builds the
-  // group's quantizer table and scale outputs, then publishes ready[g]
-  auto signal = [&](int g) {
-    int last = 0;
-    if (lane == 0) {
-      __threadfence();  // the block's column maxima (ordered by the barrier) before the count
-      const int need = min(pl.spg, pl.n_slabs - g * pl.spg) * pl.n_chunks;
-      last = atomicAdd(ws.done + g, 1) == need - 1;
-    }
-    last = __shfl_sync(0xffffffffu, last, 0);
-    if (!last) return;
-    __threadfence();
-    const int64_t col0 = static_cast<int64_t>(g) * pl.spg * D;
-    const int n4 = min(pl.spg, pl.n_slabs - g * pl.spg) * (D / 4);
-    const float4* a4 = reinterpret_cast<const float4*>(ws.amax + col0);
-    float4* t4 = reinterpret_cast<float4*>(ws.qtab + col0);
-    for (int j0 = 0; j0 < n4; j0 += 4 * 32) {
-      float4 a[4];
+  for (int k = 0; k < NS - 1; ++k) issue(k);
+  int it = 0;  // chunks consumed (ring position)
+  for (int k = 0;; ++k) {
+    const int slab = team + k * T;
+    if (slab >= pl.n_slabs) break;
+    // ---- A: column maxima of this block's run
+    float cmax[VE];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int j = j0 + u * 32 + lane;
-        a[u] = j < n4 ? __ldcg(a4 + j) : make_float4(0.f, 0.f, 0.f, 0.f);
-      }
+    for (int e = 0; e < VE; ++e) cmax[e] = 0.0f;
+    for (int r = lo; r < hi; ++r, ++it) {
+      issue((it + NS - 1) % NS);
+      cp_async_wait<NS - 1>();  // this thread's copies of chunk `it` have landed
+      const uint4* st = stages + (it % NS) * Sh::kStageVecs + tid;
+      if constexpr (DT == HQ_DTYPE_F32) {
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int j = j0 + u * 32 + lane;
-        if (j >= n4) continue;
-        const Quantizer q0 = quantizer_for<DT>(a[u].x), q1 = quantizer_for<DT>(a[u].y);
-        const Quantizer q2 = quantizer_for<DT>(a[u].z), q3 = quantizer_for<DT>(a[u].w);
-        t4[2 * j] = make_float4(q0.scale, q0.rcp, q1.scale, q1.rcp);
-        t4[2 * j + 1] = make_float4(q2.scale, q2.rcp, q3.scale, q3.rcp);
-        const int64_t c = col0 + 4 * static_cast<int64_t>(j);
-        if (sc32) {
-          sc32[c] = q0.scale;
-          sc32[c + 1] = q1.scale;
-          sc32[c + 2] = q2.scale;
-          sc32[c + 3] = q3.scale;
-        }
-        if (sc16) {
-          sc16[c] = __float2half_rn(q0.scale);
-          sc16[c + 1] = __float2half_rn(q1.scale);
-          sc16[c + 2] = __float2half_rn(q2.scale);
-          sc16[c + 3] = __float2half_rn(q3.scale);
-        }
-      }
-    }
-    __threadfence();
-    __syncwarp();
-    if (lane == 0) atomicExch(ws.ready + g, 1);
-  };
-
-  if (control && lane == 0) {
-    for (int k = 0; k < NS; ++k) decode(atomicAdd(ws.next, 1), k);
-  }
-  __syncthreads();
-  if (!control) {
-    for (int k = 0; k < NS - 1; ++k) issue(k, k);
-  }
-  int pend_g = -1;  // control warp: group of this block's last A item, not yet counted
-  for (int i = 0;; ++i) {
-    const int* in = s_info[i % R];
-    if (in[0] >= pl.total) break;
-    const int slab = in[1], chunk = in[2], g = in[3], kind = in[4], b = in[5], h = in[6];
-    const bool valid = in[7] != 0;
-    const uint4* st = stages + (i % NS) * Sh::kStageVecs + tid;
-    if (!control) {
-      issue((i + NS - 1) % R, (i + NS - 1) % NS);
-      cp_async_wait<NS - 1>();  // this thread's copies of item i have landed
-      if (kind != kItemB && valid) {
-        float cmax[VE];
-        if constexpr (DT == HQ_DTYPE_F32) {
-#pragma unroll
-          for (int e = 0; e < VE; ++e) cmax[e] = 0.0f;
-#pragma unroll
-          for (int p = 0; p < Sh::kPasses; ++p) {
-            float f[VE];
-            Vec16<DT>::unpack(st[p * kKCompute], f);
-#pragma unroll
-            for (int e = 0; e < VE; ++e) cmax[e] = fmaxf(cmax[e], fabsf(f[e]));
-          }
-        } else {
-          uint4 m = st[0];
-#pragma unroll
-          for (int p = 1; p < Sh::kPasses; ++p) {
-            const uint4 d = st[p * kKCompute];
-            m.x = absmax_x2<DT>(m.x, d.x);
-            m.y = absmax_x2<DT>(m.y, d.y);
-            m.z = absmax_x2<DT>(m.z, d.z);
-            m.w = absmax_x2<DT>(m.w, d.w);
-          }
+        for (int p = 0; p < Sh::kPasses; ++p) {
           float f[VE];
-          Vec16<DT>::unpack(m, f);
+          Vec16<DT>::unpack(st[p * kThreads], f);
 #pragma unroll
-          for (int e = 0; e < VE; ++e) cmax[e] = fabsf(f[e]);
+          for (int e = 0; e < VE; ++e) cmax[e] = fmaxf(cmax[e], fabsf(f[e]));
         }
-        // lanes of one warp that share a column group differ in bits >= log2(kVecPerRow)
+      } else {
+        uint4 m = st[0];
 #pragma unroll
-        for (int off = Sh::kVecPerRow; off < 32; off <<= 1)
-#pragma unroll
-          for (int e = 0; e < VE; ++e)
-            cmax[e] = fmaxf(cmax[e], __shfl_xor_sync(0xffffffffu, cmax[e], off));
-        if (red_writer) {
-          float* row = table + ((i & 1) * Sh::kRedRows + red_row) * D + cg * VE;
-#pragma unroll
-          for (int e = 0; e < VE; e += 4)
-            *reinterpret_cast<float4*>(row + e) = make_float4(cmax[e], cmax[e + 1], cmax[e + 2], cmax[e + 3]);
+        for (int p = 1; p < Sh::kPasses; ++p) {
+          const uint4 d = st[p * kThreads];
+          m.x = absmax_x2<DT>(m.x, d.x);
+          m.y = absmax_x2<DT>(m.y, d.y);
+          m.z = absmax_x2<DT>(m.z, d.z);
+          m.w = absmax_x2<DT>(m.w, d.w);
         }
-      }
-    } else if (lane == 0) {
-      decode(atomicAdd(ws.next, 1), (i + NS) % R);
-    }
-    __syncthreads();  // table rows, decoded item i+NS
-    if (!control) {
-      if (kind != kItemB && valid && tid < D) {
-        const float* col = table + (i & 1) * Sh::kRedRows * D + tid;
-        float m = col[0];
+        float f[VE];
+        Vec16<DT>::unpack(m, f);
 #pragma unroll
-        for (int w = 1; w < Sh::kRedRows; ++w) m = fmaxf(m, col[w * D]);
-        if (kind == kItemFused) {  // whole slab in this item: the maximum is final
-          const Quantizer qz = quantizer_for<DT>(m);
-          qs[tid] = make_float2(qz.scale, qz.rcp);
-          const int64_t so = static_cast<int64_t>(slab) * D + tid;
-          if (sc32) sc32[so] = qz.scale;
-          if (sc16) sc16[so] = __float2half_rn(qz.scale);
-        } else {
-          atomicMax(ws.amax + static_cast<int64_t>(slab) * D + tid, __float_as_uint(m));
-        }
-      }
-    } else {
-      if (pend_g >= 0) signal(pend_g);  // the previous item's maxima are ordered by the barrier
-      pend_g = kind == kItemA && valid ? g : -1;
-      if (kind == kItemB) {
-        int ok = 0;
-        if (valid) {
-          if (lane == 0) {
-            for (uint32_t it = 0; it < kSpinLimit; ++it) {
-              if (*reinterpret_cast<volatile int*>(ws.ready + g) != 0) {
-                ok = 1;
-                break;
-              }
-              __nanosleep(64);
-            }
-            __threadfence();
-            if (!ok) report_error(ws.status, HQ_ERR_DEVICE_TIMEOUT);
-          }
-          ok = __shfl_sync(0xffffffffu, ok, 0);
-          if (ok) {
-            const float4* t4 = reinterpret_cast<const float4*>(ws.qtab + static_cast<int64_t>(slab) * D);
-            float4* d4 = reinterpret_cast<float4*>(qs);
-            for (int j = lane; j < D / 2; j += 32) d4[j] = __ldcg(t4 + j);
-          }
-        }
-        if (lane == 0) s_ok = ok;  // gave up: status word set, this chunk's codes are not written
+        for (int e = 0; e < VE; ++e) cmax[e] = fmaxf(cmax[e], fabsf(f[e]));
       }
     }
-    if (kind != kItemA) {
-      __syncthreads();  // quantizer row qs[] of the slab
-      if (!control && valid && (kind == kItemFused || s_ok)) {
-        Quantizer qz[VE];
-        F2 rcp2[VE / 2], ns2[VE / 2];
-        const float4* q4 = reinterpret_cast<const float4*>(qs + cg * VE);
+    // lanes of one warp that share a column group differ in bits >= log2(kVecPerRow)
 #pragma unroll
-        for (int e = 0; e < VE / 2; ++e) {
-          const float4 t = q4[e];
-          qz[2 * e].scale = t.x;
-          qz[2 * e].rcp = t.y;
-          qz[2 * e + 1].scale = t.z;
-          qz[2 * e + 1].rcp = t.w;
-          rcp2[e] = f2_make(t.y, t.w);
-          ns2[e] = f2_make(-t.x, -t.z);
+    for (int off = Sh::kVecPerRow; off < 32; off <<= 1)
+#pragma unroll
+      for (int e = 0; e < VE; ++e) cmax[e] = fmaxf(cmax[e], __shfl_xor_sync(0xffffffffu, cmax[e], off));
+    if (red_writer) {
+#pragma unroll
+      for (int e = 0; e < VE; ++e) table[red_row * D + cg * VE + e] = cmax[e];
+    }
+    __syncthreads();  // block table complete; qs of the previous slab no longer read
+    float m = 0.0f;
+    if (tid < D) {
+      m = table[tid];
+#pragma unroll
+      for (int w = 1; w < Sh::kRedRows; ++w) m = fmaxf(m, table[w * D + tid]);
+    }
+    const int64_t col0 = static_cast<int64_t>(slab) * D;
+    bool ok = true;
+    if (members > 1) {
+      // publish; the returned old value is awaited, so the maximum is performed
+      // in L2 before this block is counted
+      if (tid < D && m > 0.0f) {
+        const unsigned old = atomicMax(ws.amax + col0 + tid, __float_as_uint(m));
+        if (old == 0xffffffffu) s_ok = 0;  // never: maxima are >= 0; forces the wait
+      }
+      __syncthreads();
+      if (tid == 0) {
+        __threadfence();
+        atomicAdd(ws.done + slab, 1);
+        int seen = 0;
+        for (uint32_t i = 0; i < kSpinLimit; ++i) {
+          int c;
+          asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(c) : "l"(ws.done + slab) : "memory");
+          if (c >= members) {
+            seen = 1;
+            break;
+          }
+          __nanosleep(64);
         }
-        int8_t* qbase = q + static_cast<int64_t>(b) * qsb + static_cast<int64_t>(h) * qsh + cg * VE;
-        const int row0 = chunk * Sh::kRowsPerChunk;
+        if (!seen) report_error(ws.status, HQ_ERR_DEVICE_TIMEOUT);
+        s_ok = seen;
+      }
+      __syncthreads();
+      ok = s_ok != 0;  // gave up: status word set, this slab's codes are not written
+      if (ok && tid < D) m = __uint_as_float(__ldcg(ws.amax + col0 + tid));
+    }
+    if (ok && tid < D) {
+      const Quantizer qz = quantizer_for<DT>(m);
+      qs[tid] = make_float2(qz.scale, qz.rcp);
+      if (rank == 0) {  // one block per slab writes the scale outputs
+        if (sc32) sc32[col0 + tid] = qz.scale;
+        if (sc16) sc16[col0 + tid] = __float2half_rn(qz.scale);
+      }
+    }
+    __syncthreads();  // qs ready; table free for the next slab
+    // ---- B: codes of the same run
+    Quantizer qz[VE];
+    F2 rcp2[VE / 2], ns2[VE / 2];
+    {
+      const float4* q4 = reinterpret_cast<const float4*>(qs + cg * VE);
+#pragma unroll
+      for (int e = 0; e < VE / 2; ++e) {
+        const float4 t = q4[e];
+        qz[2 * e].scale = t.x;
+        qz[2 * e].rcp = t.y;
+        qz[2 * e + 1].scale = t.z;
+        qz[2 * e + 1].rcp = t.w;
+        rcp2[e] = f2_make(t.y, t.w);
+        ns2[e] = f2_make(-t.x, -t.z);
+      }
+    }
+    const int b = slab / H, h = slab - (slab / H) * H;
+    int8_t* qbase = q + static_cast<int64_t>(b) * qsb + static_cast<int64_t>(h) * qsh + cg * VE;
+    for (int r = lo; r < hi; ++r, ++it) {
+      issue((it + NS - 1) % NS);
+      cp_async_wait<NS - 1>();
+      const uint4* st = stages + (it % NS) * Sh::kStageVecs + tid;
+      if (ok) {
+        const int row0 = r * Sh::kRowsPerChunk;
 #pragma unroll
         for (int p = 0; p < Sh::kPasses; ++p) {
           const int s = row0 + p * Sh::kRowSlots + rs;
-          if (s < S) quant_vec_store<DT>(st[p * kKCompute], ns2, rcp2, qz, qbase + static_cast<int64_t>(s) * qss);
+          if (s < S) quant_vec_store<DT>(st[p * kThreads], ns2, rcp2, qz, qbase + static_cast<int64_t>(s) * qss);
         }
       }
     }
   }
-  __syncthreads();  // maxima of the block's last item
-  if (control && pend_g >= 0) signal(pend_g);
-  if (!control) cp_async_wait<0>();
+  cp_async_wait<0>();
 }
 
 // ------------------------------------------------------------------ append
@@ -668,59 +567,50 @@ static int launch_quant_v(const void* x, const int64_t* xs, int B, int H, int S,
 }
 
 template <int DT, int D>
-static KPlan plan_quant_k(int B, int H, int S) {
-  using Sh = KShape<DT, D>;
-  KPlan pl;
-  pl.n_slabs = B * H;
-  pl.n_chunks = (S + Sh::kRowsPerChunk - 1) / Sh::kRowsPerChunk;
-  const size_t slab_bytes = static_cast<size_t>(S) * D * Elem<DT>::kBytes;
-  pl.spg = static_cast<int>(kGroupBytes / (slab_bytes ? slab_bytes : 1));
-  if (pl.spg < 1) pl.spg = 1;
-  if (pl.spg > pl.n_slabs) pl.spg = pl.n_slabs;
-  pl.n_groups = (pl.n_slabs + pl.spg - 1) / pl.spg;
-  pl.fused = pl.n_chunks == 1;
-  pl.total = pl.fused ? pl.n_slabs : 2 * pl.n_groups * pl.spg * pl.n_chunks;
-  return pl;
-}
-
-template <int DT, int D>
 static int launch_quant_k(const void* x, const int64_t* xs, int B, int H, int S, int8_t* q,
                           const int64_t* qs, float* s32, uint16_t* s16, void* wsp,
                           cudaStream_t st) {
-  const KPlan pl = plan_quant_k<DT, D>(B, H, S);
-  char* w = static_cast<char*>(wsp);
-  const size_t nbh = static_cast<size_t>(B) * H;
-  KWorkspace ws;
-  ws.status = reinterpret_cast<int*>(w);
-  ws.next = reinterpret_cast<int*>(w + 4);
-  ws.done = reinterpret_cast<int*>(w + 256);
-  ws.ready = reinterpret_cast<int*>(w + 256 + align256(sizeof(int) * nbh));
-  ws.amax = reinterpret_cast<unsigned*>(w + 256 + 2 * align256(sizeof(int) * nbh));
-  ws.qtab = reinterpret_cast<float2*>(w + 256 + 2 * align256(sizeof(int) * nbh) +
-                                      align256(sizeof(unsigned) * nbh * D));
-  // status, queue head, counters, flags and maxima start at zero (the table need not)
-  const size_t clear = 256 + 2 * align256(sizeof(int) * nbh) + sizeof(unsigned) * nbh * D;
-  cudaError_t e = cudaMemsetAsync(wsp, 0, clear, st);
-  if (e != cudaSuccess) return static_cast<int>(e);
+  using Sh = KShape<DT, D>;
   auto kern = quant_k_kernel<DT, D>;
-  constexpr size_t smem = KShape<DT, D>::kSmem;
+  constexpr size_t smem = Sh::kSmem;
   int dev = 0;
   cudaGetDevice(&dev);
   static std::atomic<int> occ_cache[64];
   int per_sm = (dev >= 0 && dev < 64) ? occ_cache[dev].load(std::memory_order_relaxed) : 0;
+  cudaError_t e;
   if (per_sm <= 0) {
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return static_cast<int>(e);
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kKThreads, smem);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem);
     if (e != cudaSuccess) return static_cast<int>(e);
     if (per_sm <= 0) return HQ_ERR_UNSUPPORTED;
     if (dev >= 0 && dev < 64) occ_cache[dev].store(per_sm, std::memory_order_relaxed);
   }
-  int64_t grid = static_cast<int64_t>(per_sm) * sm_count(dev);
-  if (grid > pl.total) grid = pl.total;
-  if (static_cast<int64_t>(2) * pl.n_groups * pl.spg * pl.n_chunks >= (int64_t(1) << 31))
-    return HQ_ERR_UNSUPPORTED;
-  kern<<<static_cast<unsigned>(grid), kKThreads, smem, st>>>(
+  KPlan pl;
+  pl.n_slabs = B * H;
+  pl.n_chunks = (S + Sh::kRowsPerChunk - 1) / Sh::kRowsPerChunk;
+  // Blocks of a team wait for one another: the grid never exceeds what is
+  // resident at once.  Teams: as many slabs in flight as fit in kTeamBytes, no
+  // more teams than slabs, and no team larger than a slab has chunks.
+  const int64_t resident = static_cast<int64_t>(per_sm) * sm_count(dev);
+  const size_t slab_bytes = static_cast<size_t>(S) * D * Elem<DT>::kBytes;
+  int64_t teams = static_cast<int64_t>(kTeamBytes / (slab_bytes ? slab_bytes : 1));
+  teams = std::max<int64_t>(teams, (resident + pl.n_chunks - 1) / pl.n_chunks);
+  teams = std::min<int64_t>(std::max<int64_t>(teams, 1), pl.n_slabs);
+  pl.teams = static_cast<int>(teams);
+  int64_t grid = std::min<int64_t>(resident, teams * pl.n_chunks);
+  grid = std::max<int64_t>(grid, teams);
+  char* w = static_cast<char*>(wsp);
+  const size_t nbh = static_cast<size_t>(B) * H;
+  KWorkspace ws;
+  ws.status = reinterpret_cast<int*>(w);
+  ws.done = reinterpret_cast<int*>(w + 256);
+  ws.amax = reinterpret_cast<unsigned*>(w + 256 + align256(sizeof(int) * nbh));
+  // status, per-slab counters and maxima start at zero
+  const size_t clear = 256 + align256(sizeof(int) * nbh) + sizeof(unsigned) * nbh * D;
+  e = cudaMemsetAsync(wsp, 0, clear, st);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  kern<<<static_cast<unsigned>(grid), kThreads, smem, st>>>(
       static_cast<const char*>(x), xs[0], xs[1], xs[2], H, S, pl, q, qs[0], qs[1], qs[2], s32,
       reinterpret_cast<__half*>(s16), ws);
   return finish_launch();
@@ -774,8 +664,7 @@ using namespace hq;
 extern "C" size_t hq_quant_k_workspace_bytes(int B, int H, int D) {
   if (B < 0 || H < 0 || D < 0) return 0;
   const size_t nbh = static_cast<size_t>(B) * H;
-  return 256 + 2 * align256(sizeof(int) * nbh) + align256(sizeof(unsigned) * nbh * D) +
-         align256(sizeof(float2) * nbh * D);
+  return 256 + align256(sizeof(int) * nbh) + align256(sizeof(unsigned) * nbh * D);
 }
 
 extern "C" int hq_quant_k_perchannel(const void* x, int x_dtype, const int64_t x_strides[4], int B,

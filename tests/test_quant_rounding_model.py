@@ -143,33 +143,49 @@ def _fma32(a, b, c):
     return r
 
 
-def _markstein_check(amaxs, xs_of, codes_only=False):
+def _markstein(xs, s, y, steps):
+    S = np.full(xs.size, s, np.float32)
+    Y = np.full(xs.size, y, np.float32)
+    q = (xs.astype(np.float64) * np.float64(y)).astype(np.float32)
+    for _ in range(steps):
+        q = _fma32(_fma32(-q, S, xs), Y, q)
+    return q
+
+
+def _markstein_check(amaxs, xs_of, steps=1):
+    """Codes of the kernel quotient (``steps`` FMA corrections) equal the reference's."""
     for a in amaxs:
         s = np.float32(np.maximum(np.float32(a), np.float32(1e-8)) / np.float32(127))
         y = np.float32(np.float32(1) / s)
         xs = xs_of(a)
         xs = np.concatenate([xs, -xs]).astype(np.float32)
-        S = np.full(xs.size, s, np.float32)
-        Y = np.full(xs.size, y, np.float32)
-        q0 = (xs.astype(np.float64) * np.float64(y)).astype(np.float32)
-        q1 = _fma32(_fma32(-q0, S, xs), Y, q0)
-        q2 = _fma32(_fma32(-q1, S, xs), Y, q1)
-        if codes_only:
-            np.testing.assert_array_equal(np.rint(q2), np.rint(xs / s))
-        else:
-            np.testing.assert_array_equal(q2, xs / s)
+        np.testing.assert_array_equal(np.rint(_markstein(xs, s, y, steps)), np.rint(xs / s))
 
 
 @pytest.mark.parametrize("bits", [7, 10])
 def test_branch_free_quotient_16bit(bits):
-    """The 16-bit quantize kernels compute RN(x / s) as q0 = x * y,
-    q1 = fma(fma(-q0, s, x), y, q0), q2 = fma(fma(-q1, s, x), y, q1) with
-    y = RN(1 / s): for every bf16 / fp16 pair (x, amax), |x| <= amax, q2 is the
-    IEEE quotient, so rint(q2) is the reference code."""
+    """The 16-bit quantize kernels compute the code as rint(q1) with q0 = x * y,
+    q1 = fma(fma(-q0, s, x), y, q0), y = RN(1 / s) (hq_common.cuh, quot_pair):
+    for every bf16 / fp16 pair (x, amax), |x| <= amax, rint(q1) equals the
+    reference code rint(RN(x / s)) (q1 itself may differ from the IEEE quotient
+    in its last bit, never across a rounding boundary of the code)."""
     def xs_of(a):
         v = np.concatenate([_binade(bits, e) for e in range(-16, 1)] + [np.zeros(1)])
         return v[v <= a]
     _markstein_check(_binade(bits, 0), xs_of)
+
+
+def test_uncorrected_quotient_would_not_be_exact():
+    """Without the correction step (rint(RN(x * y))) some bf16 codes differ:
+    the FMA step is needed."""
+    bad = 0
+    for a in _binade(7, 0):
+        s = np.float32(np.float32(a) / np.float32(127))
+        y = np.float32(np.float32(1) / s)
+        v = np.concatenate([_binade(7, e) for e in range(-16, 1)])
+        xs = v[v <= a].astype(np.float32)
+        bad += int(np.count_nonzero(np.rint(_markstein(xs, s, y, 0)) != np.rint(xs / s)))
+    assert bad > 0
 
 
 def test_branch_free_quotient_clamped_amax():
@@ -179,4 +195,4 @@ def test_branch_free_quotient_clamped_amax():
     def xs_of(a):
         v = np.concatenate([_binade(7, e) for e in range(-133, -26)] + [np.zeros(1)])
         return v[v < 1e-8]
-    _markstein_check([0.0], xs_of, codes_only=True)
+    _markstein_check([0.0], xs_of)
