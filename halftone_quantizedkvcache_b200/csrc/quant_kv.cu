@@ -7,12 +7,12 @@
 // for K, read each column twice with a 256-byte stride.  Here:
 //
 //   * V per token: each row of D elements is read once with 16-byte vector
-//     loads by D*esize/16 lanes, reduced with warp shuffles, and written as
-//     packed int8 (8 codes per 16-byte input vector).
-//   * K per channel: an ordered work queue over 32 KB chunks of whole rows.
-//     For each group of slabs (<= 24 MB of input) one pass publishes the
-//     column maxima and a second pass, one group later, re-reads the chunks
-//     from L2 and writes codes, so HBM sees 1 read + 1 int8 write per element.
+//     loads by 4-8 lanes holding several vectors each, reduced with 2-3 warp
+//     shuffle rounds, and written as packed int8 (8 codes per 16-byte input
+//     vector).
+//   * K per channel: teams of blocks take one (b, h) slab at a time; a first
+//     pass publishes the column maxima, a second pass re-reads the chunks from
+//     L2 and writes codes, so HBM sees 1 read + 1 int8 write per element.
 //   * Append: one block per (b, h) quantizes the few new tokens of K (per
 //     channel over the new tokens; scale not stored) and V (per token; scale
 //     stored), exactly as the reference's update() does on a non-empty layer.
@@ -31,7 +31,10 @@ template <int DT, int D>
 struct VShape {
   static constexpr int kVecElems = 16 / Elem<DT>::kBytes;   // elements per 16-byte vector
   static constexpr int kVecPerRow = D / kVecElems;
-  static constexpr int kLanesPerRow = kVecPerRow < 32 ? kVecPerRow : 32;
+  // few lanes per row, several vectors per lane: the row maximum then costs 2-3
+  // shuffle rounds per row instead of 4-5 (at most 8 vectors in flight per lane)
+  static constexpr int kLanesPerRow =
+      kVecPerRow <= 4 ? kVecPerRow : (kVecPerRow / 8 > 4 ? kVecPerRow / 8 : 4);
   static constexpr int kVecPerLane = kVecPerRow / kLanesPerRow;
   static constexpr int kRowsPerWarp = 32 / kLanesPerRow;
 };
@@ -196,9 +199,11 @@ __global__ void __launch_bounds__(kThreads) quant_v_kernel(
 #pragma unroll
     for (int it = 0; it < IT; ++it) {
       const int s = s0 + it * Sh::kRowsPerWarp;
-      Quantizer qz;
-      qz.scale = __shfl_sync(0xffffffffu, mine.scale, group_base + it);
-      qz.rcp = __shfl_sync(0xffffffffu, mine.rcp, group_base + it);
+      Quantizer qz = mine;  // one row group: every lane holds its row's maximum
+      if constexpr (IT > 1) {
+        qz.scale = __shfl_sync(0xffffffffu, mine.scale, group_base + it);
+        qz.rcp = __shfl_sync(0xffffffffu, mine.rcp, group_base + it);
+      }
       if (s >= S) continue;
       Quantizer qzv[VE];
       F2 rcp2[VE / 2], ns2[VE / 2];
