@@ -10,9 +10,11 @@
 //     loads by 4-8 lanes holding several vectors each, reduced with 2-3 warp
 //     shuffle rounds, and written as packed int8 (8 codes per 16-byte input
 //     vector).
-//   * K per channel: teams of blocks take one (b, h) slab at a time; a first
-//     pass publishes the column maxima, a second pass re-reads the chunks from
-//     L2 and writes codes, so HBM sees 1 read + 1 int8 write per element.
+//   * K per channel: teams of blocks take one (b, h) slab at a time; pass A
+//     publishes the column maxima, pass B re-reads the chunks from L2 and
+//     writes codes, so HBM sees 1 read + 1 int8 write per element; on large
+//     inputs the two blocks of an SM split the passes (one HBM-bound, one
+//     compute-bound).
 //   * Append: one block per (b, h) quantizes the few new tokens of K (per
 //     channel over the new tokens; scale not stored) and V (per token; scale
 //     stored), exactly as the reference's update() does on a non-empty layer.
@@ -224,17 +226,25 @@ __global__ void __launch_bounds__(kThreads) quant_v_kernel(
 
 // ------------------------------------------------------------------ K per channel
 // A (b, h) slab of S x D is cut into chunks of kRowsPerChunk whole rows (32 KB
-// of input).  The persistent grid (every block resident) is split into teams;
-// team t handles slabs t, t + T, t + 2T, ..., one at a time, every block of the
-// team taking one contiguous run of the slab's chunks:
-//   A  stream the run, fold column maxima in registers; reduce over the block;
-//      publish to the slab's global maxima (one atomicMax per column, waited
-//      for), count the block, and wait (bounded) until the whole team counted;
-//   B  re-read the run - from L2: the team read the slab moments before, and T
-//      is chosen so that T slabs fit in kTeamBytes - and write codes.
-// Chunks stream through a kKStages-deep shared-memory ring with cp.async; the
-// ring runs ahead across the A / B / next-slab boundaries, so HBM stays busy
-// while a block waits for its team.  A team of one block needs no exchange.
+// of input).  Each slab is processed in two passes over its chunks:
+//   A  read the chunks and fold column maxima in registers; reduce over the
+//      block and publish to the slab's global maxima (one atomicMax per column,
+//      waited for), then count the block for the slab;
+//   B  once every A block of the slab is counted, re-read the chunks - from L2,
+//      they were read moments before - and write codes.
+// The persistent grid (every block resident) is split into teams; team t
+// handles slabs t, t + T, ..., and a team block takes one contiguous run of
+// each slab's chunks.  Paired grids (large inputs): the two blocks of a pair
+// (blockIdx i and i + G/2 - normally the two blocks of one SM) split the
+// passes: the first runs pass A only (HBM-bound), the second pass B only
+// (compute-bound), so every SM keeps both kinds of work in flight; the A side
+// runs at most two slabs ahead of the B side (bounded L2 footprint: T slabs
+// being re-read and T being read, T chosen to fit kTeamBytes).  Small grids:
+// every block runs A then B of its run, waiting for its team in between.
+// Waits are bounded and only point to lower slab indices (no cycle); a block
+// that gives up sets the status word and skips its codes.
+// Chunks stream through a kKStages-deep shared-memory ring with cp.async that
+// runs ahead across pass and slab boundaries.
 constexpr int kKStages = 3;
 constexpr size_t kTeamBytes = size_t(64) << 20;  // input of the slabs in flight
 
@@ -255,15 +265,32 @@ struct KShape {
   static constexpr size_t kSmem = kQsOff + size_t(D) * 8;
 };
 
+constexpr int kMaxSmIds = 1024;  // per-SM arrival counters (paired grids)
+
 struct KWorkspace {
   int* status;        // [1]
-  int* done;          // [B*H] blocks of the team that published the slab's maxima
+  int* roles;         // [2] blocks that took role A / role B (paired grids)
+  int* sm_slot;       // [kMaxSmIds] blocks that started on each SM (paired grids)
+  int* a_done;        // [B*H] A blocks that published the slab's maxima
+  int* b_done;        // [B*H] B blocks that finished the slab (paired grids)
   unsigned* amax;     // [B*H*D] column absmax as float bits (all >= 0)
 };
 
 struct KPlan {
   int n_slabs, n_chunks, teams;
+  int paired;         // blocks i < G/2 run pass A, blocks i >= G/2 pass B
 };
+
+// bounded wait until *cnt >= target (thread-uniform call by one thread)
+__device__ __forceinline__ bool wait_count(const int* cnt, int target) {
+  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+    int c;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(c) : "l"(cnt) : "memory");
+    if (c >= target) return true;
+    __nanosleep(64);
+  }
+  return false;
+}
 
 __host__ __device__ inline size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
 
@@ -292,7 +319,8 @@ __global__ void __launch_bounds__(kThreads, 2) quant_k_kernel(
   extern __shared__ __align__(128) unsigned char smem[];
   uint4* stages = reinterpret_cast<uint4*>(smem);
   float* table = reinterpret_cast<float*>(smem + Sh::kTableOff);  // [kRedRows][D]
-  float2* qs = reinterpret_cast<float2*>(smem + Sh::kQsOff);      // [D] (scale, rcp)
+  float* qr = reinterpret_cast<float*>(smem + Sh::kQsOff);
+  float* qn = qr + D;
   __shared__ int s_ok;
   const int tid = threadIdx.x;
   const int lane = tid & 31, warp = tid >> 5;
@@ -300,19 +328,46 @@ __global__ void __launch_bounds__(kThreads, 2) quant_k_kernel(
   const int rs = tid / Sh::kVecPerRow;      // row slot
   const int red_row = Sh::kVecPerRow <= 32 ? warp : rs;
   const bool red_writer = Sh::kVecPerRow <= 32 ? lane < Sh::kVecPerRow : true;
-  const int G = gridDim.x, T = pl.teams;
-  const int team = blockIdx.x % T, rank = blockIdx.x / T;
-  const int members = (G - team + T - 1) / T;   // blocks b < G with b % T == team
+  const int T = pl.teams;
+  const int half = pl.paired ? gridDim.x / 2 : gridDim.x;   // blocks per role
+  int idx = blockIdx.x, role = 0;
+  if (pl.paired) {
+    // the first block to start on an SM runs pass A, the second pass B, so that
+    // each SM holds one HBM-bound and one compute-bound block; the index within
+    // the role comes from a counter (a full role hands the block to the other)
+    __shared__ int s_role[2];
+    if (tid == 0) {
+      unsigned smid;
+      asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+      int r = smid < kMaxSmIds ? (atomicAdd(ws.sm_slot + smid, 1) & 1) : 0;
+      int i = atomicAdd(ws.roles + r, 1);
+      if (i >= half) {
+        r ^= 1;
+        i = atomicAdd(ws.roles + r, 1);
+      }
+      s_role[0] = r;
+      s_role[1] = i;
+    }
+    __syncthreads();
+    role = s_role[0];
+    idx = s_role[1];
+  }
+  const bool run_a = !pl.paired || role == 0;
+  const bool run_b = !pl.paired || role == 1;
+  const int team = idx % T, rank = idx / T;
+  const int members = (half - team + T - 1) / T;   // role blocks of the team
   const int lo = static_cast<int>(static_cast<int64_t>(pl.n_chunks) * rank / members);
   const int hi = static_cast<int>(static_cast<int64_t>(pl.n_chunks) * (rank + 1) / members);
+  const int n_k = team < pl.n_slabs ? (pl.n_slabs - team + T - 1) / T : 0;
   const uint64_t pol_keep = l2_policy_keep(), pol_drop = l2_policy_drop();
 
-  // prefetch cursor over (slab k of the team, pass, chunk r)
-  int pf_k = 0, pf_pass = 0, pf_r = lo;
+  // prefetch cursor over (slab k of the team, pass, chunk r): the passes this
+  // block runs, A before B for each slab
+  int pf_k = 0, pf_pass = run_a ? 0 : 1, pf_r = lo;
   const bool empty = lo >= hi;
   auto issue = [&](int stage) {
-    const int slab = team + pf_k * T;
-    if (!empty && slab < pl.n_slabs) {
+    if (!empty && pf_k < n_k) {
+      const int slab = team + pf_k * T;
       const int b = slab / H, h = slab - (slab / H) * H;
       const char* base = x + (static_cast<int64_t>(b) * xsb + static_cast<int64_t>(h) * xsh) * EB + cg * 16;
       const int row0 = pf_r * Sh::kRowsPerChunk;
@@ -326,8 +381,10 @@ __global__ void __launch_bounds__(kThreads, 2) quant_k_kernel(
       }
       if (++pf_r >= hi) {
         pf_r = lo;
-        if (++pf_pass == 2) {
-          pf_pass = 0;
+        if (pf_pass == 0 && run_b) {
+          pf_pass = 1;
+        } else {
+          pf_pass = run_a ? 0 : 1;
           ++pf_k;
         }
       }
@@ -337,125 +394,149 @@ __global__ void __launch_bounds__(kThreads, 2) quant_k_kernel(
 
   for (int k = 0; k < NS - 1; ++k) issue(k);
   int it = 0;  // chunks consumed (ring position)
-  for (int k = 0;; ++k) {
+  for (int k = 0; k < n_k; ++k) {
     const int slab = team + k * T;
-    if (slab >= pl.n_slabs) break;
-    // ---- A: column maxima of this block's run
-    float cmax[VE];
+    const int64_t col0 = static_cast<int64_t>(slab) * D;
+    bool ok = true;
+    if (run_a) {
+      // paired: stay at most two slabs ahead of the B side
+      if (pl.paired && k >= 2) {
+        if (tid == 0) {
+          const bool seen = wait_count(ws.b_done + (slab - 2 * T), members);
+          if (!seen) report_error(ws.status, HQ_ERR_DEVICE_TIMEOUT);
+        }
+        __syncthreads();
+      }
+      // ---- A: column maxima of this block's run
+      float cmax[VE];
 #pragma unroll
-    for (int e = 0; e < VE; ++e) cmax[e] = 0.0f;
-    for (int r = lo; r < hi; ++r, ++it) {
-      issue((it + NS - 1) % NS);
-      cp_async_wait<NS - 1>();  // this thread's copies of chunk `it` have landed
-      const uint4* st = stages + (it % NS) * Sh::kStageVecs + tid;
-      if constexpr (DT == HQ_DTYPE_F32) {
+      for (int e = 0; e < VE; ++e) cmax[e] = 0.0f;
+      for (int r = lo; r < hi; ++r, ++it) {
+        issue((it + NS - 1) % NS);
+        cp_async_wait<NS - 1>();  // this thread's copies of chunk `it` have landed
+        const uint4* st = stages + (it % NS) * Sh::kStageVecs + tid;
+        if constexpr (DT == HQ_DTYPE_F32) {
 #pragma unroll
-        for (int p = 0; p < Sh::kPasses; ++p) {
+          for (int p = 0; p < Sh::kPasses; ++p) {
+            float f[VE];
+            Vec16<DT>::unpack(st[p * kThreads], f);
+#pragma unroll
+            for (int e = 0; e < VE; ++e) cmax[e] = fmaxf(cmax[e], fabsf(f[e]));
+          }
+        } else {
+          uint4 m = st[0];
+#pragma unroll
+          for (int p = 1; p < Sh::kPasses; ++p) {
+            const uint4 d = st[p * kThreads];
+            m.x = absmax_x2<DT>(m.x, d.x);
+            m.y = absmax_x2<DT>(m.y, d.y);
+            m.z = absmax_x2<DT>(m.z, d.z);
+            m.w = absmax_x2<DT>(m.w, d.w);
+          }
           float f[VE];
-          Vec16<DT>::unpack(st[p * kThreads], f);
+          Vec16<DT>::unpack(m, f);
 #pragma unroll
           for (int e = 0; e < VE; ++e) cmax[e] = fmaxf(cmax[e], fabsf(f[e]));
         }
+      }
+      // lanes of one warp that share a column group differ in bits >= log2(kVecPerRow)
+#pragma unroll
+      for (int off = Sh::kVecPerRow; off < 32; off <<= 1)
+#pragma unroll
+        for (int e = 0; e < VE; ++e) cmax[e] = fmaxf(cmax[e], __shfl_xor_sync(0xffffffffu, cmax[e], off));
+      if (red_writer) {
+#pragma unroll
+        for (int e = 0; e < VE; ++e) table[red_row * D + cg * VE + e] = cmax[e];
+      }
+      __syncthreads();  // block table complete; qs of the previous slab no longer read
+      float m = 0.0f;
+      if (tid < D) {
+        m = table[tid];
+#pragma unroll
+        for (int w = 1; w < Sh::kRedRows; ++w) m = fmaxf(m, table[w * D + tid]);
+      }
+      if (members == 1 && !pl.paired) {
+        // the whole slab is this block's run: the block maximum is final
+        if (tid < D) {
+          const Quantizer qz = quantizer_for<DT>(m);
+          qr[tid] = qz.rcp;
+          qn[tid] = -qz.scale;
+          if (sc32) sc32[col0 + tid] = qz.scale;
+          if (sc16) sc16[col0 + tid] = __float2half_rn(qz.scale);
+        }
+        __syncthreads();  // qs ready; table free for the next slab
       } else {
-        uint4 m = st[0];
-#pragma unroll
-        for (int p = 1; p < Sh::kPasses; ++p) {
-          const uint4 d = st[p * kThreads];
-          m.x = absmax_x2<DT>(m.x, d.x);
-          m.y = absmax_x2<DT>(m.y, d.y);
-          m.z = absmax_x2<DT>(m.z, d.z);
-          m.w = absmax_x2<DT>(m.w, d.w);
+        // publish; the returned old value is awaited, so the maximum is
+        // performed in L2 before this block is counted
+        if (tid < D && m > 0.0f) {
+          const unsigned old = atomicMax(ws.amax + col0 + tid, __float_as_uint(m));
+          if (old == 0xffffffffu) s_ok = 0;  // never: maxima are >= 0; forces the wait
         }
-        float f[VE];
-        Vec16<DT>::unpack(m, f);
-#pragma unroll
-        for (int e = 0; e < VE; ++e) cmax[e] = fmaxf(cmax[e], fabsf(f[e]));
+        __syncthreads();  // table free for the next slab
+        if (tid == 0) {
+          __threadfence();
+          atomicAdd(ws.a_done + slab, 1);
+        }
       }
     }
-    // lanes of one warp that share a column group differ in bits >= log2(kVecPerRow)
-#pragma unroll
-    for (int off = Sh::kVecPerRow; off < 32; off <<= 1)
-#pragma unroll
-      for (int e = 0; e < VE; ++e) cmax[e] = fmaxf(cmax[e], __shfl_xor_sync(0xffffffffu, cmax[e], off));
-    if (red_writer) {
-#pragma unroll
-      for (int e = 0; e < VE; ++e) table[red_row * D + cg * VE + e] = cmax[e];
-    }
-    __syncthreads();  // block table complete; qs of the previous slab no longer read
-    float m = 0.0f;
-    if (tid < D) {
-      m = table[tid];
-#pragma unroll
-      for (int w = 1; w < Sh::kRedRows; ++w) m = fmaxf(m, table[w * D + tid]);
-    }
-    const int64_t col0 = static_cast<int64_t>(slab) * D;
-    bool ok = true;
-    if (members > 1) {
-      // publish; the returned old value is awaited, so the maximum is performed
-      // in L2 before this block is counted
-      if (tid < D && m > 0.0f) {
-        const unsigned old = atomicMax(ws.amax + col0 + tid, __float_as_uint(m));
-        if (old == 0xffffffffu) s_ok = 0;  // never: maxima are >= 0; forces the wait
-      }
-      __syncthreads();
-      if (tid == 0) {
-        __threadfence();
-        atomicAdd(ws.done + slab, 1);
-        int seen = 0;
-        for (uint32_t i = 0; i < kSpinLimit; ++i) {
-          int c;
-          asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(c) : "l"(ws.done + slab) : "memory");
-          if (c >= members) {
-            seen = 1;
-            break;
+    if (run_b) {
+      if (pl.paired || members > 1) {
+        // every A block of the slab has published: quantizers from the maxima
+        if (tid == 0) {
+          const bool seen = wait_count(ws.a_done + slab, members);
+          if (!seen) report_error(ws.status, HQ_ERR_DEVICE_TIMEOUT);
+          s_ok = seen;
+        }
+        __syncthreads();
+        ok = s_ok != 0;  // gave up: status word set, this slab's codes are not written
+        if (ok && tid < D) {
+          const Quantizer qz = quantizer_for<DT>(__uint_as_float(__ldcg(ws.amax + col0 + tid)));
+          qr[tid] = qz.rcp;
+          qn[tid] = -qz.scale;
+          if (rank == 0) {  // one block per slab writes the scale outputs
+            if (sc32) sc32[col0 + tid] = qz.scale;
+            if (sc16) sc16[col0 + tid] = __float2half_rn(qz.scale);
           }
-          __nanosleep(64);
         }
-        if (!seen) report_error(ws.status, HQ_ERR_DEVICE_TIMEOUT);
-        s_ok = seen;
+        __syncthreads();  // qs ready
       }
-      __syncthreads();
-      ok = s_ok != 0;  // gave up: status word set, this slab's codes are not written
-      if (ok && tid < D) m = __uint_as_float(__ldcg(ws.amax + col0 + tid));
-    }
-    if (ok && tid < D) {
-      const Quantizer qz = quantizer_for<DT>(m);
-      qs[tid] = make_float2(qz.scale, qz.rcp);
-      if (rank == 0) {  // one block per slab writes the scale outputs
-        if (sc32) sc32[col0 + tid] = qz.scale;
-        if (sc16) sc16[col0 + tid] = __float2half_rn(qz.scale);
-      }
-    }
-    __syncthreads();  // qs ready; table free for the next slab
-    // ---- B: codes of the same run
-    Quantizer qz[VE];
-    F2 rcp2[VE / 2], ns2[VE / 2];
-    {
-      const float4* q4 = reinterpret_cast<const float4*>(qs + cg * VE);
+      // ---- B: codes of the run
+      Quantizer qz[VE];
+      F2 rcp2[VE / 2], ns2[VE / 2];
+      {
+        const float4* r4 = reinterpret_cast<const float4*>(qr + cg * VE);
+        const float4* n4 = reinterpret_cast<const float4*>(qn + cg * VE);
 #pragma unroll
-      for (int e = 0; e < VE / 2; ++e) {
-        const float4 t = q4[e];
-        qz[2 * e].scale = t.x;
-        qz[2 * e].rcp = t.y;
-        qz[2 * e + 1].scale = t.z;
-        qz[2 * e + 1].rcp = t.w;
-        rcp2[e] = f2_make(t.y, t.w);
-        ns2[e] = f2_make(-t.x, -t.z);
-      }
-    }
-    const int b = slab / H, h = slab - (slab / H) * H;
-    int8_t* qbase = q + static_cast<int64_t>(b) * qsb + static_cast<int64_t>(h) * qsh + cg * VE;
-    for (int r = lo; r < hi; ++r, ++it) {
-      issue((it + NS - 1) % NS);
-      cp_async_wait<NS - 1>();
-      const uint4* st = stages + (it % NS) * Sh::kStageVecs + tid;
-      if (ok) {
-        const int row0 = r * Sh::kRowsPerChunk;
-#pragma unroll
-        for (int p = 0; p < Sh::kPasses; ++p) {
-          const int s = row0 + p * Sh::kRowSlots + rs;
-          if (s < S) quant_vec_store<DT>(st[p * kThreads], ns2, rcp2, qz, qbase + static_cast<int64_t>(s) * qss);
+        for (int e = 0; e < VE / 4; ++e) {
+          const float4 r = r4[e], n = n4[e];
+          rcp2[2 * e] = f2_make(r.x, r.y);
+          rcp2[2 * e + 1] = f2_make(r.z, r.w);
+          ns2[2 * e] = f2_make(n.x, n.y);
+          ns2[2 * e + 1] = f2_make(n.z, n.w);
+          qz[4 * e + 0] = {-n.x, r.x};
+          qz[4 * e + 1] = {-n.y, r.y};
+          qz[4 * e + 2] = {-n.z, r.z};
+          qz[4 * e + 3] = {-n.w, r.w};
         }
+      }
+      const int b = slab / H, h = slab - (slab / H) * H;
+      int8_t* qbase = q + static_cast<int64_t>(b) * qsb + static_cast<int64_t>(h) * qsh + cg * VE;
+      for (int r = lo; r < hi; ++r, ++it) {
+        issue((it + NS - 1) % NS);
+        cp_async_wait<NS - 1>();
+        const uint4* st = stages + (it % NS) * Sh::kStageVecs + tid;
+        if (ok) {
+          const int row0 = r * Sh::kRowsPerChunk;
+#pragma unroll
+          for (int p = 0; p < Sh::kPasses; ++p) {
+            const int s = row0 + p * Sh::kRowSlots + rs;
+            if (s < S) quant_vec_store<DT>(st[p * kThreads], ns2, rcp2, qz, qbase + static_cast<int64_t>(s) * qss);
+          }
+        }
+      }
+      if (pl.paired) {
+        __syncthreads();  // qs is rewritten for the next slab; the run is consumed
+        if (tid == 0) atomicAdd(ws.b_done + slab, 1);
       }
     }
   }
@@ -594,25 +675,39 @@ static int launch_quant_k(const void* x, const int64_t* xs, int B, int H, int S,
   KPlan pl;
   pl.n_slabs = B * H;
   pl.n_chunks = (S + Sh::kRowsPerChunk - 1) / Sh::kRowsPerChunk;
-  // Blocks of a team wait for one another: the grid never exceeds what is
-  // resident at once.  Teams: as many slabs in flight as fit in kTeamBytes, no
-  // more teams than slabs, and no team larger than a slab has chunks.
+  // Blocks wait for one another: the grid never exceeds what is resident at
+  // once.  Paired when every role block still gets >= 2 chunks per slab pass on
+  // average; teams: as many slabs in flight as fit in kTeamBytes (paired: two
+  // per team), no more teams than slabs, no team larger than a slab has chunks.
   const int64_t resident = static_cast<int64_t>(per_sm) * sm_count(dev);
   const size_t slab_bytes = static_cast<size_t>(S) * D * Elem<DT>::kBytes;
-  int64_t teams = static_cast<int64_t>(kTeamBytes / (slab_bytes ? slab_bytes : 1));
-  teams = std::max<int64_t>(teams, (resident + pl.n_chunks - 1) / pl.n_chunks);
+  const int64_t total_chunks = static_cast<int64_t>(pl.n_slabs) * pl.n_chunks;
+  pl.paired = resident >= 4 && total_chunks >= 4 * resident && pl.n_chunks > 1;
+  const int64_t role_blocks = pl.paired ? resident / 2 : resident;
+  int64_t teams = static_cast<int64_t>(kTeamBytes / ((pl.paired ? 2 : 1) * (slab_bytes ? slab_bytes : 1)));
+  teams = std::max<int64_t>(teams, (role_blocks + pl.n_chunks - 1) / pl.n_chunks);
   teams = std::min<int64_t>(std::max<int64_t>(teams, 1), pl.n_slabs);
   pl.teams = static_cast<int>(teams);
-  int64_t grid = std::min<int64_t>(resident, teams * pl.n_chunks);
-  grid = std::max<int64_t>(grid, teams);
+  int64_t grid;
+  if (pl.paired) {
+    grid = 2 * role_blocks;
+  } else {
+    grid = std::min<int64_t>(resident, teams * pl.n_chunks);
+    grid = std::max<int64_t>(grid, teams);
+  }
   char* w = static_cast<char*>(wsp);
   const size_t nbh = static_cast<size_t>(B) * H;
   KWorkspace ws;
   ws.status = reinterpret_cast<int*>(w);
-  ws.done = reinterpret_cast<int*>(w + 256);
-  ws.amax = reinterpret_cast<unsigned*>(w + 256 + align256(sizeof(int) * nbh));
-  // status, per-slab counters and maxima start at zero
-  const size_t clear = 256 + align256(sizeof(int) * nbh) + sizeof(unsigned) * nbh * D;
+  ws.roles = reinterpret_cast<int*>(w + 8);
+  ws.sm_slot = reinterpret_cast<int*>(w + 256);
+  char* w2 = w + 256 + sizeof(int) * kMaxSmIds;
+  ws.a_done = reinterpret_cast<int*>(w2);
+  ws.b_done = reinterpret_cast<int*>(w2 + align256(sizeof(int) * nbh));
+  ws.amax = reinterpret_cast<unsigned*>(w2 + 2 * align256(sizeof(int) * nbh));
+  // status, role and SM counters, per-slab counters and maxima start at zero
+  const size_t clear = 256 + sizeof(int) * kMaxSmIds + 2 * align256(sizeof(int) * nbh) +
+                       sizeof(unsigned) * nbh * D;
   e = cudaMemsetAsync(wsp, 0, clear, st);
   if (e != cudaSuccess) return static_cast<int>(e);
   kern<<<static_cast<unsigned>(grid), kThreads, smem, st>>>(
@@ -669,7 +764,8 @@ using namespace hq;
 extern "C" size_t hq_quant_k_workspace_bytes(int B, int H, int D) {
   if (B < 0 || H < 0 || D < 0) return 0;
   const size_t nbh = static_cast<size_t>(B) * H;
-  return 256 + align256(sizeof(int) * nbh) + align256(sizeof(unsigned) * nbh * D);
+  return 256 + sizeof(int) * kMaxSmIds + 2 * align256(sizeof(int) * nbh) +
+         align256(sizeof(unsigned) * nbh * D);
 }
 
 extern "C" int hq_quant_k_perchannel(const void* x, int x_dtype, const int64_t x_strides[4], int B,
