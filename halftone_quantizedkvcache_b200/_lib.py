@@ -7,6 +7,7 @@ loaded, every op raises ``RuntimeError``.
 from __future__ import annotations
 
 import ctypes
+import functools
 import os
 import threading
 
@@ -85,8 +86,14 @@ def check(status: int, what: str) -> None:
         raise HalftoneError(what, status)
 
 
-def strides(seq, n) -> ctypes.Array:
+@functools.lru_cache(maxsize=8192)
+def _strides_cached(seq: tuple, n: int) -> ctypes.Array:
     arr = (_i64_4 if n == 4 else _i64_3)()
     for i, v in enumerate(seq):
         arr[i] = int(v)
     return arr
+
+
+def strides(seq, n) -> ctypes.Array:
+    """Element strides as a C ``int64_t[n]`` (shared per value: the library only reads them)."""
+    return _strides_cached(seq if type(seq) is tuple else tuple(seq), n)

@@ -32,7 +32,7 @@ import torch
 import torch.nn.functional as F
 from transformers.cache_utils import DynamicCache
 
-from .. import kernels
+from .. import _lib, kernels
 
 Q_DIMS = (3,)  # per-token q fake quantization, as the reference default (line 93)
 _ALIGN = 256   # token capacity granularity
@@ -45,7 +45,7 @@ def _round_up(n: int, m: int) -> int:
 class _LayerStore:
     """Capacity buffers of one layer: codes ``[B,H,cap,D]``, fp16 scales."""
 
-    __slots__ = ("k", "v", "k_sc", "v_sc", "length")
+    __slots__ = ("k", "v", "k_sc", "v_sc", "length", "st")
 
     def __init__(self, B, H, D, cap, device):
         self.k = torch.empty((B, H, cap, D), dtype=torch.int8, device=device)
@@ -53,6 +53,17 @@ class _LayerStore:
         self.k_sc = torch.empty((B, H, 1, D), dtype=torch.float16, device=device)
         self.v_sc = torch.empty((B, H, cap, 1), dtype=torch.float16, device=device)
         self.length = 0
+        self._strides()
+
+    def _strides(self) -> None:
+        """C stride arrays of the buffers, for the direct decode-step calls."""
+        k, v, ksc, vsc = self.k, self.v, self.k_sc, self.v_sc
+        self.st = (
+            _lib.strides(k.stride(), 4), _lib.strides(v.stride(), 4),                # append dst
+            _lib.strides(vsc.stride()[:3], 3),                                        # append v scale
+            _lib.strides((k.stride(0), k.stride(1), k.stride(2)), 3),                 # decode K/V
+            _lib.strides((ksc.stride(0), ksc.stride(1), ksc.stride(3)), 3),           # decode K scale
+            _lib.strides((vsc.stride(0), vsc.stride(1), vsc.stride(2)), 3))           # decode V scale
 
     @property
     def capacity(self) -> int:
@@ -69,6 +80,7 @@ class _LayerStore:
         new.v_sc[:, :, :L].copy_(self.v_sc[:, :, :L])
         new.k_sc.copy_(self.k_sc)
         self.k, self.v, self.k_sc, self.v_sc = new.k, new.v, new.k_sc, new.v_sc
+        self.st = new.st
 
     def codes(self):
         L = self.length
@@ -78,6 +90,54 @@ class _LayerStore:
 def _tag(t: torch.Tensor, store: _LayerStore) -> torch.Tensor:
     t._hq_store = store
     return t
+
+
+_DTYPES = {torch.float32: _lib.DTYPE_F32, torch.bfloat16: _lib.DTYPE_BF16,
+           torch.float16: _lib.DTYPE_F16}
+
+
+def _append_direct(st: _LayerStore, k_new: torch.Tensor, v_new: torch.Tensor, L: int,
+                   S_new: int) -> bool:
+    """The append of a decode step straight through the C ABI (``hq_append_kv``): the
+    destinations are rows L.. of the layer's own buffers, addressed by pointer
+    offset.  Returns False (caller takes the general path) for unusual inputs."""
+    dt = _DTYPES.get(k_new.dtype)
+    if (dt is None or v_new.dtype != k_new.dtype or k_new.shape != v_new.shape or
+            not k_new.is_cuda or k_new.stride(-1) != 1 or v_new.stride(-1) != 1):
+        return False
+    B, H, _, D = k_new.shape
+    k, v, vsc = st.k, st.v, st.v_sc
+    s_k, s_v, s_vsc = st.st[0], st.st[1], st.st[2]
+    rc = _lib.lib().hq_append_kv(
+        k_new.data_ptr(), v_new.data_ptr(), dt, _lib.strides(k_new.stride(), 4),
+        _lib.strides(v_new.stride(), 4), B, H, S_new, D,
+        k.data_ptr() + L * k.stride(2), s_k, v.data_ptr() + L * v.stride(2), s_v,
+        None, vsc.data_ptr() + 2 * L * vsc.stride(2), s_vsc, kernels._stream(k_new.device))
+    _lib.check(rc, "hq_append_kv")
+    return True
+
+
+def _decode_direct(st: _LayerStore, query: torch.Tensor, n_rep: int, scaling: float,
+                   q_quant: bool):
+    """The decode step straight through the C ABI (``hq_decode_int8``) on the layer's
+    buffers: q ``[B,Hq,1,D]`` in, ``[B,1,Hq,D]`` out.  None for unusual inputs."""
+    dt = _DTYPES.get(query.dtype)
+    B, Hq, _, D = query.shape
+    k, v, ksc, vsc = st.k, st.v, st.k_sc, st.v_sc
+    Hkv, S = k.shape[1], st.length
+    if dt is None or query.stride(3) != 1 or k.stride(2) != D or Hkv * n_rep != Hq:
+        return None
+    out = torch.empty((B, 1, Hq, D), dtype=query.dtype, device=query.device)
+    ws = kernels.decode_workspace(query.device, B, Hq, Hkv, S, D)
+    qs = query.stride()
+    rc = _lib.lib().hq_decode_int8(
+        query.data_ptr(), dt, _lib.strides((qs[0], qs[1], 1), 3), k.data_ptr(), v.data_ptr(),
+        st.st[3], ksc.data_ptr(), vsc.data_ptr(), _lib.DTYPE_F16, st.st[4], st.st[5],
+        B, Hq, Hkv, S, D, float(scaling), int(q_quant), out.data_ptr(),
+        _lib.strides((Hq * D, D, 1), 3), None, ws.data_ptr(), ws.numel(),
+        kernels._stream(query.device))
+    _lib.check(rc, "hq_decode_int8")
+    return out
 
 
 class QuantizedKVCache(DynamicCache):
@@ -134,20 +194,24 @@ class QuantizedKVCache(DynamicCache):
                 raise ValueError("QuantizedKVCache.update: batch/head shape changed for this layer")
             L = st.length
             st.reserve(L + S_new)
-            kdst, vdst = st.k[:, :, L:L + S_new], st.v[:, :, L:L + S_new]
-            vsc = st.v_sc[:, :, L:L + S_new]
-            if S_new <= 64:
-                kernels.append_kv(key_states, value_states, kdst, vdst, v_scale_dst=vsc)
+            if S_new <= 64 and _append_direct(st, key_states, value_states, L, S_new):
+                pass  # the decode-step path: one launch, no views
             else:
-                # codes with the new tokens' own per-channel scale; that scale is not kept
-                kernels.quant_k_perchannel(key_states, out=kdst, scale_dtype=None)
-                kernels.quant_v_pertoken(value_states, out=vdst, scale_out=vsc)
+                kdst, vdst = st.k[:, :, L:L + S_new], st.v[:, :, L:L + S_new]
+                vsc = st.v_sc[:, :, L:L + S_new]
+                if S_new <= 64:
+                    kernels.append_kv(key_states, value_states, kdst, vdst, v_scale_dst=vsc)
+                else:
+                    # codes with the new tokens' own per-channel scale; that scale is not kept
+                    kernels.quant_k_perchannel(key_states, out=kdst, scale_dtype=None)
+                    kernels.quant_v_pertoken(value_states, out=vdst, scale_out=vsc)
             st.length = L + S_new
-        k, v, k_sc, v_sc = st.codes()
+        L = st.length
+        k, v = st.k[:, :, :L], st.v[:, :, :L]
         if self._fused():
-            return _tag(k.view(k.shape), st), _tag(v.view(v.shape), st)
-        return (kernels.dequant(k, k_sc, key_states.dtype, per_channel=True),
-                kernels.dequant(v, v_sc, value_states.dtype, per_channel=False))
+            return _tag(k, st), _tag(v, st)
+        return (kernels.dequant(k, st.k_sc, key_states.dtype, per_channel=True),
+                kernels.dequant(v, st.v_sc[:, :, :L], value_states.dtype, per_channel=False))
 
     def get_seq_length(self, layer_idx=0, cache_position=None):
         st = self._store.get(layer_idx)
@@ -215,13 +279,15 @@ def quantized_attention_forward(module, query, key, value, attention_mask, scali
             raise ValueError("quantized_attention_forward: unexpected decode mask width")
         q_quant = Q_DIMS is not None and tuple(Q_DIMS) == (3,)
         q = query if (Q_DIMS is None or q_quant) else _fake_quant(query, Q_DIMS)
-        k, v, k_sc, v_sc = st.codes()
-        out = torch.empty((B, 1, Hq, D), dtype=query.dtype, device=query.device)
         if attention_mask is not None and attention_mask.shape[-1] == st.length and st.length > 1:
             if bool((attention_mask != 0).any()):
                 raise NotImplementedError("padded decode masks are not supported by the int8 kernel")
-        kernels.int8_decode_attn(q[:, :, 0, :], k, k_sc, v, v_sc, module.num_key_value_groups,
-                                 sm_scale=scaling, q_quant=q_quant, out=out[:, 0])
+        out = _decode_direct(st, q, module.num_key_value_groups, scaling, q_quant)
+        if out is None:
+            k, v, k_sc, v_sc = st.codes()
+            out = torch.empty((B, 1, Hq, D), dtype=query.dtype, device=query.device)
+            kernels.int8_decode_attn(q[:, :, 0, :], k, k_sc, v, v_sc, module.num_key_value_groups,
+                                     sm_scale=scaling, q_quant=q_quant, out=out[:, 0])
         return out, None
     if st is not None:
         k, v, k_sc, v_sc = st.codes()
@@ -254,9 +320,16 @@ def uninstall(module=None) -> None:
         module.eager_attention_forward = orig
 
 
+_qwen3 = None
+
+
 def is_installed(module=None) -> bool:
+    global _qwen3
     if module is None:
-        import transformers.models.qwen3.modeling_qwen3 as module
+        if _qwen3 is None:
+            import transformers.models.qwen3.modeling_qwen3 as mod
+            _qwen3 = mod
+        module = _qwen3
     return module.eager_attention_forward is quantized_attention_forward
 
 

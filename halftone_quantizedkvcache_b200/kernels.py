@@ -39,7 +39,13 @@ def _cuda(t: torch.Tensor, what: str) -> None:
         raise ValueError(f"{what}: expected a CUDA tensor (there is no CPU path)")
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def _stream(dev: torch.device) -> int:
+    """Handle of the current CUDA stream of ``dev``."""
+    if _raw_stream is not None:
+        return _raw_stream(dev.index if dev.index is not None else torch.cuda.current_device())
     return torch.cuda.current_stream(dev).cuda_stream
 
 
@@ -241,11 +247,24 @@ def _as_bhsd(t: torch.Tensor):
     return t.unsqueeze(0) if t.dim() == 3 else t
 
 
-def _decode_ws(dev, B, Hq, Hkv, S, D):
-    nb = _lib.lib().hq_decode_workspace_bytes(B, Hq, Hkv, S, D)
-    if nb == 0:
-        raise ValueError(f"decode: unsupported shape B={B} Hq={Hq} Hkv={Hkv} S={S} D={D}")
+_decode_ws_bytes: dict = {}
+
+
+def decode_workspace(dev, B, Hq, Hkv, S, D) -> torch.Tensor:
+    """The (zero-initialised, reused) decode workspace for this shape on ``dev``.
+    Its size depends on S only through the tile count, so it is cached per tile count."""
+    key = (B, Hq, Hkv, (S + 127) // 128, D)
+    nb = _decode_ws_bytes.get(key)
+    if nb is None:
+        # the size grows with S: the largest S of the 128-token bucket covers it
+        nb = _lib.lib().hq_decode_workspace_bytes(B, Hq, Hkv, max(key[3] * 128, 1), D)
+        if nb == 0:
+            raise ValueError(f"decode: unsupported shape B={B} Hq={Hq} Hkv={Hkv} S={S} D={D}")
+        _decode_ws_bytes[key] = nb
     return WORKSPACES.get(dev, "decode", nb)
+
+
+_decode_ws = decode_workspace
 
 
 def _kv_strides(k, v):
