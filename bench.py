@@ -171,9 +171,11 @@ def make_layer_caches(torch, kernels, n_layers, S, device, gen, kv="int8"):
     return caches
 
 
-def time_graph(torch, fn, steps, warmup, stream, clocks_index=None, label=None):
+def time_graph(torch, fn, steps, warmup, stream, clocks_index=None, label=None, barrier=None):
     """Capture fn() in a CUDA graph, replay warmup + steps; returns (ms/step, clocks).
-    ``label`` names an NVTX range around the timed replays (for ncu --nvtx-include)."""
+    ``label`` names an NVTX range around the timed replays (for ncu --nvtx-include);
+    ``barrier`` (multi-rank runs) is called after a synchronize on both sides of
+    the timed replays."""
     fn()  # first call outside capture: kernel attributes, workspaces
     torch.cuda.synchronize()
     g = torch.cuda.CUDAGraph()
@@ -182,6 +184,9 @@ def time_graph(torch, fn, steps, warmup, stream, clocks_index=None, label=None):
     for _ in range(warmup):
         g.replay()
     torch.cuda.synchronize()
+    if barrier:
+        barrier()
+        torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     clk = Clocks(clocks_index) if clocks_index is not None else None
     if clk:
@@ -194,6 +199,8 @@ def time_graph(torch, fn, steps, warmup, stream, clocks_index=None, label=None):
             g.replay()
         ev1.record(stream)
     torch.cuda.synchronize()
+    if barrier:
+        barrier()
     if label:
         torch.cuda.nvtx.range_pop()
     if clk:
@@ -273,6 +280,52 @@ def reference_arm(args):
     return 0
 
 
+def run_seq_sharded(torch, dist, sharding, kernels, caches, q, out, sm_scale, device, stream,
+                    world, args):
+    """One long sequence split across the ranks (S_HEAD tokens each): the
+    exchange fused into the decode kernel over peer memory, and the library
+    baseline (partials, NCCL all_gather, combine kernel), both per layer."""
+    nl = len(caches)
+    res = {"workload": f"one sequence of S={S_HEAD * world} split across {world} ranks "
+                       f"({S_HEAD} tokens each), B={B}, Hq={HQ}, Hkv={HKV}, {nl} layers"}
+    gbs = lambda ms: round(world * nl * decode_bytes(B, HQ, HKV, S_HEAD, D) / (ms * 1e-3) / 1e9, 1)  # noqa: E731
+
+    def timed(fn, label):
+        with torch.cuda.stream(stream):
+            ms, _ = time_graph(torch, fn, min(args.steps, 100), min(args.warmup, 5), stream,
+                               label=label, barrier=dist.barrier)
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    peer = sharding.PeerShardedDecode(B, HQ, HKV, device)
+
+    def fused_step():
+        for l, (k8, ks, v8, vs) in enumerate(caches):
+            peer(q[l], k8, ks, v8, vs, sm_scale=sm_scale, out=out[l])
+
+    ms = timed(fused_step, "seq_sharded_fused_step")
+    with torch.cuda.stream(stream):
+        st = kernels.read_status("decode")
+    peer.close()
+    res["fused"] = {"us_per_layer": round(ms * 1e3 / nl, 3), "gbs": gbs(ms),
+                    "device_status": st,
+                    "exchange": "inside the decode kernel: each rank's last block per (b, kv "
+                                "head) stores its (m, l, o) into every rank's buffer over "
+                                "NVLink, release flags, bounded acquire wait, merge"}
+    seq = sharding.SequenceShardedDecode(B, HQ, D, device)
+
+    def nccl_step():
+        for l, (k8, ks, v8, vs) in enumerate(caches):
+            seq(q[l], k8, ks, v8, vs, sm_scale=sm_scale, out=out[l])
+
+    ms = timed(nccl_step, "seq_sharded_nccl_step")
+    res["nccl"] = {"us_per_layer": round(ms * 1e3 / nl, 3), "gbs": gbs(ms),
+                   "exchange": "per layer: split kernel writes (m, l, o) partials, NCCL "
+                               "all_gather, combine kernel"}
+    return res
+
+
 # ---------------------------------------------------------------- our arm
 def main():
     args = parse()
@@ -317,7 +370,7 @@ def main():
     with torch.cuda.stream(stream):
         ms, clocks = time_graph(torch, step, args.steps, args.warmup, stream,
                                 clocks_index=torch.cuda.current_device() if rank == 0 else None,
-                                label="decode_step")
+                                label="decode_step", barrier=dist.barrier if world > 1 else None)
     if world > 1:
         t = torch.tensor([ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -329,26 +382,8 @@ def main():
 
     seq_sharded = None
     if world > 1 and not args.no_extras:
-        seq = sharding.SequenceShardedDecode(B, HQ, D, device)
-
-        def seq_step():
-            for l, (k8, ks, v8, vs) in enumerate(caches):
-                seq(q[l], k8, ks, v8, vs, sm_scale=sm_scale, out=out[l])
-
-        with torch.cuda.stream(stream):
-            ms_seq, _ = time_graph(torch, seq_step, min(args.steps, 100), min(args.warmup, 5),
-                                   stream, label="seq_sharded_step")
-        t = torch.tensor([ms_seq], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_seq = float(t.item())
-        seq_sharded = {
-            "workload": f"one sequence of S={S_HEAD * world} split across {world} ranks "
-                        f"({S_HEAD} tokens each), {nl} layers",
-            "us_per_layer": round(ms_seq * 1e3 / nl, 3),
-            "gbs": round(world * nl * decode_bytes(B, HQ, HKV, S_HEAD, D) / (ms_seq * 1e-3) / 1e9, 1),
-            "exchange": "per layer: split kernel writes (m, l, o) partials, NCCL all_gather, "
-                        "combine kernel"}
-        del seq
+        seq_sharded = run_seq_sharded(torch, dist, sharding, kernels, caches, q, out, sm_scale,
+                                      device, stream, world, args)
     per_layer = decode_bytes(B, HQ, HKV, S_HEAD, D)
     value = world * nl * per_layer / (ms * 1e-3) / 1e9
     us_layer = ms * 1e3 / nl
@@ -458,12 +493,17 @@ def run_e2e(torch, kernels, QuantizedKVCache, attn_fwd, caches, device, stream, 
         for _ in range(warmup):
             one_step()
         torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+            torch.cuda.synchronize()
         ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         ev0.record(stream)
         for _ in range(steps):
             one_step()
         ev1.record(stream)
         torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
     ms = ev0.elapsed_time(ev1) / steps
     if world > 1:
         t = torch.tensor([ms], device=device)
@@ -501,7 +541,8 @@ def run_batched(torch, kernels, device, stream, world, dist, peak, B_all=64, S=8
             kernels.int8_decode_attn(q[l], k8, ks, v8, vs, HQ // HKV, sm_scale=sm_scale, out=out[l])
 
     with torch.cuda.stream(stream):
-        ms, _ = time_graph(torch, step, 20, 3, stream, label="batched_step")
+        ms, _ = time_graph(torch, step, 20, 3, stream, label="batched_step",
+                           barrier=dist.barrier if world > 1 else None)
     if world > 1:
         t = torch.tensor([ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)

@@ -25,6 +25,7 @@
 #include <cudaTypedefs.h>
 
 #include <atomic>
+#include <cstring>
 #include <cmath>
 
 #include "hq_common.cuh"
@@ -36,6 +37,10 @@ int current_sm_count();
 namespace dec {
 
 constexpr int kD = 128;
+constexpr int kMaxPeers = 8;
+// Longest wait of one block for the partials of the other ranks (a rank that
+// never launches turns into HQ_ERR_DEVICE_TIMEOUT in the status word).
+constexpr uint64_t kPeerWaitNs = 2000000000ull;
 constexpr int kThreads = 128;
 constexpr int kWarps = kThreads / 32;
 constexpr int kTile = 64;
@@ -83,6 +88,9 @@ struct Params {
   int* ws_status;
   int n_split;
   int tiles_per_split;
+  // sequence-sharded exchange over peer memory (world == 0: this GPU's output only)
+  int world, rank;
+  char* peer[kMaxPeers];  // receive buffers of all ranks (this rank's own is local)
 };
 
 __device__ __forceinline__ uint4 lds128(const void* p) {
@@ -146,6 +154,114 @@ __device__ __forceinline__ void emit(const Params& p, int b, int hq, int d, floa
 
 // Workspace rows of the split partials: m, l, two pad words, o[kD] (o 16-byte aligned).
 constexpr int kPartRow = kD + 4;
+
+// Receive buffer of one rank for the sequence-sharded exchange (in that rank's
+// memory, zero-filled once):
+//   gen   [B*Hkv]                  u32 launches completed per (b, kv head) (local)
+//   flag  [2][world][B*Hkv]        u32 epoch of the partial that rank r wrote
+//   part  [2][world][B*Hq][kPartRow] float (m, l, -, -, o[kD]) written by rank r
+// The two halves alternate with the epoch parity, so a rank that is one launch
+// ahead never overwrites what a slower rank is still reading.
+__host__ __device__ inline size_t peer_flag_off(int B, int Hkv) {
+  return (sizeof(unsigned) * static_cast<size_t>(B) * Hkv + 255) & ~size_t(255);
+}
+__host__ __device__ inline size_t peer_part_off(int B, int Hkv, int world) {
+  return peer_flag_off(B, Hkv) +
+         ((sizeof(unsigned) * 2 * static_cast<size_t>(world) * B * Hkv + 255) & ~size_t(255));
+}
+__host__ __device__ inline size_t peer_bytes(int B, int Hq, int Hkv, int world) {
+  return peer_part_off(B, Hkv, world) +
+         sizeof(float) * 2 * static_cast<size_t>(world) * B * Hq * kPartRow;
+}
+
+// Final (M, L, O) of the NREP q heads of (b, kvh), channel d per thread: the
+// output (or partial) of this GPU, or - when the sequence is sharded over peer
+// memory - this rank's partial stored into every rank's receive buffer, a
+// release flag per rank, a bounded wait for every rank's flag, and the merge of
+// the world partials into the output.  Called by all threads of one block.
+template <int NREP, int QDT>
+__device__ __forceinline__ void finish_heads(const Params& p, int b, int kvh, int d,
+                                             const float (&M)[NREP], const float (&L)[NREP],
+                                             const float (&O)[NREP]) {
+  if (p.world == 0) {
+#pragma unroll
+    for (int r = 0; r < NREP; ++r) emit<QDT>(p, b, kvh * NREP + r, d, M[r], L[r], O[r]);
+    return;
+  }
+  __shared__ int s_ok;
+  const int B = gridDim.z, W = p.world;
+  const int unit = b * p.Hkv + kvh;
+  const size_t foff = peer_flag_off(B, p.Hkv), poff = peer_part_off(B, p.Hkv, W);
+  unsigned* gen = reinterpret_cast<unsigned*>(p.peer[p.rank]);
+  const unsigned epoch = gen[unit] + 1u;  // this unit's launch count + 1, the same on every rank
+  const int half = epoch & 1u;
+  // 1. this rank's partial into slot [half][rank] of every rank's buffer
+  for (int w = 0; w < W; ++w) {
+    float* row = reinterpret_cast<float*>(p.peer[w] + poff) +
+                 ((static_cast<size_t>(half) * W + p.rank) * B * p.Hq + b * p.Hq + kvh * NREP) * kPartRow;
+#pragma unroll
+    for (int r = 0; r < NREP; ++r) {
+      if (d == 0) {
+        row[r * kPartRow] = M[r];
+        row[r * kPartRow + 1] = L[r];
+      }
+      row[r * kPartRow + 4 + d] = O[r];
+    }
+  }
+  __threadfence_system();  // this thread's peer stores are visible before any flag
+  __syncthreads();
+  if (d < 32) {
+    // lane w: release flag [half][rank][unit] in rank w's buffer, then wait for
+    // flag [half][w][unit] in this rank's buffer (bounded by kPeerWaitNs)
+    int ok = 1;
+    if (d < W) {
+      unsigned* f = reinterpret_cast<unsigned*>(p.peer[d] + foff) +
+                    (static_cast<size_t>(half) * W + p.rank) * B * p.Hkv + unit;
+      asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(epoch) : "memory");
+      const unsigned* mine = reinterpret_cast<const unsigned*>(p.peer[p.rank] + foff) +
+                             (static_cast<size_t>(half) * W + d) * B * p.Hkv + unit;
+      ok = 0;
+      const uint64_t t0 = global_ns();
+      for (uint32_t i = 0; i < kSpinLimit; ++i) {
+        unsigned v;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
+        if (v == epoch) {
+          ok = 1;
+          break;
+        }
+        if ((i & 63) == 63 && global_ns() - t0 > kPeerWaitNs) break;
+        __nanosleep(64);
+      }
+    }
+    ok = __all_sync(0xffffffffu, ok);
+    if (d == 0) {
+      if (!ok) report_error(p.ws_status, HQ_ERR_DEVICE_TIMEOUT);
+      s_ok = ok;
+    }
+  }
+  __syncthreads();
+  if (!s_ok) return;  // gave up: status word set, no output
+  // 3. merge the world partials (rows written by remote GPUs: read through L2)
+  const float* base = reinterpret_cast<const float*>(p.peer[p.rank] + poff) +
+                      static_cast<size_t>(half) * W * B * p.Hq * kPartRow;
+#pragma unroll
+  for (int r = 0; r < NREP; ++r) {
+    const int hq = kvh * NREP + r;
+    float Mt = -INFINITY;
+    for (int w = 0; w < W; ++w)
+      Mt = fmaxf(Mt, __ldcg(base + (static_cast<size_t>(w) * B * p.Hq + b * p.Hq + hq) * kPartRow));
+    float Lt = 0.0f, Ot = 0.0f;
+    for (int w = 0; w < W; ++w) {
+      const float* row = base + (static_cast<size_t>(w) * B * p.Hq + b * p.Hq + hq) * kPartRow;
+      const float m = __ldcg(row);
+      const float f = m == -INFINITY ? 0.0f : exp2f(m - Mt);
+      Lt += f * __ldcg(row + 1);
+      Ot += f * __ldcg(row + 4 + d);
+    }
+    emit<QDT>(p, b, hq, d, Mt, Lt, Ot);
+  }
+  if (d == 0) gen[unit] = epoch;
+}
 
 // Publishes one split's (m, l, o) for q head hq; thread d writes o[d].
 __device__ __forceinline__ void publish_split(const Params& p, int b, int hq, int split, int d,
@@ -255,9 +371,8 @@ __device__ __forceinline__ void merge_splits(const Params& p, int b, int kvh, fl
     }
     __syncthreads();  // scratch, s_red and s_l are reused by the next chunk
   }
-#pragma unroll
-  for (int r = 0; r < NREP; ++r) emit<QDT>(p, b, kvh * NREP + r, tid, M[r], L[r], O[r]);
   if (tid == 0) p.ws_count[b * p.Hkv + kvh] = 0;  // ready for the next launch
+  finish_heads<NREP, QDT>(p, b, kvh, tid, M, L, O);
 }
 
 template <int NREP, int KVDT, int SDT, int QDT>
@@ -527,8 +642,7 @@ __global__ void __launch_bounds__(kThreads, 3) decode_kernel(const Params p) {
   }
 
   if (p.n_split == 1) {
-#pragma unroll
-    for (int r = 0; r < NREP; ++r) emit<QDT>(p, b, kvh * NREP + r, d, Ms[r], Ls[r], Os[r]);
+    finish_heads<NREP, QDT>(p, b, kvh, d, Ms, Ls, Os);
     return;
   }
 
@@ -1044,8 +1158,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(
     Os[r] = O;
   }
   if (p.n_split == 1) {
-#pragma unroll
-    for (int r = 0; r < NREP; ++r) emit<QDT>(p, b, kvh * NREP + r, d, Ms[r], Ls[r], Os[r]);
+    finish_heads<NREP, QDT>(p, b, kvh, d, Ms, Ls, Os);
     return;
   }
 #pragma unroll
@@ -1104,10 +1217,13 @@ inline int max_splits(int units, int tiles, int sms) {
 }
 
 // Picks the tile count per split that minimises (waves x tiles per block).
-inline Plan make_plan(int units, int S, int slots, int sms, int tile = kTile) {
+// one_wave: only plans whose grid fits the resident slots (units <= slots).
+inline Plan make_plan(int units, int S, int slots, int sms, int tile = kTile,
+                      bool one_wave = false) {
   const int tiles = (S + tile - 1) / tile;
   if (tiles <= 0) return {1, 1};
-  const int cap = max_splits(units, tiles, sms);
+  int cap = max_splits(units, tiles, sms);
+  if (one_wave && cap > slots / units) cap = slots / units;
   Plan best{1, tiles};
   double best_cost = 1e30;
   for (int c = 1; c <= tiles; ++c) {
@@ -1219,7 +1335,11 @@ int launch_mma(Params p, int B, void* ws, size_t ws_bytes, cudaStream_t st) {
     if (dev >= 0 && dev < 64) occ[dev].store(per_sm, std::memory_order_relaxed);
   }
   const int sms = sm_count(dev);
-  const Plan pl = make_plan(B * p.Hkv, p.S, per_sm * sms, sms, mmak::kTileT);
+  // Sequence-sharded launches wait for the other ranks inside the grid: every
+  // block must be resident at once, so that a waiting block never holds the
+  // slot of a block another rank is waiting for.
+  if (p.world > 0 && B * p.Hkv > per_sm * sms) return HQ_ERR_UNSUPPORTED;
+  const Plan pl = make_plan(B * p.Hkv, p.S, per_sm * sms, sms, mmak::kTileT, p.world > 0);
   if (ws_bytes < workspace_bytes(B, p.Hq, p.Hkv, p.S, sms)) return HQ_ERR_WORKSPACE;
   CUtensorMap tmk, tmv;
   int rc = encode_kv_map(&tmk, p.k, p.kvsb, p.kvsh, p.S, p.Hkv, B);
@@ -1283,13 +1403,14 @@ static int check_common(const int64_t* q_strides, const int64_t* kv_strides,
   return HQ_OK;
 }
 
-extern "C" int hq_decode_int8(const void* q, int q_dtype, const int64_t q_strides[3],
+static int decode_int8_impl(const void* q, int q_dtype, const int64_t q_strides[3],
                               const int8_t* k, const int8_t* v, const int64_t kv_strides[3],
                               const void* k_scale, const void* v_scale, int scale_dtype,
                               const int64_t ksc_strides[3], const int64_t vsc_strides[3], int B,
                               int Hq, int Hkv, int S, int D, float sm_scale, int q_quant,
                               void* out, const int64_t out_strides[3], float* partial_out,
-                              void* workspace, size_t workspace_bytes, hq_stream_t stream) {
+                              void* workspace, size_t workspace_bytes, hq_stream_t stream,
+                              void* const* peer_bufs, int world, int rank) {
   int rc = check_common(q_strides, kv_strides, out_strides, partial_out, B, Hq, Hkv, S, D, workspace);
   if (rc != HQ_OK) return rc;
   // an empty cache (S == 0) may come with null K/V/v_scale pointers
@@ -1325,6 +1446,9 @@ extern "C" int hq_decode_int8(const void* q, int q_dtype, const int64_t q_stride
   p.osb = out_strides ? out_strides[0] : 0;
   p.osh = out_strides ? out_strides[1] : 0;
   p.partial_out = partial_out;
+  p.world = world;
+  p.rank = rank;
+  for (int w = 0; w < world; ++w) p.peer[w] = static_cast<char*>(peer_bufs[w]);
   const int nrep = Hq / Hkv;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
 #define HQ_Q(SDT)                                                                                \
@@ -1341,6 +1465,76 @@ extern "C" int hq_decode_int8(const void* q, int q_dtype, const int64_t q_stride
   }
 #undef HQ_Q
   return HQ_ERR_UNSUPPORTED;
+}
+
+extern "C" int hq_decode_int8(const void* q, int q_dtype, const int64_t q_strides[3],
+                              const int8_t* k, const int8_t* v, const int64_t kv_strides[3],
+                              const void* k_scale, const void* v_scale, int scale_dtype,
+                              const int64_t ksc_strides[3], const int64_t vsc_strides[3], int B,
+                              int Hq, int Hkv, int S, int D, float sm_scale, int q_quant,
+                              void* out, const int64_t out_strides[3], float* partial_out,
+                              void* workspace, size_t workspace_bytes, hq_stream_t stream) {
+  return decode_int8_impl(q, q_dtype, q_strides, k, v, kv_strides, k_scale, v_scale, scale_dtype,
+                          ksc_strides, vsc_strides, B, Hq, Hkv, S, D, sm_scale, q_quant, out,
+                          out_strides, partial_out, workspace, workspace_bytes, stream, nullptr, 0, 0);
+}
+
+// ---------------------------------------------------------------- sequence sharding over peer memory
+extern "C" size_t hq_peer_buffer_bytes(int world, int B, int Hq, int Hkv) {
+  if (world < 1 || world > kMaxPeers || B < 1 || Hq < 1 || Hkv < 1) return 0;
+  return peer_bytes(B, Hq, Hkv, world);
+}
+
+extern "C" int hq_peer_alloc(size_t bytes, void** ptr, void* ipc_handle) {
+  if (!ptr || !ipc_handle || bytes == 0) return HQ_ERR_INVALID_ARGUMENT;
+  void* d = nullptr;
+  cudaError_t e = cudaMalloc(&d, bytes);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  e = cudaMemset(d, 0, bytes);  // generation counters, flags and slots start at zero
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(ipc_handle), d);
+  if (e != cudaSuccess) {
+    cudaFree(d);
+    return static_cast<int>(e);
+  }
+  *ptr = d;
+  return HQ_OK;
+}
+
+extern "C" int hq_peer_open(const void* ipc_handle, void** ptr) {
+  if (!ptr || !ipc_handle) return HQ_ERR_INVALID_ARGUMENT;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, ipc_handle, sizeof(h));
+  const cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  return e == cudaSuccess ? HQ_OK : static_cast<int>(e);
+}
+
+extern "C" int hq_peer_close(void* ptr) {
+  const cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  return e == cudaSuccess ? HQ_OK : static_cast<int>(e);
+}
+
+extern "C" int hq_peer_free(void* ptr) {
+  const cudaError_t e = cudaFree(ptr);
+  return e == cudaSuccess ? HQ_OK : static_cast<int>(e);
+}
+
+extern "C" int hq_decode_int8_peer(const void* q, int q_dtype, const int64_t q_strides[3],
+                                   const int8_t* k, const int8_t* v, const int64_t kv_strides[3],
+                                   const void* k_scale, const void* v_scale, int scale_dtype,
+                                   const int64_t ksc_strides[3], const int64_t vsc_strides[3],
+                                   int B, int Hq, int Hkv, int S, int D, float sm_scale,
+                                   int q_quant, void* out, const int64_t out_strides[3],
+                                   void* workspace, size_t workspace_bytes,
+                                   void* const* peer_bufs, int world, int rank,
+                                   hq_stream_t stream) {
+  if (!peer_bufs || world < 1 || world > kMaxPeers || rank < 0 || rank >= world || !out)
+    return HQ_ERR_INVALID_ARGUMENT;
+  for (int w = 0; w < world; ++w)
+    if (!peer_bufs[w] || !aligned(peer_bufs[w], 256)) return HQ_ERR_INVALID_ARGUMENT;
+  return decode_int8_impl(q, q_dtype, q_strides, k, v, kv_strides, k_scale, v_scale, scale_dtype,
+                          ksc_strides, vsc_strides, B, Hq, Hkv, S, D, sm_scale, q_quant, out,
+                          out_strides, nullptr, workspace, workspace_bytes, stream, peer_bufs,
+                          world, rank);
 }
 
 extern "C" int hq_decode_dense(const void* q, const int64_t q_strides[3], const void* k,

@@ -306,8 +306,6 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait: returns false after kSpinLimit polls (each try_wait itself
-// suspends for a hardware-defined interval), never hangs.
 // 16-byte global -> shared copy; src_bytes 0 fills the slot with zeros
 __device__ __forceinline__ void cp_async16(void* dst, const void* src, int src_bytes,
                                            uint64_t pol) {
@@ -329,7 +327,15 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
                : "memory");
 }
 
+// Bounded wait: returns false after kSpinLimit polls (each try_wait itself
+// suspends for a hardware-defined interval), never hangs.
 constexpr uint32_t kSpinLimit = 1u << 22;
+// Nanoseconds of the GPU's global timer.
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   for (uint32_t i = 0; i < kSpinLimit; ++i)
     if (mbar_try_wait(bar, parity)) return true;

@@ -276,7 +276,7 @@ def _kv_strides(k, v):
 
 
 def int8_decode_attn(q, k_i8, k_sc, v_i8, v_sc, n_rep=None, *, sm_scale=None, q_quant=False,
-                     out=None, partial_out=None):
+                     out=None, partial_out=None, peers=None):
     """Int8 decode attention (split-KV), the contract of ``int8_decode_attn``
     (src/kernels/int8_decode_attn_triton.py:101-113), batched.
 
@@ -286,9 +286,15 @@ def int8_decode_attn(q, k_i8, k_sc, v_i8, v_sc, n_rep=None, *, sm_scale=None, q_
     or writes the float32 (m, l, o) partials to ``partial_out [B,Hq,D+2]`` and
     returns it.  ``q_quant`` applies the per-token fake quantization of the
     reference's patched attention (tests/qwen_kvcache_full.py:103).
+    ``peers = (buffers, world, rank)`` (``sharding.PeerShardedDecode``): the
+    cache holds this rank's token range only, and the kernel exchanges the
+    partial softmax state with the other ranks over peer memory and returns
+    the output over the whole sequence (``hq_decode_int8_peer``).
     """
     for t, n in ((q, "q"), (k_i8, "k_i8"), (k_sc, "k_sc"), (v_i8, "v_i8"), (v_sc, "v_sc")):
         _cuda(t, f"int8_decode_attn {n}")
+    if peers is not None and partial_out is not None:
+        raise ValueError("int8_decode_attn: peers and partial_out are exclusive")
     qb, restore = _as_bhd(q)
     k4, v4, ks4, vs4 = _as_bhsd(k_i8), _as_bhsd(v_i8), _as_bhsd(k_sc), _as_bhsd(v_sc)
     B, Hq, D = qb.shape
@@ -306,14 +312,21 @@ def int8_decode_attn(q, k_i8, k_sc, v_i8, v_sc, n_rep=None, *, sm_scale=None, q_
         res = out if out is not None else torch.empty((B, Hq, D), dtype=qb.dtype, device=qb.device)
     ws = _decode_ws(qb.device, B, Hq, Hkv, S, D)
     ost = _lib.strides(res.stride(), 3) if res is not None else None
+    args = (qb.data_ptr(), _dtype_code(qb, "int8_decode_attn q"), _lib.strides(qb.stride(), 3),
+            k4.data_ptr(), v4.data_ptr(), _kv_strides(k4, v4), ks4.data_ptr(), vs4.data_ptr(),
+            _dtype_code(ks4, "scale"),
+            _lib.strides((ks4.stride(0), ks4.stride(1), ks4.stride(3)), 3),
+            _lib.strides((vs4.stride(0), vs4.stride(1), vs4.stride(2)), 3), B, Hq, Hkv, S, D,
+            float(sm_scale), int(bool(q_quant)), res.data_ptr() if res is not None else None, ost)
+    if peers is not None:
+        bufs, world, rank = peers
+        rc = _lib.lib().hq_decode_int8_peer(*args, ws.data_ptr(), ws.numel(), bufs, world, rank,
+                                            _stream(qb.device))
+        check(rc, "hq_decode_int8_peer")
+        return restore(res) if out is None else res
     rc = _lib.lib().hq_decode_int8(
-        qb.data_ptr(), _dtype_code(qb, "int8_decode_attn q"), _lib.strides(qb.stride(), 3),
-        k4.data_ptr(), v4.data_ptr(), _kv_strides(k4, v4), ks4.data_ptr(), vs4.data_ptr(),
-        _dtype_code(ks4, "scale"), _lib.strides((ks4.stride(0), ks4.stride(1), ks4.stride(3)), 3),
-        _lib.strides((vs4.stride(0), vs4.stride(1), vs4.stride(2)), 3), B, Hq, Hkv, S, D,
-        float(sm_scale), int(bool(q_quant)), res.data_ptr() if res is not None else None, ost,
-        partial_out.data_ptr() if partial_out is not None else None, ws.data_ptr(), ws.numel(),
-        _stream(qb.device))
+        *args, partial_out.data_ptr() if partial_out is not None else None, ws.data_ptr(),
+        ws.numel(), _stream(qb.device))
     check(rc, "hq_decode_int8")
     if partial_out is not None:
         return partial_out

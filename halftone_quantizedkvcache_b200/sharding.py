@@ -7,18 +7,27 @@ Two partitions, as the workloads define them:
   runs the single-GPU kernels on it; there is no collective on the data path.
 * **sequence sharding** (one very long sequence): each rank owns a contiguous
   token range of the int8 cache (a multiple of the 64-token kernel tile) plus
-  the replicated per-channel K scales, computes the float32 (m, l, o) softmax
-  partials of its range with the split-KV kernel, exchanges them with one
-  ``all_gather`` (``B * Hq * (D + 2) * 4`` bytes per rank, into local memory)
-  and merges them on the device with the log-sum-exp combine kernel.
+  the replicated per-channel K scales and computes the float32 (m, l, o)
+  softmax partials of its range.  ``PeerShardedDecode`` exchanges them inside
+  the decode kernel: the block that finishes a (sequence, kv head) stores its
+  partial straight into every rank's receive buffer (CUDA IPC mappings over
+  NVLink), raises a flag per rank, waits for the other ranks' flags and
+  merges - one launch per layer, no collective library call.
+  ``SequenceShardedDecode`` is the library baseline of the same exchange: the
+  kernel writes the partials, NCCL ``all_gather`` moves them
+  (``B * Hq * (D + 2) * 4`` bytes per rank) and the combine kernel merges.
 
 The reference is single-GPU (no collectives anywhere); the partial format and
 the combine follow the flash-decoding rule its roadmap names (README.md:137).
 """
 from __future__ import annotations
 
+import ctypes
+
 import torch
 import torch.distributed as dist
+
+from . import _lib
 
 TILE = 64
 
@@ -67,3 +76,74 @@ class SequenceShardedDecode:
                                  partial_out=self.local)
         dist.all_gather_into_tensor(self.flat, self.local, group=self.group)
         return kernels.decode_combine(self.gathered, out_dtype=q.dtype, out=out)
+
+
+class PeerShardedDecode:
+    """Decode attention over a cache whose tokens are split across ranks, with
+    the partial exchange fused into the decode kernel (``hq_decode_int8_peer``).
+
+    The constructor is collective over ``group``: every rank allocates its
+    receive buffer, the CUDA IPC handles go round with ``all_gather_object``
+    and each rank maps the others' buffers.  One instance serves one
+    ``(B, Hq, Hkv)``; every rank must call it the same number of times, in the
+    same order (eagerly or by CUDA graph replay).  ``close()`` (collective)
+    unmaps and frees the buffers.  The ranks must be on distinct GPUs: the
+    kernel of one rank waits for the kernels of the others.
+    """
+
+    def __init__(self, B: int, Hq: int, Hkv: int, device, group=None):
+        L = _lib.lib()
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.device = torch.device(device)
+        if self.world > 8:
+            raise ValueError("PeerShardedDecode: at most 8 ranks")
+        nbytes = L.hq_peer_buffer_bytes(self.world, B, Hq, Hkv)
+        if nbytes == 0:
+            raise ValueError(f"PeerShardedDecode: bad shape B={B} Hq={Hq} Hkv={Hkv}")
+        own = ctypes.c_void_p()
+        handle = (ctypes.c_char * 64)()
+        with torch.cuda.device(self.device):
+            _lib.check(L.hq_peer_alloc(nbytes, ctypes.byref(own), handle), "hq_peer_alloc")
+        self._own = own.value
+        handles = [None] * self.world
+        dist.all_gather_object(handles, (str(torch.cuda.get_device_properties(self.device).uuid),
+                                         bytes(handle)), group=group)
+        if len({h[0] for h in handles}) != self.world:
+            L.hq_peer_free(self._own)
+            raise RuntimeError("PeerShardedDecode: two ranks share a GPU")
+        self._opened = []
+        self.buffers = (ctypes.c_void_p * self.world)()
+        with torch.cuda.device(self.device):
+            for w, (_, h) in enumerate(handles):
+                if w == self.rank:
+                    self.buffers[w] = self._own
+                    continue
+                ptr = ctypes.c_void_p()
+                _lib.check(L.hq_peer_open(ctypes.create_string_buffer(h, 64), ctypes.byref(ptr)),
+                           "hq_peer_open")
+                self._opened.append(ptr.value)
+                self.buffers[w] = ptr.value
+        dist.barrier(group)
+
+    def __call__(self, q, k_i8, k_sc, v_i8, v_sc, *, sm_scale=None, q_quant=False, out=None):
+        from . import kernels
+        return kernels.int8_decode_attn(q, k_i8, k_sc, v_i8, v_sc, sm_scale=sm_scale,
+                                        q_quant=q_quant, out=out,
+                                        peers=(self.buffers, self.world, self.rank))
+
+    def close(self) -> None:
+        """Collective: unmap the other ranks' buffers, then free this rank's."""
+        if self._own is None:
+            return
+        L = _lib.lib()
+        torch.cuda.synchronize(self.device)
+        with torch.cuda.device(self.device):
+            for ptr in self._opened:
+                _lib.check(L.hq_peer_close(ptr), "hq_peer_close")
+        self._opened = []
+        dist.barrier(self.group)
+        with torch.cuda.device(self.device):
+            _lib.check(L.hq_peer_free(self._own), "hq_peer_free")
+        self._own = None

@@ -212,6 +212,47 @@ HQ_API int hq_decode_int8_noalloc(const void* q, int q_dtype, const int64_t q_st
                                   float* partial_out, hq_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * Sequence-sharded decode over peer memory (no counterpart in the reference,
+ * whose cache lives on one device).  Each of `world` GPUs (one process per
+ * GPU) holds a contiguous range of the cached tokens of every sequence; one
+ * launch of hq_decode_int8_peer per rank computes the rank's partial softmax
+ * state, stores it straight into every rank's receive buffer over NVLink,
+ * raises one flag per rank, waits (bounded) for the other ranks' flags and
+ * writes the merged attention output - the same result as hq_decode_int8 over
+ * the whole sequence - on every rank.  The exchange is inside the decode
+ * kernel: no collective library call, no extra launch.
+ *
+ * Receive buffers: each rank allocates hq_peer_buffer_bytes(world, B, Hq, Hkv)
+ * bytes with hq_peer_alloc (zero-filled, plus a 64-byte CUDA IPC handle),
+ * sends the handle to the other ranks, and opens theirs with hq_peer_open.
+ * peer_bufs[w] is rank w's buffer as mapped in this process (its own buffer
+ * at w == rank).  A buffer serves one (world, B, Hq, Hkv) for its lifetime;
+ * the kernel keeps a launch counter per (b, kv head) in it, so the ranks'
+ * launches pair up in issue order (also under CUDA graph replay).  Every rank
+ * must make the same sequence of calls on the same buffers.
+ *
+ * hq_decode_int8_peer: arguments as hq_decode_int8 (S = this rank's tokens,
+ * may be 0; no partial output), plus the buffers, world (1..8) and rank.
+ * Requires B * Hkv <= resident decode blocks of the GPU (HQ_ERR_UNSUPPORTED
+ * otherwise): all blocks run at once.  A rank whose peers do not arrive
+ * within 2 s stops waiting, writes no output and sets HQ_ERR_DEVICE_TIMEOUT in
+ * the workspace status word (hq_read_status).
+ */
+HQ_API size_t hq_peer_buffer_bytes(int world, int B, int Hq, int Hkv);
+HQ_API int hq_peer_alloc(size_t bytes, void** ptr, void* ipc_handle64);
+HQ_API int hq_peer_open(const void* ipc_handle64, void** ptr);
+HQ_API int hq_peer_close(void* ptr);
+HQ_API int hq_peer_free(void* ptr);
+HQ_API int hq_decode_int8_peer(const void* q, int q_dtype, const int64_t q_strides[3],
+                               const int8_t* k, const int8_t* v, const int64_t kv_strides[3],
+                               const void* k_scale, const void* v_scale, int scale_dtype,
+                               const int64_t ksc_strides[3], const int64_t vsc_strides[3], int B,
+                               int Hq, int Hkv, int S, int D, float sm_scale, int q_quant,
+                               void* out, const int64_t out_strides[3], void* workspace,
+                               size_t workspace_bytes, void* const* peer_bufs, int world,
+                               int rank, hq_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * Reads (and synchronises `stream` for) the device status word at the start
  * of a quantize-K or decode workspace: HQ_OK, or HQ_ERR_DEVICE_TIMEOUT if a
  * bounded device wait gave up during an earlier call on that workspace.

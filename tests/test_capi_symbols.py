@@ -91,3 +91,35 @@ def test_missing_library_fails_loudly(monkeypatch):
     monkeypatch.setattr(_lib, "LIB_PATH", "/nonexistent/libhalftone_b200.so")
     with pytest.raises(RuntimeError, match="missing"):
         _lib.lib()
+
+
+def test_peer_buffer_layout():
+    """gen [B*Hkv] u32 | flag [2][world][B*Hkv] u32 | part [2][world][B*Hq][D+4] f32,
+    each of the first two padded to 256 bytes."""
+    L = _lib.lib()
+    a256 = lambda n: (n + 255) // 256 * 256  # noqa: E731
+    for world, B, Hq, Hkv in ((1, 1, 16, 8), (2, 1, 16, 8), (8, 4, 32, 8), (3, 5, 8, 8)):
+        want = a256(4 * B * Hkv) + a256(4 * 2 * world * B * Hkv) + 4 * 2 * world * B * Hq * 132
+        assert L.hq_peer_buffer_bytes(world, B, Hq, Hkv) == want
+    assert L.hq_peer_buffer_bytes(0, 1, 16, 8) == 0
+    assert L.hq_peer_buffer_bytes(9, 1, 16, 8) == 0
+    assert L.hq_peer_buffer_bytes(2, 0, 16, 8) == 0
+
+
+def test_peer_argument_errors_return_before_any_launch():
+    L = _lib.lib()
+    st3 = _lib.strides((0, 0, 1), 3)
+    kv = _lib.strides((0, 0, 128), 3)
+    bufs = (ctypes.c_void_p * 8)(*([256] * 8))
+    base = [16, 1, st3, 16, 16, kv, 16, 16, 0, st3, st3, 1, 16, 8, 64, 128, 0.1, 0, 16, st3,
+            256, 1 << 20]
+    for world, rank in ((0, 0), (9, 0), (2, 2), (2, -1)):
+        assert L.hq_decode_int8_peer(*base, bufs, world, rank, None) == -1
+    assert L.hq_decode_int8_peer(*base, None, 2, 0, None) == -1
+    bad = (ctypes.c_void_p * 2)(256, 320)              # second buffer not 256-byte aligned
+    assert L.hq_decode_int8_peer(*base, bad, 2, 0, None) == -1
+    no_out = list(base)
+    no_out[18] = None
+    assert L.hq_decode_int8_peer(*no_out, bufs, 2, 0, None) == -1
+    assert L.hq_peer_alloc(0, ctypes.byref(ctypes.c_void_p()), (ctypes.c_char * 64)()) == -1
+    assert L.hq_peer_open(None, ctypes.byref(ctypes.c_void_p())) == -1
