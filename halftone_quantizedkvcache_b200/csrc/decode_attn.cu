@@ -157,110 +157,127 @@ constexpr int kPartRow = kD + 4;
 
 // Receive buffer of one rank for the sequence-sharded exchange (in that rank's
 // memory, zero-filled once):
-//   gen   [B*Hkv]                  u32 launches completed per (b, kv head) (local)
-//   flag  [2][world][B*Hkv]        u32 epoch of the partial that rank r wrote
-//   part  [2][world][B*Hq][kPartRow] float (m, l, -, -, o[kD]) written by rank r
-// The two halves alternate with the epoch parity, so a rank that is one launch
-// ahead never overwrites what a slower rank is still reading.
-__host__ __device__ inline size_t peer_flag_off(int B, int Hkv) {
+//   gen   [B*Hkv]                          u32 launches completed per (b, kv head)
+//   part  [2][world][B*Hq][kPartRow]       u64 words written by rank r: m, l, -, -, o[kD]
+// Every word carries its value in the low half and the epoch of the launch
+// that wrote it (launch count + 1, the same on every rank) in the high half,
+// stored and loaded as one 64-bit access, so a receiver that reads the epoch it
+// waits for has the value with it: no fence and no separate flag (the
+// value-plus-flag words of NCCL's low-latency protocol, at 64-bit width).  The
+// two halves alternate with the epoch parity: a rank can write epoch e + 2 into
+// a half only after every rank finished epoch e + 1, hence finished reading e.
+__host__ __device__ inline size_t peer_part_off(int B, int Hkv) {
   return (sizeof(unsigned) * static_cast<size_t>(B) * Hkv + 255) & ~size_t(255);
 }
-__host__ __device__ inline size_t peer_part_off(int B, int Hkv, int world) {
-  return peer_flag_off(B, Hkv) +
-         ((sizeof(unsigned) * 2 * static_cast<size_t>(world) * B * Hkv + 255) & ~size_t(255));
-}
 __host__ __device__ inline size_t peer_bytes(int B, int Hq, int Hkv, int world) {
-  return peer_part_off(B, Hkv, world) +
-         sizeof(float) * 2 * static_cast<size_t>(world) * B * Hq * kPartRow;
+  return peer_part_off(B, Hkv) +
+         sizeof(uint64_t) * 2 * static_cast<size_t>(world) * B * Hq * kPartRow;
+}
+
+__device__ __forceinline__ void st_word(uint64_t* a, float v, unsigned epoch) {
+  const uint64_t w = (static_cast<uint64_t>(epoch) << 32) | __float_as_uint(v);
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(a), "l"(w) : "memory");
+}
+
+// Bounded wait for the word at `a` to carry `epoch`; t0 is the time of this
+// thread's first miss (0 before it), so one thread waits kPeerWaitNs at most.
+__device__ __forceinline__ bool wait_word(const uint64_t* a, unsigned epoch, float& v,
+                                          uint64_t& t0) {
+  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+    uint64_t w;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(a) : "memory");
+    if (static_cast<unsigned>(w >> 32) == epoch) {
+      v = __uint_as_float(static_cast<unsigned>(w));
+      return true;
+    }
+    if (t0 == 0) {
+      t0 = global_ns();
+    } else if ((i & 15) == 15 && global_ns() - t0 > kPeerWaitNs) {
+      return false;
+    }
+    __nanosleep(32);
+  }
+  return false;
+}
+
+// This block's launch count for (b, kvh) in a sequence-sharded launch (read at
+// the start of the kernel, so its latency hides behind the token loop).
+__device__ __forceinline__ unsigned peer_gen(const Params& p, int b, int kvh) {
+  return p.world > 1 ? __ldcg(reinterpret_cast<const unsigned*>(p.peer[p.rank]) + b * p.Hkv + kvh)
+                     : 0u;
 }
 
 // Final (M, L, O) of the NREP q heads of (b, kvh), channel d per thread: the
-// output (or partial) of this GPU, or - when the sequence is sharded over peer
-// memory - this rank's partial stored into every rank's receive buffer, a
-// release flag per rank, a bounded wait for every rank's flag, and the merge of
-// the world partials into the output.  Called by all threads of one block.
+// output (or partial) of this GPU, or - when the sequence is sharded over
+// several ranks - this rank's (m, l, o) words stored into every other rank's
+// receive buffer, then the words of ranks 0 .. world-1 merged in rank order as
+// they arrive (the same arithmetic, so the same output, on every rank).
+// Called by all threads of one block; gen0 = peer_gen(p, b, kvh).
 template <int NREP, int QDT>
 __device__ __forceinline__ void finish_heads(const Params& p, int b, int kvh, int d,
                                              const float (&M)[NREP], const float (&L)[NREP],
-                                             const float (&O)[NREP]) {
-  if (p.world == 0) {
+                                             const float (&O)[NREP], unsigned gen0) {
+  if (p.world <= 1) {
 #pragma unroll
     for (int r = 0; r < NREP; ++r) emit<QDT>(p, b, kvh * NREP + r, d, M[r], L[r], O[r]);
     return;
   }
-  __shared__ int s_ok;
   const int B = gridDim.z, W = p.world;
-  const int unit = b * p.Hkv + kvh;
-  const size_t foff = peer_flag_off(B, p.Hkv), poff = peer_part_off(B, p.Hkv, W);
-  unsigned* gen = reinterpret_cast<unsigned*>(p.peer[p.rank]);
-  const unsigned epoch = gen[unit] + 1u;  // this unit's launch count + 1, the same on every rank
-  const int half = epoch & 1u;
-  // 1. this rank's partial into slot [half][rank] of every rank's buffer
+  const size_t poff = peer_part_off(B, p.Hkv);
+  const unsigned epoch = gen0 + 1u;
+  const size_t half = static_cast<size_t>(epoch & 1u) * W;
+  const size_t head0 = static_cast<size_t>(b) * p.Hq + kvh * NREP;
+  // 1. this rank's words into slot [half][rank] of the other ranks' buffers
   for (int w = 0; w < W; ++w) {
-    float* row = reinterpret_cast<float*>(p.peer[w] + poff) +
-                 ((static_cast<size_t>(half) * W + p.rank) * B * p.Hq + b * p.Hq + kvh * NREP) * kPartRow;
+    if (w == p.rank) continue;
+    uint64_t* row = reinterpret_cast<uint64_t*>(p.peer[w] + poff) +
+                    ((half + p.rank) * B * p.Hq + head0) * kPartRow;
 #pragma unroll
     for (int r = 0; r < NREP; ++r) {
       if (d == 0) {
-        row[r * kPartRow] = M[r];
-        row[r * kPartRow + 1] = L[r];
+        st_word(row + r * kPartRow, M[r], epoch);
+        st_word(row + r * kPartRow + 1, L[r], epoch);
       }
-      row[r * kPartRow + 4 + d] = O[r];
+      st_word(row + r * kPartRow + 4 + d, O[r], epoch);
     }
   }
-  __threadfence_system();  // this thread's peer stores are visible before any flag
-  __syncthreads();
-  if (d < 32) {
-    // lane w: release flag [half][rank][unit] in rank w's buffer, then wait for
-    // flag [half][w][unit] in this rank's buffer (bounded by kPeerWaitNs)
-    int ok = 1;
-    if (d < W) {
-      unsigned* f = reinterpret_cast<unsigned*>(p.peer[d] + foff) +
-                    (static_cast<size_t>(half) * W + p.rank) * B * p.Hkv + unit;
-      asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(epoch) : "memory");
-      const unsigned* mine = reinterpret_cast<const unsigned*>(p.peer[p.rank] + foff) +
-                             (static_cast<size_t>(half) * W + d) * B * p.Hkv + unit;
-      ok = 0;
-      const uint64_t t0 = global_ns();
-      for (uint32_t i = 0; i < kSpinLimit; ++i) {
-        unsigned v;
-        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
-        if (v == epoch) {
-          ok = 1;
-          break;
-        }
-        if ((i & 63) == 63 && global_ns() - t0 > kPeerWaitNs) break;
-        __nanosleep(64);
-      }
-    }
-    ok = __all_sync(0xffffffffu, ok);
-    if (d == 0) {
-      if (!ok) report_error(p.ws_status, HQ_ERR_DEVICE_TIMEOUT);
-      s_ok = ok;
-    }
-  }
-  __syncthreads();
-  if (!s_ok) return;  // gave up: status word set, no output
-  // 3. merge the world partials (rows written by remote GPUs: read through L2)
-  const float* base = reinterpret_cast<const float*>(p.peer[p.rank] + poff) +
-                      static_cast<size_t>(half) * W * B * p.Hq * kPartRow;
+  // 2. online merge over ranks 0 .. W-1 (bounded waits for the remote words)
+  const uint64_t* base = reinterpret_cast<const uint64_t*>(p.peer[p.rank] + poff) +
+                         half * B * p.Hq * kPartRow;
+  float Mt[NREP], Lt[NREP], Ot[NREP];
 #pragma unroll
   for (int r = 0; r < NREP; ++r) {
-    const int hq = kvh * NREP + r;
-    float Mt = -INFINITY;
-    for (int w = 0; w < W; ++w)
-      Mt = fmaxf(Mt, __ldcg(base + (static_cast<size_t>(w) * B * p.Hq + b * p.Hq + hq) * kPartRow));
-    float Lt = 0.0f, Ot = 0.0f;
-    for (int w = 0; w < W; ++w) {
-      const float* row = base + (static_cast<size_t>(w) * B * p.Hq + b * p.Hq + hq) * kPartRow;
-      const float m = __ldcg(row);
-      const float f = m == -INFINITY ? 0.0f : exp2f(m - Mt);
-      Lt += f * __ldcg(row + 1);
-      Ot += f * __ldcg(row + 4 + d);
-    }
-    emit<QDT>(p, b, hq, d, Mt, Lt, Ot);
+    Mt[r] = -INFINITY;
+    Lt[r] = 0.0f;
+    Ot[r] = 0.0f;
   }
-  if (d == 0) gen[unit] = epoch;
+  bool ok = true;
+  uint64_t t0 = 0;
+  for (int w = 0; w < W && ok; ++w) {
+    const uint64_t* row = base + (static_cast<size_t>(w) * B * p.Hq + head0) * kPartRow;
+#pragma unroll
+    for (int r = 0; r < NREP; ++r) {
+      float m = M[r], l = L[r], o = O[r];
+      if (w != p.rank) {
+        ok = ok && wait_word(row + r * kPartRow, epoch, m, t0) &&
+             wait_word(row + r * kPartRow + 1, epoch, l, t0) &&
+             wait_word(row + r * kPartRow + 4 + d, epoch, o, t0);
+      }
+      const float mn = fmaxf(Mt[r], m);
+      const float a = Mt[r] == -INFINITY ? 0.0f : exp2f(Mt[r] - mn);
+      const float f = m == -INFINITY ? 0.0f : exp2f(m - mn);
+      Lt[r] = Lt[r] * a + l * f;
+      Ot[r] = Ot[r] * a + o * f;
+      Mt[r] = mn;
+    }
+  }
+  if (__syncthreads_or(!ok)) {  // gave up: status word set, no output
+    if (d == 0) report_error(p.ws_status, HQ_ERR_DEVICE_TIMEOUT);
+    return;
+  }
+#pragma unroll
+  for (int r = 0; r < NREP; ++r) emit<QDT>(p, b, kvh * NREP + r, d, Mt[r], Lt[r], Ot[r]);
+  if (d == 0) reinterpret_cast<unsigned*>(p.peer[p.rank])[b * p.Hkv + kvh] = epoch;
 }
 
 // Publishes one split's (m, l, o) for q head hq; thread d writes o[d].
@@ -284,7 +301,7 @@ __device__ __forceinline__ void publish_split(const Params& p, int b, int hq, in
 // aligned, scratch_floats floats.
 template <int NREP, int QDT>
 __device__ __forceinline__ void merge_splits(const Params& p, int b, int kvh, float* scratch,
-                                             int scratch_floats) {
+                                             int scratch_floats, unsigned gen0) {
   constexpr int kRowVec = kPartRow / 4;  // 16-byte pieces per partial row
   __shared__ float s_red[kWarps][NREP];
   __shared__ float s_l[kWarps][NREP];
@@ -372,7 +389,7 @@ __device__ __forceinline__ void merge_splits(const Params& p, int b, int kvh, fl
     __syncthreads();  // scratch, s_red and s_l are reused by the next chunk
   }
   if (tid == 0) p.ws_count[b * p.Hkv + kvh] = 0;  // ready for the next launch
-  finish_heads<NREP, QDT>(p, b, kvh, tid, M, L, O);
+  finish_heads<NREP, QDT>(p, b, kvh, tid, M, L, O, gen0);
 }
 
 template <int NREP, int KVDT, int SDT, int QDT>
@@ -642,7 +659,7 @@ __global__ void __launch_bounds__(kThreads, 3) decode_kernel(const Params p) {
   }
 
   if (p.n_split == 1) {
-    finish_heads<NREP, QDT>(p, b, kvh, d, Ms, Ls, Os);
+    finish_heads<NREP, QDT>(p, b, kvh, d, Ms, Ls, Os, peer_gen(p, b, kvh));
     return;
   }
 
@@ -659,7 +676,8 @@ __global__ void __launch_bounds__(kThreads, 3) decode_kernel(const Params p) {
   if (!s_last) return;
   __threadfence();
 
-  merge_splits<NREP, QDT>(p, b, kvh, reinterpret_cast<float*>(ring), C::SMEM_STAGES / 4);
+  merge_splits<NREP, QDT>(p, b, kvh, reinterpret_cast<float*>(ring), C::SMEM_STAGES / 4,
+                          peer_gen(p, b, kvh));
 }
 
 // ------------------------------------------------------------------ int8 tensor-core kernel
@@ -781,6 +799,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, t4 = lane & 3;
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const unsigned gen0 = peer_gen(p, b, kvh);
   const int s_begin = split * p.tiles_per_split * kTileT;
   const int s_end = min(p.S, s_begin + p.tiles_per_split * kTileT);
   const int ntok = max(0, s_end - s_begin);
@@ -1158,7 +1177,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(
     Os[r] = O;
   }
   if (p.n_split == 1) {
-    finish_heads<NREP, QDT>(p, b, kvh, d, Ms, Ls, Os);
+    finish_heads<NREP, QDT>(p, b, kvh, d, Ms, Ls, Os, gen0);
     return;
   }
 #pragma unroll
@@ -1172,7 +1191,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-  merge_splits<NREP, QDT>(p, b, kvh, reinterpret_cast<float*>(ring), C::RING / 4);
+  merge_splits<NREP, QDT>(p, b, kvh, reinterpret_cast<float*>(ring), C::RING / 4, gen0);
 }
 
 }  // namespace mmak

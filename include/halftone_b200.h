@@ -216,27 +216,33 @@ HQ_API int hq_decode_int8_noalloc(const void* q, int q_dtype, const int64_t q_st
  * whose cache lives on one device).  Each of `world` GPUs (one process per
  * GPU) holds a contiguous range of the cached tokens of every sequence; one
  * launch of hq_decode_int8_peer per rank computes the rank's partial softmax
- * state, stores it straight into every rank's receive buffer over NVLink,
- * raises one flag per rank, waits (bounded) for the other ranks' flags and
- * writes the merged attention output - the same result as hq_decode_int8 over
- * the whole sequence - on every rank.  The exchange is inside the decode
- * kernel: no collective library call, no extra launch.
+ * state (m, l, o), stores it straight into the other ranks' receive buffers
+ * over NVLink as 64-bit words that carry the value and the launch's epoch
+ * together (no fence, no separate flag), waits (bounded) for the other ranks'
+ * words and writes the merged attention output - the result of
+ * hq_decode_int8 over the whole sequence - on every rank.  The ranks merge in
+ * rank order with the same arithmetic, so their outputs are identical.  The
+ * exchange is inside the decode kernel: no collective library call, no extra
+ * launch.
  *
  * Receive buffers: each rank allocates hq_peer_buffer_bytes(world, B, Hq, Hkv)
  * bytes with hq_peer_alloc (zero-filled, plus a 64-byte CUDA IPC handle),
  * sends the handle to the other ranks, and opens theirs with hq_peer_open.
  * peer_bufs[w] is rank w's buffer as mapped in this process (its own buffer
- * at w == rank).  A buffer serves one (world, B, Hq, Hkv) for its lifetime;
- * the kernel keeps a launch counter per (b, kv head) in it, so the ranks'
- * launches pair up in issue order (also under CUDA graph replay).  Every rank
- * must make the same sequence of calls on the same buffers.
+ * at w == rank).  Layout: gen [B*Hkv] u32 (launches completed per sequence and
+ * kv head, padded to 256 bytes), then part [2][world][B*Hq][D+4] u64 words
+ * (m, l, two unused, o[D]; value bits low, epoch high; the halves alternate
+ * with the epoch parity).  A buffer serves one (world, B, Hq, Hkv) for its
+ * lifetime; the ranks' launches pair up in issue order (also under CUDA graph
+ * replay): every rank must make the same sequence of calls on the same buffers.
  *
  * hq_decode_int8_peer: arguments as hq_decode_int8 (S = this rank's tokens,
  * may be 0; no partial output), plus the buffers, world (1..8) and rank.
  * Requires B * Hkv <= resident decode blocks of the GPU (HQ_ERR_UNSUPPORTED
  * otherwise): all blocks run at once.  A rank whose peers do not arrive
  * within 2 s stops waiting, writes no output and sets HQ_ERR_DEVICE_TIMEOUT in
- * the workspace status word (hq_read_status).
+ * the workspace status word (hq_read_status); the buffers of all ranks must
+ * then be freed and allocated again.
  */
 HQ_API size_t hq_peer_buffer_bytes(int world, int B, int Hq, int Hkv);
 HQ_API int hq_peer_alloc(size_t bytes, void** ptr, void* ipc_handle64);

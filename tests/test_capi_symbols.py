@@ -94,12 +94,11 @@ def test_missing_library_fails_loudly(monkeypatch):
 
 
 def test_peer_buffer_layout():
-    """gen [B*Hkv] u32 | flag [2][world][B*Hkv] u32 | part [2][world][B*Hq][D+4] f32,
-    each of the first two padded to 256 bytes."""
+    """gen [B*Hkv] u32 padded to 256 bytes | part [2][world][B*Hq][D+4] u64 words."""
     L = _lib.lib()
     a256 = lambda n: (n + 255) // 256 * 256  # noqa: E731
     for world, B, Hq, Hkv in ((1, 1, 16, 8), (2, 1, 16, 8), (8, 4, 32, 8), (3, 5, 8, 8)):
-        want = a256(4 * B * Hkv) + a256(4 * 2 * world * B * Hkv) + 4 * 2 * world * B * Hq * 132
+        want = a256(4 * B * Hkv) + 8 * 2 * world * B * Hq * 132
         assert L.hq_peer_buffer_bytes(world, B, Hq, Hkv) == want
     assert L.hq_peer_buffer_bytes(0, 1, 16, 8) == 0
     assert L.hq_peer_buffer_bytes(9, 1, 16, 8) == 0

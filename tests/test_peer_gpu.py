@@ -1,13 +1,16 @@
 """Sequence-sharded decode with the partial exchange inside the decode kernel
 (``hq_decode_int8_peer``, ``sharding.PeerShardedDecode``).
 
-One GPU: a world of one rank (the kernel stores its partial into its own
-receive buffer, raises and waits for its own flag, merges one partial) must
-give exactly the output of ``hq_decode_int8``, eagerly, on repeated calls (the
-two buffer halves alternate) and under CUDA graph replay; a world of two
-ranks whose second rank never runs must stop waiting, report
-HQ_ERR_DEVICE_TIMEOUT in the status word and leave the context usable (the
-flag nothing sets is the planted failure; no GPU fault is involved).
+One GPU: a world of one rank must give exactly the output of
+``hq_decode_int8``, eagerly and under CUDA graph replay.  The merge is checked
+by playing one rank of a world of 2 or 3 whose other ranks' words are already
+in its receive buffer (written beforehand from their partials, with the
+epoch of the launch): the launch stores its own words into the other buffers
+(checked bit for bit), merges without waiting and must match the oracle over
+the whole sequence, identically for every rank played.  A world of two whose
+second rank never runs must stop waiting, report HQ_ERR_DEVICE_TIMEOUT in the
+status word and leave the context usable (the word nothing writes is the
+planted failure; no GPU fault is involved).
 
 Two or more GPUs: ``tests/mp_peer_decode.py`` runs under torchrun, one rank
 per GPU, and checks every rank's output against the oracle over the whole
@@ -85,6 +88,65 @@ def test_world_of_one_equals_single_gpu(B, Hq, Hkv, S):
         del g
     finally:
         _lib.lib().hq_peer_free(buf)
+
+
+def _rows(part, epoch):
+    """float32 partial [B, Hq, D+2] (m, l, o) -> u64 words [B*Hq, D+4] (m, l, -, -, o),
+    value bits low, epoch high."""
+    B, Hq, D2 = part.shape
+    rows = torch.zeros((B * Hq, D2 + 2), dtype=torch.float32, device=part.device)
+    rows[:, 0:2] = part.reshape(B * Hq, D2)[:, 0:2]
+    rows[:, 4:] = part.reshape(B * Hq, D2)[:, 2:]
+    return (rows.view(torch.int32).to(torch.int64) & 0xFFFFFFFF) | (int(epoch) << 32)
+
+
+@pytest.mark.parametrize("world", [2, 3])
+@pytest.mark.parametrize("B,Hq,Hkv,S", [(1, 16, 8, 32768), (2, 32, 8, 5000), (1, 16, 4, 100)])
+def test_rank_merge_with_prewritten_words(world, B, Hq, Hkv, S):
+    from halftone_quantizedkvcache_b200 import sharding
+    from oracle import attention as oa
+    c = _case(40 + S, B, Hq, Hkv, S)
+    full = kernels.int8_decode_attn(c["q"], c["k_i8"], c["k_sc"], c["v_i8"], c["v_sc"])
+    ref = oa.decode_int8(c["q"].float().cpu().numpy(), c["k_i8"].cpu().numpy(),
+                         c["k_sc"].cpu().numpy(), c["v_i8"].cpu().numpy(),
+                         c["v_sc"].cpu().numpy(), acc="f64")
+    shards, parts = [], []
+    for r in range(world):
+        s0, s1 = sharding.sequence_range(S, world, r)
+        sh = (c["k_i8"][:, :, s0:s1].contiguous(), c["v_i8"][:, :, s0:s1].contiguous(),
+              c["v_sc"][:, :, s0:s1].contiguous())
+        part = torch.empty((B, Hq, 130), dtype=torch.float32, device="cuda")
+        kernels.int8_decode_attn(c["q"], sh[0], c["k_sc"], sh[1], sh[2], partial_out=part)
+        shards.append(sh)
+        parts.append(part)
+    L = _lib.lib()
+    nbytes = L.hq_peer_buffer_bytes(world, B, Hq, Hkv)
+    poff = (4 * B * Hkv + 255) // 256 * 256
+    outs = []
+    for me in range(world):
+        bufs = [torch.zeros(nbytes, dtype=torch.uint8, device="cuda") for _ in range(world)]
+        words = [b[poff:].view(torch.int64).view(2, world, B * Hq, 132) for b in bufs]
+        ptrs = (ctypes.c_void_p * world)(*[b.data_ptr() for b in bufs])
+        for epoch in (1, 2, 3):
+            for w in range(world):
+                if w != me:
+                    words[me][epoch & 1, w] = _rows(parts[w], epoch)
+            k8, v8, vs = shards[me]
+            out = kernels.int8_decode_attn(c["q"], k8, c["k_sc"], v8, vs,
+                                           peers=(ptrs, world, me))
+            torch.cuda.synchronize()
+            assert kernels.read_status("decode") == 0
+            gen = bufs[me][:4 * B * Hkv].view(torch.int32)
+            assert torch.all(gen == epoch)
+            for w in range(world):
+                if w != me:   # this rank's words, bit for bit, in every other buffer
+                    assert torch.equal(words[w][epoch & 1, me][:, [0, 1] + list(range(4, 132))],
+                                       _rows(parts[me], epoch)[:, [0, 1] + list(range(4, 132))])
+            np.testing.assert_allclose(out.float().cpu().numpy(), ref, atol=1e-3, rtol=2.0 ** -7)
+            torch.testing.assert_close(out.float(), full.float(), atol=1e-3, rtol=2.0 ** -7)
+        outs.append(out)
+    for o in outs[1:]:
+        assert torch.equal(o, outs[0])   # every rank merges in rank order: same output
 
 
 def test_absent_rank_times_out_and_context_survives():
