@@ -88,6 +88,11 @@ struct Params {
   int* ws_status;
   int n_split;
   int tiles_per_split;
+  // device-resident cache length (int8 path only): when set, S above is the
+  // capacity the tensor maps cover and the length is *seq_len, read at kernel
+  // start; the split count stays fixed and the tiles per split follow the length
+  const int* seq_len;
+  int S_plan;  // host: the length the split count is planned for
   // sequence-sharded exchange over peer memory (world == 0: this GPU's output only)
   int world, rank;
   char* peer[kMaxPeers];  // receive buffers of all ranks (this rank's own is local)
@@ -800,8 +805,13 @@ __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(
   const int g = lane >> 2, t4 = lane & 3;
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const unsigned gen0 = peer_gen(p, b, kvh);
-  const int s_begin = split * p.tiles_per_split * kTileT;
-  const int s_end = min(p.S, s_begin + p.tiles_per_split * kTileT);
+  int S = p.S, tps = p.tiles_per_split;
+  if (p.seq_len) {
+    S = min(max(__ldcg(p.seq_len), 0), p.S);
+    tps = max(1, ((S + kTileT - 1) / kTileT + p.n_split - 1) / p.n_split);
+  }
+  const int s_begin = split * tps * kTileT;
+  const int s_end = min(S, s_begin + tps * kTileT);
   const int ntok = max(0, s_end - s_begin);
   const int ntiles = (ntok + kTileT - 1) / kTileT;
 
@@ -1358,8 +1368,9 @@ int launch_mma(Params p, int B, void* ws, size_t ws_bytes, cudaStream_t st) {
   // block must be resident at once, so that a waiting block never holds the
   // slot of a block another rank is waiting for.
   if (p.world > 0 && B * p.Hkv > per_sm * sms) return HQ_ERR_UNSUPPORTED;
-  const Plan pl = make_plan(B * p.Hkv, p.S, per_sm * sms, sms, mmak::kTileT, p.world > 0);
-  if (ws_bytes < workspace_bytes(B, p.Hq, p.Hkv, p.S, sms)) return HQ_ERR_WORKSPACE;
+  const int S_plan = p.seq_len ? p.S_plan : p.S;
+  const Plan pl = make_plan(B * p.Hkv, S_plan, per_sm * sms, sms, mmak::kTileT, p.world > 0);
+  if (ws_bytes < workspace_bytes(B, p.Hq, p.Hkv, S_plan, sms)) return HQ_ERR_WORKSPACE;
   CUtensorMap tmk, tmv;
   int rc = encode_kv_map(&tmk, p.k, p.kvsb, p.kvsh, p.S, p.Hkv, B);
   if (rc == HQ_OK) rc = encode_kv_map(&tmv, p.v, p.kvsb, p.kvsh, p.S, p.Hkv, B);
@@ -1429,7 +1440,8 @@ static int decode_int8_impl(const void* q, int q_dtype, const int64_t q_strides[
                               int Hq, int Hkv, int S, int D, float sm_scale, int q_quant,
                               void* out, const int64_t out_strides[3], float* partial_out,
                               void* workspace, size_t workspace_bytes, hq_stream_t stream,
-                              void* const* peer_bufs, int world, int rank) {
+                              void* const* peer_bufs, int world, int rank,
+                              const int* seq_len = nullptr, int S_plan = 0) {
   int rc = check_common(q_strides, kv_strides, out_strides, partial_out, B, Hq, Hkv, S, D, workspace);
   if (rc != HQ_OK) return rc;
   // an empty cache (S == 0) may come with null K/V/v_scale pointers
@@ -1468,6 +1480,8 @@ static int decode_int8_impl(const void* q, int q_dtype, const int64_t q_strides[
   p.world = world;
   p.rank = rank;
   for (int w = 0; w < world; ++w) p.peer[w] = static_cast<char*>(peer_bufs[w]);
+  p.seq_len = seq_len;
+  p.S_plan = S_plan < 0 ? 0 : (S_plan > S ? S : S_plan);
   const int nrep = Hq / Hkv;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
 #define HQ_Q(SDT)                                                                                \
@@ -1496,6 +1510,23 @@ extern "C" int hq_decode_int8(const void* q, int q_dtype, const int64_t q_stride
   return decode_int8_impl(q, q_dtype, q_strides, k, v, kv_strides, k_scale, v_scale, scale_dtype,
                           ksc_strides, vsc_strides, B, Hq, Hkv, S, D, sm_scale, q_quant, out,
                           out_strides, partial_out, workspace, workspace_bytes, stream, nullptr, 0, 0);
+}
+
+// ---------------------------------------------------------------- device-resident length
+extern "C" int hq_decode_int8_len(const void* q, int q_dtype, const int64_t q_strides[3],
+                                  const int8_t* k, const int8_t* v, const int64_t kv_strides[3],
+                                  const void* k_scale, const void* v_scale, int scale_dtype,
+                                  const int64_t ksc_strides[3], const int64_t vsc_strides[3],
+                                  int B, int Hq, int Hkv, int S_max, const int* seq_len,
+                                  int S_plan, int D, float sm_scale, int q_quant, void* out,
+                                  const int64_t out_strides[3], void* workspace,
+                                  size_t workspace_bytes, hq_stream_t stream) {
+  if (!seq_len || !aligned(seq_len, 4)) return HQ_ERR_INVALID_ARGUMENT;
+  if (S_max > 0 && (!k || !v || !v_scale)) return HQ_ERR_INVALID_ARGUMENT;
+  return decode_int8_impl(q, q_dtype, q_strides, k, v, kv_strides, k_scale, v_scale, scale_dtype,
+                          ksc_strides, vsc_strides, B, Hq, Hkv, S_max, D, sm_scale, q_quant, out,
+                          out_strides, nullptr, workspace, workspace_bytes, stream, nullptr, 0, 0,
+                          seq_len, S_plan);
 }
 
 // ---------------------------------------------------------------- sequence sharding over peer memory

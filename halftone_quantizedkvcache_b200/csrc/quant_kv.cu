@@ -551,13 +551,29 @@ __global__ void __launch_bounds__(D) append_kernel(
     int64_t vsb, int64_t vsh, int64_t vss, int H, int S_new, int8_t* __restrict__ kq,
     int64_t kqb, int64_t kqh, int64_t kqs, int8_t* __restrict__ vq, int64_t vqb, int64_t vqh,
     int64_t vqs, float* __restrict__ vs32, __half* __restrict__ vs16, int64_t vssb, int64_t vssh,
-    int64_t vsss) {
+    int64_t vsss, int* __restrict__ lens, int cap) {
   using E = Elem<DT>;
   using T = typename E::T;
   constexpr int kW = D / 32;
   __shared__ float wmax[kW];
+  __shared__ int s_row0;
   const int d = threadIdx.x;
   const int64_t b = blockIdx.x / H, h = blockIdx.x % H;
+  // device-resident length: the new rows go to lens[0] .. lens[0] + S_new - 1
+  int64_t row0 = 0;
+  if (lens) {
+    if (d == 0) s_row0 = __ldcg(lens);
+    __syncthreads();
+    row0 = s_row0;
+    if (row0 < 0 || row0 + S_new > cap) {  // full cache: nothing is written
+      if (d == 0) report_error(lens + 2, HQ_ERR_INVALID_ARGUMENT);
+      return;
+    }
+    kq += row0 * kqs;
+    vq += row0 * vqs;
+    if (vs32) vs32 += row0 * vsss;
+    if (vs16) vs16 += row0 * vsss;
+  }
   const T* kp = reinterpret_cast<const T*>(k) + b * ksb + h * ksh + d;
   const T* vp = reinterpret_cast<const T*>(v) + b * vsb + h * vsh + d;
   // K: per-channel over the S_new new tokens
@@ -584,6 +600,17 @@ __global__ void __launch_bounds__(D) append_kernel(
       const int64_t so = b * vssb + h * vssh + s * vsss;
       if (vs32) vs32[so] = qv.scale;
       if (vs16) vs16[so] = __float2half_rn(qv.scale);
+    }
+  }
+  if (lens) {
+    // every block has read lens[0]; the last one to arrive advances it
+    __syncthreads();
+    if (d == 0) {
+      __threadfence();
+      if (atomicAdd(lens + 1, 1) == static_cast<int>(gridDim.x) - 1) {
+        lens[1] = 0;
+        lens[0] = static_cast<int>(row0) + S_new;
+      }
     }
   }
 }
@@ -720,13 +747,13 @@ template <int DT, int D>
 static int launch_append(const void* k, const void* v, const int64_t* ks, const int64_t* vs,
                          int B, int H, int S_new, int8_t* kq, const int64_t* kqs, int8_t* vq,
                          const int64_t* vqs, float* v32, uint16_t* v16, const int64_t* vss,
-                         cudaStream_t st) {
+                         int* lens, int cap, cudaStream_t st) {
   const int64_t z[3] = {0, 0, 0};
   if (!vss) vss = z;
   append_kernel<DT, D><<<B * H, D, 0, st>>>(
       static_cast<const char*>(k), static_cast<const char*>(v), ks[0], ks[1], ks[2], vs[0], vs[1],
       vs[2], H, S_new, kq, kqs[0], kqs[1], kqs[2], vq, vqs[0], vqs[1], vqs[2], v32,
-      reinterpret_cast<__half*>(v16), vss[0], vss[1], vss[2]);
+      reinterpret_cast<__half*>(v16), vss[0], vss[1], vss[2], lens, cap);
   return finish_launch();
 }
 
@@ -821,7 +848,30 @@ extern "C" int hq_append_kv(const void* k_new, const void* v_new, int x_dtype,
   HQ_DISPATCH_X(x_dtype, HQ_DISPATCH_D(D, return launch_append<kDT, kD>(
                                               k_new, v_new, k_strides, v_strides, B, H, S_new,
                                               k_dst, kq_strides, v_dst, vq_strides, v_scale_f32,
-                                              v_scale_f16, vs_strides, st);))
+                                              v_scale_f16, vs_strides, nullptr, 0, st);))
+}
+
+extern "C" int hq_append_kv_at(const void* k_new, const void* v_new, int x_dtype,
+                               const int64_t k_strides[4], const int64_t v_strides[4], int B,
+                               int H, int S_new, int D, int8_t* k_cache,
+                               const int64_t kq_strides[4], int8_t* v_cache,
+                               const int64_t vq_strides[4], float* v_scale_f32,
+                               uint16_t* v_scale_f16, const int64_t vs_strides[3], int capacity,
+                               int* lens, hq_stream_t stream) {
+  if (!k_new || !v_new || !k_cache || !v_cache || !k_strides || !v_strides || !kq_strides ||
+      !vq_strides || !lens || !aligned(lens, 4) || B < 0 || H < 0 || S_new < 1 || S_new > 64 ||
+      capacity < 0)
+    return HQ_ERR_INVALID_ARGUMENT;
+  if ((v_scale_f32 || v_scale_f16) && !vs_strides) return HQ_ERR_INVALID_ARGUMENT;
+  if (k_strides[3] != 1 || v_strides[3] != 1 || kq_strides[3] != 1 || vq_strides[3] != 1)
+    return HQ_ERR_INVALID_ARGUMENT;
+  if (!valid_dtype_x(x_dtype)) return HQ_ERR_UNSUPPORTED;
+  if (B == 0 || H == 0) return HQ_OK;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  HQ_DISPATCH_X(x_dtype, HQ_DISPATCH_D(D, return launch_append<kDT, kD>(
+                                              k_new, v_new, k_strides, v_strides, B, H, S_new,
+                                              k_cache, kq_strides, v_cache, vq_strides, v_scale_f32,
+                                              v_scale_f16, vs_strides, lens, capacity, st);))
 }
 
 extern "C" int hq_dequant(const int8_t* q, const int64_t q_strides[4], int B, int H, int S, int D,

@@ -45,14 +45,16 @@ def _round_up(n: int, m: int) -> int:
 class _LayerStore:
     """Capacity buffers of one layer: codes ``[B,H,cap,D]``, fp16 scales."""
 
-    __slots__ = ("k", "v", "k_sc", "v_sc", "length", "st")
+    __slots__ = ("k", "v", "k_sc", "v_sc", "length", "st", "lens")
 
-    def __init__(self, B, H, D, cap, device):
+    def __init__(self, B, H, D, cap, device, device_length=False):
         self.k = torch.empty((B, H, cap, D), dtype=torch.int8, device=device)
         self.v = torch.empty((B, H, cap, D), dtype=torch.int8, device=device)
         self.k_sc = torch.empty((B, H, 1, D), dtype=torch.float16, device=device)
         self.v_sc = torch.empty((B, H, cap, 1), dtype=torch.float16, device=device)
         self.length = 0
+        # {length, ticket, status, -} on the device (graph-replayable decode steps)
+        self.lens = torch.zeros(4, dtype=torch.int32, device=device) if device_length else None
         self._strides()
 
     def _strides(self) -> None:
@@ -72,6 +74,11 @@ class _LayerStore:
     def reserve(self, n: int) -> None:
         if n <= self.capacity:
             return
+        if self.lens is not None:
+            # captured graphs hold the buffer addresses: no reallocation in this mode
+            raise RuntimeError(
+                f"QuantizedKVCache: capacity {self.capacity} exhausted ({n} tokens) with "
+                "device_lengths=True; construct the cache with a larger capacity")
         B, H, cap, D = self.k.shape
         new = _LayerStore(B, H, D, _round_up(max(2 * cap, n), _ALIGN), self.k.device)
         L = self.length
@@ -117,6 +124,24 @@ def _append_direct(st: _LayerStore, k_new: torch.Tensor, v_new: torch.Tensor, L:
     return True
 
 
+def _append_at(st: _LayerStore, k_new: torch.Tensor, v_new: torch.Tensor, S_new: int) -> None:
+    """Device-length append (``hq_append_kv_at``): rows at ``lens[0]``, which the
+    launch advances; the call is the same for every token, so it replays in a graph."""
+    dt = _DTYPES.get(k_new.dtype)
+    if (dt is None or v_new.dtype != k_new.dtype or k_new.shape != v_new.shape or
+            not k_new.is_cuda or k_new.stride(-1) != 1 or v_new.stride(-1) != 1):
+        kernels.append_kv_at(k_new, v_new, st.k, st.v, st.v_sc, st.lens)
+        return
+    B, H, _, D = k_new.shape
+    k, v, vsc = st.k, st.v, st.v_sc
+    rc = _lib.lib().hq_append_kv_at(
+        k_new.data_ptr(), v_new.data_ptr(), dt, _lib.strides(k_new.stride(), 4),
+        _lib.strides(v_new.stride(), 4), B, H, S_new, D, k.data_ptr(), st.st[0], v.data_ptr(),
+        st.st[1], None, vsc.data_ptr(), st.st[2], k.shape[2], st.lens.data_ptr(),
+        kernels._stream(k_new.device))
+    _lib.check(rc, "hq_append_kv_at")
+
+
 def _decode_direct(st: _LayerStore, query: torch.Tensor, n_rep: int, scaling: float,
                    q_quant: bool):
     """The decode step straight through the C ABI (``hq_decode_int8``) on the layer's
@@ -130,6 +155,16 @@ def _decode_direct(st: _LayerStore, query: torch.Tensor, n_rep: int, scaling: fl
     out = torch.empty((B, 1, Hq, D), dtype=query.dtype, device=query.device)
     ws = kernels.decode_workspace(query.device, B, Hq, Hkv, S, D)
     qs = query.stride()
+    if st.lens is not None:
+        # length on the device; the split count is planned for the host's count
+        rc = _lib.lib().hq_decode_int8_len(
+            query.data_ptr(), dt, _lib.strides((qs[0], qs[1], 1), 3), k.data_ptr(), v.data_ptr(),
+            st.st[3], ksc.data_ptr(), vsc.data_ptr(), _lib.DTYPE_F16, st.st[4], st.st[5],
+            B, Hq, Hkv, k.shape[2], st.lens.data_ptr(), S, D, float(scaling), int(q_quant),
+            out.data_ptr(), _lib.strides((Hq * D, D, 1), 3), ws.data_ptr(), ws.numel(),
+            kernels._stream(query.device))
+        _lib.check(rc, "hq_decode_int8_len")
+        return out
     rc = _lib.lib().hq_decode_int8(
         query.data_ptr(), dt, _lib.strides((qs[0], qs[1], 1), 3), k.data_ptr(), v.data_ptr(),
         st.st[3], ksc.data_ptr(), vsc.data_ptr(), _lib.DTYPE_F16, st.st[4], st.st[5],
@@ -141,15 +176,41 @@ def _decode_direct(st: _LayerStore, query: torch.Tensor, n_rep: int, scaling: fl
 
 
 class QuantizedKVCache(DynamicCache):
-    """int8 KV cache, drop-in for the reference's ``QuantizedKVCache``."""
+    """int8 KV cache, drop-in for the reference's ``QuantizedKVCache``.
 
-    def __init__(self, mode: str = "auto", capacity: int | None = None):
+    ``device_lengths=True`` keeps each layer's length on the device as well:
+    single-token (<= 64) appends write at the device length and advance it, and
+    the fused decode reads it, so a decode step (``update`` + the patched
+    attention for every layer) captured once with ``torch.cuda.graph`` replays
+    for every later token.  It needs ``mode="fused"`` and a ``capacity`` that
+    covers the whole session (buffers are never reallocated in this mode).
+    The host-side length (``get_seq_length``, the ``_lens`` view) advances on
+    eager calls only; after graph replays call ``sync_lengths()``.
+    """
+
+    def __init__(self, mode: str = "auto", capacity: int | None = None,
+                 device_lengths: bool = False):
         super().__init__()
         if mode not in ("auto", "fused", "dequant"):
             raise ValueError(f"mode must be auto, fused or dequant, not {mode!r}")
+        if device_lengths and mode != "fused":
+            raise ValueError("device_lengths=True needs mode='fused'")
         self.mode = mode
         self.capacity = capacity
+        self.device_lengths = device_lengths
         self._store: dict[int, _LayerStore] = {}
+
+    def sync_lengths(self) -> dict:
+        """Read the device lengths back into the host view (synchronises);
+        raises if a device-side append found its layer full."""
+        for i, st in self._store.items():
+            if st.lens is not None:
+                length, _, status, _ = (int(x) for x in st.lens.tolist())
+                if status != 0:
+                    raise RuntimeError(f"QuantizedKVCache: layer {i}: append past the capacity "
+                                       f"{st.capacity} (status {status})")
+                st.length = length
+        return self._lens
 
     # -- reference-compatible views (tests/qwen_kvcache_full.py:34-36)
     @property
@@ -183,18 +244,22 @@ class QuantizedKVCache(DynamicCache):
         st = self._store.get(layer_idx)
         if st is None:
             cap = _round_up(max(S_new + _ALIGN, self.capacity or 0), _ALIGN)
-            st = _LayerStore(B, H, D, cap, key_states.device)
+            st = _LayerStore(B, H, D, cap, key_states.device, self.device_lengths)
             kernels.quant_k_perchannel(key_states, out=st.k[:, :, :S_new], scale_out=st.k_sc)
             kernels.quant_v_pertoken(value_states, out=st.v[:, :, :S_new],
                                      scale_out=st.v_sc[:, :, :S_new])
             st.length = S_new
+            if st.lens is not None:
+                st.lens[0].fill_(S_new)
             self._store[layer_idx] = st
         else:
             if st.k.shape[0] != B or st.k.shape[1] != H or st.k.shape[3] != D:
                 raise ValueError("QuantizedKVCache.update: batch/head shape changed for this layer")
             L = st.length
             st.reserve(L + S_new)
-            if S_new <= 64 and _append_direct(st, key_states, value_states, L, S_new):
+            if st.lens is not None and S_new <= 64:
+                _append_at(st, key_states, value_states, S_new)  # position on the device
+            elif S_new <= 64 and _append_direct(st, key_states, value_states, L, S_new):
                 pass  # the decode-step path: one launch, no views
             else:
                 kdst, vdst = st.k[:, :, L:L + S_new], st.v[:, :, L:L + S_new]
@@ -205,6 +270,8 @@ class QuantizedKVCache(DynamicCache):
                     # codes with the new tokens' own per-channel scale; that scale is not kept
                     kernels.quant_k_perchannel(key_states, out=kdst, scale_dtype=None)
                     kernels.quant_v_pertoken(value_states, out=vdst, scale_out=vsc)
+                if st.lens is not None:  # eager multi-token append: host length is current
+                    st.lens[0].fill_(L + S_new)
             st.length = L + S_new
         L = st.length
         k, v = st.k[:, :, :L], st.v[:, :, :L]
@@ -284,10 +351,17 @@ def quantized_attention_forward(module, query, key, value, attention_mask, scali
                 raise NotImplementedError("padded decode masks are not supported by the int8 kernel")
         out = _decode_direct(st, q, module.num_key_value_groups, scaling, q_quant)
         if out is None:
-            k, v, k_sc, v_sc = st.codes()
             out = torch.empty((B, 1, Hq, D), dtype=query.dtype, device=query.device)
-            kernels.int8_decode_attn(q[:, :, 0, :], k, k_sc, v, v_sc, module.num_key_value_groups,
-                                     sm_scale=scaling, q_quant=q_quant, out=out[:, 0])
+            if st.lens is not None:  # capacity buffers, length on the device
+                kernels.int8_decode_attn(q[:, :, 0, :], st.k, st.k_sc, st.v, st.v_sc,
+                                         module.num_key_value_groups, sm_scale=scaling,
+                                         q_quant=q_quant, out=out[:, 0], seq_len=st.lens,
+                                         s_plan=st.length)
+            else:
+                k, v, k_sc, v_sc = st.codes()
+                kernels.int8_decode_attn(q[:, :, 0, :], k, k_sc, v, v_sc,
+                                         module.num_key_value_groups, sm_scale=scaling,
+                                         q_quant=q_quant, out=out[:, 0])
         return out, None
     if st is not None:
         k, v, k_sc, v_sc = st.codes()

@@ -77,6 +77,11 @@ class _Workspaces:
         with self._lock:
             buf = self._bufs.get(key)
             if buf is None or buf.numel() < nbytes:
+                if torch.cuda.is_current_stream_capturing():
+                    # memory made during a capture belongs to the graph's pool
+                    raise RuntimeError(
+                        f"{kind} workspace of {nbytes} bytes needed during CUDA graph capture: "
+                        "run the same call once on this stream before capturing it")
                 buf = torch.zeros(max(nbytes, 4096), dtype=torch.uint8, device=dev)
                 self._bufs[key] = buf
             return buf
@@ -207,6 +212,49 @@ def append_kv(k_new: torch.Tensor, v_new: torch.Tensor, k_dst: torch.Tensor, v_d
     check(rc, "hq_append_kv")
 
 
+def append_kv_at(k_new: torch.Tensor, v_new: torch.Tensor, k_cache: torch.Tensor,
+                 v_cache: torch.Tensor, v_scale_cache: torch.Tensor, lens: torch.Tensor) -> None:
+    """``append_kv`` at the device-resident length ``lens[0]`` (``hq_append_kv_at``).
+
+    ``k_cache`` / ``v_cache`` are the whole int8 capacity buffers ``[B,H,cap,D]``
+    and ``v_scale_cache`` their fp16 or fp32 per-token scales ``[B,H,cap,1]``;
+    ``lens`` is an int32 ``[4]`` CUDA tensor ``{length, ticket, status, -}``.
+    The new rows go to ``lens[0]`` onward and the launch advances ``lens[0]``
+    by ``S_new`` on the device, so the same call can be captured in a CUDA
+    graph and replayed for every later token.  A full cache writes nothing and
+    sets ``lens[2]``.
+    """
+    _check_bhsd(k_new, "append_kv_at")
+    _check_bhsd(v_new, "append_kv_at")
+    if k_new.shape != v_new.shape or k_new.dtype != v_new.dtype:
+        raise ValueError("append_kv_at: key and value must match in shape and dtype")
+    B, H, S_new, D = k_new.shape
+    if S_new > 64:
+        raise ValueError("append_kv_at: at most 64 new tokens per call")
+    cap = k_cache.shape[2]
+    for t in (k_cache, v_cache):
+        if (t.dim() != 4 or tuple(t.shape[:2]) != (B, H) or t.shape[3] != D or
+                t.dtype != torch.int8 or t.stride(-1) != 1 or t.shape[2] != cap):
+            raise ValueError("append_kv_at: caches must be int8 [B,H,cap,D] buffers")
+    if tuple(v_scale_cache.shape[:3]) != (B, H, cap):
+        raise ValueError("append_kv_at: v_scale_cache must be [B,H,cap,1]")
+    if lens.dtype != torch.int32 or lens.numel() < 4 or not lens.is_cuda:
+        raise ValueError("append_kv_at: lens must be an int32 CUDA tensor of 4 elements")
+    k_new = k_new if k_new.stride(-1) == 1 else k_new.contiguous()
+    v_new = v_new if v_new.stride(-1) == 1 else v_new.contiguous()
+    f32 = v_scale_cache.dtype == torch.float32
+    if not f32 and v_scale_cache.dtype != torch.float16:
+        raise TypeError("append_kv_at: v_scale_cache must be float16 or float32")
+    rc = _lib.lib().hq_append_kv_at(
+        k_new.data_ptr(), v_new.data_ptr(), _dtype_code(k_new, "append_kv_at"),
+        _lib.strides(k_new.stride(), 4), _lib.strides(v_new.stride(), 4), B, H, S_new, D,
+        k_cache.data_ptr(), _lib.strides(k_cache.stride(), 4), v_cache.data_ptr(),
+        _lib.strides(v_cache.stride(), 4), v_scale_cache.data_ptr() if f32 else None,
+        None if f32 else v_scale_cache.data_ptr(), _lib.strides(v_scale_cache.stride()[:3], 3),
+        cap, lens.data_ptr(), _stream(k_new.device))
+    check(rc, "hq_append_kv_at")
+
+
 def dequant(q: torch.Tensor, scale: torch.Tensor, dtype: torch.dtype, per_channel: bool,
             out: torch.Tensor | None = None) -> torch.Tensor:
     """``dtype(float(q) * float(scale))`` for an int8 cache tensor ``[B,H,S,D]``.
@@ -276,7 +324,7 @@ def _kv_strides(k, v):
 
 
 def int8_decode_attn(q, k_i8, k_sc, v_i8, v_sc, n_rep=None, *, sm_scale=None, q_quant=False,
-                     out=None, partial_out=None, peers=None):
+                     out=None, partial_out=None, peers=None, seq_len=None, s_plan=None):
     """Int8 decode attention (split-KV), the contract of ``int8_decode_attn``
     (src/kernels/int8_decode_attn_triton.py:101-113), batched.
 
@@ -290,11 +338,18 @@ def int8_decode_attn(q, k_i8, k_sc, v_i8, v_sc, n_rep=None, *, sm_scale=None, q_
     cache holds this rank's token range only, and the kernel exchanges the
     partial softmax state with the other ranks over peer memory and returns
     the output over the whole sequence (``hq_decode_int8_peer``).
+    ``seq_len`` (int32 CUDA tensor, first element): the cache length lives on
+    the device and K/V/v_sc are capacity buffers; the kernel attends over the
+    first ``seq_len[0]`` tokens with a split count planned for ``s_plan``
+    tokens (default: the capacity) - ``hq_decode_int8_len``, replayable in a
+    CUDA graph while the length grows.
     """
     for t, n in ((q, "q"), (k_i8, "k_i8"), (k_sc, "k_sc"), (v_i8, "v_i8"), (v_sc, "v_sc")):
         _cuda(t, f"int8_decode_attn {n}")
     if peers is not None and partial_out is not None:
         raise ValueError("int8_decode_attn: peers and partial_out are exclusive")
+    if seq_len is not None and (peers is not None or partial_out is not None):
+        raise ValueError("int8_decode_attn: seq_len excludes peers and partial_out")
     qb, restore = _as_bhd(q)
     k4, v4, ks4, vs4 = _as_bhsd(k_i8), _as_bhsd(v_i8), _as_bhsd(k_sc), _as_bhsd(v_sc)
     B, Hq, D = qb.shape
@@ -310,6 +365,21 @@ def int8_decode_attn(q, k_i8, k_sc, v_i8, v_sc, n_rep=None, *, sm_scale=None, q_
     res = None
     if partial_out is None:
         res = out if out is not None else torch.empty((B, Hq, D), dtype=qb.dtype, device=qb.device)
+    if seq_len is not None:
+        if seq_len.dtype != torch.int32 or not seq_len.is_cuda or seq_len.numel() < 1:
+            raise ValueError("int8_decode_attn: seq_len must be an int32 CUDA tensor")
+        plan = S if s_plan is None else max(0, min(int(s_plan), S))
+        ws = _decode_ws(qb.device, B, Hq, Hkv, plan, D)
+        rc = _lib.lib().hq_decode_int8_len(
+            qb.data_ptr(), _dtype_code(qb, "int8_decode_attn q"), _lib.strides(qb.stride(), 3),
+            k4.data_ptr(), v4.data_ptr(), _kv_strides(k4, v4), ks4.data_ptr(), vs4.data_ptr(),
+            _dtype_code(ks4, "scale"),
+            _lib.strides((ks4.stride(0), ks4.stride(1), ks4.stride(3)), 3),
+            _lib.strides((vs4.stride(0), vs4.stride(1), vs4.stride(2)), 3), B, Hq, Hkv, S,
+            seq_len.data_ptr(), plan, D, float(sm_scale), int(bool(q_quant)), res.data_ptr(),
+            _lib.strides(res.stride(), 3), ws.data_ptr(), ws.numel(), _stream(qb.device))
+        check(rc, "hq_decode_int8_len")
+        return restore(res) if out is None else res
     ws = _decode_ws(qb.device, B, Hq, Hkv, S, D)
     ost = _lib.strides(res.stride(), 3) if res is not None else None
     args = (qb.data_ptr(), _dtype_code(qb, "int8_decode_attn q"), _lib.strides(qb.stride(), 3),

@@ -212,6 +212,49 @@ HQ_API int hq_decode_int8_noalloc(const void* q, int q_dtype, const int64_t q_st
                                   float* partial_out, hq_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * Device-resident cache length, for a decode step captured once as a CUDA
+ * graph and replayed for every later token.  The reference keeps the length
+ * as host state (QuantizedKVCache._lens, tests/qwen_kvcache_full.py:36,56-62)
+ * and grows the cache with torch.cat (:51-53), so its step cannot be replayed;
+ * these two entry points replace the append of update() and the decode call
+ * of quantized_attention_forward (:95-113) with launches whose arguments do
+ * not change from one token to the next.
+ *
+ * lens     int32[4] in device memory: {length, ticket, status, unused}; the
+ *          caller sets length and zeroes the rest once.
+ *
+ * hq_append_kv_at: hq_append_kv with k_cache / v_cache / v_scale_* addressing
+ *   row 0 of capacity buffers ([B, H, capacity, D] codes, [B, H, capacity]
+ *   scales): the S_new new rows go to lens[0] .. lens[0] + S_new - 1 and the
+ *   launch advances lens[0] by S_new (its last block to finish, through the
+ *   ticket lens[1]).  If lens[0] + S_new > capacity nothing is written,
+ *   lens[0] stays, and lens[2] is set to HQ_ERR_INVALID_ARGUMENT
+ *   (hq_read_status(lens + 2, stream) reads it).
+ *
+ * hq_decode_int8_len: hq_decode_int8 (no partial output) over the first
+ *   *seq_len tokens of K/V/v_scale buffers that hold S_max tokens (the
+ *   capacity); *seq_len is read by the kernel, clamped to [0, S_max].  The
+ *   split count is planned on the host for S_plan tokens (the length expected
+ *   when the graph replays; 0 <= S_plan <= S_max) and stays fixed; the tokens
+ *   per split follow the device length.  workspace: at least
+ *   hq_decode_workspace_bytes(B, Hq, Hkv, S_plan, D) bytes, as hq_decode_int8.
+ */
+HQ_API int hq_append_kv_at(const void* k_new, const void* v_new, int x_dtype,
+                           const int64_t k_strides[4], const int64_t v_strides[4], int B, int H,
+                           int S_new, int D, int8_t* k_cache, const int64_t kq_strides[4],
+                           int8_t* v_cache, const int64_t vq_strides[4], float* v_scale_f32,
+                           uint16_t* v_scale_f16, const int64_t vs_strides[3], int capacity,
+                           int* lens, hq_stream_t stream);
+HQ_API int hq_decode_int8_len(const void* q, int q_dtype, const int64_t q_strides[3],
+                              const int8_t* k, const int8_t* v, const int64_t kv_strides[3],
+                              const void* k_scale, const void* v_scale, int scale_dtype,
+                              const int64_t ksc_strides[3], const int64_t vsc_strides[3], int B,
+                              int Hq, int Hkv, int S_max, const int* seq_len, int S_plan, int D,
+                              float sm_scale, int q_quant, void* out,
+                              const int64_t out_strides[3], void* workspace,
+                              size_t workspace_bytes, hq_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * Sequence-sharded decode over peer memory (no counterpart in the reference,
  * whose cache lives on one device).  Each of `world` GPUs (one process per
  * GPU) holds a contiguous range of the cached tokens of every sequence; one

@@ -83,6 +83,10 @@ def test_golden_edge_cases(golden):
     ((32, 8, 256, 128), "bf16"),     # 256 slabs of 2 chunks: one block range spans slabs
     ((16, 8, 300, 64), "f16"),       # ragged 3-chunk slabs
     ((4, 8, 16384, 128), "bf16"),    # 4 MB slabs: several groups, A / B phases interleave
+    ((3, 5, 37000, 128), "bf16"),    # 15 slabs of 9.5 MB, ragged last chunk
+    ((2, 3, 5000, 64), "f32"),       # f32 rows of 256 bytes, ragged last chunk
+    ((1, 2, 100, 256), "f32"),       # rows of 64 16-byte vectors: a warp covers half a row
+    ((64, 8, 1000, 128), "f16"),     # 512 small slabs
 ])
 def test_random_vs_oracle(shape, dt):
     rng = np.random.default_rng(hash(shape) % 2**32)
