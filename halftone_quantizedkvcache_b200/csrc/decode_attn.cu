@@ -80,6 +80,10 @@ struct Params {
   int Hq, Hkv, S;
   float qk_scale;  // sm_scale * log2(e)
   int q_quant;
+  // programmatic dependent launch: K/V codes and scales are not written by the
+  // kernel launched before this one, so they are requested before that kernel
+  // completes; q, the K scales and every global write wait for it
+  int overlap;
   void* out;
   int64_t osb, osh;
   float* partial_out;  // [B*Hq][kD+2] or null
@@ -412,7 +416,6 @@ __global__ void __launch_bounds__(kThreads, 3) decode_kernel(const Params p) {
   __shared__ float red[kWarps][NREP];
   __shared__ float wl[C::NG][NREP];
   __shared__ float wm[kWarps][NREP];
-  __shared__ float cM[NREP], cL[NREP];
   __shared__ int s_last;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -798,12 +801,15 @@ __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(
   uint32_t* qtab = reinterpret_cast<uint32_t*>(empty + kStagesM);
   __shared__ float red[kWarps][NREP];
   __shared__ float qmax_s[NREP];
-  __shared__ float cM[NREP], cL[NREP];
   __shared__ int s_last;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, t4 = lane & 3;
-  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int kvh = blockIdx.x, split = blockIdx.y, b = blockIdx.z;
+  // an overlapped launch after this one may be scheduled now: its blocks take
+  // the slots of this grid's blocks as they exit, and wait for this grid's
+  // completion before reading q or writing anything
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const unsigned gen0 = peer_gen(p, b, kvh);
   int S = p.S, tps = p.tiles_per_split;
   if (p.seq_len) {
@@ -839,16 +845,19 @@ __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(
   // The small loads (q, K scales, first V scales) go out before this block's
   // first TMA copy and only one stage is requested until q' is ready: the
   // grid's opening burst of tile copies would otherwise queue ahead of them.
+  // Overlapped launches instead request every stage and the V scales while
+  // the previous kernel finishes, and load q and the K scales after it.
   const int d = tid;
   typename SE::T ks_raw;
   typename QE::T q_raw[NREP];
-  {
+  auto load_q = [&] {
     const auto* qp = reinterpret_cast<const typename QE::T*>(p.q);
     const auto* kp = reinterpret_cast<const typename SE::T*>(p.ksc);
     ks_raw = kp[b * p.kscb + kvh * p.ksch + d * p.kscd];
 #pragma unroll
     for (int r = 0; r < NREP; ++r) q_raw[r] = qp[b * p.qsb + (kvh * NREP + r) * p.qsh + d];
-  }
+  };
+  if (!p.overlap) load_q();
   float vs_a[2], vs_b[2];
   load_vs(0, vs_a);
   load_vs(1, vs_b);
@@ -862,7 +871,12 @@ __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(
   // zero the p' staging (columns 3 and 7 stay zero)
   for (int i = tid; i < C::LIMB / 4; i += kThreads) reinterpret_cast<uint32_t*>(plimb)[i] = 0;
   __syncthreads();
-  if (tid == 0 && ntiles > 0) issue(0);
+  if (tid == 0)
+    for (int t = 0; t < min(p.overlap ? kStagesM : 1, ntiles); ++t) issue(t);
+  if (p.overlap) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    load_q();
+  }
 
   // ---- q prologue: q' = q_in * k_scale * sm_scale * log2(e), thread owns channel d
   {
@@ -903,7 +917,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(
     }
     __syncthreads();
   }
-  if (tid == 0)
+  if (tid == 0 && !p.overlap)
     for (int t = 1; t < min(kStagesM, ntiles); ++t) issue(t);
 
   // q' limb B-fragments, built by the whole block into qtab: word
@@ -1381,7 +1395,23 @@ int launch_mma(Params p, int B, void* ws, size_t ws_bytes, cudaStream_t st) {
   p.ws_part = reinterpret_cast<float*>(w + 256 + align256(sizeof(int) * static_cast<size_t>(B) * p.Hkv));
   p.n_split = pl.n_split;
   p.tiles_per_split = pl.tiles_per_split;
-  dim3 grid(pl.n_split, p.Hkv, B);
+  // kv head fastest: the blocks dispatched last are the last splits, which hold
+  // the remainder tiles (the shortest runs)
+  dim3 grid(p.Hkv, pl.n_split, B);
+  if (p.overlap) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = C::SMEM;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tmk, tmv, p);
+    return e == cudaSuccess ? HQ_OK : static_cast<int>(e);
+  }
   kern<<<grid, kThreads, C::SMEM, st>>>(tmk, tmv, p);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? HQ_OK : static_cast<int>(e);
@@ -1441,7 +1471,7 @@ static int decode_int8_impl(const void* q, int q_dtype, const int64_t q_strides[
                               void* out, const int64_t out_strides[3], float* partial_out,
                               void* workspace, size_t workspace_bytes, hq_stream_t stream,
                               void* const* peer_bufs, int world, int rank,
-                              const int* seq_len = nullptr, int S_plan = 0) {
+                              const int* seq_len = nullptr, int S_plan = 0, int overlap = 0) {
   int rc = check_common(q_strides, kv_strides, out_strides, partial_out, B, Hq, Hkv, S, D, workspace);
   if (rc != HQ_OK) return rc;
   // an empty cache (S == 0) may come with null K/V/v_scale pointers
@@ -1482,6 +1512,7 @@ static int decode_int8_impl(const void* q, int q_dtype, const int64_t q_strides[
   for (int w = 0; w < world; ++w) p.peer[w] = static_cast<char*>(peer_bufs[w]);
   p.seq_len = seq_len;
   p.S_plan = S_plan < 0 ? 0 : (S_plan > S ? S : S_plan);
+  p.overlap = overlap;
   const int nrep = Hq / Hkv;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
 #define HQ_Q(SDT)                                                                                \
@@ -1510,6 +1541,21 @@ extern "C" int hq_decode_int8(const void* q, int q_dtype, const int64_t q_stride
   return decode_int8_impl(q, q_dtype, q_strides, k, v, kv_strides, k_scale, v_scale, scale_dtype,
                           ksc_strides, vsc_strides, B, Hq, Hkv, S, D, sm_scale, q_quant, out,
                           out_strides, partial_out, workspace, workspace_bytes, stream, nullptr, 0, 0);
+}
+
+extern "C" int hq_decode_int8_ex(const void* q, int q_dtype, const int64_t q_strides[3],
+                                 const int8_t* k, const int8_t* v, const int64_t kv_strides[3],
+                                 const void* k_scale, const void* v_scale, int scale_dtype,
+                                 const int64_t ksc_strides[3], const int64_t vsc_strides[3], int B,
+                                 int Hq, int Hkv, int S, int D, float sm_scale, int q_quant,
+                                 void* out, const int64_t out_strides[3], float* partial_out,
+                                 void* workspace, size_t workspace_bytes, unsigned flags,
+                                 hq_stream_t stream) {
+  if (flags & ~static_cast<unsigned>(HQ_DECODE_OVERLAP_PREVIOUS)) return HQ_ERR_INVALID_ARGUMENT;
+  return decode_int8_impl(q, q_dtype, q_strides, k, v, kv_strides, k_scale, v_scale, scale_dtype,
+                          ksc_strides, vsc_strides, B, Hq, Hkv, S, D, sm_scale, q_quant, out,
+                          out_strides, partial_out, workspace, workspace_bytes, stream, nullptr, 0,
+                          0, nullptr, 0, (flags & HQ_DECODE_OVERLAP_PREVIOUS) ? 1 : 0);
 }
 
 // ---------------------------------------------------------------- device-resident length

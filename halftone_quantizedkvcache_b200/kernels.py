@@ -324,7 +324,8 @@ def _kv_strides(k, v):
 
 
 def int8_decode_attn(q, k_i8, k_sc, v_i8, v_sc, n_rep=None, *, sm_scale=None, q_quant=False,
-                     out=None, partial_out=None, peers=None, seq_len=None, s_plan=None):
+                     out=None, partial_out=None, peers=None, seq_len=None, s_plan=None,
+                     overlap_prev=False):
     """Int8 decode attention (split-KV), the contract of ``int8_decode_attn``
     (src/kernels/int8_decode_attn_triton.py:101-113), batched.
 
@@ -343,6 +344,9 @@ def int8_decode_attn(q, k_i8, k_sc, v_i8, v_sc, n_rep=None, *, sm_scale=None, q_
     first ``seq_len[0]`` tokens with a split count planned for ``s_plan``
     tokens (default: the capacity) - ``hq_decode_int8_len``, replayable in a
     CUDA graph while the length grows.
+    ``overlap_prev``: the cache is not written by the kernel launched just
+    before this call on the stream; the launch overlaps that kernel's tail
+    (programmatic dependent launch, ``hq_decode_int8_ex``).
     """
     for t, n in ((q, "q"), (k_i8, "k_i8"), (k_sc, "k_sc"), (v_i8, "v_i8"), (v_sc, "v_sc")):
         _cuda(t, f"int8_decode_attn {n}")
@@ -350,6 +354,8 @@ def int8_decode_attn(q, k_i8, k_sc, v_i8, v_sc, n_rep=None, *, sm_scale=None, q_
         raise ValueError("int8_decode_attn: peers and partial_out are exclusive")
     if seq_len is not None and (peers is not None or partial_out is not None):
         raise ValueError("int8_decode_attn: seq_len excludes peers and partial_out")
+    if overlap_prev and (peers is not None or seq_len is not None):
+        raise ValueError("int8_decode_attn: overlap_prev excludes peers and seq_len")
     qb, restore = _as_bhd(q)
     k4, v4, ks4, vs4 = _as_bhsd(k_i8), _as_bhsd(v_i8), _as_bhsd(k_sc), _as_bhsd(v_sc)
     B, Hq, D = qb.shape
@@ -394,10 +400,16 @@ def int8_decode_attn(q, k_i8, k_sc, v_i8, v_sc, n_rep=None, *, sm_scale=None, q_
                                             _stream(qb.device))
         check(rc, "hq_decode_int8_peer")
         return restore(res) if out is None else res
-    rc = _lib.lib().hq_decode_int8(
-        *args, partial_out.data_ptr() if partial_out is not None else None, ws.data_ptr(),
-        ws.numel(), _stream(qb.device))
-    check(rc, "hq_decode_int8")
+    if overlap_prev:
+        rc = _lib.lib().hq_decode_int8_ex(
+            *args, partial_out.data_ptr() if partial_out is not None else None, ws.data_ptr(),
+            ws.numel(), 1, _stream(qb.device))
+        check(rc, "hq_decode_int8_ex")
+    else:
+        rc = _lib.lib().hq_decode_int8(
+            *args, partial_out.data_ptr() if partial_out is not None else None, ws.data_ptr(),
+            ws.numel(), _stream(qb.device))
+        check(rc, "hq_decode_int8")
     if partial_out is not None:
         return partial_out
     return restore(res) if out is None else res

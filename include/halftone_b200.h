@@ -166,6 +166,27 @@ HQ_API int hq_decode_int8(const void* q, int q_dtype, const int64_t q_strides[3]
                    hq_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * hq_decode_int8 with launch options (no counterpart in the reference).
+ * flags: 0, or HQ_DECODE_OVERLAP_PREVIOUS - the K/V codes and the V scales
+ *   read by this call are not written by the kernel enqueued just before it on
+ *   `stream`.  The launch then uses programmatic dependent launch: its blocks
+ *   may start, and request their K/V tiles and V scales, while that kernel is
+ *   still finishing; q, the K scales and every write of this call wait for its
+ *   completion (and for all memory it wrote).  Typical use: decode launches of
+ *   consecutive layers, or a decode whose cache was appended to earlier.
+ *   With flags == 0 this is hq_decode_int8.
+ */
+enum { HQ_DECODE_OVERLAP_PREVIOUS = 1 };
+HQ_API int hq_decode_int8_ex(const void* q, int q_dtype, const int64_t q_strides[3],
+                             const int8_t* k, const int8_t* v, const int64_t kv_strides[3],
+                             const void* k_scale, const void* v_scale, int scale_dtype,
+                             const int64_t ksc_strides[3], const int64_t vsc_strides[3], int B,
+                             int Hq, int Hkv, int S, int D, float sm_scale, int q_quant,
+                             void* out, const int64_t out_strides[3], float* partial_out,
+                             void* workspace, size_t workspace_bytes, unsigned flags,
+                             hq_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * Same-design dense twin: identical tiling over bf16/f16 K/V (kv_dtype), no
  * scales.  Replaces fp16_decode_attn (src/kernels/int8_decode_attn_triton.py:116-127,
  * kernel :67-97).  Arguments as hq_decode_int8; q_dtype must equal kv_dtype.

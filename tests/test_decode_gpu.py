@@ -169,3 +169,44 @@ def test_repeatable_and_status_clean():
     b = run_int8(c)[1]
     np.testing.assert_array_equal(a, b)
     assert kernels.read_status("decode") == 0
+
+
+@pytest.mark.parametrize("S", [700, 32768])
+def test_overlapped_launches_match_serial(S):
+    """HQ_DECODE_OVERLAP_PREVIOUS (programmatic dependent launch): consecutive
+    decodes of several layers, eagerly and replayed from a CUDA graph, give the
+    serial launches' outputs bit for bit; each layer's q is written by the kernel
+    just before its decode, so q must wait for it."""
+    layers = 6
+    cs = [oin.decode_case(300 + S + i, 1, 16, 8, S, 128) for i in range(layers)]
+    caches = [(dev(c["k_i8"]), dev(c["k_sc"]), dev(c["v_i8"]), dev(c["v_sc"])) for c in cs]
+    q_src = torch.stack([dev(c["q"], "bf16") for c in cs])
+    q = torch.empty_like(q_src)
+    serial = torch.empty_like(q_src)
+    over = torch.empty_like(q_src)
+
+    def step(out, overlap):
+        for i, (k8, ks, v8, vs) in enumerate(caches):
+            q[i].copy_(q_src[i])  # the kernel before each decode writes its q
+            kernels.int8_decode_attn(q[i], k8, ks, v8, vs, 2, out=out[i], overlap_prev=overlap)
+
+    step(serial, False)
+    step(over, True)
+    torch.cuda.synchronize()
+    assert torch.equal(serial, over)
+    for i, c in enumerate(cs):
+        close(over[i].float().cpu().numpy(), oracle_int8(c), atol=2e-2, rtol=2e-2)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        step(over, True)  # this stream's workspace exists before the capture
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            step(over, True)
+        over.zero_()
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize()
+    assert torch.equal(serial, over)
+    assert kernels.read_status("decode") == 0
+    del g
