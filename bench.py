@@ -670,7 +670,49 @@ def run_extras(torch, kernels, device, gen, stream, us_int8, peak):
     res["quant_write"]["append_us"] = round(ma * 1e3 / 1024, 3)
     del k, v, k8, v8
     torch.cuda.empty_cache()
+    res["prefill"] = run_prefill(torch, kernels, device, gen, stream)
     return res
+
+
+def run_prefill(torch, kernels, device, gen, stream, S=512, nl=LAYERS):
+    """Prefill attention of config 1 (B=1, Hq=16, Hkv=8, D=128, 512 tokens, causal)
+    over the int8 cache of 28 layers: the fused kernel against the reference's
+    path (dequantize K and V, then its torch attention math), one CUDA graph each."""
+    from halftone_quantizedkvcache_b200.integration.quantized_attention import (
+        _fake_quant, _reference_math)
+    sm_scale = 1.0 / math.sqrt(D)
+    caches = make_layer_caches(torch, kernels, nl, S, device, gen)
+    caches = [(k8, ks.half(), v8, vs.half()) for (k8, ks, v8, vs) in caches]  # fp16 cache scales
+    q = torch.randn((nl, B, HQ, S, D), generator=gen, device=device).to(torch.bfloat16)
+    out = torch.empty((nl, B, S, HQ, D), dtype=torch.bfloat16, device=device)
+    allowed = torch.arange(S, device=device)[None, :] <= torch.arange(S, device=device)[:, None]
+    mask = torch.zeros((S, S), dtype=torch.bfloat16, device=device).masked_fill(
+        ~allowed, torch.finfo(torch.bfloat16).min)[None, None]
+    module = _Attn(HQ // HKV, D)
+
+    def fused():
+        for l, (k8, ks, v8, vs) in enumerate(caches):
+            kernels.int8_prefill_attn(q[l], k8, ks, v8, vs, HQ // HKV, sm_scale=sm_scale,
+                                      q_quant=True, out=out[l])
+
+    def reference_path():
+        for l, (k8, ks, v8, vs) in enumerate(caches):
+            kd = kernels.dequant(k8, ks, torch.bfloat16, per_channel=True)
+            vd = kernels.dequant(v8, vs, torch.bfloat16, per_channel=False)
+            out[l].copy_(_reference_math(module, _fake_quant(q[l], (3,)), kd, vd, mask, sm_scale,
+                                         0.0))
+    with torch.cuda.stream(stream):
+        mf, _ = time_graph(torch, fused, 100, 5, stream)
+        mr, _ = time_graph(torch, reference_path, 100, 5, stream)
+    flops = 4 * B * HQ * D * S * (S + 1) / 2  # causal QK^T and PV
+    del caches
+    torch.cuda.empty_cache()
+    return {"workload": f"causal prefill B={B}, Hq={HQ}, Hkv={HKV}, D={D}, {S} tokens over the "
+                        f"int8 cache (fp16 scales), {nl} layers per CUDA graph",
+            "fused_us_per_layer": round(mf * 1e3 / nl, 3),
+            "reference_path_us_per_layer": round(mr * 1e3 / nl, 3),
+            "speedup": round(mr / mf, 3),
+            "fused_tflops": round(flops / (mf * 1e-3 / nl) / 1e12, 2)}
 
 
 def profile_only(args, torch, kernels, device, gen, stream):

@@ -45,7 +45,7 @@ def _round_up(n: int, m: int) -> int:
 class _LayerStore:
     """Capacity buffers of one layer: codes ``[B,H,cap,D]``, fp16 scales."""
 
-    __slots__ = ("k", "v", "k_sc", "v_sc", "length", "st", "lens")
+    __slots__ = ("k", "v", "k_sc", "v_sc", "length", "st", "lens", "prefill")
 
     def __init__(self, B, H, D, cap, device, device_length=False):
         self.k = torch.empty((B, H, cap, D), dtype=torch.int8, device=device)
@@ -55,6 +55,7 @@ class _LayerStore:
         self.length = 0
         # {length, ticket, status, -} on the device (graph-replayable decode steps)
         self.lens = torch.zeros(4, dtype=torch.int32, device=device) if device_length else None
+        self.prefill = False  # fused int8 prefill attention over this store
         self._strides()
 
     def _strides(self) -> None:
@@ -186,18 +187,28 @@ class QuantizedKVCache(DynamicCache):
     covers the whole session (buffers are never reallocated in this mode).
     The host-side length (``get_seq_length``, the ``_lens`` view) advances on
     eager calls only; after graph replays call ``sync_lengths()``.
+
+    ``fused_prefill=True`` (fused mode): multi-token steps (prefill, or an
+    append of several tokens) under a causal mask attend over the int8 cache
+    with one CUDA kernel (``kernels.int8_prefill_attn``) instead of
+    dequantizing it and running the reference's torch math; the result is the
+    same attention in float32 on the same 16-bit inputs (the reference rounds
+    its scores to bf16 first).
     """
 
     def __init__(self, mode: str = "auto", capacity: int | None = None,
-                 device_lengths: bool = False):
+                 device_lengths: bool = False, fused_prefill: bool = False):
         super().__init__()
         if mode not in ("auto", "fused", "dequant"):
             raise ValueError(f"mode must be auto, fused or dequant, not {mode!r}")
         if device_lengths and mode != "fused":
             raise ValueError("device_lengths=True needs mode='fused'")
+        if fused_prefill and mode != "fused":
+            raise ValueError("fused_prefill=True needs mode='fused'")
         self.mode = mode
         self.capacity = capacity
         self.device_lengths = device_lengths
+        self.fused_prefill = fused_prefill
         self._store: dict[int, _LayerStore] = {}
 
     def sync_lengths(self) -> dict:
@@ -245,6 +256,7 @@ class QuantizedKVCache(DynamicCache):
         if st is None:
             cap = _round_up(max(S_new + _ALIGN, self.capacity or 0), _ALIGN)
             st = _LayerStore(B, H, D, cap, key_states.device, self.device_lengths)
+            st.prefill = self.fused_prefill
             kernels.quant_k_perchannel(key_states, out=st.k[:, :, :S_new], scale_out=st.k_sc)
             kernels.quant_v_pertoken(value_states, out=st.v[:, :, :S_new],
                                      scale_out=st.v_sc[:, :, :S_new])
@@ -331,6 +343,22 @@ def _reference_math(module, q, key, value, attention_mask, scaling, dropout):
     return torch.matmul(attn, v).transpose(1, 2).contiguous()
 
 
+def _is_causal(mask, Sq: int, S: int) -> bool:
+    """True when the additive mask is the causal mask of the last Sq of S tokens
+    (0 where key j <= S - Sq + i, a large negative value elsewhere), which the
+    fused prefill kernel applies itself.  Synchronises (prefill only)."""
+    if mask is None:
+        return Sq == 1
+    m = mask[..., :S]
+    if m.shape[-2] != Sq or m.shape[-1] != S:
+        return False
+    allowed = torch.arange(S, device=m.device)[None, :] <= (
+        torch.arange(Sq, device=m.device)[:, None] + (S - Sq))
+    blocked = m <= torch.finfo(m.dtype).min / 2 if m.dtype.is_floating_point else m == 0
+    ok = torch.where(allowed, m == 0, blocked)
+    return bool(ok.all())
+
+
 def quantized_attention_forward(module, query, key, value, attention_mask, scaling=None,
                                 dropout=0.0, **kwargs):
     """Replacement for Qwen3's ``eager_attention_forward`` (tests/qwen_kvcache_full.py:95-113).
@@ -365,6 +393,12 @@ def quantized_attention_forward(module, query, key, value, attention_mask, scali
         return out, None
     if st is not None:
         k, v, k_sc, v_sc = st.codes()
+        if (st.prefill and Q_DIMS in (None, (3,)) and query.dtype in (torch.bfloat16, torch.float16)
+                and D == 128 and not (module.training and dropout > 0.0)
+                and _is_causal(attention_mask, Sq, st.length)):
+            out = kernels.int8_prefill_attn(query, k, k_sc, v, v_sc, module.num_key_value_groups,
+                                            sm_scale=scaling, q_quant=Q_DIMS is not None)
+            return out, None
         key = kernels.dequant(k, k_sc, query.dtype, per_channel=True)
         value = kernels.dequant(v, v_sc, query.dtype, per_channel=False)
     q = _fake_quant(query, Q_DIMS) if Q_DIMS is not None else query

@@ -415,6 +415,52 @@ def int8_decode_attn(q, k_i8, k_sc, v_i8, v_sc, n_rep=None, *, sm_scale=None, q_
     return restore(res) if out is None else res
 
 
+def int8_prefill_attn(q, k_i8, k_sc, v_i8, v_sc, n_rep=None, *, sm_scale=None, q_quant=False,
+                      out=None):
+    """Causal prefill attention over an int8 cache (``hq_prefill_int8``).
+
+    The prefill branch of the reference's patched attention
+    (tests/qwen_kvcache_full.py:95-113) over the cache its update() returns
+    dequantized (:64-65), in one launch: q ``[B,Hq,Sq,D]`` (bf16/f16), codes
+    ``[B,Hkv,S,D]`` with ``S >= Sq`` (the last Sq tokens are the queries'),
+    k_sc ``[B,Hkv,1,D]``, v_sc ``[B,Hkv,S,1]`` (f16/f32).  Query i attends keys
+    ``0 .. S - Sq + i``.  Returns ``[B,Sq,Hq,D]`` in q's dtype (or writes ``out``,
+    a tensor of that shape).
+    """
+    for t, n in ((q, "q"), (k_i8, "k_i8"), (k_sc, "k_sc"), (v_i8, "v_i8"), (v_sc, "v_sc")):
+        _cuda(t, f"int8_prefill_attn {n}")
+    if q.dim() != 4 or k_i8.dim() != 4:
+        raise ValueError("int8_prefill_attn: q [B,Hq,Sq,D] and K/V [B,Hkv,S,D] expected")
+    B, Hq, Sq, D = q.shape
+    _, Hkv, S, _ = k_i8.shape
+    if q.dtype not in (torch.bfloat16, torch.float16):
+        raise TypeError("int8_prefill_attn: q must be bfloat16 or float16")
+    if k_i8.dtype != torch.int8 or v_i8.dtype != torch.int8:
+        raise TypeError("int8_prefill_attn: K/V must be int8")
+    if k_sc.dtype != v_sc.dtype or k_sc.dtype not in (torch.float16, torch.float32):
+        raise TypeError("int8_prefill_attn: scales must both be float16 or float32")
+    if n_rep is not None and n_rep * Hkv != Hq:
+        raise ValueError("int8_prefill_attn: n_rep * H_kv != H_q")
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(D)
+    q = q if _rows_ok(q) else q.contiguous()
+    if out is None:
+        out = torch.empty((B, Sq, Hq, D), dtype=q.dtype, device=q.device)
+    elif tuple(out.shape) != (B, Sq, Hq, D) or out.dtype != q.dtype:
+        raise ValueError("int8_prefill_attn: out must be [B,Sq,Hq,D] of q's dtype")
+    os_ = out.stride()
+    rc = _lib.lib().hq_prefill_int8(
+        q.data_ptr(), _dtype_code(q, "int8_prefill_attn q"), _lib.strides(q.stride(), 4),
+        k_i8.data_ptr(), v_i8.data_ptr(), _kv_strides(k_i8, v_i8), k_sc.data_ptr(),
+        v_sc.data_ptr(), _dtype_code(k_sc, "scale"),
+        _lib.strides((k_sc.stride(0), k_sc.stride(1), k_sc.stride(3)), 3),
+        _lib.strides((v_sc.stride(0), v_sc.stride(1), v_sc.stride(2)), 3), B, Hq, Hkv, Sq, S, D,
+        float(sm_scale), int(bool(q_quant)), out.data_ptr(),
+        _lib.strides((os_[0], os_[2], os_[1], os_[3]), 4), _stream(q.device))
+    check(rc, "hq_prefill_int8")
+    return out
+
+
 def fp16_decode_attn(q, k, v, n_rep=None, *, sm_scale=None, q_quant=False, out=None,
                      partial_out=None):
     """Dense twin with the same tiling (src/kernels/int8_decode_attn_triton.py:116-127);

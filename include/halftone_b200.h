@@ -187,6 +187,32 @@ HQ_API int hq_decode_int8_ex(const void* q, int q_dtype, const int64_t q_strides
                              hq_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * Causal prefill attention over an int8 cache (Sq >= 1 new queries).
+ * Replaces the prefill branch of quantized_attention_forward
+ * (tests/qwen_kvcache_full.py:95-113) over the dequantized cache that
+ * QuantizedKVCache.update returns (:64-65): K/V dequantized to q_dtype as the
+ * reference does, q per-token fake quantization when q_quant, float32 softmax
+ * of q K^T * sm_scale with query i attending keys 0 .. S - Sq + i.
+ *
+ * q        [B, Hq, Sq, D] of q_dtype (BF16 or F16), strides q_strides[4].
+ * k, v     int8 [B, Hkv, S, D] with strides kv_strides[3] = (b, h, s); the
+ *          last Sq cached tokens are the queries' own.
+ * k_scale  [B, Hkv, D] (ksc_strides[3]); v_scale [B, Hkv, S] (vsc_strides[3]);
+ *          scale_dtype F32 or F16.
+ * out      logical [B, Hq, Sq, D] of q_dtype addressed by out_strides[4]
+ *          (the reference's [B, Sq, Hq, D] output is strides
+ *          (Sq*Hq*D, D, Hq*D, 1)).
+ * Requires D == 128, Hq % Hkv == 0, S >= Sq, 16-byte aligned q and code rows.
+ * No workspace.
+ */
+HQ_API int hq_prefill_int8(const void* q, int q_dtype, const int64_t q_strides[4],
+                           const int8_t* k, const int8_t* v, const int64_t kv_strides[3],
+                           const void* k_scale, const void* v_scale, int scale_dtype,
+                           const int64_t ksc_strides[3], const int64_t vsc_strides[3], int B,
+                           int Hq, int Hkv, int Sq, int S, int D, float sm_scale, int q_quant,
+                           void* out, const int64_t out_strides[4], hq_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * Same-design dense twin: identical tiling over bf16/f16 K/V (kv_dtype), no
  * scales.  Replaces fp16_decode_attn (src/kernels/int8_decode_attn_triton.py:116-127,
  * kernel :67-97).  Arguments as hq_decode_int8; q_dtype must equal kv_dtype.

@@ -9,6 +9,8 @@
   attention above.
 * ``quant_dequant`` restates the per-token q fake quantization of the HF patch
   (tests/qwen_kvcache_full.py:19-23,103).
+* ``prefill_int8`` restates the patch's prefill branch (causal, several
+  queries) over the dequantized cache that update() returns (:64-65,95-113).
 * ``split_partials`` / ``lse_combine`` restate the flash-decoding split: each
   sequence chunk yields (m, l, o) with m the running max of the base-2 scaled
   scores, l = sum 2^(s - m), o = sum 2^(s - m) v; the combine rescales by
@@ -74,6 +76,38 @@ def decode_int8(q, k_i8, k_sc, v_i8, v_sc, n_rep=None, sm_scale=None, acc="f32")
     out = page_attention_reference(np.asarray(q, np.float32)[:, :, None, :], k, v, n_rep,
                                    sm_scale, acc)
     return out[:, :, 0, :]
+
+
+def prefill_int8(q, k_i8, k_sc, v_i8, v_sc, n_rep=None, sm_scale=None, dtype="bf16",
+                 q_quant=True, acc="f64"):
+    """The prefill branch of the reference's patched attention over its cache
+    (tests/qwen_kvcache_full.py:95-113 on the update() return value, :64-65).
+
+    q ``[B, Hq, Sq, D]`` (values of ``dtype``); codes ``[B, Hkv, S, D]`` with
+    ``S >= Sq``; k_sc ``[B, Hkv, 1, D]``, v_sc ``[B, Hkv, S, 1]``.  K and V are
+    dequantized and rounded to ``dtype`` as update() returns them, q is
+    per-token fake-quantized (line 103, ``q_quant``), the scores
+    ``q K^T * sm_scale`` are masked causally (query i sees keys <= S - Sq + i)
+    and the softmax and ``P V`` run in ``acc`` precision without the
+    reference's intermediate bf16 roundings.  Returns ``[B, Sq, Hq, D]``.
+    """
+    dt = np.float64 if acc == "f64" else np.float32
+    B, Hq, Sq, D = q.shape
+    _, Hkv, S, _ = k_i8.shape
+    n_rep = Hq // Hkv if n_rep is None else n_rep
+    sm_scale = 1.0 / math.sqrt(D) if sm_scale is None else sm_scale
+    k = cast(dequantize_int8(k_i8, np.asarray(k_sc, np.float32)), dtype).astype(dt)
+    v = cast(dequantize_int8(v_i8, np.asarray(v_sc, np.float32)), dtype).astype(dt)
+    qq = quant_dequant(q, (3,), dtype) if q_quant else np.asarray(q, np.float32)
+    qg = qq.astype(dt).reshape(B, Hkv, n_rep, Sq, D)
+    scores = np.matmul(qg, np.swapaxes(k, -1, -2)[:, :, None]) * dt(sm_scale)
+    allowed = np.arange(S)[None, :] <= np.arange(Sq)[:, None] + (S - Sq)
+    scores = np.where(allowed, scores, -np.inf)
+    scores = scores - scores.max(axis=-1, keepdims=True)
+    p = np.exp(scores)
+    p = p / p.sum(axis=-1, keepdims=True)
+    out = np.matmul(p, v[:, :, None]).reshape(B, Hq, Sq, D)
+    return np.ascontiguousarray(out.transpose(0, 2, 1, 3))
 
 
 def decode_dense(q, k, v, n_rep=None, sm_scale=None, acc="f32"):
