@@ -110,8 +110,11 @@ def test_prefill_through_the_cache():
     ref = oa.prefill_int8(q, fused._k_i8[0].cpu().numpy(), fused._k_sc[0].float().cpu().numpy(),
                           fused._v_i8[0].cpu().numpy(), fused._v_sc[0].float().cpu().numpy(), 2)
     check(of, ref, "fused prefill")
-    # the reference math rounds its scores to bf16: same result within that noise
-    torch.testing.assert_close(of.float(), op.float(), atol=6e-2, rtol=6e-2)
+    # the reference math rounds its scores to bf16 before the softmax: the kernel
+    # is at least as close to the float64 attention as that path is
+    err_ours = np.abs(of.float().cpu().numpy() - ref)
+    err_refpath = np.abs(op.float().cpu().numpy() - ref)
+    assert err_ours.max() <= err_refpath.max() and err_ours.mean() <= err_refpath.mean()
     # a padding-style mask (not causal): both caches take the reference math
     bad = mask.clone()
     bad[..., :5] = torch.finfo(torch.bfloat16).min
