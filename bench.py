@@ -649,12 +649,19 @@ def run_extras(torch, kernels, device, gen, stream, us_int8, peak):
             k, out=k8, scale_dtype=None, scale_f32_out=ks), 20, 3, stream)
         mv, _ = time_graph(torch, lambda: kernels.quant_v_pertoken(
             v, out=v8, scale_dtype=None, scale_f32_out=vs), 20, 3, stream)
+        ks_static = kernels.calibrate_k_scale([k])
+        ms_, _ = time_graph(torch, lambda: kernels.quant_k_static(k, ks_static, out=k8), 20, 3,
+                            stream)
     res["quant_write"] = {
         "workload": "B=8, Hkv=8, S=32768, D=128 bf16 -> int8 + fp32 scales (1.07 GB input, > L2)",
         "k_gbs": round(kb / (mk * 1e-3) / 1e9, 1), "k_us": round(mk * 1e3, 2),
         "k_frac_of_peak": round(kb / (mk * 1e-3) / 1e9 / peak, 4),
         "v_gbs": round(vb / (mv * 1e-3) / 1e9, 1), "v_us": round(mv * 1e3, 2),
-        "v_frac_of_peak": round(vb / (mv * 1e-3) / 1e9 / peak, 4)}
+        "v_frac_of_peak": round(vb / (mv * 1e-3) / 1e9 / peak, 4),
+        "k_static_gbs": round((3 * n + Hq_ * D * 4) / (ms_ * 1e-3) / 1e9, 1),
+        "k_static_us": round(ms_ * 1e3, 2),
+        "k_static_frac_of_peak": round((3 * n + Hq_ * D * 4) / (ms_ * 1e-3) / 1e9 / peak, 4),
+        "k_static_note": "K with calibrated static per-channel scales (no column maximum)"}
     # -- 1024 single-token appends (B=8, Hkv=8): fused append kernel latency
     kn = torch.randn((Bq, Hq_, 1, D), generator=gen, device=device).to(torch.bfloat16)
     vn = torch.randn((Bq, Hq_, 1, D), generator=gen, device=device).to(torch.bfloat16)

@@ -33,6 +33,9 @@ SIGNATURES = {
     "hq_quant_k_perchannel": (_I, [_P, _I, _A4, _I, _I, _I, _I, _P, _A4, _P, _P, _P, _Z, _P]),
     "hq_quant_v_pertoken": (_I, [_P, _I, _A4, _I, _I, _I, _I, _P, _A4, _P, _P, _A4, _P]),
     "hq_append_kv": (_I, [_P, _P, _I, _A4, _A4, _I, _I, _I, _I, _P, _A4, _P, _A4, _P, _P, _A4, _P]),
+    "hq_quant_k_static": (_I, [_P, _I, _A4, _I, _I, _I, _I, _P, _I, _A4, _P, _A4, _P]),
+    "hq_append_kv_static": (_I, [_P, _P, _I, _A4, _A4, _I, _I, _I, _I, _P, _I, _A4, _P, _A4, _P,
+                                 _A4, _P, _P, _A4, _P]),
     "hq_dequant": (_I, [_P, _A4, _I, _I, _I, _I, _P, _I, _A4, _I, _P, _I, _A4, _P]),
     "hq_decode_workspace_bytes": (_Z, [_I, _I, _I, _I, _I]),
     "hq_decode_int8": (_I, [_P, _I, _A4, _P, _P, _A4, _P, _P, _I, _A4, _A4, _I, _I, _I, _I, _I,

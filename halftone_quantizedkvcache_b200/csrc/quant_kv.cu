@@ -543,6 +543,69 @@ __global__ void __launch_bounds__(kThreads, 2) quant_k_kernel(
   cp_async_wait<0>();
 }
 
+// ------------------------------------------------------------------ K per channel, static scales
+// Codes for given (calibrated) per-channel scales: q = clamp(rint(x / s[d]), +-127),
+// the reference's quantize_int8 rule (reference/page_attention_int8_pytorch.py:23-30)
+// with the scale supplied instead of found.  No maximum is searched, so it is a
+// single streaming pass like the V kernel.  Values beyond the calibrated range
+// clamp to +-127; NaN codes to 0.
+//
+// rint(x * RN(1/s)) equals rint(RN(x / s)) whenever the exact residual
+// x * RN(1/s) - k stays within 0.5 - 2^-15 of the integer k and |k| <= 128 (the
+// reciprocal's relative error moves the quotient by at most 128 * 2^-24 there);
+// other elements take the IEEE divide, and |k| > 128 clamps either way.
+__device__ __forceinline__ int static_code(float x, float s, float rcp) {
+  float k = rintf(x * rcp);
+  if (fabsf(k) <= 128.0f && fabsf(__fmaf_rn(x, rcp, -k)) > kTieGuard) k = rintf(__fdiv_rn(x, s));
+  if (k != k) k = 0.0f;
+  return static_cast<int>(fminf(fmaxf(k, -127.0f), 127.0f));
+}
+
+// grid = (row blocks, slabs); each thread quantizes one 16-byte vector of IT rows.
+template <int DT, int D, int SDT>
+__global__ void __launch_bounds__(kThreads) quant_k_static_kernel(
+    const char* __restrict__ x, int64_t xsb, int64_t xsh, int64_t xss, int H, int S, int n_slabs,
+    const void* __restrict__ scale, int64_t ssb, int64_t ssh, int64_t ssd, int8_t* __restrict__ q,
+    int64_t qsb, int64_t qsh, int64_t qss) {
+  constexpr int EB = Elem<DT>::kBytes;
+  constexpr int VE = 16 / EB;
+  constexpr int VPR = D / VE;
+  constexpr int RS = kThreads / VPR;
+  constexpr int IT = 4;
+  const int cg = threadIdx.x % VPR, rs = threadIdx.x / VPR;
+  const auto* sp = reinterpret_cast<const typename Elem<SDT>::T*>(scale);
+  for (int slab = blockIdx.y; slab < n_slabs; slab += gridDim.y) {
+    const int b = slab / H, h = slab - (slab / H) * H;
+    float sc[VE], rc[VE];
+#pragma unroll
+    for (int e = 0; e < VE; ++e) {
+      sc[e] = Elem<SDT>::to_f32(sp[b * ssb + h * ssh + (cg * VE + e) * ssd]);
+      rc[e] = __frcp_rn(sc[e]);
+    }
+    const char* base = x + (static_cast<int64_t>(b) * xsb + static_cast<int64_t>(h) * xsh) * EB + cg * 16;
+    int8_t* qbase = q + static_cast<int64_t>(b) * qsb + static_cast<int64_t>(h) * qsh + cg * VE;
+    for (int r0 = blockIdx.x * RS * IT; r0 < S; r0 += gridDim.x * RS * IT) {
+      uint4 v[IT];
+#pragma unroll
+      for (int it = 0; it < IT; ++it) {
+        const int s = r0 + it * RS + rs;
+        v[it] = s < S ? ldg_stream(base + static_cast<int64_t>(s) * xss * EB) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int it = 0; it < IT; ++it) {
+        const int s = r0 + it * RS + rs;
+        if (s >= S) continue;
+        float f[VE];
+        Vec16<DT>::unpack(v[it], f);
+        int c[VE];
+#pragma unroll
+        for (int e = 0; e < VE; ++e) c[e] = static_code(f[e], sc[e], rc[e]);
+        store_codes<VE>(qbase + static_cast<int64_t>(s) * qss, c);
+      }
+    }
+  }
+}
+
 // ------------------------------------------------------------------ append
 // One block of D threads per (b, h); thread d owns channel d.
 template <int DT, int D>
@@ -551,7 +614,8 @@ __global__ void __launch_bounds__(D) append_kernel(
     int64_t vsb, int64_t vsh, int64_t vss, int H, int S_new, int8_t* __restrict__ kq,
     int64_t kqb, int64_t kqh, int64_t kqs, int8_t* __restrict__ vq, int64_t vqb, int64_t vqh,
     int64_t vqs, float* __restrict__ vs32, __half* __restrict__ vs16, int64_t vssb, int64_t vssh,
-    int64_t vsss, int* __restrict__ lens, int cap) {
+    int64_t vsss, int* __restrict__ lens, int cap, const void* __restrict__ kst, int kst_f16,
+    int64_t kstb, int64_t ksth, int64_t kstd) {
   using E = Elem<DT>;
   using T = typename E::T;
   constexpr int kW = D / 32;
@@ -576,12 +640,22 @@ __global__ void __launch_bounds__(D) append_kernel(
   }
   const T* kp = reinterpret_cast<const T*>(k) + b * ksb + h * ksh + d;
   const T* vp = reinterpret_cast<const T*>(v) + b * vsb + h * vsh + d;
-  // K: per-channel over the S_new new tokens
-  float amax = 0.0f;
-  for (int s = 0; s < S_new; ++s) amax = fmaxf(amax, fabsf(E::to_f32(kp[s * kss])));
-  const Quantizer qk = Quantizer::from_amax(amax);
-  for (int s = 0; s < S_new; ++s)
-    kq[b * kqb + h * kqh + s * kqs + d] = static_cast<int8_t>(qk.code(E::to_f32(kp[s * kss])));
+  if (kst) {
+    // K with the given static per-channel scale of channel d
+    const int64_t si = b * kstb + h * ksth + d * kstd;
+    const float sk = kst_f16 ? __half2float(reinterpret_cast<const __half*>(kst)[si])
+                             : reinterpret_cast<const float*>(kst)[si];
+    const float rk = __frcp_rn(sk);
+    for (int s = 0; s < S_new; ++s)
+      kq[b * kqb + h * kqh + s * kqs + d] = static_cast<int8_t>(static_code(E::to_f32(kp[s * kss]), sk, rk));
+  } else {
+    // K: per-channel over the S_new new tokens
+    float amax = 0.0f;
+    for (int s = 0; s < S_new; ++s) amax = fmaxf(amax, fabsf(E::to_f32(kp[s * kss])));
+    const Quantizer qk = Quantizer::from_amax(amax);
+    for (int s = 0; s < S_new; ++s)
+      kq[b * kqb + h * kqh + s * kqs + d] = static_cast<int8_t>(qk.code(E::to_f32(kp[s * kss])));
+  }
   // V: per token over D
   for (int s = 0; s < S_new; ++s) {
     const float xv = E::to_f32(vp[s * vss]);
@@ -747,13 +821,38 @@ template <int DT, int D>
 static int launch_append(const void* k, const void* v, const int64_t* ks, const int64_t* vs,
                          int B, int H, int S_new, int8_t* kq, const int64_t* kqs, int8_t* vq,
                          const int64_t* vqs, float* v32, uint16_t* v16, const int64_t* vss,
-                         int* lens, int cap, cudaStream_t st) {
+                         int* lens, int cap, cudaStream_t st, const void* k_static = nullptr,
+                         int k_static_f16 = 0, const int64_t* kss = nullptr) {
   const int64_t z[3] = {0, 0, 0};
   if (!vss) vss = z;
+  if (!kss) kss = z;
   append_kernel<DT, D><<<B * H, D, 0, st>>>(
       static_cast<const char*>(k), static_cast<const char*>(v), ks[0], ks[1], ks[2], vs[0], vs[1],
       vs[2], H, S_new, kq, kqs[0], kqs[1], kqs[2], vq, vqs[0], vqs[1], vqs[2], v32,
-      reinterpret_cast<__half*>(v16), vss[0], vss[1], vss[2], lens, cap);
+      reinterpret_cast<__half*>(v16), vss[0], vss[1], vss[2], lens, cap, k_static, k_static_f16,
+      kss[0], kss[1], kss[2]);
+  return finish_launch();
+}
+
+template <int DT, int D>
+static int launch_quant_k_static(const void* x, const int64_t* xs, int B, int H, int S,
+                                 const void* scale, int scale_dtype, const int64_t* ss, int8_t* q,
+                                 const int64_t* qs, cudaStream_t st) {
+  constexpr int VPR = D / (16 / Elem<DT>::kBytes);
+  constexpr int rows_per_block = (kThreads / VPR) * 4;
+  const int n_slabs = B * H;
+  // enough row blocks per slab to put ~8 blocks on every SM, at least one
+  const int64_t want = std::max<int64_t>(1, 8LL * current_sm_count() / std::max(n_slabs, 1));
+  const int64_t need = (S + rows_per_block - 1) / rows_per_block;
+  dim3 grid(static_cast<unsigned>(std::min(want, need)), n_slabs < 65535 ? n_slabs : 65535);
+  if (scale_dtype == HQ_DTYPE_F16)
+    quant_k_static_kernel<DT, D, HQ_DTYPE_F16><<<grid, kThreads, 0, st>>>(
+        static_cast<const char*>(x), xs[0], xs[1], xs[2], H, S, n_slabs, scale, ss[0], ss[1], ss[2],
+        q, qs[0], qs[1], qs[2]);
+  else
+    quant_k_static_kernel<DT, D, HQ_DTYPE_F32><<<grid, kThreads, 0, st>>>(
+        static_cast<const char*>(x), xs[0], xs[1], xs[2], H, S, n_slabs, scale, ss[0], ss[1], ss[2],
+        q, qs[0], qs[1], qs[2]);
   return finish_launch();
 }
 
@@ -849,6 +948,50 @@ extern "C" int hq_append_kv(const void* k_new, const void* v_new, int x_dtype,
                                               k_new, v_new, k_strides, v_strides, B, H, S_new,
                                               k_dst, kq_strides, v_dst, vq_strides, v_scale_f32,
                                               v_scale_f16, vs_strides, nullptr, 0, st);))
+}
+
+extern "C" int hq_quant_k_static(const void* x, int x_dtype, const int64_t x_strides[4], int B,
+                                 int H, int S, int D, const void* k_scale, int scale_dtype,
+                                 const int64_t scale_strides[3], int8_t* q,
+                                 const int64_t q_strides[4], hq_stream_t stream) {
+  if (!x || !q || !k_scale || !x_strides || !q_strides || !scale_strides || B < 0 || H < 0 || S < 1)
+    return HQ_ERR_INVALID_ARGUMENT;
+  if (!valid_dtype_x(x_dtype) || (scale_dtype != HQ_DTYPE_F32 && scale_dtype != HQ_DTYPE_F16))
+    return HQ_ERR_UNSUPPORTED;
+  if (B == 0 || H == 0) return HQ_OK;
+  if (!rows16(x, x_strides, x_dtype) || q_strides[3] != 1 || !aligned(q, 8) ||
+      q_strides[0] % 8 || q_strides[1] % 8 || q_strides[2] % 8)
+    return HQ_ERR_INVALID_ARGUMENT;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  HQ_DISPATCH_X(x_dtype, HQ_DISPATCH_D(D, return launch_quant_k_static<kDT, kD>(
+                                              x, x_strides, B, H, S, k_scale, scale_dtype,
+                                              scale_strides, q, q_strides, st);))
+}
+
+extern "C" int hq_append_kv_static(const void* k_new, const void* v_new, int x_dtype,
+                                   const int64_t k_strides[4], const int64_t v_strides[4], int B,
+                                   int H, int S_new, int D, const void* k_scale, int scale_dtype,
+                                   const int64_t k_scale_strides[3], int8_t* k_dst,
+                                   const int64_t kq_strides[4], int8_t* v_dst,
+                                   const int64_t vq_strides[4], float* v_scale_f32,
+                                   uint16_t* v_scale_f16, const int64_t vs_strides[3],
+                                   hq_stream_t stream) {
+  if (!k_new || !v_new || !k_dst || !v_dst || !k_strides || !v_strides || !kq_strides ||
+      !vq_strides || !k_scale || !k_scale_strides || B < 0 || H < 0 || S_new < 1 || S_new > 64)
+    return HQ_ERR_INVALID_ARGUMENT;
+  if ((v_scale_f32 || v_scale_f16) && !vs_strides) return HQ_ERR_INVALID_ARGUMENT;
+  if (k_strides[3] != 1 || v_strides[3] != 1 || kq_strides[3] != 1 || vq_strides[3] != 1)
+    return HQ_ERR_INVALID_ARGUMENT;
+  if (!valid_dtype_x(x_dtype) || (scale_dtype != HQ_DTYPE_F32 && scale_dtype != HQ_DTYPE_F16))
+    return HQ_ERR_UNSUPPORTED;
+  if (B == 0 || H == 0) return HQ_OK;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  HQ_DISPATCH_X(x_dtype, HQ_DISPATCH_D(D, return launch_append<kDT, kD>(
+                                              k_new, v_new, k_strides, v_strides, B, H, S_new,
+                                              k_dst, kq_strides, v_dst, vq_strides, v_scale_f32,
+                                              v_scale_f16, vs_strides, nullptr, 0, st, k_scale,
+                                              scale_dtype == HQ_DTYPE_F16 ? 1 : 0,
+                                              k_scale_strides);))
 }
 
 extern "C" int hq_append_kv_at(const void* k_new, const void* v_new, int x_dtype,

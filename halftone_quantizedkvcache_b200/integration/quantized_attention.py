@@ -194,10 +194,19 @@ class QuantizedKVCache(DynamicCache):
     dequantizing it and running the reference's torch math; the result is the
     same attention in float32 on the same 16-bit inputs (the reference rounds
     its scores to bf16 first).
+
+    ``static_k_scale``: calibrated per-channel K scales (``kernels.calibrate_k_scale``),
+    one tensor for every layer or a sequence / dict indexed by layer; each is
+    ``[H, D]`` or ``[1|B, H, 1, D]``.  K is then coded with that scale on every
+    write (``kernels.quant_k_static``; appends with ``hq_append_kv_static``), no
+    per-step column maximum is searched, and the stored K scale is that scale
+    (float16).  This is the reference roadmap's static quantization
+    (README.md:140), not its default rule; V stays per token.
     """
 
     def __init__(self, mode: str = "auto", capacity: int | None = None,
-                 device_lengths: bool = False, fused_prefill: bool = False):
+                 device_lengths: bool = False, fused_prefill: bool = False,
+                 static_k_scale=None):
         super().__init__()
         if mode not in ("auto", "fused", "dequant"):
             raise ValueError(f"mode must be auto, fused or dequant, not {mode!r}")
@@ -209,6 +218,9 @@ class QuantizedKVCache(DynamicCache):
         self.capacity = capacity
         self.device_lengths = device_lengths
         self.fused_prefill = fused_prefill
+        if static_k_scale is not None and device_lengths:
+            raise ValueError("static_k_scale and device_lengths are not combined")
+        self.static_k_scale = static_k_scale
         self._store: dict[int, _LayerStore] = {}
 
     def sync_lengths(self) -> dict:
@@ -257,7 +269,12 @@ class QuantizedKVCache(DynamicCache):
             cap = _round_up(max(S_new + _ALIGN, self.capacity or 0), _ALIGN)
             st = _LayerStore(B, H, D, cap, key_states.device, self.device_lengths)
             st.prefill = self.fused_prefill
-            kernels.quant_k_perchannel(key_states, out=st.k[:, :, :S_new], scale_out=st.k_sc)
+            ks = self._static_scale(layer_idx)
+            if ks is not None:
+                kernels.quant_k_static(key_states, ks, out=st.k[:, :, :S_new])
+                st.k_sc.copy_(ks.reshape(-1, H, 1, D).expand(B, H, 1, D))
+            else:
+                kernels.quant_k_perchannel(key_states, out=st.k[:, :, :S_new], scale_out=st.k_sc)
             kernels.quant_v_pertoken(value_states, out=st.v[:, :, :S_new],
                                      scale_out=st.v_sc[:, :, :S_new])
             st.length = S_new
@@ -269,7 +286,17 @@ class QuantizedKVCache(DynamicCache):
                 raise ValueError("QuantizedKVCache.update: batch/head shape changed for this layer")
             L = st.length
             st.reserve(L + S_new)
-            if st.lens is not None and S_new <= 64:
+            ks = self._static_scale(layer_idx)
+            if ks is not None:
+                kdst, vdst = st.k[:, :, L:L + S_new], st.v[:, :, L:L + S_new]
+                vsc = st.v_sc[:, :, L:L + S_new]
+                if S_new <= 64:
+                    kernels.append_kv(key_states, value_states, kdst, vdst, v_scale_dst=vsc,
+                                      k_scale_static=ks)
+                else:
+                    kernels.quant_k_static(key_states, ks, out=kdst)
+                    kernels.quant_v_pertoken(value_states, out=vdst, scale_out=vsc)
+            elif st.lens is not None and S_new <= 64:
                 _append_at(st, key_states, value_states, S_new)  # position on the device
             elif S_new <= 64 and _append_direct(st, key_states, value_states, L, S_new):
                 pass  # the decode-step path: one launch, no views
@@ -291,6 +318,12 @@ class QuantizedKVCache(DynamicCache):
             return _tag(k, st), _tag(v, st)
         return (kernels.dequant(k, st.k_sc, key_states.dtype, per_channel=True),
                 kernels.dequant(v, st.v_sc[:, :, :L], value_states.dtype, per_channel=False))
+
+    def _static_scale(self, layer_idx):
+        s = self.static_k_scale
+        if s is None or isinstance(s, torch.Tensor):
+            return s
+        return s[layer_idx]
 
     def get_seq_length(self, layer_idx=0, cache_position=None):
         st = self._store.get(layer_idx)

@@ -139,6 +139,65 @@ def quant_k_perchannel(x: torch.Tensor, *, out: torch.Tensor | None = None,
     return q, s16
 
 
+def _static_scale(scale: torch.Tensor, B: int, H: int, D: int, what: str):
+    """A static K scale given as [H, D], [1|B, H, 1, D] or [1|B, H, D] -> (tensor, C strides
+    (b, h, d)); a batch extent of 1 broadcasts over the batch."""
+    _cuda(scale, what)
+    if scale.dtype not in (torch.float16, torch.float32):
+        raise TypeError(f"{what}: the static scale must be float16 or float32")
+    t = scale
+    if t.dim() == 2:
+        t = t.unsqueeze(0)
+    elif t.dim() == 4:
+        if t.shape[2] != 1:
+            raise ValueError(f"{what}: a 4-d static scale must be [B,H,1,D]")
+        t = t[:, :, 0, :]
+    if t.dim() != 3 or t.shape[1] != H or t.shape[2] != D or t.shape[0] not in (1, B):
+        raise ValueError(f"{what}: static scale shape {tuple(scale.shape)} does not fit "
+                         f"B={B}, H={H}, D={D}")
+    sb = 0 if t.shape[0] == 1 else t.stride(0)
+    return t, _lib.strides((sb, t.stride(1), t.stride(2)), 3)
+
+
+def quant_k_static(x: torch.Tensor, scale: torch.Tensor, *,
+                   out: torch.Tensor | None = None) -> torch.Tensor:
+    """K per channel with a static (calibrated) scale: ``clamp(rint(x / scale[d]), +-127)``.
+
+    The rule of ``quantize_int8`` (reference/page_attention_int8_pytorch.py:23-30)
+    with the scale supplied instead of found - the reference roadmap's static
+    quantization (README.md:140), which skips the per-step column maximum.
+    ``scale``: ``[H, D]`` or ``[1|B, H, 1, D]`` (float32 or float16), positive.
+    Returns int8 codes ``[B,H,S,D]`` (or writes ``out``).
+    """
+    _check_bhsd(x, "quant_k_static")
+    B, H, S, D = x.shape
+    x = _rowmajor(x)
+    sc, sst = _static_scale(scale, B, H, D, "quant_k_static")
+    q = out if out is not None else torch.empty((B, H, S, D), dtype=torch.int8, device=x.device)
+    if q.shape != x.shape or q.dtype != torch.int8 or q.device != x.device:
+        raise ValueError("quant_k_static: out must be int8 with x's shape and device")
+    rc = _lib.lib().hq_quant_k_static(
+        x.data_ptr(), _dtype_code(x, "quant_k_static"), _lib.strides(x.stride(), 4), B, H, S, D,
+        sc.data_ptr(), _dtype_code(sc, "quant_k_static scale"), sst, q.data_ptr(),
+        _lib.strides(q.stride(), 4), _stream(x.device))
+    check(rc, "hq_quant_k_static")
+    return q
+
+
+def calibrate_k_scale(samples, dtype: torch.dtype = torch.float32) -> torch.Tensor:
+    """Static per-channel K scales ``[1, H, 1, D]`` from calibration samples
+    (K tensors ``[B, H, S, D]``): ``max(|x|) / 127`` over every sample, batch and
+    token, clamped at 1e-8 as ``quantize_int8`` does; the division is done in
+    float64 and rounded once."""
+    amax = None
+    for x in samples:
+        m = x.detach().abs().amax(dim=(0, 2), keepdim=True).float()
+        amax = m if amax is None else torch.maximum(amax, m)
+    if amax is None:
+        raise ValueError("calibrate_k_scale: no samples")
+    return (amax.clamp(min=1e-8).double() / 127.0).to(dtype)
+
+
 def quant_v_pertoken(x: torch.Tensor, *, out: torch.Tensor | None = None,
                      scale_dtype: torch.dtype | None = torch.float16,
                      scale_out: torch.Tensor | None = None,
@@ -179,7 +238,8 @@ def quant_v_pertoken(x: torch.Tensor, *, out: torch.Tensor | None = None,
 
 def append_kv(k_new: torch.Tensor, v_new: torch.Tensor, k_dst: torch.Tensor, v_dst: torch.Tensor,
               v_scale_dst: torch.Tensor | None = None,
-              v_scale_f32_dst: torch.Tensor | None = None) -> None:
+              v_scale_f32_dst: torch.Tensor | None = None,
+              k_scale_static: torch.Tensor | None = None) -> None:
     """Append ``S_new <= 64`` tokens with the reference update rule in one launch.
 
     New K codes use the per-channel scale of the new tokens (not stored: the
@@ -202,6 +262,19 @@ def append_kv(k_new: torch.Tensor, v_new: torch.Tensor, k_dst: torch.Tensor, v_d
     v_new = v_new if v_new.stride(-1) == 1 else v_new.contiguous()
     ref = v_scale_dst if v_scale_dst is not None else v_scale_f32_dst
     sst = _lib.strides(ref.stride()[:3], 3) if ref is not None else None
+    if k_scale_static is not None:  # K codes with the static scale (hq_append_kv_static)
+        ksc, kst = _static_scale(k_scale_static, B, H, D, "append_kv")
+        rc = _lib.lib().hq_append_kv_static(
+            k_new.data_ptr(), v_new.data_ptr(), _dtype_code(k_new, "append_kv"),
+            _lib.strides(k_new.stride(), 4), _lib.strides(v_new.stride(), 4), B, H, S_new, D,
+            ksc.data_ptr(), _dtype_code(ksc, "append_kv k scale"), kst,
+            k_dst.data_ptr(), _lib.strides(k_dst.stride(), 4), v_dst.data_ptr(),
+            _lib.strides(v_dst.stride(), 4),
+            v_scale_f32_dst.data_ptr() if v_scale_f32_dst is not None else None,
+            v_scale_dst.data_ptr() if v_scale_dst is not None else None, sst,
+            _stream(k_new.device))
+        check(rc, "hq_append_kv_static")
+        return
     rc = _lib.lib().hq_append_kv(
         k_new.data_ptr(), v_new.data_ptr(), _dtype_code(k_new, "append_kv"),
         _lib.strides(k_new.stride(), 4), _lib.strides(v_new.stride(), 4), B, H, S_new, D,

@@ -119,6 +119,36 @@ HQ_API int hq_append_kv(const void* k_new, const void* v_new, int x_dtype, const
                  hq_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * Quantize-on-write with static (calibrated) K scales: the reference's
+ * roadmap item "static quantization from calibration distributions - drop the
+ * per-step findmax" (README.md:140); the reference itself has no such path.
+ * Codes are the rule of quantize_int8 (reference/page_attention_int8_pytorch.py:23-30)
+ * with the scale given instead of found: q = clamp(rint(x / k_scale[d]), -127, 127)
+ * (IEEE division, round half to even; values past the calibrated range clamp,
+ * NaN codes to 0).  One streaming pass, no workspace.
+ *
+ * hq_quant_k_static: x [B, H, S, D] (F32/BF16/F16) -> q [B, H, S, D] int8.
+ *   k_scale [B, H, D] of scale_dtype (F32/F16) addressed by scale_strides[3]
+ *   = (b, h, d); a stride of 0 broadcasts (one calibrated scale per head and
+ *   channel for every sequence).  Scales must be positive and finite.
+ * hq_append_kv_static: hq_append_kv with the K codes of the new tokens made
+ *   with the static scale (k_scale, scale_dtype, k_scale_strides as above)
+ *   instead of their own per-call maximum; V as in hq_append_kv.
+ */
+HQ_API int hq_quant_k_static(const void* x, int x_dtype, const int64_t x_strides[4], int B, int H,
+                             int S, int D, const void* k_scale, int scale_dtype,
+                             const int64_t scale_strides[3], int8_t* q, const int64_t q_strides[4],
+                             hq_stream_t stream);
+HQ_API int hq_append_kv_static(const void* k_new, const void* v_new, int x_dtype,
+                               const int64_t k_strides[4], const int64_t v_strides[4], int B,
+                               int H, int S_new, int D, const void* k_scale, int scale_dtype,
+                               const int64_t k_scale_strides[3], int8_t* k_dst,
+                               const int64_t kq_strides[4], int8_t* v_dst,
+                               const int64_t vq_strides[4], float* v_scale_f32,
+                               uint16_t* v_scale_f16, const int64_t vs_strides[3],
+                               hq_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * Dequantize an int8 cache tensor: out = dtype(float(code) * float(scale)).
  * Replaces the read path of QuantizedKVCache.update
  * (tests/qwen_kvcache_full.py:64-65) and dequantize_int8

@@ -103,6 +103,19 @@ def quant_v_pertoken(x: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
     return quantize_int8(x, (3,))
 
 
+def quant_k_static(x: np.ndarray, scale: np.ndarray) -> np.ndarray:
+    """Codes of ``x [B, H, S, D]`` for a given per-channel scale (broadcast as
+    ``[.., H, 1, D]``): the code step of ``quantize_int8``
+    (reference/page_attention_int8_pytorch.py:23-30) - IEEE float32 division,
+    round half to even, clamp to +-127 - with the scale supplied (static
+    quantization, the reference roadmap item README.md:140)."""
+    xf = np.asarray(x, np.float32)
+    s = np.asarray(scale, np.float32)
+    with np.errstate(divide="ignore", invalid="ignore", over="ignore"):
+        q = np.clip(np.rint(xf / s), -127, 127)
+    return np.nan_to_num(q, nan=0.0).astype(np.int8)
+
+
 def to_f16(scale: np.ndarray) -> np.ndarray:
     """``scale.to(torch.float16)`` (round to nearest even; overflow -> inf)."""
     with np.errstate(over="ignore"):
