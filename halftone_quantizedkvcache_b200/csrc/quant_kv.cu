@@ -548,7 +548,7 @@ __global__ void __launch_bounds__(kThreads, 2) quant_k_kernel(
 // the reference's quantize_int8 rule (reference/page_attention_int8_pytorch.py:23-30)
 // with the scale supplied instead of found.  No maximum is searched, so it is a
 // single streaming pass like the V kernel.  Values beyond the calibrated range
-// clamp to +-127; NaN codes to 0.
+// clamp to +-127; NaN inputs give an unspecified code.
 //
 // rint(x * RN(1/s)) equals rint(RN(x / s)) whenever the exact residual
 // x * RN(1/s) - k stays within 0.5 - 2^-15 of the integer k and |k| <= 128 (the
@@ -559,6 +559,43 @@ __device__ __forceinline__ int static_code(float x, float s, float rcp) {
   if (fabsf(k) <= 128.0f && fabsf(__fmaf_rn(x, rcp, -k)) > kTieGuard) k = rintf(__fdiv_rn(x, s));
   if (k != k) k = 0.0f;
   return static_cast<int>(fminf(fmaxf(k, -127.0f), 127.0f));
+}
+
+// One 16-byte vector with per-element static scales (sc, rc = RN(1/sc); r2 the
+// reciprocals as pairs).  16-bit inputs: packed x * r + 1.5 * 2^23 (the code in
+// the low byte), clamped to +-127, with the exact path for the whole vector
+// when any residual lies within 2^-15 of a tie; f32 inputs element by element.
+template <int DT>
+__device__ __forceinline__ void static_vec_store(const uint4& v, const F2* r2, const float* sc,
+                                                 const float* rc, int8_t* dst) {
+  constexpr int VE = Vec16<DT>::N;
+  if constexpr (DT != HQ_DTYPE_F32) {
+    F2 x[VE / 2], y[VE / 2];
+    vec_to_f2<DT>(v, x);
+    float dev = 0.0f;
+#pragma unroll
+    for (int p = 0; p < VE / 2; ++p) y[p] = quant_pair(x[p], r2[p], dev);
+    if (dev <= kTieGuard) {
+      const float lo = 12582912.0f - 127.0f, hi = 12582912.0f + 127.0f;
+#pragma unroll
+      for (int p = 0; p < VE / 2; ++p) {
+        float a, b;
+        f2_split(y[p], a, b);
+        y[p] = f2_make(fminf(fmaxf(a, lo), hi), fminf(fmaxf(b, lo), hi));
+      }
+      uint2 w;
+      w.x = pack_low_bytes(y[0], y[1]);
+      w.y = pack_low_bytes(y[2], y[3]);
+      *reinterpret_cast<uint2*>(dst) = w;
+      return;
+    }
+  }
+  float f[VE];
+  Vec16<DT>::unpack(v, f);
+  int c[VE];
+#pragma unroll
+  for (int e = 0; e < VE; ++e) c[e] = static_code(f[e], sc[e], rc[e]);
+  store_codes<VE>(dst, c);
 }
 
 // grid = (row blocks, slabs); each thread quantizes one 16-byte vector of IT rows.
@@ -577,11 +614,14 @@ __global__ void __launch_bounds__(kThreads) quant_k_static_kernel(
   for (int slab = blockIdx.y; slab < n_slabs; slab += gridDim.y) {
     const int b = slab / H, h = slab - (slab / H) * H;
     float sc[VE], rc[VE];
+    F2 r2[VE / 2];
 #pragma unroll
     for (int e = 0; e < VE; ++e) {
       sc[e] = Elem<SDT>::to_f32(sp[b * ssb + h * ssh + (cg * VE + e) * ssd]);
       rc[e] = __frcp_rn(sc[e]);
     }
+#pragma unroll
+    for (int p = 0; p < VE / 2; ++p) r2[p] = f2_make(rc[2 * p], rc[2 * p + 1]);
     const char* base = x + (static_cast<int64_t>(b) * xsb + static_cast<int64_t>(h) * xsh) * EB + cg * 16;
     int8_t* qbase = q + static_cast<int64_t>(b) * qsb + static_cast<int64_t>(h) * qsh + cg * VE;
     for (int r0 = blockIdx.x * RS * IT; r0 < S; r0 += gridDim.x * RS * IT) {
@@ -594,13 +634,7 @@ __global__ void __launch_bounds__(kThreads) quant_k_static_kernel(
 #pragma unroll
       for (int it = 0; it < IT; ++it) {
         const int s = r0 + it * RS + rs;
-        if (s >= S) continue;
-        float f[VE];
-        Vec16<DT>::unpack(v[it], f);
-        int c[VE];
-#pragma unroll
-        for (int e = 0; e < VE; ++e) c[e] = static_code(f[e], sc[e], rc[e]);
-        store_codes<VE>(qbase + static_cast<int64_t>(s) * qss, c);
+        if (s < S) static_vec_store<DT>(v[it], r2, sc, rc, qbase + static_cast<int64_t>(s) * qss);
       }
     }
   }

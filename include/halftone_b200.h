@@ -124,8 +124,8 @@ HQ_API int hq_append_kv(const void* k_new, const void* v_new, int x_dtype, const
  * per-step findmax" (README.md:140); the reference itself has no such path.
  * Codes are the rule of quantize_int8 (reference/page_attention_int8_pytorch.py:23-30)
  * with the scale given instead of found: q = clamp(rint(x / k_scale[d]), -127, 127)
- * (IEEE division, round half to even; values past the calibrated range clamp,
- * NaN codes to 0).  One streaming pass, no workspace.
+ * (IEEE division, round half to even; values past the calibrated range clamp;
+ * NaN inputs give an unspecified code).  One streaming pass, no workspace.
  *
  * hq_quant_k_static: x [B, H, S, D] (F32/BF16/F16) -> q [B, H, S, D] int8.
  *   k_scale [B, H, D] of scale_dtype (F32/F16) addressed by scale_strides[3]
