@@ -12,7 +12,9 @@
 // torch kernels; here one launch reads the int8 codes once per q tile:
 //
 //   * grid = (q tiles of 64 rows, q head, batch), the longest (last) q tiles
-//     first; 4 warps, 16 q rows each;
+//     first; 8 warps: warps w and w + 4 share q rows 16 w .. 16 w + 15 and take
+//     alternate key tiles (two tiles per step), then merge their softmax states
+//     in shared memory - the causal rows of the last q tile cost half the steps;
 //   * q rows are fake-quantized in the prologue and kept in shared memory as
 //     bf16/f16 (A-fragments by ldmatrix in every key tile);
 //   * 64-token K/V tiles: int8 codes are loaded into registers one tile ahead,
@@ -37,12 +39,12 @@ namespace hq {
 namespace pre {
 
 constexpr int kD = 128;
-constexpr int kThreads = 128;
+constexpr int kThreads = 256;
 constexpr int kRows = 64;    // q rows per block (16 per warp)
 constexpr int kKeys = 64;    // keys per tile
 constexpr int kRowB = kD * 2;  // bytes of one 16-bit row
 constexpr float kLog2e = 1.4426950408889634f;
-constexpr int kSmem = (kRows + 2 * kKeys) * kRowB + kD * 4;
+constexpr int kSmem = (kRows + 4 * kKeys) * kRowB + kD * 4;  // q, 2 K tiles, 2 V tiles, K scales
 
 struct Params {
   const void* q;
@@ -84,13 +86,13 @@ template <int DT>
 __device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
                                          uint32_t b1) {
   if constexpr (DT == HQ_DTYPE_BF16) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
         "{%8, %9}, {%0, %1, %2, %3};"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
   } else {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
         "{%8, %9}, {%0, %1, %2, %3};"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -138,10 +140,11 @@ __global__ void __launch_bounds__(kThreads) prefill_kernel(const Params p) {
   using QT = typename E::T;
   extern __shared__ __align__(128) unsigned char smem_raw[];
   unsigned char* qs = smem_raw;                    // 16 KB: the q tile
-  unsigned char* ks = qs + kRows * kRowB;          // 16 KB: dequantized K tile
-  unsigned char* vs = ks + kKeys * kRowB;          // 16 KB: dequantized V tile
-  float* ksc = reinterpret_cast<float*>(vs + kKeys * kRowB);  // K scales of the kv head
+  unsigned char* ks = qs + kRows * kRowB;          // 2 x 16 KB: dequantized K tiles
+  unsigned char* vs = ks + 2 * kKeys * kRowB;      // 2 x 16 KB: dequantized V tiles
+  float* ksc = reinterpret_cast<float*>(vs + 2 * kKeys * kRowB);  // K scales of the kv head
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int rw = warp & 3, kp = warp >> 2;  // q rows 16 rw .., key tiles of parity kp
   const int g = lane >> 2, t = lane & 3;
   const int n_qt = (p.Sq + kRows - 1) / kRows;
   const int qt = n_qt - 1 - static_cast<int>(blockIdx.x);  // longest rows first
@@ -150,15 +153,15 @@ __global__ void __launch_bounds__(kThreads) prefill_kernel(const Params p) {
   const int i0 = qt * kRows;
   const int off = p.S - p.Sq;  // key index of query 0
 
-  // ---- q tile: 2 threads per row, 64 elements each; per-row fake quantization
+  // ---- q tile: 4 threads per row, 32 elements each; per-row fake quantization
   {
-    const int r = tid >> 1, half = tid & 1;
+    const int r = tid >> 2, quarter = tid & 3;
     const int i = i0 + r;
     const QT* src = reinterpret_cast<const QT*>(p.q) + b * p.qsb + hq * p.qsh +
-                    static_cast<int64_t>(i < p.Sq ? i : 0) * p.qsi + half * 64;
-    float x[64];
+                    static_cast<int64_t>(i < p.Sq ? i : 0) * p.qsi + quarter * 32;
+    float x[32];
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {
+    for (int c = 0; c < 4; ++c) {
       const uint4 w = i < p.Sq ? *reinterpret_cast<const uint4*>(src + 8 * c) : make_uint4(0, 0, 0, 0);
       float f[8];
       Vec16<DT>::unpack(w, f);
@@ -168,29 +171,32 @@ __global__ void __launch_bounds__(kThreads) prefill_kernel(const Params p) {
     if (p.q_quant) {
       float m = 0.0f;
 #pragma unroll
-      for (int e = 0; e < 64; ++e) m = fmaxf(m, fabsf(x[e]));
+      for (int e = 0; e < 32; ++e) m = fmaxf(m, fabsf(x[e]));
       m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+      m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
       const Quantizer qz = Quantizer::from_amax(m);
 #pragma unroll
-      for (int e = 0; e < 64; ++e) x[e] = E::round(static_cast<float>(qz.code(x[e])) * qz.scale);
+      for (int e = 0; e < 32; ++e) x[e] = E::round(static_cast<float>(qz.code(x[e])) * qz.scale);
     }
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {
+    for (int c = 0; c < 4; ++c) {
       uint4 w;
       w.x = E::pack(x[8 * c], x[8 * c + 1]);
       w.y = E::pack(x[8 * c + 2], x[8 * c + 3]);
       w.z = E::pack(x[8 * c + 4], x[8 * c + 5]);
       w.w = E::pack(x[8 * c + 6], x[8 * c + 7]);
-      *reinterpret_cast<uint4*>(qs + sw(r, half * 8 + c)) = w;
+      *reinterpret_cast<uint4*>(qs + sw(r, quarter * 4 + c)) = w;
     }
   }
   // ---- K scales of the kv head, one per channel
   {
     const auto* kp = reinterpret_cast<const typename SE::T*>(p.ksc) + b * p.kscb + hk * p.ksch;
-    ksc[tid] = SE::to_f32(kp[tid * p.kscd]);
+    if (tid < kD) ksc[tid] = SE::to_f32(kp[tid * p.kscd]);
   }
-  const int pc = tid & 7;       // 16-byte piece of a code row (channels 16 pc .. 16 pc + 15)
-  const int rr = tid >> 3;      // rows rr, rr + 16, rr + 32, rr + 48 of each tile
+  // dequantization: threads 0-127 fill the even tile of a step, 128-255 the odd one
+  const int half = tid >> 7;
+  const int pc = tid & 7;         // 16-byte piece of a code row (channels 16 pc .. 16 pc + 15)
+  const int rr = (tid & 127) >> 3;  // rows rr, rr + 16, rr + 32, rr + 48 of the tile
   const int last_key = min(p.S - 1, off + min(i0 + kRows, p.Sq) - 1);
   const int n_kt = last_key >= 0 ? last_key / kKeys + 1 : 0;
   const int8_t* kbase = p.k + b * p.kvsb + hk * p.kvsh;
@@ -198,7 +204,7 @@ __global__ void __launch_bounds__(kThreads) prefill_kernel(const Params p) {
   const auto* vsp = reinterpret_cast<const typename SE::T*>(p.vsc) + b * p.vscb + hk * p.vsch;
   uint4 kc[4], vc[4];
   float vsc[4];
-  auto load_tile = [&](int kt) {
+  auto load_tile = [&](int kt) {  // this thread's rows of tile kt
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int s = kt * kKeys + rr + 16 * j;
@@ -208,31 +214,35 @@ __global__ void __launch_bounds__(kThreads) prefill_kernel(const Params p) {
       vsc[j] = in ? SE::to_f32(vsp[s * p.vscs]) : 0.0f;
     }
   };
-  if (n_kt > 0) load_tile(0);
+  const int n_steps = (n_kt + 1) / 2;  // two key tiles per step
+  if (n_steps > 0) load_tile(half);
   __syncthreads();  // q tile and K scales complete
 
   float o[16][4];
 #pragma unroll
   for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
   float m_lo = -INFINITY, m_hi = -INFINITY, l_lo = 0.0f, l_hi = 0.0f;
-  const int row_lo = i0 + warp * 16 + g, row_hi = row_lo + 8;  // query indices
+  const int row_lo = i0 + rw * 16 + g, row_hi = row_lo + 8;  // query indices
   const int lim_lo = row_lo < p.Sq ? off + row_lo : -1;        // last key of each row
   const int lim_hi = row_hi < p.Sq ? off + row_hi : -1;
 
-  for (int kt = 0; kt < n_kt; ++kt) {
-    // dequantize the tile held in registers into shared memory
-    __syncthreads();  // the previous tile's reads are done
+  unsigned char* kst = ks + kp * kKeys * kRowB;  // this warp's K / V tile of each step
+  unsigned char* vst = vs + kp * kKeys * kRowB;
+  for (int step = 0; step < n_steps; ++step) {
+    // dequantize the two tiles held in registers into shared memory
+    __syncthreads();  // the previous step's reads are done
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int r = rr + 16 * j;
-      dq_store<DT>(ks, r, pc, kc[j], ksc + 16 * pc);
+      dq_store<DT>(ks + half * kKeys * kRowB, r, pc, kc[j], ksc + 16 * pc);
       float vv[16];
 #pragma unroll
       for (int e = 0; e < 16; ++e) vv[e] = vsc[j];
-      dq_store<DT>(vs, r, pc, vc[j], vv);
+      dq_store<DT>(vs + half * kKeys * kRowB, r, pc, vc[j], vv);
     }
     __syncthreads();
-    if (kt + 1 < n_kt) load_tile(kt + 1);  // in flight during this tile's math
+    if (step + 1 < n_steps) load_tile(2 * (step + 1) + half);  // in flight during the math
+    const int kt = 2 * step + kp;
 
     // ---- S = q K^T for 64 keys: 8 n-tiles of 8 keys
     float sacc[8][4];
@@ -242,12 +252,12 @@ __global__ void __launch_bounds__(kThreads) prefill_kernel(const Params p) {
     for (int kk = 0; kk < 8; ++kk) {
       // q A-fragment of this warp's 16 rows, channels 16 kk .. 16 kk + 15
       uint32_t qa[4];
-      ldsm4(smem_u32(qs) + sw(warp * 16 + (lane & 15), 2 * kk + (lane >> 4)), qa);
+      ldsm4(smem_u32(qs) + sw(rw * 16 + (lane & 15), 2 * kk + (lane >> 4)), qa);
 #pragma unroll
       for (int np = 0; np < 4; ++np) {  // pairs of n-tiles
         uint32_t bfr[4];
         const int key = np * 16 + ((lane >> 4) << 3) + (lane & 7);
-        ldsm4(smem_u32(ks) + sw(key, 2 * kk + ((lane >> 3) & 1)), bfr);
+        ldsm4(smem_u32(kst) + sw(key, 2 * kk + ((lane >> 3) & 1)), bfr);
         mma16816<DT>(sacc[2 * np], qa, bfr[0], bfr[1]);
         mma16816<DT>(sacc[2 * np + 1], qa, bfr[2], bfr[3]);
       }
@@ -317,12 +327,45 @@ __global__ void __launch_bounds__(kThreads) prefill_kernel(const Params p) {
       for (int np = 0; np < 8; ++np) {  // pairs of 8-channel n-tiles
         uint32_t bfr[4];
         const int key = 16 * kk + (((lane >> 3) & 1) << 3) + (lane & 7);
-        ldsm4t(smem_u32(vs) + sw(key, 2 * np + (lane >> 4)), bfr);
+        ldsm4t(smem_u32(vst) + sw(key, 2 * np + (lane >> 4)), bfr);
         mma16816<DT>(o[2 * np], ah, bfr[0], bfr[1]);
         mma16816<DT>(o[2 * np], al, bfr[0], bfr[1]);
         mma16816<DT>(o[2 * np + 1], ah, bfr[2], bfr[3]);
         mma16816<DT>(o[2 * np + 1], al, bfr[2], bfr[3]);
       }
+    }
+  }
+  // ---- merge the odd-tile warps' state into the even-tile warps (same rows)
+  __syncthreads();  // every warp is done with the tiles: reuse K / V as scratch
+  float* mo = reinterpret_cast<float*>(ks);            // [4 warps][16][4][32 lanes]
+  float* ml = reinterpret_cast<float*>(vs);            // [4 warps][4][32 lanes]
+  if (kp == 1) {
+#pragma unroll
+    for (int n = 0; n < 16; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) mo[((rw * 16 + n) * 4 + e) * 32 + lane] = o[n][e];
+    ml[(rw * 4 + 0) * 32 + lane] = m_lo;
+    ml[(rw * 4 + 1) * 32 + lane] = m_hi;
+    ml[(rw * 4 + 2) * 32 + lane] = l_lo;
+    ml[(rw * 4 + 3) * 32 + lane] = l_hi;
+  }
+  __syncthreads();
+  if (kp == 1) return;
+  {
+    const float m2_lo = ml[(rw * 4 + 0) * 32 + lane], m2_hi = ml[(rw * 4 + 1) * 32 + lane];
+    const float mn_lo = fmaxf(m_lo, m2_lo), mn_hi = fmaxf(m_hi, m2_hi);
+    const float a_lo = m_lo == -INFINITY ? 0.0f : exp2f(m_lo - mn_lo);
+    const float a_hi = m_hi == -INFINITY ? 0.0f : exp2f(m_hi - mn_hi);
+    const float b_lo = m2_lo == -INFINITY ? 0.0f : exp2f(m2_lo - mn_lo);
+    const float b_hi = m2_hi == -INFINITY ? 0.0f : exp2f(m2_hi - mn_hi);
+    l_lo = l_lo * a_lo + ml[(rw * 4 + 2) * 32 + lane] * b_lo;
+    l_hi = l_hi * a_hi + ml[(rw * 4 + 3) * 32 + lane] * b_hi;
+#pragma unroll
+    for (int n = 0; n < 16; ++n) {
+      o[n][0] = o[n][0] * a_lo + mo[((rw * 16 + n) * 4 + 0) * 32 + lane] * b_lo;
+      o[n][1] = o[n][1] * a_lo + mo[((rw * 16 + n) * 4 + 1) * 32 + lane] * b_lo;
+      o[n][2] = o[n][2] * a_hi + mo[((rw * 16 + n) * 4 + 2) * 32 + lane] * b_hi;
+      o[n][3] = o[n][3] * a_hi + mo[((rw * 16 + n) * 4 + 3) * 32 + lane] * b_hi;
     }
   }
   // ---- normalise and store [b, i, hq, :]
