@@ -1,12 +1,15 @@
 /*
  * halftone_b200.h — C ABI of the B200 (sm_100a) int8 KV-cache kernels.
  *
- * Two hot paths of the Halftone int8 KV cache, as plain C entry points:
+ * The hot paths of the Halftone int8 KV cache, as plain C entry points:
  *   1. quantize-on-write: symmetric int8, K per channel (absmax over tokens),
- *      V per token (absmax over head_dim), round half to even;
- *   2. split-KV (flash-decoding) decode attention over int8 K/V with register
- *      dequantization and a float32 online softmax, plus a same-design dense
- *      (bf16/f16) twin and the log-sum-exp combine of partial results.
+ *      V per token (absmax over head_dim), round half to even; the fused
+ *      append of new tokens; static calibrated K scales;
+ *   2. split-KV (flash-decoding) decode attention over int8 K/V with a float32
+ *      online softmax, plus a same-design dense (bf16/f16) twin, the
+ *      log-sum-exp combine of partial results, a device-resident-length
+ *      variant (graph replay) and a sequence-sharded variant over peer memory;
+ *   3. causal prefill attention over the int8 cache.
  *
  * Conventions (every entry point):
  *   - Pointers are device pointers; sizes and strides are in ELEMENTS of the
@@ -19,7 +22,9 @@
  *   - The return value is HQ_OK (0), a negative hq_status for argument errors
  *     (nothing is launched), or a positive cudaError_t from the launch.
  *   - No C++ exception crosses this boundary; entry points are reentrant and
- *     keep no global mutable state besides a per-device SM-count cache.
+ *     keep no global mutable state besides per-device caches of the SM count,
+ *     kernel occupancy and kernel attributes (set once per device), and the
+ *     static scratch of hq_decode_int8_noalloc.
  */
 #ifndef HALFTONE_B200_H_
 #define HALFTONE_B200_H_
