@@ -63,7 +63,8 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="layer caches per step (profiling runs use a few; default 28)")
-    ap.add_argument("--only", choices=["all", "decode", "twin", "quant", "prefill"], default="all",
+    ap.add_argument("--only", choices=["all", "decode", "twin", "quant", "prefill", "kstatic"],
+                    default="all",
                     help="profiling: run one kernel family on a small case and exit")
     return ap.parse_args()
 
@@ -740,6 +741,13 @@ def profile_only(args, torch, kernels, device, gen, stream):
                         kernels.int8_decode_attn(q, *c, HQ // HKV, sm_scale=sm_scale, out=o)
                     else:
                         kernels.fp16_decode_attn(q, *c, HQ // HKV, sm_scale=sm_scale, out=o)
+        elif args.only == "kstatic":
+            x = torch.randn((2, 8, 32768, D), generator=gen, device=device).to(torch.bfloat16)
+            y = torch.empty(x.shape, dtype=torch.int8, device=device)
+            s = kernels.calibrate_k_scale([x])
+            torch.cuda.synchronize()
+            for _ in range(args.warmup + args.steps):
+                kernels.quant_k_static(x, s, out=y)
         elif args.only == "prefill":
             caches = make_layer_caches(torch, kernels, args.layers, 512, device, gen)
             caches = [(k8, ks.half(), v8, vs.half()) for (k8, ks, v8, vs) in caches]
