@@ -499,16 +499,18 @@ def run_e2e(torch, kernels, QuantizedKVCache, attn_fwd, caches, device, stream, 
         torch.stack(outs, out=d_out)  # the step's result, gathered by one kernel
         h_out.copy_(d_out, non_blocking=True)
 
-    def timed(run, n):
+    def timed(run, n, label):
         if world > 1:
             dist.barrier()
             torch.cuda.synchronize()
         ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.nvtx.range_push(label)
         ev0.record(stream)
         for _ in range(n):
             run()
         ev1.record(stream)
         torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
         if world > 1:
             dist.barrier()
         ms = ev0.elapsed_time(ev1) / n
@@ -522,14 +524,14 @@ def run_e2e(torch, kernels, QuantizedKVCache, attn_fwd, caches, device, stream, 
         for _ in range(2):
             one_step()               # eager: workspaces and kernel attributes set up
         torch.cuda.synchronize()
-        ms_eager = timed(one_step, eager_steps)
+        ms_eager = timed(one_step, eager_steps, "e2e_eager_step")
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=stream):
             one_step()               # recorded, not run: the device lengths stay
         for _ in range(warmup):
             g.replay()
         torch.cuda.synchronize()
-        ms = timed(g.replay, steps)
+        ms = timed(g.replay, steps, "e2e_step")
         done = 2 + eager_steps + warmup + steps
         lens = cache.sync_lengths()
         if any(n != S_HEAD + done for n in lens.values()):
