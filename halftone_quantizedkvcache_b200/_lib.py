@@ -53,6 +53,9 @@ SIGNATURES = {
                              _I, _P, _P]),
     "hq_decode_int8_len": (_I, [_P, _I, _A4, _P, _P, _A4, _P, _P, _I, _A4, _A4, _I, _I, _I, _I, _P,
                                 _I, _I, _F, _I, _P, _A4, _P, _Z, _P]),
+    "hq_decode_append_int8_len": (_I, [_P, _I, _A4, _P, _P, _A4, _A4, _P, _P, _A4, _P, _P, _I, _A4,
+                                       _A4, _I, _I, _I, _I, _P, _I, _I, _F, _I, _P, _A4, _P, _Z,
+                                       _P]),
     "hq_peer_buffer_bytes": (_Z, [_I, _I, _I, _I]),
     "hq_peer_alloc": (_I, [_Z, ctypes.POINTER(ctypes.c_void_p), _P]),
     "hq_peer_open": (_I, [_P, ctypes.POINTER(ctypes.c_void_p)]),

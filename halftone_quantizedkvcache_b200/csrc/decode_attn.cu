@@ -97,6 +97,14 @@ struct Params {
   // start; the split count stays fixed and the tiles per split follow the length
   const int* seq_len;
   int S_plan;  // host: the length the split count is planned for
+  // fused append (with seq_len): the token at row *seq_len is written by this
+  // launch from k_new / v_new [B, Hkv, 1, D] (q's dtype), by one extra block per
+  // (b, kv head) - split n_split - 1 - which also contributes the token's
+  // softmax partial; the other splits attend over rows [0, *seq_len); the last
+  // block of the grid advances *seq_len
+  const void* k_new;
+  const void* v_new;
+  int64_t knb, knh, vnb, vnh;
   // sequence-sharded exchange over peer memory (world == 0: this GPU's output only)
   int world, rank;
   char* peer[kMaxPeers];  // receive buffers of all ranks (this rank's own is local)
@@ -783,6 +791,121 @@ __device__ __forceinline__ int pv_k(int p) {
   return 16 * th + 4 * ((w & 7) >> 1) + (w & 1) + 2 * (w >> 3);
 }
 
+// Fused append: counts this block on the grid ticket (in the workspace, after
+// the status word) once all its threads have read the length; the last block of
+// the grid advances the length by the appended token (unless the cache is full).
+__device__ __forceinline__ void grid_arrive(const Params& p, int S) {
+  int* ticket = p.ws_status + 32;
+  __threadfence();  // this block's reads of the length come first
+  const int total = static_cast<int>(gridDim.x * gridDim.y * gridDim.z);
+  if (atomicAdd(ticket, 1) == total - 1) {
+    *ticket = 0;
+    if (S < p.S) *const_cast<int*>(p.seq_len) = S + 1;
+  }
+}
+
+// The extra split of a fused append, one block per (b, kv head), thread d owns
+// channel d: quantizes the new token exactly as hq_append_kv does (K per channel
+// over this one token - its scale is not stored; V per token, scale stored in the
+// cache's scale dtype), writes its codes at row S, and publishes the token's
+// softmax partial for the NREP q heads - the score q'.K in float32 from the codes
+// and the stored K scale, l = 1, o = V dequantized with the stored V scale - then
+// takes the split ticket like every other split (and merges if it is last).
+template <int NREP, int SDT, int QDT>
+__device__ void append_split(const Params& p, int b, int kvh, int S, unsigned char* ring,
+                             int scratch_floats, float (&red)[kWarps][NREP], int& s_last) {
+  using QE = Elem<QDT>;
+  using SE = Elem<SDT>;
+  const int d = threadIdx.x, lane = d & 31, warp = d >> 5;
+  const bool room = S < p.S;
+  const float xk = QE::to_f32(reinterpret_cast<const typename QE::T*>(p.k_new)[b * p.knb + kvh * p.knh + d]);
+  const float xv = QE::to_f32(reinterpret_cast<const typename QE::T*>(p.v_new)[b * p.vnb + kvh * p.vnh + d]);
+  const float ks = SE::to_f32(reinterpret_cast<const typename SE::T*>(p.ksc)[b * p.kscb + kvh * p.ksch + d * p.kscd]);
+  float qv[NREP];
+#pragma unroll
+  for (int r = 0; r < NREP; ++r)
+    qv[r] = QE::to_f32(reinterpret_cast<const typename QE::T*>(p.q)[b * p.qsb + (kvh * NREP + r) * p.qsh + d]);
+  // V row maximum and, with q_quant, the q row maxima (one reduction)
+  __shared__ float vred[kWarps];
+  {
+    const float mv = warp_max(fabsf(xv), 1);
+    if (lane == 0) vred[warp] = mv;
+    if (p.q_quant) {
+#pragma unroll
+      for (int r = 0; r < NREP; ++r) {
+        const float m = warp_max(fabsf(qv[r]), 1);
+        if (lane == 0) red[warp][r] = m;
+      }
+    }
+  }
+  __syncthreads();
+  if (p.seq_len && d == 32) grid_arrive(p, S);
+  float mv = vred[0];
+#pragma unroll
+  for (int w = 1; w < kWarps; ++w) mv = fmaxf(mv, vred[w]);
+  const Quantizer qk = Quantizer::from_amax(fabsf(xk));
+  const Quantizer qvz = Quantizer::from_amax(mv);
+  const int ck = qk.code(xk), cv = qvz.code(xv);
+  const typename SE::T vs_stored = SE::from_f32(qvz.scale);
+  if (room) {
+    int8_t* kc = const_cast<int8_t*>(reinterpret_cast<const int8_t*>(p.k)) + b * p.kvsb + kvh * p.kvsh +
+                 static_cast<int64_t>(S) * kD + d;
+    int8_t* vc = const_cast<int8_t*>(reinterpret_cast<const int8_t*>(p.v)) + b * p.kvsb + kvh * p.kvsh +
+                 static_cast<int64_t>(S) * kD + d;
+    *kc = static_cast<int8_t>(ck);
+    *vc = static_cast<int8_t>(cv);
+    if (d == 0) {
+      auto* vsp = const_cast<typename SE::T*>(reinterpret_cast<const typename SE::T*>(p.vsc));
+      vsp[b * p.vscb + kvh * p.vsch + static_cast<int64_t>(S) * p.vscs] = vs_stored;
+    }
+  } else if (d == 0) {
+    report_error(p.ws_status, HQ_ERR_INVALID_ARGUMENT);
+  }
+  // scores of the new token (base 2), as the main splits define them
+  if (p.q_quant) {
+#pragma unroll
+    for (int r = 0; r < NREP; ++r) {
+      float m = red[0][r];
+#pragma unroll
+      for (int w = 1; w < kWarps; ++w) m = fmaxf(m, red[w][r]);
+      const Quantizer qz = Quantizer::from_amax(m);
+      qv[r] = QE::to_f32(QE::from_f32(static_cast<float>(qz.code(qv[r])) * qz.scale));
+    }
+  }
+  __syncthreads();  // red is reused below
+#pragma unroll
+  for (int r = 0; r < NREP; ++r) {
+    float part = qv[r] * ks * p.qk_scale * static_cast<float>(ck);
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+    if (lane == 0) red[warp][r] = part;
+  }
+  __syncthreads();
+  float Ms[NREP], Ls[NREP], Os[NREP];
+#pragma unroll
+  for (int r = 0; r < NREP; ++r) {
+    float sc = red[0][r];
+#pragma unroll
+    for (int w = 1; w < kWarps; ++w) sc += red[w][r];
+    Ms[r] = room ? sc : -INFINITY;
+    Ls[r] = room ? 1.0f : 0.0f;
+    Os[r] = room ? static_cast<float>(cv) * SE::to_f32(vs_stored) : 0.0f;
+  }
+  const int split = p.n_split - 1;
+#pragma unroll
+  for (int r = 0; r < NREP; ++r) publish_split(p, b, kvh * NREP + r, split, d, Ms[r], Ls[r], Os[r]);
+  __syncthreads();
+  if (d == 0) {
+    __threadfence();
+    const int ticket = atomicAdd(p.ws_count + b * p.Hkv + kvh, 1);
+    s_last = ticket == p.n_split - 1;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  merge_splits<NREP, QDT>(p, b, kvh, reinterpret_cast<float*>(ring), scratch_floats, 0u);
+}
+
 template <int NREP, int SDT, int QDT>
 __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(
     const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
@@ -814,7 +937,12 @@ __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(
   int S = p.S, tps = p.tiles_per_split;
   if (p.seq_len) {
     S = min(max(__ldcg(p.seq_len), 0), p.S);
-    tps = max(1, ((S + kTileT - 1) / kTileT + p.n_split - 1) / p.n_split);
+    const int n_main = p.k_new ? p.n_split - 1 : p.n_split;
+    tps = max(1, ((S + kTileT - 1) / kTileT + n_main - 1) / n_main);
+  }
+  if (p.k_new && split == p.n_split - 1) {
+    append_split<NREP, SDT, QDT>(p, b, kvh, S, ring, C::RING / 4, red, s_last);
+    return;
   }
   const int s_begin = split * tps * kTileT;
   const int s_end = min(S, s_begin + tps * kTileT);
@@ -873,6 +1001,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(
   __syncthreads();
   if (tid == 0)
     for (int t = 0; t < min(p.overlap ? kStagesM : 1, ntiles); ++t) issue(t);
+  if (p.k_new && tid == 32) grid_arrive(p, S);  // every thread has read the length
   if (p.overlap) {
     asm volatile("griddepcontrol.wait;" ::: "memory");
     load_q();
@@ -1385,6 +1514,11 @@ int launch_mma(Params p, int B, void* ws, size_t ws_bytes, cudaStream_t st) {
   const int S_plan = p.seq_len ? p.S_plan : p.S;
   const Plan pl = make_plan(B * p.Hkv, S_plan, per_sm * sms, sms, mmak::kTileT, p.world > 0);
   if (ws_bytes < workspace_bytes(B, p.Hq, p.Hkv, S_plan, sms)) return HQ_ERR_WORKSPACE;
+  // fused append: one more partial row per head (the appended token's split)
+  const int n_rows = pl.n_split + (p.k_new ? 1 : 0);
+  if (p.k_new && ws_bytes < 256 + align256(sizeof(int) * static_cast<size_t>(B) * p.Hkv) +
+                                sizeof(float) * static_cast<size_t>(B) * p.Hq * n_rows * kPartRow)
+    return HQ_ERR_WORKSPACE;
   CUtensorMap tmk, tmv;
   int rc = encode_kv_map(&tmk, p.k, p.kvsb, p.kvsh, p.S, p.Hkv, B);
   if (rc == HQ_OK) rc = encode_kv_map(&tmv, p.v, p.kvsb, p.kvsh, p.S, p.Hkv, B);
@@ -1393,11 +1527,11 @@ int launch_mma(Params p, int B, void* ws, size_t ws_bytes, cudaStream_t st) {
   p.ws_status = reinterpret_cast<int*>(w);
   p.ws_count = reinterpret_cast<int*>(w + 256);
   p.ws_part = reinterpret_cast<float*>(w + 256 + align256(sizeof(int) * static_cast<size_t>(B) * p.Hkv));
-  p.n_split = pl.n_split;
+  p.n_split = n_rows;
   p.tiles_per_split = pl.tiles_per_split;
   // kv head fastest: the blocks dispatched last are the last splits, which hold
   // the remainder tiles (the shortest runs)
-  dim3 grid(p.Hkv, pl.n_split, B);
+  dim3 grid(p.Hkv, n_rows, B);
   if (p.overlap) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
@@ -1471,7 +1605,10 @@ static int decode_int8_impl(const void* q, int q_dtype, const int64_t q_strides[
                               void* out, const int64_t out_strides[3], float* partial_out,
                               void* workspace, size_t workspace_bytes, hq_stream_t stream,
                               void* const* peer_bufs, int world, int rank,
-                              const int* seq_len = nullptr, int S_plan = 0, int overlap = 0) {
+                              const int* seq_len = nullptr, int S_plan = 0, int overlap = 0,
+                              const void* k_new = nullptr, const void* v_new = nullptr,
+                              const int64_t* kn_strides = nullptr,
+                              const int64_t* vn_strides = nullptr) {
   int rc = check_common(q_strides, kv_strides, out_strides, partial_out, B, Hq, Hkv, S, D, workspace);
   if (rc != HQ_OK) return rc;
   // an empty cache (S == 0) may come with null K/V/v_scale pointers
@@ -1513,6 +1650,14 @@ static int decode_int8_impl(const void* q, int q_dtype, const int64_t q_strides[
   p.seq_len = seq_len;
   p.S_plan = S_plan < 0 ? 0 : (S_plan > S ? S : S_plan);
   p.overlap = overlap;
+  p.k_new = k_new;
+  p.v_new = v_new;
+  if (k_new) {
+    p.knb = kn_strides[0];
+    p.knh = kn_strides[1];
+    p.vnb = vn_strides[0];
+    p.vnh = vn_strides[1];
+  }
   const int nrep = Hq / Hkv;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
 #define HQ_Q(SDT)                                                                                \
@@ -1573,6 +1718,23 @@ extern "C" int hq_decode_int8_len(const void* q, int q_dtype, const int64_t q_st
                           ksc_strides, vsc_strides, B, Hq, Hkv, S_max, D, sm_scale, q_quant, out,
                           out_strides, nullptr, workspace, workspace_bytes, stream, nullptr, 0, 0,
                           seq_len, S_plan);
+}
+
+extern "C" int hq_decode_append_int8_len(
+    const void* q, int q_dtype, const int64_t q_strides[3], const void* k_new, const void* v_new,
+    const int64_t kn_strides[3], const int64_t vn_strides[3], int8_t* k, int8_t* v,
+    const int64_t kv_strides[3], const void* k_scale, void* v_scale, int scale_dtype,
+    const int64_t ksc_strides[3], const int64_t vsc_strides[3], int B, int Hq, int Hkv, int S_max,
+    int* seq_len, int S_plan, int D, float sm_scale, int q_quant, void* out,
+    const int64_t out_strides[3], void* workspace, size_t workspace_bytes, hq_stream_t stream) {
+  if (!seq_len || !aligned(seq_len, 4) || !k_new || !v_new || !kn_strides || !vn_strides ||
+      S_max < 1 || !k || !v || !v_scale)
+    return HQ_ERR_INVALID_ARGUMENT;
+  if (!aligned(workspace, 256)) return HQ_ERR_WORKSPACE;
+  return decode_int8_impl(q, q_dtype, q_strides, k, v, kv_strides, k_scale, v_scale, scale_dtype,
+                          ksc_strides, vsc_strides, B, Hq, Hkv, S_max, D, sm_scale, q_quant, out,
+                          out_strides, nullptr, workspace, workspace_bytes, stream, nullptr, 0, 0,
+                          seq_len, S_plan, 0, k_new, v_new, kn_strides, vn_strides);
 }
 
 // ---------------------------------------------------------------- sequence sharding over peer memory

@@ -45,7 +45,7 @@ def _round_up(n: int, m: int) -> int:
 class _LayerStore:
     """Capacity buffers of one layer: codes ``[B,H,cap,D]``, fp16 scales."""
 
-    __slots__ = ("k", "v", "k_sc", "v_sc", "length", "st", "lens", "prefill")
+    __slots__ = ("k", "v", "k_sc", "v_sc", "length", "st", "lens", "prefill", "pending")
 
     def __init__(self, B, H, D, cap, device, device_length=False):
         self.k = torch.empty((B, H, cap, D), dtype=torch.int8, device=device)
@@ -56,6 +56,7 @@ class _LayerStore:
         # {length, ticket, status, -} on the device (graph-replayable decode steps)
         self.lens = torch.zeros(4, dtype=torch.int32, device=device) if device_length else None
         self.prefill = False  # fused int8 prefill attention over this store
+        self.pending = None   # a one-token append left to the next decode (fused_append)
         self._strides()
 
     def _strides(self) -> None:
@@ -90,7 +91,15 @@ class _LayerStore:
         self.k, self.v, self.k_sc, self.v_sc = new.k, new.v, new.k_sc, new.v_sc
         self.st = new.st
 
+    def flush(self) -> None:
+        """Writes a pending one-token append with its own kernel (no decode followed it)."""
+        if self.pending is not None:
+            k_new, v_new = self.pending
+            self.pending = None
+            _append_at(self, k_new, v_new, 1)
+
     def codes(self):
+        self.flush()
         L = self.length
         return self.k[:, :, :L], self.v[:, :, :L], self.k_sc, self.v_sc[:, :, :L]
 
@@ -156,6 +165,15 @@ def _decode_direct(st: _LayerStore, query: torch.Tensor, n_rep: int, scaling: fl
     out = torch.empty((B, 1, Hq, D), dtype=query.dtype, device=query.device)
     ws = kernels.decode_workspace(query.device, B, Hq, Hkv, S, D)
     qs = query.stride()
+    if st.lens is not None and st.pending is not None:
+        k_new, v_new = st.pending
+        if k_new.dtype == query.dtype:
+            st.pending = None
+            kernels.int8_decode_attn(query[:, :, 0, :], k, ksc, v, vsc, n_rep, sm_scale=scaling,
+                                     q_quant=q_quant, out=out[:, 0], seq_len=st.lens,
+                                     s_plan=S - 1, append=(k_new, v_new))
+            return out
+        st.flush()
     if st.lens is not None:
         # length on the device; the split count is planned for the host's count
         rc = _lib.lib().hq_decode_int8_len(
@@ -202,11 +220,17 @@ class QuantizedKVCache(DynamicCache):
     per-step column maximum is searched, and the stored K scale is that scale
     (float16).  This is the reference roadmap's static quantization
     (README.md:140), not its default rule; V stays per token.
+
+    ``fused_append=True`` (with ``device_lengths``): a one-token ``update`` is left
+    pending and the patched attention that follows performs it inside the decode
+    launch (``hq_decode_append_int8_len``) - one kernel per layer and step instead
+    of two.  Anything that reads the cache first (another ``update``, the code
+    views, ``sync_lengths``) writes the pending token with the append kernel.
     """
 
     def __init__(self, mode: str = "auto", capacity: int | None = None,
                  device_lengths: bool = False, fused_prefill: bool = False,
-                 static_k_scale=None):
+                 static_k_scale=None, fused_append: bool = False):
         super().__init__()
         if mode not in ("auto", "fused", "dequant"):
             raise ValueError(f"mode must be auto, fused or dequant, not {mode!r}")
@@ -220,12 +244,16 @@ class QuantizedKVCache(DynamicCache):
         self.fused_prefill = fused_prefill
         if static_k_scale is not None and device_lengths:
             raise ValueError("static_k_scale and device_lengths are not combined")
+        if fused_append and not device_lengths:
+            raise ValueError("fused_append needs device_lengths=True")
+        self.fused_append = fused_append
         self.static_k_scale = static_k_scale
         self._store: dict[int, _LayerStore] = {}
 
     def sync_lengths(self) -> dict:
         """Read the device lengths back into the host view (synchronises);
         raises if a device-side append found its layer full."""
+        self._flush()
         for i, st in self._store.items():
             if st.lens is not None:
                 length, _, status, _ = (int(x) for x in st.lens.tolist())
@@ -235,13 +263,19 @@ class QuantizedKVCache(DynamicCache):
                 st.length = length
         return self._lens
 
+    def _flush(self) -> None:
+        for st in self._store.values():
+            st.flush()
+
     # -- reference-compatible views (tests/qwen_kvcache_full.py:34-36)
     @property
     def _k_i8(self):
+        self._flush()
         return {i: s.k[:, :, : s.length] for i, s in self._store.items()}
 
     @property
     def _v_i8(self):
+        self._flush()
         return {i: s.v[:, :, : s.length] for i, s in self._store.items()}
 
     @property
@@ -250,6 +284,7 @@ class QuantizedKVCache(DynamicCache):
 
     @property
     def _v_sc(self):
+        self._flush()
         return {i: s.v_sc[:, :, : s.length] for i, s in self._store.items()}
 
     @property
@@ -284,6 +319,7 @@ class QuantizedKVCache(DynamicCache):
         else:
             if st.k.shape[0] != B or st.k.shape[1] != H or st.k.shape[3] != D:
                 raise ValueError("QuantizedKVCache.update: batch/head shape changed for this layer")
+            st.flush()
             L = st.length
             st.reserve(L + S_new)
             ks = self._static_scale(layer_idx)
@@ -296,6 +332,10 @@ class QuantizedKVCache(DynamicCache):
                 else:
                     kernels.quant_k_static(key_states, ks, out=kdst)
                     kernels.quant_v_pertoken(value_states, out=vdst, scale_out=vsc)
+            elif (st.lens is not None and S_new == 1 and self.fused_append and
+                  key_states.dtype == value_states.dtype and key_states.stride(-1) == 1 and
+                  value_states.stride(-1) == 1):
+                st.pending = (key_states, value_states)  # written by the decode launch
             elif st.lens is not None and S_new <= 64:
                 _append_at(st, key_states, value_states, S_new)  # position on the device
             elif S_new <= 64 and _append_direct(st, key_states, value_states, L, S_new):
@@ -412,6 +452,7 @@ def quantized_attention_forward(module, query, key, value, attention_mask, scali
                 raise NotImplementedError("padded decode masks are not supported by the int8 kernel")
         out = _decode_direct(st, q, module.num_key_value_groups, scaling, q_quant)
         if out is None:
+            st.flush()
             out = torch.empty((B, 1, Hq, D), dtype=query.dtype, device=query.device)
             if st.lens is not None:  # capacity buffers, length on the device
                 kernels.int8_decode_attn(q[:, :, 0, :], st.k, st.k_sc, st.v, st.v_sc,

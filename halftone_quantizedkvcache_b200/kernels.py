@@ -398,7 +398,7 @@ def _kv_strides(k, v):
 
 def int8_decode_attn(q, k_i8, k_sc, v_i8, v_sc, n_rep=None, *, sm_scale=None, q_quant=False,
                      out=None, partial_out=None, peers=None, seq_len=None, s_plan=None,
-                     overlap_prev=False):
+                     overlap_prev=False, append=None):
     """Int8 decode attention (split-KV), the contract of ``int8_decode_attn``
     (src/kernels/int8_decode_attn_triton.py:101-113), batched.
 
@@ -417,6 +417,10 @@ def int8_decode_attn(q, k_i8, k_sc, v_i8, v_sc, n_rep=None, *, sm_scale=None, q_
     first ``seq_len[0]`` tokens with a split count planned for ``s_plan``
     tokens (default: the capacity) - ``hq_decode_int8_len``, replayable in a
     CUDA graph while the length grows.
+    ``append=(k_new, v_new)`` (with ``seq_len``): the token ``[B,Hkv,1,D]`` (q's
+    dtype) is quantized by the reference's update rule, written at row
+    ``seq_len[0]`` and attended to in the same launch, which advances the length
+    (``hq_decode_append_int8_len``; v_sc must then be the writable capacity buffer).
     ``overlap_prev``: the cache is not written by the kernel launched just
     before this call on the stream; the launch overlaps that kernel's tail
     (programmatic dependent launch, ``hq_decode_int8_ex``).
@@ -444,10 +448,30 @@ def int8_decode_attn(q, k_i8, k_sc, v_i8, v_sc, n_rep=None, *, sm_scale=None, q_
     res = None
     if partial_out is None:
         res = out if out is not None else torch.empty((B, Hq, D), dtype=qb.dtype, device=qb.device)
+    if append is not None and seq_len is None:
+        raise ValueError("int8_decode_attn: append needs seq_len")
     if seq_len is not None:
         if seq_len.dtype != torch.int32 or not seq_len.is_cuda or seq_len.numel() < 1:
             raise ValueError("int8_decode_attn: seq_len must be an int32 CUDA tensor")
         plan = S if s_plan is None else max(0, min(int(s_plan), S))
+        if append is not None:
+            kn, vn = (_as_bhsd(t) for t in append)
+            for t in (kn, vn):
+                _cuda(t, "int8_decode_attn append")
+                if (tuple(t.shape) != (B, Hkv, 1, D) or t.dtype != qb.dtype or t.stride(3) != 1):
+                    raise ValueError("int8_decode_attn: append tensors must be [B,Hkv,1,D] of q's dtype")
+            ws = _decode_ws(qb.device, B, Hq, Hkv, plan + 128, D)
+            rc = _lib.lib().hq_decode_append_int8_len(
+                qb.data_ptr(), _dtype_code(qb, "int8_decode_attn q"), _lib.strides(qb.stride(), 3),
+                kn.data_ptr(), vn.data_ptr(), _lib.strides(kn.stride()[:3], 3),
+                _lib.strides(vn.stride()[:3], 3), k4.data_ptr(), v4.data_ptr(),
+                _kv_strides(k4, v4), ks4.data_ptr(), vs4.data_ptr(), _dtype_code(ks4, "scale"),
+                _lib.strides((ks4.stride(0), ks4.stride(1), ks4.stride(3)), 3),
+                _lib.strides((vs4.stride(0), vs4.stride(1), vs4.stride(2)), 3), B, Hq, Hkv, S,
+                seq_len.data_ptr(), plan, D, float(sm_scale), int(bool(q_quant)), res.data_ptr(),
+                _lib.strides(res.stride(), 3), ws.data_ptr(), ws.numel(), _stream(qb.device))
+            check(rc, "hq_decode_append_int8_len")
+            return restore(res) if out is None else res
         ws = _decode_ws(qb.device, B, Hq, Hkv, plan, D)
         rc = _lib.lib().hq_decode_int8_len(
             qb.data_ptr(), _dtype_code(qb, "int8_decode_attn q"), _lib.strides(qb.stride(), 3),

@@ -327,6 +327,28 @@ HQ_API int hq_append_kv_at(const void* k_new, const void* v_new, int x_dtype,
                            int8_t* v_cache, const int64_t vq_strides[4], float* v_scale_f32,
                            uint16_t* v_scale_f16, const int64_t vs_strides[3], int capacity,
                            int* lens, hq_stream_t stream);
+/* hq_decode_append_int8_len: hq_append_kv_at (one token) and hq_decode_int8_len
+ *   in one launch.  k_new / v_new [B, Hkv, 1, D] of q_dtype (strides kn_strides /
+ *   vn_strides, (b, h, s)) are quantized by the reference's update rule (K with
+ *   this token's own per-channel scale, which is not stored; V per token, scale
+ *   stored in scale_dtype) and written at row lens[0] of k / v / v_scale by one
+ *   extra block per (sequence, kv head), which also contributes the token's
+ *   softmax partial; the other blocks attend over rows [0, lens[0]); the launch
+ *   advances lens[0] by one.  The output equals the two-launch sequence to float
+ *   round-off.  A full cache (lens[0] == S_max) writes nothing, attends over the
+ *   cached rows and sets HQ_ERR_INVALID_ARGUMENT in the workspace status word.
+ *   workspace: hq_decode_workspace_bytes(B, Hq, Hkv, S_plan + 128, D) bytes.
+ */
+HQ_API int hq_decode_append_int8_len(const void* q, int q_dtype, const int64_t q_strides[3],
+                                     const void* k_new, const void* v_new,
+                                     const int64_t kn_strides[3], const int64_t vn_strides[3],
+                                     int8_t* k, int8_t* v, const int64_t kv_strides[3],
+                                     const void* k_scale, void* v_scale, int scale_dtype,
+                                     const int64_t ksc_strides[3], const int64_t vsc_strides[3],
+                                     int B, int Hq, int Hkv, int S_max, int* seq_len, int S_plan,
+                                     int D, float sm_scale, int q_quant, void* out,
+                                     const int64_t out_strides[3], void* workspace,
+                                     size_t workspace_bytes, hq_stream_t stream);
 HQ_API int hq_decode_int8_len(const void* q, int q_dtype, const int64_t q_strides[3],
                               const int8_t* k, const int8_t* v, const int64_t kv_strides[3],
                               const void* k_scale, const void* v_scale, int scale_dtype,
