@@ -469,7 +469,7 @@ def run_e2e(torch, kernels, QuantizedKVCache, attn_fwd, caches, device, stream, 
     module = _Attn(HQ // HKV, D)
     nl = len(caches)
     eager_steps = min(steps, 50)
-    cache = QuantizedKVCache(mode="fused", device_lengths=True,
+    cache = QuantizedKVCache(mode="fused", device_lengths=True, fused_append=True,
                              capacity=S_HEAD + 2 * (steps + warmup) + eager_steps + 512)
     # prefill through the public API: dequantize our codes back to bf16 and update()
     with torch.cuda.stream(stream):
@@ -543,9 +543,10 @@ def run_e2e(torch, kernels, QuantizedKVCache, attn_fwd, caches, device, stream, 
     del cache
     return {"value": round(gbs, 2), "unit": "GB/s", "h2d_bytes_per_step": nl * per_layer_in,
             "d2h_bytes_per_step": nl * B * HQ * D * 2, "ms_per_step": round(ms, 4),
-            "path": "QuantizedKVCache(device_lengths=True).update + quantized_attention_forward "
-                    "per layer, the step (H2D copy, 28 layers, D2H copy) captured once as a CUDA "
-                    "graph and replayed per token; fp16 cache scales",
+            "path": "QuantizedKVCache(device_lengths=True, fused_append=True).update + "
+                    "quantized_attention_forward per layer (append inside the decode launch), the "
+                    "step (H2D copy, 28 layers, D2H copy) captured once as a CUDA graph and "
+                    "replayed per token; fp16 cache scales",
             "eager": {"value": round(per_step / (ms_eager * 1e-3) / 1e9, 2),
                       "ms_per_step": round(ms_eager, 4),
                       "path": "the same calls made eagerly from Python every step"}}

@@ -167,11 +167,19 @@ def _decode_direct(st: _LayerStore, query: torch.Tensor, n_rep: int, scaling: fl
     qs = query.stride()
     if st.lens is not None and st.pending is not None:
         k_new, v_new = st.pending
-        if k_new.dtype == query.dtype:
+        if k_new.dtype == query.dtype and k_new.shape == (B, Hkv, 1, D):
+            # the pending one-token append, inside the decode launch
             st.pending = None
-            kernels.int8_decode_attn(query[:, :, 0, :], k, ksc, v, vsc, n_rep, sm_scale=scaling,
-                                     q_quant=q_quant, out=out[:, 0], seq_len=st.lens,
-                                     s_plan=S - 1, append=(k_new, v_new))
+            wsa = kernels.decode_workspace(query.device, B, Hq, Hkv, S - 1 + 128, D)
+            rc = _lib.lib().hq_decode_append_int8_len(
+                query.data_ptr(), dt, _lib.strides((qs[0], qs[1], 1), 3), k_new.data_ptr(),
+                v_new.data_ptr(), _lib.strides(k_new.stride()[:3], 3),
+                _lib.strides(v_new.stride()[:3], 3), k.data_ptr(), v.data_ptr(), st.st[3],
+                ksc.data_ptr(), vsc.data_ptr(), _lib.DTYPE_F16, st.st[4], st.st[5], B, Hq, Hkv,
+                k.shape[2], st.lens.data_ptr(), S - 1, D, float(scaling), int(q_quant),
+                out.data_ptr(), _lib.strides((Hq * D, D, 1), 3), wsa.data_ptr(), wsa.numel(),
+                kernels._stream(query.device))
+            _lib.check(rc, "hq_decode_append_int8_len")
             return out
         st.flush()
     if st.lens is not None:
