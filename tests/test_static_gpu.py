@@ -97,3 +97,21 @@ def test_calibrate_k_scale():
     s = kernels.calibrate_k_scale([dev(x, "bf16") for x in xs])
     amax = np.maximum(*[np.abs(x).max(axis=(0, 2), keepdims=True) for x in xs])
     np.testing.assert_array_equal(s.cpu().numpy(), (amax.astype(np.float64) / 127.0).astype(np.float32))
+
+
+@pytest.mark.parametrize("dt", ["f16", "bf16"])
+def test_static_clamp_bounds_and_tiny_scales(dt):
+    """Inputs well past the calibrated range (the 16-bit input clamp) and scales so
+    small that 127 * s is below the fp16 normal range (the exact path)."""
+    rng = np.random.default_rng(17)
+    x = oin.normal(rng, (1, 4, 256, 128), dt) * np.float32(3.0)
+    x = oq.cast(x, dt)
+    s = np.abs(rng.standard_normal((1, 4, 1, 128))).astype(np.float32) * np.float32(0.01) + np.float32(1e-3)
+    q = kernels.quant_k_static(dev(x, dt), dev(s))
+    ref = oq.quant_k_static(x, s)
+    np.testing.assert_array_equal(q.cpu().numpy(), ref)
+    assert (np.abs(ref) == 127).mean() > 0.3
+    tiny = np.full((1, 4, 1, 128), 1e-7, np.float32)
+    xt = oq.cast(oin.normal(rng, (1, 4, 64, 128), dt) * np.float32(1e-5), dt)
+    q2 = kernels.quant_k_static(dev(xt, dt), dev(tiny))
+    np.testing.assert_array_equal(q2.cpu().numpy(), oq.quant_k_static(xt, tiny))
