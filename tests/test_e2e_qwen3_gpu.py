@@ -91,3 +91,56 @@ def test_fused_decode_within_reference_noise(layers, n0, nd, batch):
           f" oracle fp32-vs-bf16 max {float(floor.max()):.4f} mean {float(floor.mean()):.5f}")
     assert float(err.max()) <= 2.0 * float(floor.max()) + 1e-2
     assert float(err.mean()) <= 2.0 * float(floor.mean()) + 1e-3
+
+
+def test_whole_model_decode_step_as_one_cuda_graph():
+    """The full decode step of the model (embedding, every layer's projections,
+    RoPE, cache update + int8 attention, MLP, LM head) captured once as a CUDA
+    graph over QuantizedKVCache(device_lengths=True, fused_append=True) and
+    replayed per token, with the token id and position in static tensors.
+    Against the eager fused path on the same teacher-forced tokens: within twice
+    the reference's own bf16-vs-float32 drift (the split plan of a replayed step
+    is the one planned at capture, so the float32 sums are grouped differently)."""
+    layers, n0, nd, batch = 2, 64, 48, 1
+    model = build(layers)
+    ids = tokens(model, batch, n0 + nd)
+    a = ours(model, ids, n0, "fused")
+    b = oracle(model, ids, n0)
+    b32 = oracle(model, ids, n0, fp32_math=True)
+    with torch.no_grad(), installed():
+        cache = QuantizedKVCache(mode="fused", capacity=n0 + nd + 256, device_lengths=True,
+                                 fused_append=True)
+        logits = [model(ids[:, :n0], past_key_values=cache, use_cache=True).logits[:, -1].float()]
+        tok = torch.empty((batch, 1), dtype=torch.long, device="cuda")
+        pos = torch.empty((batch, 1), dtype=torch.long, device="cuda")
+        masks = {"full_attention": None}
+
+        def step():
+            return model(input_ids=tok, position_ids=pos, attention_mask=masks,
+                         past_key_values=cache, use_cache=True).logits[:, -1]
+
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            tok.copy_(ids[:, n0:n0 + 1])
+            pos.fill_(n0)
+            logits.append(step().float())          # eager step: workspaces exist
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                out = step()                       # recorded, not run
+            for t in range(n0 + 1, n0 + nd):
+                tok.copy_(ids[:, t:t + 1])
+                pos.fill_(t)
+                g.replay()
+                logits.append(out.float().clone())
+            torch.cuda.synchronize()
+        lens = cache.sync_lengths()
+        del g
+    assert all(v == n0 + nd for v in lens.values())
+    gl = torch.stack(logits, 1)
+    err, floor = (gl - a).abs(), (b32 - b).abs()
+    print(f"graph-vs-eager max {float(err.max()):.4f} mean {float(err.mean()):.5f}; "
+          f"reference drift max {float(floor.max()):.4f} mean {float(floor.mean()):.5f}")
+    assert torch.equal(gl[:, 0], a[:, 0])  # prefill: the same eager path
+    assert float(err.max()) <= 2.0 * float(floor.max()) + 1e-2
+    assert float(err.mean()) <= 2.0 * float(floor.mean()) + 1e-3
