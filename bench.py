@@ -684,6 +684,81 @@ def run_extras(torch, kernels, device, gen, stream, us_int8, peak):
     del k, v, k8, v8
     torch.cuda.empty_cache()
     res["prefill"] = run_prefill(torch, kernels, device, gen, stream)
+    res["model_decode_step"] = run_model_step(torch, device)
+    return res
+
+
+def run_model_step(torch, device, n0=512, nd=64):
+    """Config 1's model (Qwen3-0.6B architecture, random init, bf16, 28 layers) through
+    HF transformers with QuantizedKVCache and the patched attention: prefill 512 tokens,
+    then one decode step per token - the whole forward (all layers, the int8 cache
+    update and attention, the LM head) captured once as a CUDA graph and replayed,
+    against the same step run eagerly.  Per-token latency."""
+    from transformers import Qwen3Config, Qwen3ForCausalLM
+
+    from halftone_quantizedkvcache_b200.integration import QuantizedKVCache, installed
+    cfg = Qwen3Config(vocab_size=151936, hidden_size=1024, intermediate_size=3072,
+                      num_hidden_layers=LAYERS, num_attention_heads=HQ, num_key_value_heads=HKV,
+                      head_dim=D, rope_theta=1e6, max_position_embeddings=40960, rms_norm_eps=1e-6,
+                      tie_word_embeddings=True, attention_bias=False, use_sliding_window=False)
+    cfg._attn_implementation = "eager"
+    torch.manual_seed(0)
+    with torch.device(device):
+        model = Qwen3ForCausalLM(cfg).to(torch.bfloat16).eval()
+    g = torch.Generator().manual_seed(1)
+    ids = torch.randint(0, cfg.vocab_size, (1, n0 + 2 * nd + 8), generator=g).to(device)
+    res = {"workload": f"Qwen3-0.6B architecture (random init, bf16, {LAYERS} layers), prefill "
+                       f"{n0} tokens, decode steps at S~{n0}-{n0 + 2 * nd}, batch 1"}
+    with torch.no_grad(), installed():
+        def run(graph):
+            cache = QuantizedKVCache(mode="fused", capacity=n0 + 2 * nd + 256,
+                                     device_lengths=graph, fused_append=graph)
+            model(ids[:, :n0], past_key_values=cache, use_cache=True)
+            tok = torch.empty((1, 1), dtype=torch.long, device=device)
+            pos = torch.empty((1, 1), dtype=torch.long, device=device)
+            masks = {"full_attention": None}
+            st = torch.cuda.Stream(device)
+            st.wait_stream(torch.cuda.current_stream(device))
+            with torch.cuda.stream(st):
+                def step():
+                    return model(input_ids=tok, position_ids=pos, attention_mask=masks,
+                                 past_key_values=cache, use_cache=True).logits
+                t = n0
+                tok.copy_(ids[:, t:t + 1])
+                pos.fill_(t)
+                step()
+                t += 1
+                run_step = step
+                if graph:
+                    gr = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(gr, stream=st):
+                        step()
+                    run_step = gr.replay
+                for _ in range(3):
+                    tok.copy_(ids[:, t:t + 1])
+                    pos.fill_(t)
+                    run_step()
+                    t += 1
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(st)
+                for _ in range(nd):
+                    tok.copy_(ids[:, t:t + 1])
+                    pos.fill_(t)
+                    run_step()
+                    t += 1
+                e1.record(st)
+                torch.cuda.synchronize()
+                if graph:
+                    del gr
+            return e0.elapsed_time(e1) / nd
+
+        ms_graph = run(True)
+        ms_eager = run(False)
+    del model
+    torch.cuda.empty_cache()
+    res.update({"ms_per_token_graph": round(ms_graph, 4), "ms_per_token_eager": round(ms_eager, 4),
+                "speedup": round(ms_eager / ms_graph, 2)})
     return res
 
 

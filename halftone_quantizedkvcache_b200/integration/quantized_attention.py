@@ -163,14 +163,17 @@ def _decode_direct(st: _LayerStore, query: torch.Tensor, n_rep: int, scaling: fl
     if dt is None or query.stride(3) != 1 or k.stride(2) != D or Hkv * n_rep != Hq:
         return None
     out = torch.empty((B, 1, Hq, D), dtype=query.dtype, device=query.device)
-    ws = kernels.decode_workspace(query.device, B, Hq, Hkv, S, D)
+    # with the length on the device a captured step replays at every later length, so the
+    # workspace is sized once for the buffer's capacity: a capture never has to grow it
+    cap = k.shape[2] if st.lens is not None else S
+    ws = kernels.decode_workspace(query.device, B, Hq, Hkv, cap, D)
     qs = query.stride()
     if st.lens is not None and st.pending is not None:
         k_new, v_new = st.pending
         if k_new.dtype == query.dtype and k_new.shape == (B, Hkv, 1, D):
             # the pending one-token append, inside the decode launch
             st.pending = None
-            wsa = kernels.decode_workspace(query.device, B, Hq, Hkv, S - 1 + 128, D)
+            wsa = kernels.decode_workspace(query.device, B, Hq, Hkv, cap + 128, D)
             rc = _lib.lib().hq_decode_append_int8_len(
                 query.data_ptr(), dt, _lib.strides((qs[0], qs[1], 1), 3), k_new.data_ptr(),
                 v_new.data_ptr(), _lib.strides(k_new.stride()[:3], 3),
