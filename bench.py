@@ -63,7 +63,7 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="layer caches per step (profiling runs use a few; default 28)")
-    ap.add_argument("--only", choices=["all", "decode", "twin", "quant", "prefill", "kstatic"],
+    ap.add_argument("--only", choices=["all", "decode", "twin", "quant", "prefill", "kstatic", "kblock"],
                     default="all",
                     help="profiling: run one kernel family on a small case and exit")
     return ap.parse_args()
@@ -684,7 +684,90 @@ def run_extras(torch, kernels, device, gen, stream, us_int8, peak):
     del k, v, k8, v8
     torch.cuda.empty_cache()
     res["prefill"] = run_prefill(torch, kernels, device, gen, stream)
+    res["kblock"] = run_kblock(torch, kernels, device, gen, stream, us_int8, peak)
     res["model_decode_step"] = run_model_step(torch, device)
+    return res
+
+
+def make_kblock_caches(torch, kernels, n_layers, S, device, gen, block=128):
+    """n_layers block-wise K caches (K per 128-token block and channel, V per token,
+    fp16 V scales) of outlier K and normal V, written by the product's kernel."""
+    caches = []
+    for _ in range(n_layers):
+        k = torch.randn((B, HKV, S, D), generator=gen, device=device)
+        ch = torch.stack([torch.randperm(D, generator=gen, device=device)[:4] for _ in range(B * HKV)])
+        gain = torch.ones((B * HKV, D), device=device).scatter_(1, ch, 20.0).view(B, HKV, 1, D)
+        k = (k * gain).to(torch.bfloat16)
+        v = torch.randn((B, HKV, S, D), generator=gen, device=device).to(torch.bfloat16)
+        c = kernels.kblock_alloc(B, HKV, S, D, block_tokens=block, device=device)
+        kernels.kblock_write(k, v, 0, c)
+        caches.append(c)
+        del k, v
+    return caches
+
+
+def kblock_decode_bytes(b, hq, hkv, s, d, block=128):
+    """K and V codes, fp16 V scales, f32 K block scales, q in and out (bf16)."""
+    return b * (hkv * s * (2 * d + 2) + hkv * (-(-s // block)) * d * 4 + 2 * hq * d * 2)
+
+
+def run_kblock(torch, kernels, device, gen, stream, us_int8, peak, S=S_HEAD):
+    """The opt-in block-wise per-channel K layout: decode at config 2's shape
+    (28 layers per CUDA graph), the bulk write of config 4 and the one-token append."""
+    sm_scale = 1.0 / math.sqrt(D)
+    res = {"workload": f"B={B}, Hq={HQ}, Hkv={HKV}, D={D}, S={S}, 128-token K blocks, "
+                       f"{LAYERS} layers per CUDA graph; write: B=8, Hkv=8, S=32768 bf16"}
+    caches = make_kblock_caches(torch, kernels, LAYERS, S, device, gen)
+    q = torch.randn((LAYERS, B, HQ, D), generator=gen, device=device).to(torch.bfloat16)
+    o = torch.empty_like(q)
+
+    def step():
+        for l, c in enumerate(caches):
+            kernels.kblock_decode(q[l], c, S, sm_scale=sm_scale, out=o[l])
+    with torch.cuda.stream(stream):
+        ms, _ = time_graph(torch, step, 200, 10, stream)
+    us = ms * 1e3 / LAYERS
+    gbs = kblock_decode_bytes(B, HQ, HKV, S, D) / us / 1e3
+    res.update({"decode_us_per_layer": round(us, 3), "decode_gbs": round(gbs, 1),
+                "decode_frac_of_peak": round(gbs / peak, 4),
+                "vs_int8_decode": round(us_int8 / us, 3)})
+    # one-token append into an open block (re-codes the block's channels whose scale grew)
+    c0 = caches[0]
+    kn = torch.randn((B, HKV, 1, D), generator=gen, device=device).to(torch.bfloat16)
+    big = kernels.kblock_alloc(B, HKV, S + 512, D, device=device)
+    kernels.kblock_write(torch.randn((B, HKV, S - 64, D), generator=gen, device=device)
+                         .to(torch.bfloat16), None, 0, big)
+    pos = [S - 64]
+
+    def app():
+        kernels.kblock_write(kn, kn, pos[0], big)
+    with torch.cuda.stream(stream):
+        app()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(64):
+            pos[0] = S - 63 + i
+            app()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    res["append_us"] = round(e0.elapsed_time(e1) * 1e3 / 64, 3)
+    del caches, big, c0
+    torch.cuda.empty_cache()
+    # bulk write of config 4 (K block-wise + V per token)
+    Bw, Hw, Sw = 8, 8, 32768
+    x = torch.randn((Bw, Hw, Sw, D), generator=gen, device=device).to(torch.bfloat16)
+    cw = kernels.kblock_alloc(Bw, Hw, Sw, D, device=device)
+
+    def wr():
+        kernels.kblock_write(x, x, 0, cw)
+    with torch.cuda.stream(stream):
+        mw, _ = time_graph(torch, wr, 20, 3, stream)
+    nbytes = Bw * Hw * Sw * D * (2 + 2 + 1 + 1) + Bw * Hw * Sw * 2 + Bw * Hw * (Sw // 128) * D * 4
+    res.update({"write_us": round(mw * 1e3, 2), "write_gbs": round(nbytes / mw / 1e6, 1),
+                "write_frac_of_peak": round(nbytes / mw / 1e6 / peak, 4)})
+    del x, cw
+    torch.cuda.empty_cache()
     return res
 
 
@@ -819,6 +902,14 @@ def profile_only(args, torch, kernels, device, gen, stream):
                         kernels.int8_decode_attn(q, *c, HQ // HKV, sm_scale=sm_scale, out=o)
                     else:
                         kernels.fp16_decode_attn(q, *c, HQ // HKV, sm_scale=sm_scale, out=o)
+        elif args.only == "kblock":
+            caches = make_kblock_caches(torch, kernels, args.layers, S_HEAD, device, gen)
+            q = torch.randn((B, HQ, D), generator=gen, device=device).to(torch.bfloat16)
+            o = torch.empty_like(q)
+            torch.cuda.synchronize()
+            for _ in range(args.warmup + args.steps):
+                for c in caches:
+                    kernels.kblock_decode(q, c, S_HEAD, sm_scale=sm_scale, out=o)
         elif args.only == "kstatic":
             x = torch.randn((2, 8, 32768, D), generator=gen, device=device).to(torch.bfloat16)
             y = torch.empty(x.shape, dtype=torch.int8, device=device)

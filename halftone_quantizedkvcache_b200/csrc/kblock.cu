@@ -1,0 +1,705 @@
+// Block-wise per-channel K layout (opt-in) for sm_100a: quantize-on-write and
+// split-KV decode attention.
+//
+// The reference quantizes K per channel over the whole prefill and then keeps
+// that first scale for every later append (tests/qwen_kvcache_full.py:54), so a
+// decoded token whose |K| exceeds the prefill's column maximum is clipped to
+// +-127.  Its roadmap names block-wise per-channel K as the production answer
+// (README.md:141).  Here the sequence is cut into blocks of BT tokens (64, 128
+// or 256); each (block, channel) gets its own scale by the reference's
+// quantizer rule (quantize_int8, reference/page_attention_int8_pytorch.py:23-30:
+// RN(max(amax, 1e-8) / 127), codes clamp(rint(x / scale), -127, 127)) applied to
+// the block's tokens.  V stays per token (the reference's rule, reduce over D).
+//
+// The invariant: after any sequence of writes, the codes and scales equal a
+// bulk block-wise quantization of every token written so far (the last block
+// over the tokens it holds).  To keep it across single-token appends the
+// originals of the open (last, incomplete) block are kept in a small tail
+// buffer [B, H, BT, D]; when a new token raises a channel's scale, that
+// channel's earlier codes in the block are re-coded from the originals.  RN is
+// monotone, so max(old scale, RN(max|new| / 127)) is exactly the scale of the
+// block's full column maximum: the stored scale is all the state the rule needs.
+//
+// Decode: a CUDA-core split-KV kernel.  The K scale varies along the contracted
+// dimension per block, so it is folded into q per block (q' = q * s_blk *
+// sm_scale * log2 e, in shared memory, once per 128-token tile); one lane per
+// token forms q' . codes with packed f32x2 FMAs over codes unpacked by byte
+// permutes; an fp32 online softmax per warp; one lane per 4 (D = 128) or 2
+// (D = 64) channels accumulates p * v_scale * codes; the 4 warps merge in shared
+// memory and the splits merge in the last block to finish (arrival ticket).
+#include <algorithm>
+#include <cmath>
+
+#include "hq_common.cuh"
+
+namespace hq {
+
+int current_sm_count();
+
+namespace kb {
+
+constexpr int kWriteThreads = 256;
+constexpr int kDecThreads = 128;   // 4 warps: one 32-token chunk each per 128-token tile
+constexpr int kTile = 128;
+
+struct WriteParams {
+  const void* k;                   // new K rows [B, H, S_new, D] (element strides)
+  int64_t ksb, ksh, kss;
+  const void* v;                   // new V rows (optional)
+  int64_t vsb, vsh, vss;
+  int8_t* kq;                      // K codes, row 0 of the [B, H, capacity, D] buffer
+  int64_t kqb, kqh, kqs;
+  float* ksc;                      // K block scales [B, H, n_blocks, D]
+  int64_t kscb, ksch, kscx;
+  void* kt;                        // K tail [B, H, BT, D]: originals of the open block
+  int64_t ktb, kth, kts;
+  int8_t* vq;                      // V codes, row 0
+  int64_t vqb, vqh, vqs;
+  float* vs32;                     // V scales, row 0 (one of the two, or none)
+  __half* vs16;
+  int64_t vssb, vssh, vsss;
+  int D, BT, pos, S_new, blk0;
+  int tail_mode;                   // 0: write the tail here, 1: leave it, 2: only write it
+};
+
+template <int DT>
+__device__ __forceinline__ void load_pair(const typename Elem<DT>::T* p, float& a, float& b) {
+  a = Elem<DT>::to_f32(p[0]);
+  b = Elem<DT>::to_f32(p[1]);
+}
+
+__device__ __forceinline__ void store_pair(int8_t* dst, int c0, int c1) {
+  *reinterpret_cast<uint16_t*>(dst) =
+      static_cast<uint16_t>((static_cast<uint32_t>(c0) & 0xffu) | ((static_cast<uint32_t>(c1) & 0xffu) << 8));
+}
+
+__device__ __forceinline__ Quantizer quantizer_of_scale(float s) {
+  Quantizer q;
+  q.scale = s;
+  q.rcp = __frcp_rn(s);
+  return q;
+}
+
+// grid (blocks touched, H, B); thread (pair j, group g) owns channels 2j, 2j+1
+// and the block's rows g, g + G, ...
+template <int DT>
+__global__ void __launch_bounds__(kWriteThreads) kblock_write_kernel(WriteParams p) {
+  using E = Elem<DT>;
+  using T = typename E::T;
+  __shared__ float smax[2 * kWriteThreads];
+  const int tid = threadIdx.x;
+  const int P = p.D / 2, G = kWriteThreads / P;
+  const int j = tid % P, g = tid / P;
+  const int c0 = 2 * j;
+  const int blk = p.blk0 + blockIdx.x;
+  const int64_t b = blockIdx.z, h = blockIdx.y;
+  const int r0 = blk * p.BT;
+  const int lo = max(r0, p.pos), hi = min(r0 + p.BT, p.pos + p.S_new);  // new rows here
+  const int n_old = lo - r0;                                             // rows already held
+  const bool keep_tail = hi < r0 + p.BT;   // the block stays open: its originals are kept
+  const T* kin = reinterpret_cast<const T*>(p.k) + b * p.ksb + h * p.ksh;
+  T* tail = reinterpret_cast<T*>(p.kt) + b * p.ktb + h * p.kth;
+
+  if (p.tail_mode == 2) {
+    if (keep_tail)
+      for (int r = lo + g; r < hi; r += G) {
+        const T* x = kin + static_cast<int64_t>(r - p.pos) * p.kss + c0;
+        T* t = tail + static_cast<int64_t>(r - r0) * p.kts + c0;
+        t[0] = x[0];
+        t[1] = x[1];
+      }
+    return;
+  }
+
+  // pass 1: column maxima over the new rows
+  float a0 = 0.0f, a1 = 0.0f;
+  for (int r = lo + g; r < hi; r += G) {
+    float x0, x1;
+    load_pair<DT>(kin + static_cast<int64_t>(r - p.pos) * p.kss + c0, x0, x1);
+    a0 = fmaxf(a0, fabsf(x0));
+    a1 = fmaxf(a1, fabsf(x1));
+  }
+  smax[g * p.D + c0] = a0;
+  smax[g * p.D + c0 + 1] = a1;
+  // the block's stored scales, read before the barrier: group 0 overwrites them below
+  float* sc = p.ksc + b * p.kscb + h * p.ksch + static_cast<int64_t>(blk) * p.kscx + c0;
+  float o0 = 0.0f, o1 = 0.0f;
+  if (n_old > 0) {
+    o0 = sc[0];
+    o1 = sc[1];
+  }
+  __syncthreads();
+  a0 = smax[c0];
+  a1 = smax[c0 + 1];
+  for (int gg = 1; gg < G; ++gg) {
+    a0 = fmaxf(a0, smax[gg * p.D + c0]);
+    a1 = fmaxf(a1, smax[gg * p.D + c0 + 1]);
+  }
+  float s0 = Quantizer::from_amax(a0).scale, s1 = Quantizer::from_amax(a1).scale;
+  bool grew = false;
+  if (n_old > 0) {
+    grew = s0 > o0 || s1 > o1;
+    s0 = fmaxf(s0, o0);
+    s1 = fmaxf(s1, o1);
+  }
+  const Quantizer q0 = quantizer_of_scale(s0), q1 = quantizer_of_scale(s1);
+  int8_t* kq = p.kq + b * p.kqb + h * p.kqh + c0;
+
+  // pass 2: codes of the new rows (and their originals while the block is open)
+  for (int r = lo + g; r < hi; r += G) {
+    const T* xp = kin + static_cast<int64_t>(r - p.pos) * p.kss + c0;
+    float x0, x1;
+    load_pair<DT>(xp, x0, x1);
+    store_pair(kq + static_cast<int64_t>(r) * p.kqs, q0.code(x0), q1.code(x1));
+    if (keep_tail && p.tail_mode == 0) {
+      T* t = tail + static_cast<int64_t>(r - r0) * p.kts + c0;
+      t[0] = xp[0];
+      t[1] = xp[1];
+    }
+  }
+  // earlier rows of the block: re-coded from their originals when a scale grew
+  // (a channel whose scale did not change gets its stored code again)
+  if (grew)
+    for (int r = r0 + g; r < lo; r += G) {
+      float x0, x1;
+      load_pair<DT>(tail + static_cast<int64_t>(r - r0) * p.kts + c0, x0, x1);
+      store_pair(kq + static_cast<int64_t>(r) * p.kqs, q0.code(x0), q1.code(x1));
+    }
+  if (g == 0) {
+    sc[0] = s0;
+    sc[1] = s1;
+  }
+
+  // V per token over D: warp w takes rows lo + w, lo + w + 8, ...
+  if (p.v) {
+    const int w = tid >> 5, lane = tid & 31;
+    const T* vin = reinterpret_cast<const T*>(p.v) + b * p.vsb + h * p.vsh;
+    int8_t* vq = p.vq + b * p.vqb + h * p.vqh;
+    for (int r = lo + w; r < hi; r += kWriteThreads / 32) {
+      const T* xr = vin + static_cast<int64_t>(r - p.pos) * p.vss;
+      float x[8];
+      float m = 0.0f;
+      const int n = p.D / 32;
+      for (int i = 0; i < n; ++i) {
+        x[i] = E::to_f32(xr[lane + 32 * i]);
+        m = fmaxf(m, fabsf(x[i]));
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+      const Quantizer qv = Quantizer::from_amax(m);
+      int8_t* dst = vq + static_cast<int64_t>(r) * p.vqs;
+      for (int i = 0; i < n; ++i) dst[lane + 32 * i] = static_cast<int8_t>(qv.code(x[i]));
+      if (lane == 0) {
+        const int64_t so = b * p.vssb + h * p.vssh + static_cast<int64_t>(r) * p.vsss;
+        if (p.vs32) p.vs32[so] = qv.scale;
+        if (p.vs16) p.vs16[so] = __float2half_rn(qv.scale);
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------ decode
+struct DecParams {
+  const void* q;                    // [B, Hq, D] of q_dtype, d contiguous
+  int64_t qsb, qsh;
+  int q_dtype;
+  const int8_t* kq;
+  int64_t kqb, kqh, kqs;
+  const float* ksc;
+  int64_t kscb, ksch, kscx;
+  const int8_t* vq;
+  int64_t vqb, vqh, vqs;
+  const void* vs;
+  int vs_f16;
+  int64_t vssb, vssh, vsss;
+  void* out;                        // [B, Hq, D] of q_dtype, d contiguous
+  int64_t osb, osh;
+  int Hkv, S, BT, tps, n_split;
+  float qscale;                     // sm_scale * log2(e)
+  float* ws_ml;                     // [B, Hq, n_split, 2] (m, l)
+  float* ws_o;                      // [B, Hq, n_split, D]
+  int* ws_cnt;                      // [B, Hkv] arrival tickets (zero between launches)
+};
+
+__device__ __forceinline__ float load_any(const void* p, int64_t i, int dt) {
+  if (dt == HQ_DTYPE_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
+  if (dt == HQ_DTYPE_F16) return __half2float(reinterpret_cast<const __half*>(p)[i]);
+  return reinterpret_cast<const float*>(p)[i];
+}
+
+__device__ __forceinline__ void store_any(void* p, int64_t i, int dt, float x) {
+  if (dt == HQ_DTYPE_BF16)
+    reinterpret_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(x);
+  else if (dt == HQ_DTYPE_F16)
+    reinterpret_cast<__half*>(p)[i] = __float2half_rn(x);
+  else
+    reinterpret_cast<float*>(p)[i] = x;
+}
+
+__device__ __forceinline__ float f2_sum(F2 x) {
+  float a, b;
+  f2_split(x, a, b);
+  return a + b;
+}
+
+template <int NR, int D>
+struct DecSmem {
+  static constexpr int kQpBlocks = 2;                 // BT = 64: two blocks per tile
+  float qf[NR * D];                                   // q * sm_scale * log2 e
+  float qp[kQpBlocks * NR * D];                       // q' per block of the tile
+  float pv[4][32][NR];                                // p * v_scale per warp and token
+  float wm[4][NR], wl[4][NR];
+  float wo[4][NR][D];
+  int last;
+};
+
+template <int NR, int D>
+__global__ void __launch_bounds__(kDecThreads) kblock_decode_kernel(DecParams p) {
+  constexpr int DPL = D / 32;                         // V channels per lane
+  constexpr int NF = DPL / 2;                         // ... as f32x2 pairs
+  __shared__ __align__(16) DecSmem<NR, D> sm;
+  const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
+  const int hk = blockIdx.x, split = blockIdx.y;
+  const int64_t b = blockIdx.z;
+  const int Hq = p.Hkv * NR;
+  for (int i = tid; i < NR * D; i += kDecThreads) {
+    const int hh = i / D, d = i % D;
+    sm.qf[i] = load_any(p.q, b * p.qsb + static_cast<int64_t>(hk * NR + hh) * p.qsh + d, p.q_dtype) *
+               p.qscale;
+  }
+  const int n_tiles = (p.S + kTile - 1) / kTile;
+  const int t_begin = split * p.tps, t_end = min(n_tiles, t_begin + p.tps);
+  const int8_t* kbase = p.kq + b * p.kqb + hk * p.kqh;
+  const int8_t* vbase = p.vq + b * p.vqb + hk * p.vqh;
+  const float* sbase = p.ksc + b * p.kscb + hk * p.ksch;
+  const int64_t vsbase = b * p.vssb + hk * p.vssh;
+  const int nbq = p.BT < kTile ? kTile / p.BT : 1;   // scale blocks per tile
+
+  float m[NR], l[NR];
+  F2 o[NR][NF];
+#pragma unroll
+  for (int hh = 0; hh < NR; ++hh) {
+    m[hh] = -INFINITY;
+    l[hh] = 0.0f;
+#pragma unroll
+    for (int f = 0; f < NF; ++f) o[hh][f].v = 0ull;
+  }
+
+  for (int tile = t_begin; tile < t_end; ++tile) {
+    const int tok0 = tile * kTile;
+    const int blkA = tok0 / p.BT;
+    __syncthreads();   // q' of the previous tile is no longer read
+    for (int i = tid; i < nbq * NR * D; i += kDecThreads) {
+      const int bi = i / (NR * D), rem = i % (NR * D), d = rem % D;
+      const int blk = blkA + bi;
+      sm.qp[i] = blk * p.BT < p.S ? sm.qf[rem] * sbase[static_cast<int64_t>(blk) * p.kscx + d] : 0.0f;
+    }
+    __syncthreads();
+    const int c0 = tok0 + 32 * w;   // this warp's chunk
+    if (c0 >= p.S) continue;
+    const int t = c0 + lane;
+    const bool valid = t < p.S;
+    const int n_valid = min(32, p.S - c0);
+    const float* qpw = sm.qp + (c0 / p.BT - blkA) * NR * D;
+
+    uint4 kr[D / 16];
+#pragma unroll
+    for (int i = 0; i < D / 16; ++i)
+      kr[i] = valid ? __ldg(reinterpret_cast<const uint4*>(kbase + static_cast<int64_t>(t) * p.kqs) + i)
+                    : make_uint4(0u, 0u, 0u, 0u);
+    uint32_t vr[32];
+#pragma unroll
+    for (int tt = 0; tt < 32; ++tt) {
+      vr[tt] = 0u;
+      if (tt < n_valid) {
+        const int8_t* row = vbase + static_cast<int64_t>(c0 + tt) * p.vqs + lane * DPL;
+        if constexpr (DPL == 4)
+          vr[tt] = __ldg(reinterpret_cast<const uint32_t*>(row));
+        else
+          vr[tt] = __ldg(reinterpret_cast<const uint16_t*>(row));
+      }
+    }
+    float sv = 0.0f;
+    if (valid)
+      sv = p.vs_f16 ? __half2float(reinterpret_cast<const __half*>(p.vs)[vsbase + static_cast<int64_t>(t) * p.vsss])
+                    : reinterpret_cast<const float*>(p.vs)[vsbase + static_cast<int64_t>(t) * p.vsss];
+
+    // scores: q' . codes
+    F2 acc[NR];
+#pragma unroll
+    for (int hh = 0; hh < NR; ++hh) acc[hh].v = 0ull;
+#pragma unroll
+    for (int i = 0; i < D / 16; ++i) {
+      const uint32_t wd[4] = {kr[i].x, kr[i].y, kr[i].z, kr[i].w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        F2 lo2, hi2;
+        s8x4_to_f2x2(wd[e], lo2, hi2);
+        const int d = 16 * i + 4 * e;
+#pragma unroll
+        for (int hh = 0; hh < NR; ++hh) {
+          const ulonglong2 qq = *reinterpret_cast<const ulonglong2*>(qpw + hh * D + d);
+          F2 qa, qb;
+          qa.v = qq.x;
+          qb.v = qq.y;
+          acc[hh] = f2_fma(lo2, qa, acc[hh]);
+          acc[hh] = f2_fma(hi2, qb, acc[hh]);
+        }
+      }
+    }
+    // online softmax (lane 0 of the chunk is always valid, so the maxima are finite)
+#pragma unroll
+    for (int hh = 0; hh < NR; ++hh) {
+      const float s = valid ? f2_sum(acc[hh]) : -INFINITY;
+      float mx = s;
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+      const float mn = fmaxf(m[hh], mx);
+      const float alpha = exp2f(m[hh] - mn);
+      const float pr = valid ? exp2f(s - mn) : 0.0f;
+      l[hh] = l[hh] * alpha + pr;
+      const F2 a2 = f2_make(alpha, alpha);
+#pragma unroll
+      for (int f = 0; f < NF; ++f) o[hh][f] = f2_mul(o[hh][f], a2);
+      m[hh] = mn;
+      sm.pv[w][lane][hh] = pr * sv;
+    }
+    __syncwarp();
+    // V: lane owns channels lane * DPL ..
+#pragma unroll
+    for (int tt = 0; tt < 32; ++tt) {
+      if (tt < n_valid) {
+        F2 c[2];
+        if constexpr (DPL == 4) {
+          s8x4_to_f2x2(vr[tt], c[0], c[1]);
+        } else {
+          F2 hi2;
+          s8x4_to_f2x2(vr[tt], c[0], hi2);
+        }
+#pragma unroll
+        for (int hh = 0; hh < NR; ++hh) {
+          const float pp = sm.pv[w][tt][hh];
+          const F2 p2 = f2_make(pp, pp);
+#pragma unroll
+          for (int f = 0; f < NF; ++f) o[hh][f] = f2_fma(c[f], p2, o[hh][f]);
+        }
+      }
+    }
+    __syncwarp();
+  }
+
+  // merge the 4 warps
+#pragma unroll
+  for (int hh = 0; hh < NR; ++hh) {
+    float lt = l[hh];
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) lt += __shfl_xor_sync(0xffffffffu, lt, off);
+    if (lane == 0) {
+      sm.wm[w][hh] = m[hh];
+      sm.wl[w][hh] = lt;
+    }
+#pragma unroll
+    for (int f = 0; f < NF; ++f) {
+      float a, c;
+      f2_split(o[hh][f], a, c);
+      sm.wo[w][hh][lane * DPL + 2 * f] = a;
+      sm.wo[w][hh][lane * DPL + 2 * f + 1] = c;
+    }
+  }
+  __syncthreads();
+  for (int i = tid; i < NR * D; i += kDecThreads) {
+    const int hh = i / D, d = i % D;
+    float M = -INFINITY;
+#pragma unroll
+    for (int ww = 0; ww < 4; ++ww) M = fmaxf(M, sm.wm[ww][hh]);
+    float L = 0.0f, O = 0.0f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int ww = 0; ww < 4; ++ww) {
+        if (sm.wm[ww][hh] == -INFINITY) continue;
+        const float e = exp2f(sm.wm[ww][hh] - M);
+        L += sm.wl[ww][hh] * e;
+        O += sm.wo[ww][hh][d] * e;
+      }
+    }
+    const int64_t hq = hk * NR + hh;
+    if (p.n_split == 1) {
+      store_any(p.out, b * p.osb + hq * p.osh + d, p.q_dtype, L > 0.0f ? O / L : 0.0f);
+    } else {
+      const int64_t row = (b * Hq + hq) * p.n_split + split;
+      p.ws_o[row * D + d] = O;
+      if (d == 0) {
+        p.ws_ml[2 * row] = M;
+        p.ws_ml[2 * row + 1] = L;
+      }
+    }
+  }
+  if (p.n_split == 1) return;
+  // the last split block of this (sequence, kv head) to arrive merges the splits
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    const int ticket = atomicAdd(p.ws_cnt + b * p.Hkv + hk, 1);
+    sm.last = ticket == p.n_split - 1;
+  }
+  __syncthreads();
+  if (!sm.last) return;
+  __threadfence();
+  for (int i = tid; i < NR * D; i += kDecThreads) {
+    const int hh = i / D, d = i % D;
+    const int64_t hq = hk * NR + hh;
+    const int64_t row0 = (b * Hq + hq) * p.n_split;
+    float M = -INFINITY;
+    for (int s = 0; s < p.n_split; ++s) M = fmaxf(M, __ldcg(p.ws_ml + 2 * (row0 + s)));
+    float L = 0.0f, O = 0.0f;
+    for (int s = 0; s < p.n_split; ++s) {
+      const float ms = __ldcg(p.ws_ml + 2 * (row0 + s));
+      if (ms == -INFINITY) continue;
+      const float e = exp2f(ms - M);
+      L += __ldcg(p.ws_ml + 2 * (row0 + s) + 1) * e;
+      O += __ldcg(p.ws_o + (row0 + s) * D + d) * e;
+    }
+    store_any(p.out, b * p.osb + hq * p.osh + d, p.q_dtype, L > 0.0f ? O / L : 0.0f);
+  }
+  if (tid == 0) p.ws_cnt[b * p.Hkv + hk] = 0;
+}
+
+// ------------------------------------------------------------------ dequant
+__global__ void kblock_dequant_kernel(const int8_t* __restrict__ kq, int64_t kqb, int64_t kqh,
+                                      int64_t kqs, const float* __restrict__ ksc, int64_t kscb,
+                                      int64_t ksch, int64_t kscx, int H, int S, int D, int BT,
+                                      void* __restrict__ out, int odt, int64_t osb, int64_t osh,
+                                      int64_t oss, int64_t n) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t d = i % D, r = i / D;
+    const int64_t s = r % S, bh = r / S;
+    const int64_t h = bh % H, b = bh / H;
+    const float c = static_cast<float>(kq[b * kqb + h * kqh + s * kqs + d]);
+    const float f = ksc[b * kscb + h * ksch + (s / BT) * kscx + d];
+    store_any(out, b * osb + h * osh + s * oss + d, odt, c * f);
+  }
+}
+
+// ------------------------------------------------------------------ host side
+struct Plan {
+  int n_split, tps;
+};
+
+static Plan plan(int B, int Hkv, int S, int sms) {
+  const int n_tiles = (S + kTile - 1) / kTile;
+  const int64_t units = static_cast<int64_t>(B) * Hkv;
+  // about 4 resident blocks of 4 warps per SM
+  int want = static_cast<int>((4LL * sms + units - 1) / units);
+  want = std::max(1, std::min(want, n_tiles));
+  const int tps = (n_tiles + want - 1) / want;
+  return {(n_tiles + tps - 1) / tps, tps};
+}
+
+static size_t al256(size_t n) { return (n + 255) & ~size_t(255); }
+
+static size_t ws_bytes(int B, int Hq, int Hkv, int S, int D, int sms) {
+  const Plan pl = plan(B, Hkv, S, sms);
+  if (pl.n_split <= 1) return 256;
+  const size_t rows = static_cast<size_t>(B) * Hq * pl.n_split;
+  return al256(sizeof(int) * static_cast<size_t>(B) * Hkv) + al256(rows * 2 * sizeof(float)) +
+         al256(rows * D * sizeof(float));
+}
+
+static bool al(const void* ptr, size_t a) { return reinterpret_cast<uintptr_t>(ptr) % a == 0; }
+
+static bool valid_bt(int bt) { return bt == 64 || bt == 128 || bt == 256; }
+
+static int done() {
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? HQ_OK : static_cast<int>(e);
+}
+
+template <int NR, int D>
+static int launch_decode(const DecParams& p, int B, cudaStream_t st) {
+  dim3 grid(p.Hkv, p.n_split, B);
+  kblock_decode_kernel<NR, D><<<grid, kDecThreads, 0, st>>>(p);
+  return done();
+}
+
+}  // namespace kb
+}  // namespace hq
+
+using namespace hq;
+using namespace hq::kb;
+
+extern "C" int hq_kblock_write(const void* k_new, const void* v_new, int x_dtype,
+                               const int64_t k_strides[4], const int64_t v_strides[4], int B,
+                               int H, int pos, int S_new, int D, int block_tokens,
+                               int8_t* k_cache, const int64_t kq_strides[4], float* k_scale,
+                               const int64_t ks_strides[3], void* k_tail,
+                               const int64_t kt_strides[4], int8_t* v_cache,
+                               const int64_t vq_strides[4], float* v_scale_f32,
+                               uint16_t* v_scale_f16, const int64_t vs_strides[3], int capacity,
+                               hq_stream_t stream) {
+  if (!k_new || !k_strides || !k_cache || !kq_strides || !k_scale || !ks_strides || !k_tail ||
+      !kt_strides || B < 0 || H < 0 || pos < 0 || S_new < 1 || capacity < 1 ||
+      static_cast<int64_t>(pos) + S_new > capacity)
+    return HQ_ERR_INVALID_ARGUMENT;
+  if (v_new && (!v_strides || !v_cache || !vq_strides || (!v_scale_f32 && !v_scale_f16) ||
+                !vs_strides || (v_scale_f32 && v_scale_f16)))
+    return HQ_ERR_INVALID_ARGUMENT;
+  if (x_dtype != HQ_DTYPE_BF16 && x_dtype != HQ_DTYPE_F16 && x_dtype != HQ_DTYPE_F32)
+    return HQ_ERR_UNSUPPORTED;
+  if ((D != 64 && D != 128 && D != 256) || !valid_bt(block_tokens)) return HQ_ERR_UNSUPPORTED;
+  if (B == 0 || H == 0) return HQ_OK;
+  // channel pairs: the last dimension contiguous, rows and pairs 2-element aligned
+  if (k_strides[3] != 1 || kq_strides[3] != 1 || ks_strides == nullptr || kt_strides[3] != 1 ||
+      !al(k_cache, 2) || kq_strides[0] % 2 || kq_strides[1] % 2 || kq_strides[2] % 2 ||
+      !al(k_scale, 8) || ks_strides[0] % 2 || ks_strides[1] % 2 || ks_strides[2] % 2)
+    return HQ_ERR_INVALID_ARGUMENT;
+  if (v_new && (v_strides[3] != 1 || vq_strides[3] != 1)) return HQ_ERR_INVALID_ARGUMENT;
+  WriteParams p{};
+  p.k = k_new;
+  p.ksb = k_strides[0]; p.ksh = k_strides[1]; p.kss = k_strides[2];
+  p.v = v_new;
+  if (v_new) {
+    p.vsb = v_strides[0]; p.vsh = v_strides[1]; p.vss = v_strides[2];
+    p.vq = v_cache;
+    p.vqb = vq_strides[0]; p.vqh = vq_strides[1]; p.vqs = vq_strides[2];
+    p.vs32 = v_scale_f32;
+    p.vs16 = reinterpret_cast<__half*>(v_scale_f16);
+    p.vssb = vs_strides[0]; p.vssh = vs_strides[1]; p.vsss = vs_strides[2];
+  }
+  p.kq = k_cache;
+  p.kqb = kq_strides[0]; p.kqh = kq_strides[1]; p.kqs = kq_strides[2];
+  p.ksc = k_scale;
+  p.kscb = ks_strides[0]; p.ksch = ks_strides[1]; p.kscx = ks_strides[2];
+  p.kt = k_tail;
+  p.ktb = kt_strides[0]; p.kth = kt_strides[1]; p.kts = kt_strides[2];
+  p.D = D;
+  p.BT = block_tokens;
+  p.pos = pos;
+  p.S_new = S_new;
+  const int blk0 = pos / block_tokens, blk1 = (pos + S_new - 1) / block_tokens;
+  p.blk0 = blk0;
+  // the first block reads the tail (its earlier rows) while the last one would write
+  // it: when both happen in different blocks the tail is written by a second launch
+  const bool old_rows = pos % block_tokens != 0;
+  const bool open_end = (pos + S_new) % block_tokens != 0;
+  const bool split_tail = blk1 > blk0 && old_rows && open_end;
+  p.tail_mode = split_tail ? 1 : 0;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  dim3 grid(blk1 - blk0 + 1, H, B);
+  switch (x_dtype) {
+    case HQ_DTYPE_BF16: kblock_write_kernel<HQ_DTYPE_BF16><<<grid, kWriteThreads, 0, st>>>(p); break;
+    case HQ_DTYPE_F16: kblock_write_kernel<HQ_DTYPE_F16><<<grid, kWriteThreads, 0, st>>>(p); break;
+    default: kblock_write_kernel<HQ_DTYPE_F32><<<grid, kWriteThreads, 0, st>>>(p); break;
+  }
+  int rc = done();
+  if (rc != HQ_OK || !split_tail) return rc;
+  p.tail_mode = 2;
+  p.blk0 = blk1;
+  p.v = nullptr;
+  dim3 g1(1, H, B);
+  switch (x_dtype) {
+    case HQ_DTYPE_BF16: kblock_write_kernel<HQ_DTYPE_BF16><<<g1, kWriteThreads, 0, st>>>(p); break;
+    case HQ_DTYPE_F16: kblock_write_kernel<HQ_DTYPE_F16><<<g1, kWriteThreads, 0, st>>>(p); break;
+    default: kblock_write_kernel<HQ_DTYPE_F32><<<g1, kWriteThreads, 0, st>>>(p); break;
+  }
+  return done();
+}
+
+extern "C" size_t hq_kblock_decode_workspace_bytes(int B, int Hq, int Hkv, int S, int D) {
+  if (B < 1 || Hkv < 1 || Hq < Hkv || Hq % Hkv || S < 1 || (D != 64 && D != 128)) return 0;
+  return ws_bytes(B, Hq, Hkv, S, D, current_sm_count());
+}
+
+extern "C" int hq_kblock_decode(const void* q, int q_dtype, const int64_t q_strides[3],
+                                const int8_t* k_cache, const int64_t kq_strides[3],
+                                const float* k_scale, const int64_t ks_strides[3],
+                                const int8_t* v_cache, const int64_t vq_strides[3],
+                                const void* v_scale, int scale_dtype,
+                                const int64_t vs_strides[3], int B, int Hq, int Hkv, int S, int D,
+                                int block_tokens, float sm_scale, void* out,
+                                const int64_t out_strides[3], void* workspace,
+                                size_t workspace_bytes, hq_stream_t stream) {
+  if (!q || !q_strides || !k_cache || !kq_strides || !k_scale || !ks_strides || !v_cache ||
+      !vq_strides || !v_scale || !vs_strides || !out || !out_strides || B < 0 || Hkv < 1 ||
+      Hq < Hkv || Hq % Hkv || S < 1)
+    return HQ_ERR_INVALID_ARGUMENT;
+  if (q_dtype != HQ_DTYPE_BF16 && q_dtype != HQ_DTYPE_F16 && q_dtype != HQ_DTYPE_F32)
+    return HQ_ERR_UNSUPPORTED;
+  if (scale_dtype != HQ_DTYPE_F32 && scale_dtype != HQ_DTYPE_F16) return HQ_ERR_UNSUPPORTED;
+  const int NR = Hq / Hkv;
+  if ((D != 64 && D != 128) || !valid_bt(block_tokens) || (NR != 1 && NR != 2 && NR != 4 && NR != 8))
+    return HQ_ERR_UNSUPPORTED;
+  if (B == 0) return HQ_OK;
+  // K rows are read as 16-byte vectors, V by 2 or 4 bytes per lane
+  if (q_strides[2] != 1 || out_strides[2] != 1 || !al(k_cache, 16) || kq_strides[0] % 16 ||
+      kq_strides[1] % 16 || kq_strides[2] % 16 || !al(v_cache, 4) || vq_strides[0] % 4 ||
+      vq_strides[1] % 4 || vq_strides[2] % 4)
+    return HQ_ERR_INVALID_ARGUMENT;
+  const int sms = current_sm_count();
+  const Plan pl = plan(B, Hkv, S, sms);
+  DecParams p{};
+  p.q = q;
+  p.qsb = q_strides[0]; p.qsh = q_strides[1];
+  p.q_dtype = q_dtype;
+  p.kq = k_cache;
+  p.kqb = kq_strides[0]; p.kqh = kq_strides[1]; p.kqs = kq_strides[2];
+  p.ksc = k_scale;
+  p.kscb = ks_strides[0]; p.ksch = ks_strides[1]; p.kscx = ks_strides[2];
+  p.vq = v_cache;
+  p.vqb = vq_strides[0]; p.vqh = vq_strides[1]; p.vqs = vq_strides[2];
+  p.vs = v_scale;
+  p.vs_f16 = scale_dtype == HQ_DTYPE_F16;
+  p.vssb = vs_strides[0]; p.vssh = vs_strides[1]; p.vsss = vs_strides[2];
+  p.out = out;
+  p.osb = out_strides[0]; p.osh = out_strides[1];
+  p.Hkv = Hkv;
+  p.S = S;
+  p.BT = block_tokens;
+  p.tps = pl.tps;
+  p.n_split = pl.n_split;
+  p.qscale = sm_scale * 1.4426950408889634f;
+  if (pl.n_split > 1) {
+    const size_t need = ws_bytes(B, Hq, Hkv, S, D, sms);
+    if (!workspace || workspace_bytes < need || !al(workspace, 256)) return HQ_ERR_WORKSPACE;
+    char* w = static_cast<char*>(workspace);
+    const size_t rows = static_cast<size_t>(B) * Hq * pl.n_split;
+    p.ws_cnt = reinterpret_cast<int*>(w);
+    w += al256(sizeof(int) * static_cast<size_t>(B) * Hkv);
+    p.ws_ml = reinterpret_cast<float*>(w);
+    w += al256(rows * 2 * sizeof(float));
+    p.ws_o = reinterpret_cast<float*>(w);
+  }
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+#define HQ_KB_NR(D_)                                              \
+  switch (NR) {                                                   \
+    case 1: return launch_decode<1, D_>(p, B, st);                \
+    case 2: return launch_decode<2, D_>(p, B, st);                \
+    case 4: return launch_decode<4, D_>(p, B, st);                \
+    default: return launch_decode<8, D_>(p, B, st);               \
+  }
+  if (D == 128) {
+    HQ_KB_NR(128)
+  } else {
+    HQ_KB_NR(64)
+  }
+#undef HQ_KB_NR
+}
+
+extern "C" int hq_kblock_dequant(const int8_t* k_cache, const int64_t kq_strides[3],
+                                 const float* k_scale, const int64_t ks_strides[3], int B, int H,
+                                 int S, int D, int block_tokens, void* out, int out_dtype,
+                                 const int64_t out_strides[4], hq_stream_t stream) {
+  if (!k_cache || !kq_strides || !k_scale || !ks_strides || !out || !out_strides || B < 0 ||
+      H < 0 || S < 0 || D < 1 || !valid_bt(block_tokens) || out_strides[3] != 1)
+    return HQ_ERR_INVALID_ARGUMENT;
+  if (out_dtype != HQ_DTYPE_BF16 && out_dtype != HQ_DTYPE_F16 && out_dtype != HQ_DTYPE_F32)
+    return HQ_ERR_UNSUPPORTED;
+  const int64_t n = static_cast<int64_t>(B) * H * S * D;
+  if (n == 0) return HQ_OK;
+  const int64_t blocks = std::min<int64_t>((n + 255) / 256, 8LL * current_sm_count());
+  kblock_dequant_kernel<<<static_cast<unsigned>(blocks), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      k_cache, kq_strides[0], kq_strides[1], kq_strides[2], k_scale, ks_strides[0], ks_strides[1],
+      ks_strides[2], H, S, D, block_tokens, out, out_dtype, out_strides[0], out_strides[1],
+      out_strides[2], n);
+  return done();
+}

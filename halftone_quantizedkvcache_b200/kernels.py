@@ -617,3 +617,105 @@ def read_status(kind: str = "decode", device=None) -> int:
     dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
     ws = WORKSPACES.get(dev, kind, 4096)
     return _lib.lib().hq_read_status(ws.data_ptr(), _stream(dev))
+
+
+# ---------------------------------------------------------------- block-wise per-channel K
+KBLOCK_TOKENS = (64, 128, 256)
+
+
+def kblock_alloc(B: int, H: int, capacity: int, D: int, *, block_tokens: int = 128,
+                 dtype: torch.dtype = torch.bfloat16, v_scale_dtype: torch.dtype = torch.float16,
+                 device=None) -> dict:
+    """Capacity buffers of a block-wise K cache (the layout ``kblock_write`` /
+    ``kblock_decode`` use): K / V codes ``[B,H,capacity,D]`` int8, K block scales
+    ``[B,H,ceil(capacity/BT),D]`` float32, the K tail ``[B,H,BT,D]`` of ``dtype``
+    (originals of the open block) and V scales ``[B,H,capacity]``."""
+    if block_tokens not in KBLOCK_TOKENS:
+        raise ValueError(f"kblock: block_tokens must be one of {KBLOCK_TOKENS}")
+    dev = torch.device("cuda") if device is None else torch.device(device)
+    nblk = -(-capacity // block_tokens)
+    return {
+        "k": torch.zeros((B, H, capacity, D), dtype=torch.int8, device=dev),
+        "k_scale": torch.zeros((B, H, nblk, D), dtype=torch.float32, device=dev),
+        "k_tail": torch.zeros((B, H, block_tokens, D), dtype=dtype, device=dev),
+        "v": torch.zeros((B, H, capacity, D), dtype=torch.int8, device=dev),
+        "v_scale": torch.zeros((B, H, capacity), dtype=v_scale_dtype, device=dev),
+        "block_tokens": block_tokens,
+    }
+
+
+def kblock_write(k_new: torch.Tensor, v_new: torch.Tensor | None, pos: int, cache: dict) -> None:
+    """Quantize tokens ``pos .. pos+S_new-1`` (``[B,H,S_new,D]``) into a block-wise K
+    cache from ``kblock_alloc`` (``hq_kblock_write``): K per (block, channel), V per
+    token, the open block re-coded when a scale grows.  Writes must come in order."""
+    _check_bhsd(k_new, "kblock_write k")
+    k_new = k_new if k_new.stride(3) == 1 else k_new.contiguous()
+    B, H, S_new, D = k_new.shape
+    kc, ks, kt = cache["k"], cache["k_scale"], cache["k_tail"]
+    if kt.dtype != k_new.dtype:
+        raise TypeError("kblock_write: k_new must have the tail's dtype")
+    vc = vs = None
+    if v_new is not None:
+        _check_bhsd(v_new, "kblock_write v")
+        v_new = v_new if v_new.stride(3) == 1 else v_new.contiguous()
+        if v_new.shape != k_new.shape or v_new.dtype != k_new.dtype:
+            raise ValueError("kblock_write: v_new must match k_new")
+        vc, vs = cache["v"], cache["v_scale"]
+    vs32 = vs if vs is not None and vs.dtype == torch.float32 else None
+    vs16 = vs if vs is not None and vs.dtype == torch.float16 else None
+    rc = _lib.lib().hq_kblock_write(
+        k_new.data_ptr(), v_new.data_ptr() if v_new is not None else None,
+        _dtype_code(k_new, "kblock_write"), _lib.strides(k_new.stride(), 4),
+        _lib.strides(v_new.stride(), 4) if v_new is not None else None, B, H, int(pos), S_new, D,
+        int(cache["block_tokens"]), kc.data_ptr(), _lib.strides(kc.stride(), 4), ks.data_ptr(),
+        _lib.strides(ks.stride()[:3], 3), kt.data_ptr(), _lib.strides(kt.stride(), 4),
+        vc.data_ptr() if vc is not None else None,
+        _lib.strides(vc.stride(), 4) if vc is not None else None,
+        vs32.data_ptr() if vs32 is not None else None,
+        vs16.data_ptr() if vs16 is not None else None,
+        _lib.strides(vs.stride()[:3], 3) if vs is not None else None, kc.shape[2],
+        _stream(k_new.device))
+    check(rc, "hq_kblock_write")
+
+
+def kblock_decode(q: torch.Tensor, cache: dict, S: int, *, sm_scale: float | None = None,
+                  out: torch.Tensor | None = None) -> torch.Tensor:
+    """Decode attention of ``q`` (``[B,Hq,D]`` or ``[B,Hq,1,D]``) over the first ``S``
+    tokens of a block-wise K cache (``hq_kblock_decode``); output in q's layout and dtype."""
+    _cuda(q, "kblock_decode q")
+    qb, restore = _as_bhd(q)
+    if qb.stride(2) != 1:
+        qb = qb.contiguous()
+    B, Hq, D = qb.shape
+    kc, ks, vc, vs = cache["k"], cache["k_scale"], cache["v"], cache["v_scale"]
+    Hkv = kc.shape[1]
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(D)
+    res = out if out is not None else torch.empty((B, Hq, D), dtype=qb.dtype, device=qb.device)
+    nb = _lib.lib().hq_kblock_decode_workspace_bytes(B, Hq, Hkv, max(int(S), 1), D)
+    if nb == 0:
+        raise ValueError(f"kblock_decode: unsupported shape B={B} Hq={Hq} Hkv={Hkv} D={D}")
+    ws = WORKSPACES.get(qb.device, "kblock", nb)
+    rc = _lib.lib().hq_kblock_decode(
+        qb.data_ptr(), _dtype_code(qb, "kblock_decode q"), _lib.strides(qb.stride(), 3),
+        kc.data_ptr(), _lib.strides(kc.stride()[:3], 3), ks.data_ptr(),
+        _lib.strides(ks.stride()[:3], 3), vc.data_ptr(), _lib.strides(vc.stride()[:3], 3),
+        vs.data_ptr(), _dtype_code(vs, "kblock_decode v_scale"), _lib.strides(vs.stride()[:3], 3),
+        B, Hq, Hkv, int(S), D, int(cache["block_tokens"]), float(sm_scale), res.data_ptr(),
+        _lib.strides(res.stride(), 3), ws.data_ptr(), ws.numel(), _stream(qb.device))
+    check(rc, "hq_kblock_decode")
+    return restore(res)
+
+
+def kblock_dequant(cache: dict, S: int, dtype: torch.dtype = torch.float32) -> torch.Tensor:
+    """K of the first ``S`` tokens, dequantized (``hq_kblock_dequant``): ``[B,H,S,D]``."""
+    kc, ks = cache["k"], cache["k_scale"]
+    B, H, _, D = kc.shape
+    out = torch.empty((B, H, int(S), D), dtype=dtype, device=kc.device)
+    rc = _lib.lib().hq_kblock_dequant(
+        kc.data_ptr(), _lib.strides(kc.stride()[:3], 3), ks.data_ptr(),
+        _lib.strides(ks.stride()[:3], 3), B, H, int(S), D, int(cache["block_tokens"]),
+        out.data_ptr(), _dtype_code(out, "kblock_dequant"), _lib.strides(out.stride(), 4),
+        _stream(kc.device))
+    check(rc, "hq_kblock_dequant")
+    return out

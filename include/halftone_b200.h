@@ -406,6 +406,62 @@ HQ_API int hq_decode_int8_peer(const void* q, int q_dtype, const int64_t q_strid
                                int rank, hq_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * Block-wise per-channel K layout (opt-in; the reference's roadmap item
+ * "block-wise per-channel K", README.md:141).  No reference interface is
+ * replaced: these sit beside hq_append_kv / hq_decode_int8 for a cache that
+ * opts in, and remove the retained-first-scale behaviour of
+ * QuantizedKVCache.update (tests/qwen_kvcache_full.py:54).
+ *
+ * Layout (block_tokens BT = 64, 128 or 256):
+ *   k_cache  int8 [B, H, capacity, D]        (row r = token r)
+ *   k_scale  f32  [B, H, ceil(capacity/BT), D] (scale of block r / BT, channel d)
+ *   k_tail   x_dtype [B, H, BT, D]            originals of the open (last,
+ *            incomplete) block, row r % BT; the library's own state
+ *   v_cache / v_scale: as hq_quant_v_pertoken (per token).
+ * Each (block, channel) scale is the reference's rule (quantize_int8,
+ * reference/page_attention_int8_pytorch.py:23-30) over the block's tokens, so
+ * after any sequence of writes the codes and scales equal a bulk block-wise
+ * quantization of every token written so far.
+ *
+ * hq_kblock_write: writes tokens pos .. pos + S_new - 1 (k_new / v_new
+ *   [B, H, S_new, D] of x_dtype, last dim contiguous; v_new may be NULL).  An
+ *   append into an open block re-codes the block's earlier rows of the channels
+ *   whose scale grew, from k_tail.  Writes must be in order (pos = the current
+ *   length).  pos + S_new > capacity -> HQ_ERR_INVALID_ARGUMENT.
+ * hq_kblock_decode: decode attention for q [B, Hq, D] over the first S tokens
+ *   (D = 64 or 128, Hq / Hkv in {1, 2, 4, 8}); kq_strides / vq_strides are the
+ *   (b, h, s) strides of k_cache / v_cache (s a multiple of 16 bytes for K),
+ *   ks_strides the (b, h, block) strides of k_scale, vs_strides the (b, h, s)
+ *   strides of v_scale (scale_dtype F32 or F16).  out [B, Hq, D] of q_dtype.
+ *   workspace: hq_kblock_decode_workspace_bytes(B, Hq, Hkv, S, D) bytes, zero
+ *   when first used (the launch leaves it zero), 256-byte aligned.
+ * hq_kblock_dequant: out[b, h, s, d] = code * k_scale[b, h, s / BT, d] for
+ *   s < S (the read path of a block-wise K cache).
+ */
+HQ_API int hq_kblock_write(const void* k_new, const void* v_new, int x_dtype,
+                           const int64_t k_strides[4], const int64_t v_strides[4], int B, int H,
+                           int pos, int S_new, int D, int block_tokens, int8_t* k_cache,
+                           const int64_t kq_strides[4], float* k_scale,
+                           const int64_t ks_strides[3], void* k_tail,
+                           const int64_t kt_strides[4], int8_t* v_cache,
+                           const int64_t vq_strides[4], float* v_scale_f32,
+                           uint16_t* v_scale_f16, const int64_t vs_strides[3], int capacity,
+                           hq_stream_t stream);
+HQ_API size_t hq_kblock_decode_workspace_bytes(int B, int Hq, int Hkv, int S, int D);
+HQ_API int hq_kblock_decode(const void* q, int q_dtype, const int64_t q_strides[3],
+                            const int8_t* k_cache, const int64_t kq_strides[3],
+                            const float* k_scale, const int64_t ks_strides[3],
+                            const int8_t* v_cache, const int64_t vq_strides[3],
+                            const void* v_scale, int scale_dtype, const int64_t vs_strides[3],
+                            int B, int Hq, int Hkv, int S, int D, int block_tokens,
+                            float sm_scale, void* out, const int64_t out_strides[3],
+                            void* workspace, size_t workspace_bytes, hq_stream_t stream);
+HQ_API int hq_kblock_dequant(const int8_t* k_cache, const int64_t kq_strides[3],
+                             const float* k_scale, const int64_t ks_strides[3], int B, int H,
+                             int S, int D, int block_tokens, void* out, int out_dtype,
+                             const int64_t out_strides[4], hq_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * Reads (and synchronises `stream` for) the device status word at the start
  * of a quantize-K or decode workspace: HQ_OK, or HQ_ERR_DEVICE_TIMEOUT if a
  * bounded device wait gave up during an earlier call on that workspace.

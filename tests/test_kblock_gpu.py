@@ -1,0 +1,177 @@
+"""Block-wise per-channel K layout on the GPU: write, append and decode parity.
+
+Oracle: ``oracle.blockwise`` (the reference quantizer, reference/page_attention_int8_pytorch.py:23-30,
+per block of tokens; a single block is pinned to the reference's golden vectors).
+Codes and scales are bit-exact; the decode output is held to max-abs 1e-3 and
+relative 1e-3 against the float64 oracle in float32, plus bf16 rounding for bf16 output.
+"""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from halftone_quantizedkvcache_b200 import kernels
+from oracle import blockwise as ob
+from oracle import inputs as oin
+from oracle import quant as oq
+
+pytestmark = pytest.mark.gpu
+TDT = {"f32": torch.float32, "bf16": torch.bfloat16, "f16": torch.float16}
+
+
+def dev(x, dt=None):
+    t = torch.from_numpy(np.ascontiguousarray(x))
+    return (t.to(TDT[dt]) if dt else t).cuda()
+
+
+def make(B, H, S, D, dt, seed=0):
+    rng = np.random.default_rng(seed)
+    k = oin.outlier_k(rng, B, H, S, D, dt)
+    v = oin.normal(rng, (B, H, S, D), dt)
+    return k, v
+
+
+def check_cache(cache, k, v, S, block, v_scale_dt):
+    codes, scales = ob.quant_k_blockwise(k[:, :, :S], block)
+    nblk = scales.shape[2]
+    np.testing.assert_array_equal(cache["k"][:, :, :S].cpu().numpy(), codes)
+    np.testing.assert_array_equal(cache["k_scale"][:, :, :nblk].cpu().numpy(), scales)
+    vc, vs = oq.quant_v_pertoken(v[:, :, :S])
+    np.testing.assert_array_equal(cache["v"][:, :, :S].cpu().numpy(), vc)
+    want = vs[..., 0] if v_scale_dt == torch.float32 else oq.to_f16(vs[..., 0])
+    np.testing.assert_array_equal(cache["v_scale"][:, :, :S].cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("dt", ["bf16", "f16", "f32"])
+@pytest.mark.parametrize("D", [64, 128, 256])
+@pytest.mark.parametrize("block", [64, 128, 256])
+def test_bulk_write_bit_exact(dt, D, block):
+    B, H, S = 2, 3, 517
+    k, v = make(B, H, S, D, dt)
+    c = kernels.kblock_alloc(B, H, S + 40, D, block_tokens=block, dtype=TDT[dt],
+                             v_scale_dtype=torch.float32)
+    kernels.kblock_write(dev(k, dt), dev(v, dt), 0, c)
+    check_cache(c, k, v, S, block, torch.float32)
+
+
+def test_golden_single_block_through_the_kernel(golden):
+    g = golden("quant_golden.npz")
+    names = sorted({n.split("/")[0] for n in g.files if "/" in n})
+    for name in names:
+        dt = str(g[f"{name}/dtype"])
+        x = oq.unpack(g[f"{name}/x"], dt)
+        B, H, S, D = x.shape
+        c = kernels.kblock_alloc(B, H, S, D, block_tokens=256, dtype=TDT[dt])
+        kernels.kblock_write(dev(x, dt), dev(x, dt), 0, c)
+        np.testing.assert_array_equal(c["k"].cpu().numpy(), g[f"{name}/k_codes"], err_msg=name)
+        np.testing.assert_array_equal(c["k_scale"][:, :, :1].cpu().numpy(), g[f"{name}/k_scale"],
+                                      err_msg=name)
+        np.testing.assert_array_equal(c["v"].cpu().numpy(), g[f"{name}/v_codes"], err_msg=name)
+        np.testing.assert_array_equal(c["v_scale"].cpu().numpy(), g[f"{name}/v_scale_f16"][..., 0],
+                                      err_msg=name)
+
+
+@pytest.mark.parametrize("block", [64, 128])
+@pytest.mark.parametrize("dt", ["bf16", "f32"])
+def test_token_appends_equal_bulk(block, dt):
+    """Prefill then one token at a time: after every step the cache equals a bulk
+    block-wise quantization of the tokens so far (re-coding the open block)."""
+    B, H, D, P, S = 2, 2, 128, 70, 70 + 2 * block + 9
+    k, v = make(B, H, S, D, dt, seed=4)
+    # make later tokens grow the column maxima often
+    ramp = np.linspace(1.0, 3.0, S, dtype=np.float32)[None, None, :, None]
+    k = oq.cast(k * ramp, dt)
+    c = kernels.kblock_alloc(B, H, S, D, block_tokens=block, dtype=TDT[dt])
+    kd, vd = dev(k, dt), dev(v, dt)
+    kernels.kblock_write(kd[:, :, :P], vd[:, :, :P], 0, c)
+    for t in range(P, S):
+        kernels.kblock_write(kd[:, :, t:t + 1], vd[:, :, t:t + 1], t, c)
+        if t in (P, P + 1, block - 1, block, 2 * block + 3, S - 1):
+            check_cache(c, k, v, t + 1, block, torch.float16)
+
+
+def test_chunked_writes_cross_blocks():
+    """Writes of ragged sizes, including one that starts inside a block and ends
+    inside a later one (the tail written by a second launch), then appends."""
+    B, H, D, block = 1, 4, 128, 64
+    sizes = [37, 5, 150, 64, 1, 90, 1, 1, 33]
+    S = sum(sizes)
+    k, v = make(B, H, S, D, "bf16", seed=7)
+    k = oq.cast(k * np.linspace(0.5, 2.0, S, dtype=np.float32)[None, None, :, None], "bf16")
+    c = kernels.kblock_alloc(B, H, S, D, block_tokens=block)
+    kd, vd = dev(k, "bf16"), dev(v, "bf16")
+    pos = 0
+    for n in sizes:
+        kernels.kblock_write(kd[:, :, pos:pos + n], vd[:, :, pos:pos + n], pos, c)
+        pos += n
+        check_cache(c, k, v, pos, block, torch.float16)
+
+
+def test_write_errors():
+    c = kernels.kblock_alloc(1, 1, 8, 128, block_tokens=64)
+    x = torch.zeros((1, 1, 9, 128), dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(RuntimeError):
+        kernels.kblock_write(x, x, 0, c)           # past the capacity
+    with pytest.raises(ValueError):
+        kernels.kblock_alloc(1, 1, 8, 128, block_tokens=96)
+
+
+def _decode_case(B, Hq, Hkv, S, D, block, q_dt, seed):
+    k, v = make(B, Hkv, S, D, "bf16", seed)
+    q = oin.normal(np.random.default_rng(seed + 1), (B, Hq, D), q_dt)
+    return q, k, v
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,S,D,block", [
+    (1, 16, 8, 1, 128, 128), (1, 16, 8, 5, 128, 64), (2, 16, 8, 129, 128, 128),
+    (1, 8, 8, 1000, 128, 256), (3, 32, 8, 777, 128, 64), (1, 64, 8, 300, 64, 128),
+    (2, 4, 2, 4099, 64, 64), (1, 16, 8, 32768, 128, 128)])
+@pytest.mark.parametrize("q_dt,sc", [("f32", torch.float32), ("bf16", torch.float16)])
+def test_decode_matches_oracle(B, Hq, Hkv, S, D, block, q_dt, sc):
+    q, k, v = _decode_case(B, Hq, Hkv, S, D, block, q_dt, seed=S)
+    c = kernels.kblock_alloc(B, Hkv, S + 17, D, block_tokens=block, v_scale_dtype=sc)
+    kernels.kblock_write(dev(k, "bf16"), dev(v, "bf16"), 0, c)
+    out = kernels.kblock_decode(dev(q, q_dt), c, S).float().cpu().numpy()
+    vs = c["v_scale"][:, :, :S].float().cpu().numpy()
+    codes, scales = ob.quant_k_blockwise(k, block)
+    vc, _ = oq.quant_v_pertoken(v)
+    want = ob.decode_blockwise(q, codes, scales, vc, vs, block)
+    tol = 1e-3 + (2.0 ** -8 if q_dt == "bf16" else 0.0) * np.abs(want)
+    err = np.abs(out - want)
+    assert (err <= tol + 1e-3 * np.abs(want)).all(), f"max err {err.max():.3e}"
+
+
+def test_decode_after_appends_and_dequant():
+    B, Hq, Hkv, D, block, P, S = 1, 16, 8, 128, 64, 100, 180
+    q, k, v = _decode_case(B, Hq, Hkv, S, D, block, "f32", seed=11)
+    c = kernels.kblock_alloc(B, Hkv, S, D, block_tokens=block)
+    kd, vd = dev(k, "bf16"), dev(v, "bf16")
+    kernels.kblock_write(kd[:, :, :P], vd[:, :, :P], 0, c)
+    for t in range(P, S):
+        kernels.kblock_write(kd[:, :, t:t + 1], vd[:, :, t:t + 1], t, c)
+        if t % 20 == 0 or t == S - 1:
+            n = t + 1
+            out = kernels.kblock_decode(dev(q, "f32"), c, n).cpu().numpy()
+            codes, scales = ob.quant_k_blockwise(k[:, :, :n], block)
+            vc, vs = oq.quant_v_pertoken(v[:, :, :n])
+            want = ob.decode_blockwise(q, codes, scales, vc, oq.to_f16(vs[..., 0]), block)
+            np.testing.assert_allclose(out, want, atol=1e-3, rtol=1e-3)
+    deq = kernels.kblock_dequant(c, S).cpu().numpy()
+    codes, scales = ob.quant_k_blockwise(k, block)
+    np.testing.assert_array_equal(deq, ob.dequant_k_blockwise(codes, scales, block))
+
+
+def test_decode_sm_scale_and_unsupported():
+    B, Hq, Hkv, S, D = 1, 16, 8, 257, 128
+    q, k, v = _decode_case(B, Hq, Hkv, S, D, 128, "f32", seed=2)
+    c = kernels.kblock_alloc(B, Hkv, S, D)
+    kernels.kblock_write(dev(k, "bf16"), dev(v, "bf16"), 0, c)
+    out = kernels.kblock_decode(dev(q, "f32"), c, S, sm_scale=0.05).cpu().numpy()
+    codes, scales = ob.quant_k_blockwise(k, 128)
+    vc, vs = oq.quant_v_pertoken(v)
+    want = ob.decode_blockwise(q, codes, scales, vc, oq.to_f16(vs[..., 0]), 128, sm_scale=0.05)
+    np.testing.assert_allclose(out, want, atol=1e-3, rtol=1e-3)
+    q3 = torch.zeros((1, 24, D), device="cuda")
+    with pytest.raises((RuntimeError, ValueError)):
+        kernels.kblock_decode(q3, c, S)   # 24 / 8 = 3 query heads per kv head
