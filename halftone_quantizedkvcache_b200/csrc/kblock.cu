@@ -41,6 +41,7 @@ namespace kb {
 constexpr int kWriteThreads = 256;
 constexpr int kDecThreads = 128;   // 4 warps: one 32-token chunk each per 128-token tile
 constexpr int kTile = 128;
+constexpr int kMaxSplit = 128;     // splits per (sequence, kv head)
 
 struct WriteParams {
   const void* k;                   // new K rows [B, H, S_new, D] (element strides)
@@ -113,6 +114,7 @@ __global__ void __launch_bounds__(kWriteThreads) kblock_write_kernel(WriteParams
 
   // pass 1: column maxima over the new rows
   float a0 = 0.0f, a1 = 0.0f;
+#pragma unroll 8
   for (int r = lo + g; r < hi; r += G) {
     float x0, x1;
     load_pair<DT>(kin + static_cast<int64_t>(r - p.pos) * p.kss + c0, x0, x1);
@@ -146,6 +148,7 @@ __global__ void __launch_bounds__(kWriteThreads) kblock_write_kernel(WriteParams
   int8_t* kq = p.kq + b * p.kqb + h * p.kqh + c0;
 
   // pass 2: codes of the new rows (and their originals while the block is open)
+#pragma unroll 4
   for (int r = lo + g; r < hi; r += G) {
     const T* xp = kin + static_cast<int64_t>(r - p.pos) * p.kss + c0;
     float x0, x1;
@@ -159,12 +162,14 @@ __global__ void __launch_bounds__(kWriteThreads) kblock_write_kernel(WriteParams
   }
   // earlier rows of the block: re-coded from their originals when a scale grew
   // (a channel whose scale did not change gets its stored code again)
-  if (grew)
+  if (grew) {
+#pragma unroll 8
     for (int r = r0 + g; r < lo; r += G) {
       float x0, x1;
       load_pair<DT>(tail + static_cast<int64_t>(r - r0) * p.kts + c0, x0, x1);
       store_pair(kq + static_cast<int64_t>(r) * p.kqs, q0.code(x0), q1.code(x1));
     }
+  }
   if (g == 0) {
     sc[0] = s0;
     sc[1] = s1;
@@ -288,20 +293,13 @@ __global__ void __launch_bounds__(kDecThreads) kblock_decode_kernel(DecParams p)
   for (int tile = t_begin; tile < t_end; ++tile) {
     const int tok0 = tile * kTile;
     const int blkA = tok0 / p.BT;
-    __syncthreads();   // q' of the previous tile is no longer read
-    for (int i = tid; i < nbq * NR * D; i += kDecThreads) {
-      const int bi = i / (NR * D), rem = i % (NR * D), d = rem % D;
-      const int blk = blkA + bi;
-      sm.qp[i] = blk * p.BT < p.S ? sm.qf[rem] * sbase[static_cast<int64_t>(blk) * p.kscx + d] : 0.0f;
-    }
-    __syncthreads();
     const int c0 = tok0 + 32 * w;   // this warp's chunk
-    if (c0 >= p.S) continue;
+    const bool active = c0 < p.S;
     const int t = c0 + lane;
     const bool valid = t < p.S;
-    const int n_valid = min(32, p.S - c0);
-    const float* qpw = sm.qp + (c0 / p.BT - blkA) * NR * D;
-
+    const int n_valid = active ? min(32, p.S - c0) : 0;
+    // the chunk's K row (lane = token) and V rows (lane = channels) are requested
+    // first, so their latency overlaps the q' update below
     uint4 kr[D / 16];
 #pragma unroll
     for (int i = 0; i < D / 16; ++i)
@@ -323,6 +321,15 @@ __global__ void __launch_bounds__(kDecThreads) kblock_decode_kernel(DecParams p)
     if (valid)
       sv = p.vs_f16 ? __half2float(reinterpret_cast<const __half*>(p.vs)[vsbase + static_cast<int64_t>(t) * p.vsss])
                     : reinterpret_cast<const float*>(p.vs)[vsbase + static_cast<int64_t>(t) * p.vsss];
+    __syncthreads();   // q' of the previous tile is no longer read
+    for (int i = tid; i < nbq * NR * D; i += kDecThreads) {
+      const int bi = i / (NR * D), rem = i % (NR * D), d = rem % D;
+      const int blk = blkA + bi;
+      sm.qp[i] = blk * p.BT < p.S ? sm.qf[rem] * sbase[static_cast<int64_t>(blk) * p.kscx + d] : 0.0f;
+    }
+    __syncthreads();
+    if (!active) continue;
+    const float* qpw = sm.qp + (c0 / p.BT - blkA) * NR * D;
 
     // scores: q' . codes
     F2 acc[NR];
@@ -445,21 +452,54 @@ __global__ void __launch_bounds__(kDecThreads) kblock_decode_kernel(DecParams p)
   __syncthreads();
   if (!sm.last) return;
   __threadfence();
+  // split weights 2^(m_s - M) / L per head, one warp per head, all splits in parallel
+  // (the per-warp buffers are free again: every thread is past the loop above)
+  float* wts = &sm.wo[0][0][0];   // [NR][kMaxSplit]
+  for (int hh = w; hh < NR; hh += 4) {
+    const int64_t row0 = (b * Hq + hk * NR + hh) * p.n_split;
+    float mv[kMaxSplit / 32], lv[kMaxSplit / 32];
+    float M = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < kMaxSplit / 32; ++k) {
+      const int s = lane + 32 * k;
+      mv[k] = s < p.n_split ? __ldcg(p.ws_ml + 2 * (row0 + s)) : -INFINITY;
+      lv[k] = s < p.n_split ? __ldcg(p.ws_ml + 2 * (row0 + s) + 1) : 0.0f;
+      M = fmaxf(M, mv[k]);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+    float L = 0.0f;
+#pragma unroll
+    for (int k = 0; k < kMaxSplit / 32; ++k) {
+      mv[k] = mv[k] == -INFINITY ? 0.0f : exp2f(mv[k] - M);
+      L += lv[k] * mv[k];
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+    const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+#pragma unroll
+    for (int k = 0; k < kMaxSplit / 32; ++k) {
+      const int s = lane + 32 * k;
+      if (s < p.n_split) wts[hh * kMaxSplit + s] = mv[k] * inv;
+    }
+  }
+  __syncthreads();
   for (int i = tid; i < NR * D; i += kDecThreads) {
     const int hh = i / D, d = i % D;
     const int64_t hq = hk * NR + hh;
-    const int64_t row0 = (b * Hq + hq) * p.n_split;
-    float M = -INFINITY;
-    for (int s = 0; s < p.n_split; ++s) M = fmaxf(M, __ldcg(p.ws_ml + 2 * (row0 + s)));
-    float L = 0.0f, O = 0.0f;
-    for (int s = 0; s < p.n_split; ++s) {
-      const float ms = __ldcg(p.ws_ml + 2 * (row0 + s));
-      if (ms == -INFINITY) continue;
-      const float e = exp2f(ms - M);
-      L += __ldcg(p.ws_ml + 2 * (row0 + s) + 1) * e;
-      O += __ldcg(p.ws_o + (row0 + s) * D + d) * e;
+    const float* src = p.ws_o + (b * Hq + hq) * p.n_split * D + d;
+    const float* wt = wts + hh * kMaxSplit;
+    float O = 0.0f;
+    int s = 0;
+    for (; s + 8 <= p.n_split; s += 8) {
+      float ov[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) ov[u] = __ldcg(src + static_cast<int64_t>(s + u) * D);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) O += wt[s + u] * ov[u];
     }
-    store_any(p.out, b * p.osb + hq * p.osh + d, p.q_dtype, L > 0.0f ? O / L : 0.0f);
+    for (; s < p.n_split; ++s) O += wt[s] * __ldcg(src + static_cast<int64_t>(s) * D);
+    store_any(p.out, b * p.osb + hq * p.osh + d, p.q_dtype, O);
   }
   if (tid == 0) p.ws_cnt[b * p.Hkv + hk] = 0;
 }
@@ -491,7 +531,7 @@ static Plan plan(int B, int Hkv, int S, int sms) {
   const int64_t units = static_cast<int64_t>(B) * Hkv;
   // about 4 resident blocks of 4 warps per SM
   int want = static_cast<int>((4LL * sms + units - 1) / units);
-  want = std::max(1, std::min(want, n_tiles));
+  want = std::max(1, std::min(std::min(want, n_tiles), kMaxSplit));
   const int tps = (n_tiles + want - 1) / want;
   return {(n_tiles + tps - 1) / tps, tps};
 }
