@@ -737,20 +737,19 @@ def run_kblock(torch, kernels, device, gen, stream, us_int8, peak, S=S_HEAD):
     big = kernels.kblock_alloc(B, HKV, S + 512, D, device=device)
     kernels.kblock_write(torch.randn((B, HKV, S - 64, D), generator=gen, device=device)
                          .to(torch.bfloat16), None, 0, big)
-    pos = [S - 64]
-
-    def app():
-        kernels.kblock_write(kn, kn, pos[0], big)
     with torch.cuda.stream(stream):
-        app()
+        kernels.kblock_write(kn, kn, S - 64, big)   # first launch outside the capture
         torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for i in range(64):   # 64 consecutive tokens: the open block re-coded as it grows
+                kernels.kblock_write(kn, kn, S - 63 + i, big)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        for i in range(64):
-            pos[0] = S - 63 + i
-            app()
+        g.replay()
         e1.record(stream)
         torch.cuda.synchronize()
+        del g
     res["append_us"] = round(e0.elapsed_time(e1) * 1e3 / 64, 3)
     del caches, big, c0
     torch.cuda.empty_cache()

@@ -28,6 +28,7 @@
 // (D = 64) channels accumulates p * v_scale * codes; the 4 warps merge in shared
 // memory and the splits merge in the last block to finish (arrival ticket).
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 
 #include "hq_common.cuh"
@@ -83,13 +84,13 @@ __device__ __forceinline__ Quantizer quantizer_of_scale(float s) {
 
 // grid (blocks touched, H, B); thread (pair j, group g) owns channels 2j, 2j+1
 // and the block's rows g, g + G, ...
-template <int DT>
+template <int DT, int D>
 __global__ void __launch_bounds__(kWriteThreads) kblock_write_kernel(WriteParams p) {
   using E = Elem<DT>;
   using T = typename E::T;
   __shared__ float smax[2 * kWriteThreads];
   const int tid = threadIdx.x;
-  const int P = p.D / 2, G = kWriteThreads / P;
+  constexpr int P = D / 2, G = kWriteThreads / P;
   const int j = tid % P, g = tid / P;
   const int c0 = 2 * j;
   const int blk = p.blk0 + blockIdx.x;
@@ -121,8 +122,8 @@ __global__ void __launch_bounds__(kWriteThreads) kblock_write_kernel(WriteParams
     a0 = fmaxf(a0, fabsf(x0));
     a1 = fmaxf(a1, fabsf(x1));
   }
-  smax[g * p.D + c0] = a0;
-  smax[g * p.D + c0 + 1] = a1;
+  smax[g * D + c0] = a0;
+  smax[g * D + c0 + 1] = a1;
   // the block's stored scales, read before the barrier: group 0 overwrites them below
   float* sc = p.ksc + b * p.kscb + h * p.ksch + static_cast<int64_t>(blk) * p.kscx + c0;
   float o0 = 0.0f, o1 = 0.0f;
@@ -134,8 +135,8 @@ __global__ void __launch_bounds__(kWriteThreads) kblock_write_kernel(WriteParams
   a0 = smax[c0];
   a1 = smax[c0 + 1];
   for (int gg = 1; gg < G; ++gg) {
-    a0 = fmaxf(a0, smax[gg * p.D + c0]);
-    a1 = fmaxf(a1, smax[gg * p.D + c0 + 1]);
+    a0 = fmaxf(a0, smax[gg * D + c0]);
+    a1 = fmaxf(a1, smax[gg * D + c0 + 1]);
   }
   float s0 = Quantizer::from_amax(a0).scale, s1 = Quantizer::from_amax(a1).scale;
   bool grew = false;
@@ -175,29 +176,41 @@ __global__ void __launch_bounds__(kWriteThreads) kblock_write_kernel(WriteParams
     sc[1] = s1;
   }
 
-  // V per token over D: warp w takes rows lo + w, lo + w + 8, ...
+  // V per token over D: warp w takes rows lo + w, lo + w + 8, ..., four rows per round
   if (p.v) {
+    constexpr int kN = D / 32, kR = 4, kWarps = kWriteThreads / 32;
     const int w = tid >> 5, lane = tid & 31;
     const T* vin = reinterpret_cast<const T*>(p.v) + b * p.vsb + h * p.vsh;
     int8_t* vq = p.vq + b * p.vqb + h * p.vqh;
-    for (int r = lo + w; r < hi; r += kWriteThreads / 32) {
-      const T* xr = vin + static_cast<int64_t>(r - p.pos) * p.vss;
-      float x[8];
-      float m = 0.0f;
-      const int n = p.D / 32;
-      for (int i = 0; i < n; ++i) {
-        x[i] = E::to_f32(xr[lane + 32 * i]);
-        m = fmaxf(m, fabsf(x[i]));
+    for (int rb = lo + w; rb < hi; rb += kR * kWarps) {
+      float x[kR][kN], m[kR];
+#pragma unroll
+      for (int u = 0; u < kR; ++u) {
+        const int r = rb + u * kWarps;
+        m[u] = 0.0f;
+#pragma unroll
+        for (int i = 0; i < kN; ++i) {
+          x[u][i] = r < hi ? E::to_f32(vin[static_cast<int64_t>(r - p.pos) * p.vss + lane + 32 * i]) : 0.0f;
+          m[u] = fmaxf(m[u], fabsf(x[u][i]));
+        }
       }
 #pragma unroll
-      for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-      const Quantizer qv = Quantizer::from_amax(m);
-      int8_t* dst = vq + static_cast<int64_t>(r) * p.vqs;
-      for (int i = 0; i < n; ++i) dst[lane + 32 * i] = static_cast<int8_t>(qv.code(x[i]));
-      if (lane == 0) {
-        const int64_t so = b * p.vssb + h * p.vssh + static_cast<int64_t>(r) * p.vsss;
-        if (p.vs32) p.vs32[so] = qv.scale;
-        if (p.vs16) p.vs16[so] = __float2half_rn(qv.scale);
+      for (int u = 0; u < kR; ++u)
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) m[u] = fmaxf(m[u], __shfl_xor_sync(0xffffffffu, m[u], off));
+#pragma unroll
+      for (int u = 0; u < kR; ++u) {
+        const int r = rb + u * kWarps;
+        if (r >= hi) break;
+        const Quantizer qv = Quantizer::from_amax(m[u]);
+        int8_t* dst = vq + static_cast<int64_t>(r) * p.vqs;
+#pragma unroll
+        for (int i = 0; i < kN; ++i) dst[lane + 32 * i] = static_cast<int8_t>(qv.code(x[u][i]));
+        if (lane == 0) {
+          const int64_t so = b * p.vssb + h * p.vssh + static_cast<int64_t>(r) * p.vsss;
+          if (p.vs32) p.vs32[so] = qv.scale;
+          if (p.vs16) p.vs16[so] = __float2half_rn(qv.scale);
+        }
       }
     }
   }
@@ -247,30 +260,45 @@ __device__ __forceinline__ float f2_sum(F2 x) {
   return a + b;
 }
 
+// Dynamic shared memory: a 2-stage ring per warp holding its 32-token chunk of
+// K (rows XOR-swizzled by 16-byte chunk so one-lane-per-token reads are
+// conflict-free) and V, then q, the double-buffered q' and the merge scratch.
 template <int NR, int D>
-struct DecSmem {
-  static constexpr int kQpBlocks = 2;                 // BT = 64: two blocks per tile
-  float qf[NR * D];                                   // q * sm_scale * log2 e
-  float qp[kQpBlocks * NR * D];                       // q' per block of the tile
-  float pv[4][32][NR];                                // p * v_scale per warp and token
-  float wm[4][NR], wl[4][NR];
-  float wo[4][NR][D];
-  int last;
+struct DecLayout {
+  static constexpr int kStages = 2;
+  static constexpr int kStageB = 2 * 32 * D;                // K + V of one chunk
+  static constexpr int kRingB = 4 * kStages * kStageB;
+  static constexpr int kQf = NR * D;                         // floats
+  static constexpr int kQp = 2 * 2 * NR * D;                 // [buffer][block of tile][NR*D]
+  static constexpr int kPv = 4 * 32 * NR;
+  static constexpr int kBytes = kRingB + 4 * (kQf + kQp + kPv + 2 * 4 * NR) + 16;
+  static_assert(4 * NR * D * 4 <= kRingB && NR * kMaxSplit * 4 <= kRingB,
+                "merge scratch aliases the ring");
 };
 
 template <int NR, int D>
 __global__ void __launch_bounds__(kDecThreads) kblock_decode_kernel(DecParams p) {
+  using L = DecLayout<NR, D>;
   constexpr int DPL = D / 32;                         // V channels per lane
   constexpr int NF = DPL / 2;                         // ... as f32x2 pairs
-  __shared__ __align__(16) DecSmem<NR, D> sm;
+  constexpr int CPR = D / 16;                         // 16-byte chunks per row
+  constexpr int kQpPer = (2 * NR * D + kDecThreads - 1) / kDecThreads;
+  extern __shared__ __align__(128) char smem[];
+  float* qf = reinterpret_cast<float*>(smem + L::kRingB);
+  float* qp = qf + L::kQf;
+  float* pvb = qp + L::kQp;
+  float* wmb = pvb + L::kPv;
+  float* wlb = wmb + 4 * NR;
+  int* last = reinterpret_cast<int*>(wlb + 4 * NR);
   const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
   const int hk = blockIdx.x, split = blockIdx.y;
   const int64_t b = blockIdx.z;
   const int Hq = p.Hkv * NR;
+  char* ring = smem + w * L::kStages * L::kStageB;
   for (int i = tid; i < NR * D; i += kDecThreads) {
     const int hh = i / D, d = i % D;
-    sm.qf[i] = load_any(p.q, b * p.qsb + static_cast<int64_t>(hk * NR + hh) * p.qsh + d, p.q_dtype) *
-               p.qscale;
+    qf[i] = load_any(p.q, b * p.qsb + static_cast<int64_t>(hk * NR + hh) * p.qsh + d, p.q_dtype) *
+            p.qscale;
   }
   const int n_tiles = (p.S + kTile - 1) / kTile;
   const int t_begin = split * p.tps, t_end = min(n_tiles, t_begin + p.tps);
@@ -279,6 +307,54 @@ __global__ void __launch_bounds__(kDecThreads) kblock_decode_kernel(DecParams p)
   const float* sbase = p.ksc + b * p.kscb + hk * p.ksch;
   const int64_t vsbase = b * p.vssb + hk * p.vssh;
   const int nbq = p.BT < kTile ? kTile / p.BT : 1;   // scale blocks per tile
+  const int nqp = nbq * NR * D;
+
+  // the K scales of a tile's blocks (into registers) and q' = q * scale (into smem)
+  auto load_ks = [&](int tile, float* r) {
+    const int blkA = tile * kTile / p.BT;
+#pragma unroll
+    for (int k = 0; k < kQpPer; ++k) {
+      const int i = tid + k * kDecThreads;
+      r[k] = 0.0f;
+      if (i < nqp) {
+        const int bi = i / (NR * D), d = i % D;
+        const int blk = blkA + bi;
+        if (blk * p.BT < p.S) r[k] = __ldg(sbase + static_cast<int64_t>(blk) * p.kscx + d);
+      }
+    }
+  };
+  auto store_qp = [&](int buf, const float* r) {
+    float* dst = qp + buf * 2 * NR * D;
+#pragma unroll
+    for (int k = 0; k < kQpPer; ++k) {
+      const int i = tid + k * kDecThreads;
+      if (i < nqp) dst[i] = qf[i % (NR * D)] * r[k];
+    }
+  };
+  // this warp's chunk of a tile: K rows swizzled, V rows plain, one cp.async per 16 bytes
+  auto issue = [&](int tile, int stage) {
+    const int c0 = tile * kTile + 32 * w;
+    if (c0 >= p.S) return;
+    const int nv = min(32, p.S - c0);
+    char* sK = ring + stage * L::kStageB;
+    char* sV = sK + 32 * D;
+#pragma unroll
+    for (int k = 0; k < CPR; ++k) {
+      const int idx = k * 32 + lane, row = idx / CPR, ch = idx % CPR;
+      if (row < nv) {
+        cp_async16(sK + row * D + ((ch ^ (row % CPR)) * 16),
+                   kbase + static_cast<int64_t>(c0 + row) * p.kqs + ch * 16);
+        cp_async16(sV + row * D + ch * 16, vbase + static_cast<int64_t>(c0 + row) * p.vqs + ch * 16);
+      }
+    }
+  };
+  auto load_sv = [&](int tile) {
+    const int t = tile * kTile + 32 * w + lane;
+    if (t >= p.S) return 0.0f;
+    const int64_t o = vsbase + static_cast<int64_t>(t) * p.vsss;
+    return p.vs_f16 ? __half2float(reinterpret_cast<const __half*>(p.vs)[o])
+                    : reinterpret_cast<const float*>(p.vs)[o];
+  };
 
   float m[NR], l[NR];
   F2 o[NR][NF];
@@ -290,110 +366,112 @@ __global__ void __launch_bounds__(kDecThreads) kblock_decode_kernel(DecParams p)
     for (int f = 0; f < NF; ++f) o[hh][f].v = 0ull;
   }
 
-  for (int tile = t_begin; tile < t_end; ++tile) {
-    const int tok0 = tile * kTile;
-    const int blkA = tok0 / p.BT;
-    const int c0 = tok0 + 32 * w;   // this warp's chunk
-    const bool active = c0 < p.S;
-    const int t = c0 + lane;
-    const bool valid = t < p.S;
-    const int n_valid = active ? min(32, p.S - c0) : 0;
-    // the chunk's K row (lane = token) and V rows (lane = channels) are requested
-    // first, so their latency overlaps the q' update below
-    uint4 kr[D / 16];
-#pragma unroll
-    for (int i = 0; i < D / 16; ++i)
-      kr[i] = valid ? __ldg(reinterpret_cast<const uint4*>(kbase + static_cast<int64_t>(t) * p.kqs) + i)
-                    : make_uint4(0u, 0u, 0u, 0u);
-    uint32_t vr[32];
-#pragma unroll
-    for (int tt = 0; tt < 32; ++tt) {
-      vr[tt] = 0u;
-      if (tt < n_valid) {
-        const int8_t* row = vbase + static_cast<int64_t>(c0 + tt) * p.vqs + lane * DPL;
-        if constexpr (DPL == 4)
-          vr[tt] = __ldg(reinterpret_cast<const uint32_t*>(row));
-        else
-          vr[tt] = __ldg(reinterpret_cast<const uint16_t*>(row));
-      }
-    }
-    float sv = 0.0f;
-    if (valid)
-      sv = p.vs_f16 ? __half2float(reinterpret_cast<const __half*>(p.vs)[vsbase + static_cast<int64_t>(t) * p.vsss])
-                    : reinterpret_cast<const float*>(p.vs)[vsbase + static_cast<int64_t>(t) * p.vsss];
-    __syncthreads();   // q' of the previous tile is no longer read
-    for (int i = tid; i < nbq * NR * D; i += kDecThreads) {
-      const int bi = i / (NR * D), rem = i % (NR * D), d = rem % D;
-      const int blk = blkA + bi;
-      sm.qp[i] = blk * p.BT < p.S ? sm.qf[rem] * sbase[static_cast<int64_t>(blk) * p.kscx + d] : 0.0f;
-    }
-    __syncthreads();
-    if (!active) continue;
-    const float* qpw = sm.qp + (c0 / p.BT - blkA) * NR * D;
-
-    // scores: q' . codes
-    F2 acc[NR];
-#pragma unroll
-    for (int hh = 0; hh < NR; ++hh) acc[hh].v = 0ull;
-#pragma unroll
-    for (int i = 0; i < D / 16; ++i) {
-      const uint32_t wd[4] = {kr[i].x, kr[i].y, kr[i].z, kr[i].w};
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        F2 lo2, hi2;
-        s8x4_to_f2x2(wd[e], lo2, hi2);
-        const int d = 16 * i + 4 * e;
-#pragma unroll
-        for (int hh = 0; hh < NR; ++hh) {
-          const ulonglong2 qq = *reinterpret_cast<const ulonglong2*>(qpw + hh * D + d);
-          F2 qa, qb;
-          qa.v = qq.x;
-          qb.v = qq.y;
-          acc[hh] = f2_fma(lo2, qa, acc[hh]);
-          acc[hh] = f2_fma(hi2, qb, acc[hh]);
-        }
-      }
-    }
-    // online softmax (lane 0 of the chunk is always valid, so the maxima are finite)
-#pragma unroll
-    for (int hh = 0; hh < NR; ++hh) {
-      const float s = valid ? f2_sum(acc[hh]) : -INFINITY;
-      float mx = s;
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-      const float mn = fmaxf(m[hh], mx);
-      const float alpha = exp2f(m[hh] - mn);
-      const float pr = valid ? exp2f(s - mn) : 0.0f;
-      l[hh] = l[hh] * alpha + pr;
-      const F2 a2 = f2_make(alpha, alpha);
-#pragma unroll
-      for (int f = 0; f < NF; ++f) o[hh][f] = f2_mul(o[hh][f], a2);
-      m[hh] = mn;
-      sm.pv[w][lane][hh] = pr * sv;
-    }
-    __syncwarp();
-    // V: lane owns channels lane * DPL ..
-#pragma unroll
-    for (int tt = 0; tt < 32; ++tt) {
-      if (tt < n_valid) {
-        F2 c[2];
-        if constexpr (DPL == 4) {
-          s8x4_to_f2x2(vr[tt], c[0], c[1]);
-        } else {
-          F2 hi2;
-          s8x4_to_f2x2(vr[tt], c[0], hi2);
-        }
-#pragma unroll
-        for (int hh = 0; hh < NR; ++hh) {
-          const float pp = sm.pv[w][tt][hh];
-          const F2 p2 = f2_make(pp, pp);
-#pragma unroll
-          for (int f = 0; f < NF; ++f) o[hh][f] = f2_fma(c[f], p2, o[hh][f]);
-        }
-      }
-    }
-    __syncwarp();
+  float ksr[kQpPer];
+  __syncthreads();   // q (qf) is complete before the first q' is formed from it
+  if (t_begin < t_end) {
+    issue(t_begin, 0);
+    load_ks(t_begin, ksr);
+    store_qp(0, ksr);
   }
+  cp_async_commit();
+  float sv = t_begin < t_end ? load_sv(t_begin) : 0.0f;
+  for (int it = 0; t_begin + it < t_end; ++it) {
+    const int tile = t_begin + it, cur = it & 1;
+    __syncthreads();   // q'[cur] is written; q'[cur ^ 1] is no longer read
+    const bool more = tile + 1 < t_end;
+    if (more) {
+      issue(tile + 1, cur ^ 1);
+      load_ks(tile + 1, ksr);
+    }
+    cp_async_commit();
+    const float sv_next = more ? load_sv(tile + 1) : 0.0f;
+    cp_async_wait<1>();   // this tile's chunk has landed
+    __syncwarp();
+    const int tok0 = tile * kTile;
+    const int c0 = tok0 + 32 * w;
+    if (c0 < p.S) {
+      const bool valid = c0 + lane < p.S;
+      const int n_valid = min(32, p.S - c0);
+      const float* qpw = qp + cur * 2 * NR * D + (c0 / p.BT - tok0 / p.BT) * NR * D;
+      const char* sK = ring + cur * L::kStageB;
+      const char* sV = sK + 32 * D;
+      // scores: q' . codes (lane = token)
+      F2 acc[NR], acc2[NR];   // two chains per head (even / odd words)
+#pragma unroll
+      for (int hh = 0; hh < NR; ++hh) acc[hh].v = acc2[hh].v = 0ull;
+#pragma unroll
+      for (int i = 0; i < CPR; ++i) {
+        const uint4 kv = *reinterpret_cast<const uint4*>(sK + lane * D + ((i ^ (lane % CPR)) * 16));
+        const uint32_t wd[4] = {kv.x, kv.y, kv.z, kv.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          F2 lo2, hi2;
+          s8x4_to_f2x2(wd[e], lo2, hi2);
+          const int d = 16 * i + 4 * e;
+#pragma unroll
+          for (int hh = 0; hh < NR; ++hh) {
+            const ulonglong2 qq = *reinterpret_cast<const ulonglong2*>(qpw + hh * D + d);
+            F2 qa, qb;
+            qa.v = qq.x;
+            qb.v = qq.y;
+            if (e & 1) {
+              acc2[hh] = f2_fma(lo2, qa, acc2[hh]);
+              acc2[hh] = f2_fma(hi2, qb, acc2[hh]);
+            } else {
+              acc[hh] = f2_fma(lo2, qa, acc[hh]);
+              acc[hh] = f2_fma(hi2, qb, acc[hh]);
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int hh = 0; hh < NR; ++hh) acc[hh] = f2_add(acc[hh], acc2[hh]);
+      // online softmax (lane 0 of the chunk is always valid, so the maxima are finite)
+#pragma unroll
+      for (int hh = 0; hh < NR; ++hh) {
+        const float sc = valid ? f2_sum(acc[hh]) : -INFINITY;
+        float mx = sc;
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+        const float mn = fmaxf(m[hh], mx);
+        const float alpha = exp2f(m[hh] - mn);
+        const float pr = valid ? exp2f(sc - mn) : 0.0f;
+        l[hh] = l[hh] * alpha + pr;
+        const F2 a2 = f2_make(alpha, alpha);
+#pragma unroll
+        for (int f = 0; f < NF; ++f) o[hh][f] = f2_mul(o[hh][f], a2);
+        m[hh] = mn;
+        pvb[(w * 32 + lane) * NR + hh] = pr * sv;
+      }
+      __syncwarp();
+      // V: lane owns channels lane * DPL ..
+#pragma unroll 8
+      for (int tt = 0; tt < 32; ++tt) {
+        if (tt < n_valid) {
+          uint32_t word;
+          if constexpr (DPL == 4)
+            word = *reinterpret_cast<const uint32_t*>(sV + tt * D + lane * 4);
+          else
+            word = *reinterpret_cast<const uint16_t*>(sV + tt * D + lane * 2);
+          F2 c[2];
+          s8x4_to_f2x2(word, c[0], c[1]);
+#pragma unroll
+          for (int hh = 0; hh < NR; ++hh) {
+            const float pp = pvb[(w * 32 + tt) * NR + hh];
+            const F2 p2 = f2_make(pp, pp);
+#pragma unroll
+            for (int f = 0; f < NF; ++f) o[hh][f] = f2_fma(c[f], p2, o[hh][f]);
+          }
+        }
+      }
+    }
+    if (more) store_qp(cur ^ 1, ksr);
+    sv = sv_next;
+    __syncwarp();   // the stage is refilled only after every lane has read it
+  }
+  cp_async_wait<0>();
+  __syncthreads();   // the ring is free: the merge scratch below aliases it
+  float* wo = reinterpret_cast<float*>(smem);   // [4][NR][D]
 
   // merge the 4 warps
 #pragma unroll
@@ -402,15 +480,15 @@ __global__ void __launch_bounds__(kDecThreads) kblock_decode_kernel(DecParams p)
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) lt += __shfl_xor_sync(0xffffffffu, lt, off);
     if (lane == 0) {
-      sm.wm[w][hh] = m[hh];
-      sm.wl[w][hh] = lt;
+      wmb[w * NR + hh] = m[hh];
+      wlb[w * NR + hh] = lt;
     }
 #pragma unroll
     for (int f = 0; f < NF; ++f) {
       float a, c;
       f2_split(o[hh][f], a, c);
-      sm.wo[w][hh][lane * DPL + 2 * f] = a;
-      sm.wo[w][hh][lane * DPL + 2 * f + 1] = c;
+      wo[(w * NR + hh) * D + lane * DPL + 2 * f] = a;
+      wo[(w * NR + hh) * D + lane * DPL + 2 * f + 1] = c;
     }
   }
   __syncthreads();
@@ -418,15 +496,15 @@ __global__ void __launch_bounds__(kDecThreads) kblock_decode_kernel(DecParams p)
     const int hh = i / D, d = i % D;
     float M = -INFINITY;
 #pragma unroll
-    for (int ww = 0; ww < 4; ++ww) M = fmaxf(M, sm.wm[ww][hh]);
+    for (int ww = 0; ww < 4; ++ww) M = fmaxf(M, wmb[ww * NR + hh]);
     float L = 0.0f, O = 0.0f;
     if (M != -INFINITY) {
 #pragma unroll
       for (int ww = 0; ww < 4; ++ww) {
-        if (sm.wm[ww][hh] == -INFINITY) continue;
-        const float e = exp2f(sm.wm[ww][hh] - M);
-        L += sm.wl[ww][hh] * e;
-        O += sm.wo[ww][hh][d] * e;
+        if (wmb[ww * NR + hh] == -INFINITY) continue;
+        const float e = exp2f(wmb[ww * NR + hh] - M);
+        L += wlb[ww * NR + hh] * e;
+        O += wo[(ww * NR + hh) * D + d] * e;
       }
     }
     const int64_t hq = hk * NR + hh;
@@ -447,14 +525,14 @@ __global__ void __launch_bounds__(kDecThreads) kblock_decode_kernel(DecParams p)
   __syncthreads();
   if (tid == 0) {
     const int ticket = atomicAdd(p.ws_cnt + b * p.Hkv + hk, 1);
-    sm.last = ticket == p.n_split - 1;
+    *last = ticket == p.n_split - 1;
   }
   __syncthreads();
-  if (!sm.last) return;
+  if (!*last) return;
   __threadfence();
   // split weights 2^(m_s - M) / L per head, one warp per head, all splits in parallel
   // (the per-warp buffers are free again: every thread is past the loop above)
-  float* wts = &sm.wo[0][0][0];   // [NR][kMaxSplit]
+  float* wts = wo;   // [NR][kMaxSplit]
   for (int hh = w; hh < NR; hh += 4) {
     const int64_t row0 = (b * Hq + hk * NR + hh) * p.n_split;
     float mv[kMaxSplit / 32], lv[kMaxSplit / 32];
@@ -526,11 +604,11 @@ struct Plan {
   int n_split, tps;
 };
 
-static Plan plan(int B, int Hkv, int S, int sms) {
+static Plan plan(int B, int Hkv, int S, int sms, int per_sm) {
   const int n_tiles = (S + kTile - 1) / kTile;
   const int64_t units = static_cast<int64_t>(B) * Hkv;
-  // about 4 resident blocks of 4 warps per SM
-  int want = static_cast<int>((4LL * sms + units - 1) / units);
+  // one wave: as many splits as leave every block resident at once
+  int want = static_cast<int>(static_cast<int64_t>(per_sm) * sms / units);
   want = std::max(1, std::min(std::min(want, n_tiles), kMaxSplit));
   const int tps = (n_tiles + want - 1) / want;
   return {(n_tiles + tps - 1) / tps, tps};
@@ -538,8 +616,8 @@ static Plan plan(int B, int Hkv, int S, int sms) {
 
 static size_t al256(size_t n) { return (n + 255) & ~size_t(255); }
 
-static size_t ws_bytes(int B, int Hq, int Hkv, int S, int D, int sms) {
-  const Plan pl = plan(B, Hkv, S, sms);
+static size_t ws_bytes(int B, int Hq, int Hkv, int S, int D, int sms, int per_sm) {
+  const Plan pl = plan(B, Hkv, S, sms, per_sm);
   if (pl.n_split <= 1) return 256;
   const size_t rows = static_cast<size_t>(B) * Hq * pl.n_split;
   return al256(sizeof(int) * static_cast<size_t>(B) * Hkv) + al256(rows * 2 * sizeof(float)) +
@@ -555,10 +633,68 @@ static int done() {
   return e == cudaSuccess ? HQ_OK : static_cast<int>(e);
 }
 
+template <int DT>
+static void launch_write_d(const WriteParams& p, dim3 grid, cudaStream_t st) {
+  if (p.D == 64)
+    kblock_write_kernel<DT, 64><<<grid, kWriteThreads, 0, st>>>(p);
+  else if (p.D == 128)
+    kblock_write_kernel<DT, 128><<<grid, kWriteThreads, 0, st>>>(p);
+  else
+    kblock_write_kernel<DT, 256><<<grid, kWriteThreads, 0, st>>>(p);
+}
+
+static int launch_write(const WriteParams& p, int x_dtype, dim3 grid, cudaStream_t st) {
+  if (x_dtype == HQ_DTYPE_BF16)
+    launch_write_d<HQ_DTYPE_BF16>(p, grid, st);
+  else if (x_dtype == HQ_DTYPE_F16)
+    launch_write_d<HQ_DTYPE_F16>(p, grid, st);
+  else
+    launch_write_d<HQ_DTYPE_F32>(p, grid, st);
+  return done();
+}
+
+// Blocks of the decode kernel resident per SM (its dynamic shared memory opted in
+// on first use per device); -1 if the runtime refuses.
+template <int NR, int D>
+static int per_sm_blocks() {
+  constexpr int kSmem = DecLayout<NR, D>::kBytes;
+  static std::atomic<int> cache[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
+  int v = cache[dev].load(std::memory_order_acquire);
+  if (v > 0) return v;
+  if (cudaFuncSetAttribute(kblock_decode_kernel<NR, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           kSmem) != cudaSuccess)
+    return -1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kblock_decode_kernel<NR, D>, kDecThreads,
+                                                    kSmem) != cudaSuccess || n < 1)
+    return -1;
+  cache[dev].store(n, std::memory_order_release);
+  return n;
+}
+
+static int per_sm_for(int NR, int D) {
+  if (D == 128) {
+    switch (NR) {
+      case 1: return per_sm_blocks<1, 128>();
+      case 2: return per_sm_blocks<2, 128>();
+      case 4: return per_sm_blocks<4, 128>();
+      default: return per_sm_blocks<8, 128>();
+    }
+  }
+  switch (NR) {
+    case 1: return per_sm_blocks<1, 64>();
+    case 2: return per_sm_blocks<2, 64>();
+    case 4: return per_sm_blocks<4, 64>();
+    default: return per_sm_blocks<8, 64>();
+  }
+}
+
 template <int NR, int D>
 static int launch_decode(const DecParams& p, int B, cudaStream_t st) {
   dim3 grid(p.Hkv, p.n_split, B);
-  kblock_decode_kernel<NR, D><<<grid, kDecThreads, 0, st>>>(p);
+  kblock_decode_kernel<NR, D><<<grid, kDecThreads, DecLayout<NR, D>::kBytes, st>>>(p);
   return done();
 }
 
@@ -625,29 +761,21 @@ extern "C" int hq_kblock_write(const void* k_new, const void* v_new, int x_dtype
   const bool split_tail = blk1 > blk0 && old_rows && open_end;
   p.tail_mode = split_tail ? 1 : 0;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  dim3 grid(blk1 - blk0 + 1, H, B);
-  switch (x_dtype) {
-    case HQ_DTYPE_BF16: kblock_write_kernel<HQ_DTYPE_BF16><<<grid, kWriteThreads, 0, st>>>(p); break;
-    case HQ_DTYPE_F16: kblock_write_kernel<HQ_DTYPE_F16><<<grid, kWriteThreads, 0, st>>>(p); break;
-    default: kblock_write_kernel<HQ_DTYPE_F32><<<grid, kWriteThreads, 0, st>>>(p); break;
-  }
-  int rc = done();
+  int rc = launch_write(p, x_dtype, dim3(blk1 - blk0 + 1, H, B), st);
   if (rc != HQ_OK || !split_tail) return rc;
   p.tail_mode = 2;
   p.blk0 = blk1;
   p.v = nullptr;
-  dim3 g1(1, H, B);
-  switch (x_dtype) {
-    case HQ_DTYPE_BF16: kblock_write_kernel<HQ_DTYPE_BF16><<<g1, kWriteThreads, 0, st>>>(p); break;
-    case HQ_DTYPE_F16: kblock_write_kernel<HQ_DTYPE_F16><<<g1, kWriteThreads, 0, st>>>(p); break;
-    default: kblock_write_kernel<HQ_DTYPE_F32><<<g1, kWriteThreads, 0, st>>>(p); break;
-  }
-  return done();
+  return launch_write(p, x_dtype, dim3(1, H, B), st);
 }
 
 extern "C" size_t hq_kblock_decode_workspace_bytes(int B, int Hq, int Hkv, int S, int D) {
   if (B < 1 || Hkv < 1 || Hq < Hkv || Hq % Hkv || S < 1 || (D != 64 && D != 128)) return 0;
-  return ws_bytes(B, Hq, Hkv, S, D, current_sm_count());
+  const int NR = Hq / Hkv;
+  if (NR != 1 && NR != 2 && NR != 4 && NR != 8) return 0;
+  const int per_sm = per_sm_for(NR, D);
+  if (per_sm < 1) return 0;
+  return ws_bytes(B, Hq, Hkv, S, D, current_sm_count(), per_sm);
 }
 
 extern "C" int hq_kblock_decode(const void* q, int q_dtype, const int64_t q_strides[3],
@@ -672,11 +800,13 @@ extern "C" int hq_kblock_decode(const void* q, int q_dtype, const int64_t q_stri
   if (B == 0) return HQ_OK;
   // K rows are read as 16-byte vectors, V by 2 or 4 bytes per lane
   if (q_strides[2] != 1 || out_strides[2] != 1 || !al(k_cache, 16) || kq_strides[0] % 16 ||
-      kq_strides[1] % 16 || kq_strides[2] % 16 || !al(v_cache, 4) || vq_strides[0] % 4 ||
-      vq_strides[1] % 4 || vq_strides[2] % 4)
+      kq_strides[1] % 16 || kq_strides[2] % 16 || !al(v_cache, 16) || vq_strides[0] % 16 ||
+      vq_strides[1] % 16 || vq_strides[2] % 16)
     return HQ_ERR_INVALID_ARGUMENT;
   const int sms = current_sm_count();
-  const Plan pl = plan(B, Hkv, S, sms);
+  const int per_sm = per_sm_for(NR, D);
+  if (per_sm < 1) return HQ_ERR_UNSUPPORTED;
+  const Plan pl = plan(B, Hkv, S, sms, per_sm);
   DecParams p{};
   p.q = q;
   p.qsb = q_strides[0]; p.qsh = q_strides[1];
@@ -699,7 +829,7 @@ extern "C" int hq_kblock_decode(const void* q, int q_dtype, const int64_t q_stri
   p.n_split = pl.n_split;
   p.qscale = sm_scale * 1.4426950408889634f;
   if (pl.n_split > 1) {
-    const size_t need = ws_bytes(B, Hq, Hkv, S, D, sms);
+    const size_t need = ws_bytes(B, Hq, Hkv, S, D, sms, per_sm);
     if (!workspace || workspace_bytes < need || !al(workspace, 256)) return HQ_ERR_WORKSPACE;
     char* w = static_cast<char*>(workspace);
     const size_t rows = static_cast<size_t>(B) * Hq * pl.n_split;
