@@ -109,6 +109,44 @@ def _tag(t: torch.Tensor, store: _LayerStore) -> torch.Tensor:
     return t
 
 
+class _BlockStore:
+    """One layer in the block-wise per-channel K layout (``kernels.kblock_alloc``
+    buffers): K per (block of ``block_tokens`` tokens, channel), V per token."""
+
+    __slots__ = ("c", "length")
+
+    def __init__(self, B, H, D, cap, block, dtype, device):
+        self.c = kernels.kblock_alloc(B, H, cap, D, block_tokens=block, dtype=dtype,
+                                      device=device)
+        self.length = 0
+
+    def reserve(self, n: int) -> None:
+        cap = self.c["k"].shape[2]
+        if n <= cap:
+            return
+        B, H, _, D = self.c["k"].shape
+        L, bt = self.length, self.c["block_tokens"]
+        new = kernels.kblock_alloc(B, H, _round_up(max(n, 2 * cap), _ALIGN), D, block_tokens=bt,
+                                   dtype=self.c["k_tail"].dtype,
+                                   v_scale_dtype=self.c["v_scale"].dtype, device=self.c["k"].device)
+        nb = -(-L // bt)
+        for key in ("k", "v", "v_scale"):
+            new[key][:, :, :L].copy_(self.c[key][:, :, :L])
+        new["k_scale"][:, :, :nb].copy_(self.c["k_scale"][:, :, :nb])
+        new["k_tail"].copy_(self.c["k_tail"])
+        self.c = new
+
+    def codes(self):
+        L = self.length
+        return self.c["k"][:, :, :L], self.c["v"][:, :, :L]
+
+    def nbytes(self) -> int:
+        L, bt = self.length, self.c["block_tokens"]
+        k = self.c["k"][:, :, :L]
+        return (2 * k.numel() + 4 * self.c["k_scale"][:, :, :-(-L // bt)].numel()
+                + self.c["v_scale"].element_size() * self.c["v_scale"][:, :, :L].numel())
+
+
 _DTYPES = {torch.float32: _lib.DTYPE_F32, torch.bfloat16: _lib.DTYPE_BF16,
            torch.float16: _lib.DTYPE_F16}
 
@@ -241,8 +279,17 @@ class QuantizedKVCache(DynamicCache):
 
     def __init__(self, mode: str = "auto", capacity: int | None = None,
                  device_lengths: bool = False, fused_prefill: bool = False,
-                 static_k_scale=None, fused_append: bool = False):
+                 static_k_scale=None, fused_append: bool = False,
+                 k_block_tokens: int | None = None):
         super().__init__()
+        if k_block_tokens is not None:
+            if k_block_tokens not in kernels.KBLOCK_TOKENS:
+                raise ValueError(f"k_block_tokens must be one of {kernels.KBLOCK_TOKENS}")
+            if mode != "fused" or device_lengths or static_k_scale is not None or fused_prefill:
+                raise ValueError("k_block_tokens needs mode='fused' and excludes device_lengths, "
+                                 "fused_prefill and static_k_scale")
+        self.k_block_tokens = k_block_tokens
+        self._kblock: dict[int, _BlockStore] = {}
         if mode not in ("auto", "fused", "dequant"):
             raise ValueError(f"mode must be auto, fused or dequant, not {mode!r}")
         if device_lengths and mode != "fused":
@@ -310,6 +357,8 @@ class QuantizedKVCache(DynamicCache):
         if key_states.shape != value_states.shape:
             raise ValueError("QuantizedKVCache.update: key and value shapes differ")
         B, H, S_new, D = key_states.shape
+        if self.k_block_tokens is not None:
+            return self._update_blockwise(key_states, value_states, layer_idx)
         st = self._store.get(layer_idx)
         if st is None:
             cap = _round_up(max(S_new + _ALIGN, self.capacity or 0), _ALIGN)
@@ -370,6 +419,28 @@ class QuantizedKVCache(DynamicCache):
         return (kernels.dequant(k, st.k_sc, key_states.dtype, per_channel=True),
                 kernels.dequant(v, st.v_sc[:, :, :L], value_states.dtype, per_channel=False))
 
+    def _update_blockwise(self, key_states, value_states, layer_idx):
+        """The opt-in block-wise per-channel K layout: every write goes through
+        ``kernels.kblock_write`` (K per block of tokens and channel, the open block
+        re-coded as it grows; V per token).  Returns the codes tagged for the
+        patched attention, which decodes them with ``kernels.kblock_decode``."""
+        B, H, S_new, D = key_states.shape
+        st = self._kblock.get(layer_idx)
+        if st is None:
+            cap = _round_up(max(S_new + _ALIGN, self.capacity or 0), _ALIGN)
+            st = _BlockStore(B, H, D, cap, self.k_block_tokens, key_states.dtype,
+                             key_states.device)
+            self._kblock[layer_idx] = st
+        elif tuple(st.c["k"].shape[:2]) != (B, H) or st.c["k"].shape[3] != D:
+            raise ValueError("QuantizedKVCache.update: batch/head shape changed for this layer")
+        st.reserve(st.length + S_new)
+        kernels.kblock_write(key_states, value_states, st.length, st.c)
+        st.length += S_new
+        k, v = st.codes()
+        k._hq_kblock = st
+        v._hq_kblock = st
+        return k, v
+
     def _static_scale(self, layer_idx):
         s = self.static_k_scale
         if s is None or isinstance(s, torch.Tensor):
@@ -377,15 +448,16 @@ class QuantizedKVCache(DynamicCache):
         return s[layer_idx]
 
     def get_seq_length(self, layer_idx=0, cache_position=None):
-        st = self._store.get(layer_idx)
+        st = self._store.get(layer_idx) or self._kblock.get(layer_idx)
         return st.length if st is not None else 0
 
     def __len__(self):
-        return len(self._store)
+        return len(self._store) + len(self._kblock)
 
     def storage_bytes(self):
-        """int8 codes at 1 B, fp16 scales at 2 B (tests/qwen_kvcache_full.py:75-82)."""
-        b = 0
+        """int8 codes at 1 B, fp16 scales at 2 B (tests/qwen_kvcache_full.py:75-82);
+        block-wise K scales at 4 B."""
+        b = sum(s.nbytes() for s in self._kblock.values())
         for s in self._store.values():
             b += 2 * s.k[:, :, : s.length].numel()
             b += 2 * (s.k_sc.numel() + s.v_sc[:, :, : s.length].numel())
@@ -393,7 +465,8 @@ class QuantizedKVCache(DynamicCache):
 
     def fp16_equiv_bytes(self):
         """Same K/V held in fp16 (tests/qwen_kvcache_full.py:84-89)."""
-        return sum(4 * s.k[:, :, : s.length].numel() for s in self._store.values())
+        return (sum(4 * s.k[:, :, : s.length].numel() for s in self._store.values())
+                + sum(4 * s.codes()[0].numel() for s in self._kblock.values()))
 
 
 # ---------------------------------------------------------------- attention patch
@@ -443,6 +516,25 @@ def _is_causal(mask, Sq: int, S: int) -> bool:
     return bool(ok.all())
 
 
+def _blockwise_attention(module, query, st: _BlockStore, attention_mask, scaling, dropout):
+    """Attention over a block-wise K layer: decode steps with ``kernels.kblock_decode``;
+    multi-token steps on the dequantized cache with the reference's math."""
+    B, Hq, Sq, D = query.shape
+    L = st.length
+    q = _fake_quant(query, Q_DIMS) if Q_DIMS is not None else query
+    if Sq == 1 and not (module.training and dropout > 0.0):
+        if attention_mask is not None and attention_mask.shape[-1] not in (1, L):
+            raise ValueError("quantized_attention_forward: unexpected decode mask width")
+        if attention_mask is not None and attention_mask.shape[-1] == L and L > 1:
+            if bool((attention_mask != 0).any()):
+                raise NotImplementedError("padded decode masks are not supported by the int8 kernel")
+        return kernels.kblock_decode(q[:, :, 0, :], st.c, L, sm_scale=scaling).unsqueeze(1)
+    key = kernels.kblock_dequant(st.c, L, query.dtype)
+    value = kernels.dequant(st.c["v"][:, :, :L], st.c["v_scale"][:, :, :L].unsqueeze(-1),
+                            query.dtype, per_channel=False)
+    return _reference_math(module, q, key, value, attention_mask, scaling, dropout)
+
+
 def quantized_attention_forward(module, query, key, value, attention_mask, scaling=None,
                                 dropout=0.0, **kwargs):
     """Replacement for Qwen3's ``eager_attention_forward`` (tests/qwen_kvcache_full.py:95-113).
@@ -451,6 +543,9 @@ def quantized_attention_forward(module, query, key, value, attention_mask, scali
     """
     if scaling is None:
         scaling = module.head_dim ** -0.5
+    kb = getattr(key, "_hq_kblock", None)
+    if kb is not None:
+        return _blockwise_attention(module, query, kb, attention_mask, scaling, dropout), None
     st = getattr(key, "_hq_store", None)
     B, Hq, Sq, D = query.shape
     if st is not None and Sq == 1 and not (module.training and dropout > 0.0):

@@ -175,3 +175,58 @@ def test_decode_sm_scale_and_unsupported():
     q3 = torch.zeros((1, 24, D), device="cuda")
     with pytest.raises((RuntimeError, ValueError)):
         kernels.kblock_decode(q3, c, S)   # 24 / 8 = 3 query heads per kv head
+
+
+def test_cache_option_stores_the_blockwise_layout():
+    """QuantizedKVCache(k_block_tokens=64): prefill, appends past the first capacity
+    (the buffers grow), the stored layout equal to the oracle's bulk quantization."""
+    from halftone_quantizedkvcache_b200.integration import QuantizedKVCache
+    B, H, D, P, S = 1, 2, 128, 100, 600
+    k, v = make(B, H, S, D, "bf16", seed=9)
+    k = oq.cast(k * np.linspace(1.0, 2.5, S, dtype=np.float32)[None, None, :, None], "bf16")
+    kd, vd = dev(k, "bf16"), dev(v, "bf16")
+    cache = QuantizedKVCache(mode="fused", k_block_tokens=64)
+    cache.update(kd[:, :, :P], vd[:, :, :P], 0)
+    for t in range(P, S):
+        kc, _ = cache.update(kd[:, :, t:t + 1], vd[:, :, t:t + 1], 0)
+    assert cache.get_seq_length(0) == S and kc.shape[2] == S
+    st = cache._kblock[0]
+    check_cache(st.c, k, v, S, 64, torch.float16)
+    with pytest.raises(ValueError):
+        QuantizedKVCache(mode="dequant", k_block_tokens=64)
+
+
+def test_whole_model_blockwise_is_closer_to_unquantized_than_reference_rule():
+    """A 2-layer Qwen3-shaped model (random init, bf16): prefill 64, decode 48.
+    The block-wise layout re-scales each block, so decoded K is not clipped to the
+    prefill's column maxima the way the reference's retained first scale clips it
+    (tests/qwen_kvcache_full.py:54): its logits stay closer to the unquantized model's."""
+    from transformers import DynamicCache, Qwen3ForCausalLM
+
+    from halftone_quantizedkvcache_b200.integration import QuantizedKVCache, installed
+    from oracle.hf_reference import qwen3_config
+    cfg = qwen3_config(num_layers=2)
+    cfg._attn_implementation = "eager"
+    torch.manual_seed(0)
+    with torch.device("cuda"):
+        model = Qwen3ForCausalLM(cfg).to(torch.bfloat16).eval()
+    g = torch.Generator().manual_seed(1)
+    n0, nd = 64, 48
+    ids = torch.randint(0, cfg.vocab_size, (1, n0 + nd), generator=g).cuda()
+
+    @torch.no_grad()
+    def run(cache):
+        out = [model(ids[:, :n0], past_key_values=cache, use_cache=True).logits[:, -1]]
+        for t in range(n0, n0 + nd):
+            out.append(model(ids[:, t:t + 1], past_key_values=cache, use_cache=True).logits[:, -1])
+        return torch.stack(out, 1).float()
+
+    full = run(DynamicCache())
+    with installed():
+        blk = run(QuantizedKVCache(mode="fused", k_block_tokens=128))
+        ref = run(QuantizedKVCache(mode="fused"))
+    e_blk = (blk - full)[:, 1:].abs().mean().item()
+    e_ref = (ref - full)[:, 1:].abs().mean().item()
+    print(f"decode logit error vs unquantized: block-wise {e_blk:.4f}, reference rule {e_ref:.4f}")
+    assert torch.isfinite(blk).all()
+    assert e_blk < e_ref
