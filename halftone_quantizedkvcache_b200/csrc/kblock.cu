@@ -724,6 +724,7 @@ extern "C" int hq_kblock_write(const void* k_new, const void* v_new, int x_dtype
     return HQ_ERR_UNSUPPORTED;
   if ((D != 64 && D != 128 && D != 256) || !valid_bt(block_tokens)) return HQ_ERR_UNSUPPORTED;
   if (B == 0 || H == 0) return HQ_OK;
+  if (B > 65535 || H > 65535) return HQ_ERR_UNSUPPORTED;   // grid z / y limits
   // channel pairs: the last dimension contiguous, rows and pairs 2-element aligned
   if (k_strides[3] != 1 || kq_strides[3] != 1 || ks_strides == nullptr || kt_strides[3] != 1 ||
       !al(k_cache, 2) || kq_strides[0] % 2 || kq_strides[1] % 2 || kq_strides[2] % 2 ||
@@ -798,6 +799,7 @@ extern "C" int hq_kblock_decode(const void* q, int q_dtype, const int64_t q_stri
   if ((D != 64 && D != 128) || !valid_bt(block_tokens) || (NR != 1 && NR != 2 && NR != 4 && NR != 8))
     return HQ_ERR_UNSUPPORTED;
   if (B == 0) return HQ_OK;
+  if (B > 65535) return HQ_ERR_UNSUPPORTED;   // grid z limit
   // K rows are read as 16-byte vectors, V by 2 or 4 bytes per lane
   if (q_strides[2] != 1 || out_strides[2] != 1 || !al(k_cache, 16) || kq_strides[0] % 16 ||
       kq_strides[1] % 16 || kq_strides[2] % 16 || !al(v_cache, 16) || vq_strides[0] % 16 ||

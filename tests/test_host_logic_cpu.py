@@ -86,3 +86,51 @@ def test_cache_option_combinations():
         QuantizedKVCache(mode="auto", fused_prefill=True)
     with pytest.raises(ValueError):
         QuantizedKVCache(mode="fused", device_lengths=True, static_k_scale=torch.ones(8, 128))
+
+
+def test_blockwise_entry_points_reject_bad_arguments():
+    """hq_kblock_*: argument checks that return before any launch."""
+    L = _lib.lib()
+    st3 = _lib.strides((0, 0, 128), 3)
+    st4 = _lib.strides((0, 0, 128, 1), 4)
+
+    def write(**kw):
+        a = dict(k=16, v=16, dt=1, ks=st4, vs=st4, B=1, H=8, pos=0, n=4, D=128, bt=128, kc=16,
+                 kqs=st4, ksc=16, kscs=st3, kt=16, kts=st4, vc=16, vqs=st4, v32=None, v16=16,
+                 vss=st3, cap=256)
+        a.update(kw)
+        return L.hq_kblock_write(*a.values(), None)
+    assert write(k=None) == -1                 # no K input
+    assert write(pos=254) == -1                # past the capacity
+    assert write(bt=96) == -2                  # block size not compiled in
+    assert write(D=96) == -2
+    assert write(dt=3) == -2                   # int8 input
+    assert write(v32=16) == -1                 # both V scale dtypes
+    assert write(B=70000) == -2                # grid limit
+    assert write(B=0) == 0                     # nothing to do
+
+    def decode(**kw):
+        a = dict(q=16, qdt=1, qs=st3, kc=16, kqs=st3, ksc=16, kscs=st3, vc=16, vqs=st3, vsc=16,
+                 sdt=2, vss=st3, B=1, Hq=16, Hkv=8, S=64, D=128, bt=128, sm=0.1, out=16, os=st3,
+                 ws=None, wsb=0)
+        a.update(kw)
+        return L.hq_kblock_decode(*a.values(), None)
+    assert decode(Hq=24) == -2                 # 3 query heads per kv head
+    assert decode(sdt=3) == -2                 # int8 V scales
+    assert decode(S=0) == -1
+    assert decode(B=70000) == -2
+    assert decode(B=0) == 0
+    assert L.hq_kblock_decode_workspace_bytes(1, 24, 8, 64, 128) == 0
+    assert L.hq_kblock_dequant(16, st3, 16, st3, 1, 8, 64, 128, 96, 16, 1, st4, None) == -1
+    assert L.hq_kblock_dequant(16, st3, 16, st3, 1, 8, 0, 128, 128, 16, 1, st4, None) == 0
+
+
+def test_blockwise_cache_option_combinations():
+    with pytest.raises(ValueError):
+        QuantizedKVCache(mode="fused", k_block_tokens=96)
+    with pytest.raises(ValueError):
+        QuantizedKVCache(mode="auto", k_block_tokens=128)
+    with pytest.raises(ValueError):
+        QuantizedKVCache(mode="fused", k_block_tokens=128, device_lengths=True)
+    c = QuantizedKVCache(mode="fused", k_block_tokens=64)
+    assert c.get_seq_length(0) == 0 and len(c) == 0 and c.storage_bytes() == 0
