@@ -644,6 +644,20 @@ def kblock_alloc(B: int, H: int, capacity: int, D: int, *, block_tokens: int = 1
     }
 
 
+def _kblock_check(cache: dict, device, B: int, H: int, D: int, what: str) -> None:
+    """The cache's buffers must match the call's (B, H, D) and device: the library
+    addresses them from the call's counts and cannot see their sizes."""
+    kc = cache["k"]
+    cap, bt = kc.shape[2], cache["block_tokens"]
+    want = {"k": (B, H, cap, D), "v": (B, H, cap, D), "k_scale": (B, H, -(-cap // bt), D),
+            "k_tail": (B, H, bt, D), "v_scale": (B, H, cap)}
+    for name, shape in want.items():
+        t = cache[name]
+        if tuple(t.shape) != shape or t.device != device:
+            raise ValueError(f"{what}: cache['{name}'] is {tuple(t.shape)} on {t.device}, "
+                             f"expected {shape} on {device}")
+
+
 def kblock_write(k_new: torch.Tensor, v_new: torch.Tensor | None, pos: int, cache: dict) -> None:
     """Quantize tokens ``pos .. pos+S_new-1`` (``[B,H,S_new,D]``) into a block-wise K
     cache from ``kblock_alloc`` (``hq_kblock_write``): K per (block, channel), V per
@@ -654,6 +668,10 @@ def kblock_write(k_new: torch.Tensor, v_new: torch.Tensor | None, pos: int, cach
     kc, ks, kt = cache["k"], cache["k_scale"], cache["k_tail"]
     if kt.dtype != k_new.dtype:
         raise TypeError("kblock_write: k_new must have the tail's dtype")
+    _kblock_check(cache, k_new.device, B, H, D, "kblock_write")
+    if int(pos) < 0 or int(pos) + S_new > kc.shape[2]:
+        raise ValueError(f"kblock_write: tokens {int(pos)}..{int(pos) + S_new - 1} are outside "
+                         f"the capacity {kc.shape[2]}")
     vc = vs = None
     if v_new is not None:
         _check_bhsd(v_new, "kblock_write v")
@@ -689,6 +707,11 @@ def kblock_decode(q: torch.Tensor, cache: dict, S: int, *, sm_scale: float | Non
     B, Hq, D = qb.shape
     kc, ks, vc, vs = cache["k"], cache["k_scale"], cache["v"], cache["v_scale"]
     Hkv = kc.shape[1]
+    _kblock_check(cache, qb.device, B, Hkv, D, "kblock_decode")
+    if Hq % Hkv:
+        raise ValueError(f"kblock_decode: {Hq} query heads over {Hkv} kv heads")
+    if not 1 <= int(S) <= kc.shape[2]:
+        raise ValueError(f"kblock_decode: S={int(S)} outside 1..{kc.shape[2]} (the capacity)")
     if sm_scale is None:
         sm_scale = 1.0 / math.sqrt(D)
     res = out if out is not None else torch.empty((B, Hq, D), dtype=qb.dtype, device=qb.device)
@@ -711,6 +734,8 @@ def kblock_dequant(cache: dict, S: int, dtype: torch.dtype = torch.float32) -> t
     """K of the first ``S`` tokens, dequantized (``hq_kblock_dequant``): ``[B,H,S,D]``."""
     kc, ks = cache["k"], cache["k_scale"]
     B, H, _, D = kc.shape
+    if not 0 <= int(S) <= kc.shape[2]:
+        raise ValueError(f"kblock_dequant: S={int(S)} outside 0..{kc.shape[2]} (the capacity)")
     out = torch.empty((B, H, int(S), D), dtype=dtype, device=kc.device)
     rc = _lib.lib().hq_kblock_dequant(
         kc.data_ptr(), _lib.strides(kc.stride()[:3], 3), ks.data_ptr(),

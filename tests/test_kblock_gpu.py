@@ -230,3 +230,24 @@ def test_whole_model_blockwise_is_closer_to_unquantized_than_reference_rule():
     print(f"decode logit error vs unquantized: block-wise {e_blk:.4f}, reference rule {e_ref:.4f}")
     assert torch.isfinite(blk).all()
     assert e_blk < e_ref
+
+
+def test_wrappers_check_shapes_against_the_cache():
+    """The library cannot see buffer sizes: the wrappers reject calls whose counts
+    do not match the cache before anything is launched."""
+    c = kernels.kblock_alloc(1, 8, 256, 128)
+    x = torch.zeros((2, 8, 4, 128), dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(ValueError):
+        kernels.kblock_write(x, x, 0, c)                       # two sequences, cache of one
+    y = torch.zeros((1, 8, 4, 128), dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(ValueError):
+        kernels.kblock_write(y, y, 254, c)                     # past the capacity
+    kernels.kblock_write(y, y, 0, c)
+    q = torch.zeros((2, 16, 128), dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(ValueError):
+        kernels.kblock_decode(q, c, 4)                         # two sequences
+    with pytest.raises(ValueError):
+        kernels.kblock_decode(q[:1], c, 257)                   # past the capacity
+    with pytest.raises(ValueError):
+        kernels.kblock_dequant(c, 300)
+    assert kernels.kblock_decode(q[:1], c, 4).shape == (1, 16, 128)
