@@ -396,6 +396,20 @@ def _kv_strides(k, v):
     return _lib.strides((k.stride(0), k.stride(1), k.stride(2)), 3)
 
 
+def _check_cache_shapes(what: str, B: int, D: int, k4, v4, ks4=None, vs4=None) -> None:
+    """The library addresses K/V and their scales from the call's counts alone, so each
+    tensor must have the shape those counts imply: K and V ``[B,Hkv,S,D]`` (B and D
+    those of q), K scales ``[B,Hkv,1,D]``, V scales ``[B,Hkv,S,1]``."""
+    _, Hkv, S, _ = k4.shape
+    bad = k4.shape[0] != B or k4.shape[3] != D or tuple(v4.shape) != tuple(k4.shape)
+    if ks4 is not None:
+        bad = bad or tuple(ks4.shape) != (B, Hkv, 1, D) or tuple(vs4.shape) != (B, Hkv, S, 1)
+    if bad:
+        shapes = ", ".join(f"{n} {tuple(t.shape)}" for n, t in
+                           (("k", k4), ("v", v4), ("k_sc", ks4), ("v_sc", vs4)) if t is not None)
+        raise ValueError(f"{what}: shapes disagree with q's B={B}, D={D}: {shapes}")
+
+
 def int8_decode_attn(q, k_i8, k_sc, v_i8, v_sc, n_rep=None, *, sm_scale=None, q_quant=False,
                      out=None, partial_out=None, peers=None, seq_len=None, s_plan=None,
                      overlap_prev=False, append=None):
@@ -439,6 +453,11 @@ def int8_decode_attn(q, k_i8, k_sc, v_i8, v_sc, n_rep=None, *, sm_scale=None, q_
     _, Hkv, S, _ = k4.shape
     if k4.dtype != torch.int8 or v4.dtype != torch.int8:
         raise TypeError("int8_decode_attn: K/V must be int8")
+    _check_cache_shapes("int8_decode_attn", B, D, k4, v4, ks4, vs4)
+    if out is not None and tuple(out.shape) != (B, Hq, D):
+        raise ValueError(f"int8_decode_attn: out must be [B,Hq,D] = {(B, Hq, D)}")
+    if partial_out is not None and tuple(partial_out.shape) != (B, Hq, D + 2):
+        raise ValueError(f"int8_decode_attn: partial_out must be [B,Hq,D+2] = {(B, Hq, D + 2)}")
     if ks4.dtype != vs4.dtype or ks4.dtype not in (torch.float16, torch.float32):
         raise TypeError("int8_decode_attn: scales must both be float16 or float32")
     if n_rep is not None and n_rep * Hkv != Hq:
@@ -536,6 +555,7 @@ def int8_prefill_attn(q, k_i8, k_sc, v_i8, v_sc, n_rep=None, *, sm_scale=None, q
         raise TypeError("int8_prefill_attn: K/V must be int8")
     if k_sc.dtype != v_sc.dtype or k_sc.dtype not in (torch.float16, torch.float32):
         raise TypeError("int8_prefill_attn: scales must both be float16 or float32")
+    _check_cache_shapes("int8_prefill_attn", B, D, k_i8, v_i8, k_sc, v_sc)
     if n_rep is not None and n_rep * Hkv != Hq:
         raise ValueError("int8_prefill_attn: n_rep * H_kv != H_q")
     if sm_scale is None:
@@ -570,6 +590,11 @@ def fp16_decode_attn(q, k, v, n_rep=None, *, sm_scale=None, q_quant=False, out=N
     _, Hkv, S, _ = k4.shape
     if not (k4.dtype == v4.dtype == qb.dtype) or k4.dtype not in (torch.float16, torch.bfloat16):
         raise TypeError("fp16_decode_attn: q, K, V must all be float16 or all bfloat16")
+    _check_cache_shapes("fp16_decode_attn", B, D, k4, v4)
+    if out is not None and tuple(out.shape) != (B, Hq, D):
+        raise ValueError(f"fp16_decode_attn: out must be [B,Hq,D] = {(B, Hq, D)}")
+    if partial_out is not None and tuple(partial_out.shape) != (B, Hq, D + 2):
+        raise ValueError(f"fp16_decode_attn: partial_out must be [B,Hq,D+2] = {(B, Hq, D + 2)}")
     if n_rep is not None and n_rep * Hkv != Hq:
         raise ValueError("fp16_decode_attn: n_rep * H_kv != H_q")
     if sm_scale is None:

@@ -210,3 +210,25 @@ def test_overlapped_launches_match_serial(S):
     assert torch.equal(serial, over)
     assert kernels.read_status("decode") == 0
     del g
+
+
+def test_wrappers_reject_shapes_that_disagree():
+    """The library reads K/V and scales by the call's counts: the torch wrappers
+    reject tensors whose shapes disagree with q before anything is launched."""
+    q = torch.zeros((2, 16, 128), dtype=torch.bfloat16, device="cuda")
+    k = torch.zeros((1, 8, 64, 128), dtype=torch.int8, device="cuda")
+    ks = torch.ones((1, 8, 1, 128), device="cuda")
+    vs = torch.ones((1, 8, 64, 1), device="cuda")
+    with pytest.raises(ValueError):
+        kernels.int8_decode_attn(q, k, ks, k, vs, 2)              # two sequences, cache of one
+    with pytest.raises(ValueError):
+        kernels.int8_decode_attn(q[:1], k, ks, k, vs[:, :, :32], 2)  # V scales of 32 tokens
+    with pytest.raises(ValueError):
+        kernels.int8_decode_attn(q[:1], k, ks, k, vs, 2, out=torch.empty_like(q))
+    d = torch.zeros((1, 8, 64, 128), dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(ValueError):
+        kernels.fp16_decode_attn(q, d, d, 2)
+    qp = torch.zeros((1, 16, 8, 64), dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(ValueError):
+        kernels.int8_prefill_attn(qp, k, ks, k, vs, 2)            # head dim 64 against 128
+    assert kernels.int8_decode_attn(q[:1], k, ks, k, vs, 2).shape == (1, 16, 128)
