@@ -75,3 +75,18 @@ def test_blockwise_keeps_a_large_decoded_token():
     codes, scales = ob.quant_k_blockwise(seq, 128)
     deq = ob.dequant_k_blockwise(codes, scales, 128)
     assert abs(deq[0, 0, -1, 5] - 40.0) < 40.0 / 127
+
+
+def test_blockwise_decode_oracle_is_the_reference_path_for_one_block():
+    """With one block covering the sequence, the block-wise decode oracle is the
+    reference path's decode (per-channel K, reference/page_attention_int8_pytorch.py:23-34
+    then reference/page_attention_reference.py:31-54), which the golden vectors pin."""
+    from oracle import attention as oa
+    from oracle import inputs as oin
+    c = oin.decode_case(5, 2, 16, 8, 200, 128)
+    codes, scales = ob.quant_k_blockwise(c["k"], 256)
+    np.testing.assert_array_equal(codes, c["k_i8"])
+    np.testing.assert_array_equal(scales, c["k_sc"][:, :, 0:1, :].reshape(scales.shape))
+    got = ob.decode_blockwise(c["q"], codes, scales, c["v_i8"], c["v_sc"][..., 0], 256)
+    want = oa.decode_int8(c["q"], c["k_i8"], c["k_sc"], c["v_i8"], c["v_sc"], acc="f64")
+    np.testing.assert_allclose(got, want, rtol=1e-12, atol=1e-12)
