@@ -88,7 +88,7 @@ struct Params {
   int64_t osb, osh;
   float* partial_out;  // [B*Hq][kD+2] or null
   float* ws_part;      // [B*Hq][n_split][kD+2]
-  int* ws_count;       // [B*Hkv]
+  int* ws_count;       // [B*Hkv] arrival tickets
   int* ws_status;
   int n_split;
   int tiles_per_split;
@@ -97,6 +97,9 @@ struct Params {
   // start; the split count stays fixed and the tiles per split follow the length
   const int* seq_len;
   int S_plan;  // host: the length the split count is planned for
+  // host only: zero the workspace's status word and arrival tickets on the
+  // stream just before the launch (after every argument check has passed)
+  int clear_header;
   // fused append (with seq_len): the token at row *seq_len is written by this
   // launch from k_new / v_new [B, Hkv, 1, D] (q's dtype), by one extra block per
   // (b, kv head) - split n_split - 1 - which also contributes the token's
@@ -308,17 +311,33 @@ __device__ __forceinline__ void publish_split(const Params& p, int b, int hq, in
   dst[4 + d] = O;
 }
 
+// Arrival ticket of a split: adds 1 to *ctr and returns the old count, as one
+// acquire-release atomic.  Called by one thread after a block barrier: the
+// release makes the partial that every thread of the block stored before that
+// barrier visible first; the acquire makes the partials of the splits counted
+// earlier visible to the whole block after the barrier that follows.
+__device__ __forceinline__ int ticket_add(int* ctr) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(old) : "l"(ctr) : "memory");
+  return old;
+}
+
 // Run by the last block of (b, kvh) to arrive: merges the n_split partials of
 // its NREP q heads and emits them.  The rows of one head are contiguous, so the
-// block copies them into shared memory with 16-byte cp.async - one round trip
-// to L2 - then reduces the row maxima, writes one weight per row, and folds the
+// block copies them into shared memory in one round trip to L2: one bulk copy
+// per head completing on the mbarrier `bar` when the kernel provides one (the
+// int8 kernel), else 16-byte cp.async.  With at most 64 rows per head (every
+// one-wave plan) warp r then reduces head r's row maxima, weights and sum with
+// shuffles, and after one block barrier thread d folds channel d of every row.
+// Longer merges reduce the row maxima, write one weight per row, and fold the
 // rows with warp w taking rows w, w + 4, ... and lane l channels 4 l .. 4 l + 3
-// (16-byte shared loads); a last pass adds the 4 warps.  Rows beyond the scratch
-// capacity are merged in further chunks (online rescaling).  scratch: 16-byte
-// aligned, scratch_floats floats.
+// (16-byte shared loads), a last pass adding the 4 warps; rows beyond the
+// scratch capacity are merged in further chunks (online rescaling).  scratch:
+// 16-byte aligned, scratch_floats floats.
 template <int NREP, int QDT>
 __device__ __forceinline__ void merge_splits(const Params& p, int b, int kvh, float* scratch,
-                                             int scratch_floats, unsigned gen0) {
+                                             int scratch_floats, unsigned gen0,
+                                             uint64_t* bar = nullptr) {
   constexpr int kRowVec = kPartRow / 4;  // 16-byte pieces per partial row
   __shared__ float s_red[kWarps][NREP];
   __shared__ float s_l[kWarps][NREP];
@@ -329,6 +348,77 @@ __device__ __forceinline__ void merge_splits(const Params& p, int b, int kvh, fl
   float* rows_base = scratch + kWarps * NREP * kD;
   const int per_chunk = max(1, (scratch_floats - kWarps * NREP * kD) / (NREP * (kPartRow + 1)));
   float M[NREP], L[NREP], O[NREP];
+  if (n <= 64 && NREP * (n * kPartRow + 64) <= scratch_floats) {
+    // Up to 64 rows per head (every plan with one wave of blocks): all rows in
+    // one cp.async round trip, then warp r alone reduces head r's row maxima,
+    // weights and sum (two rows per lane, shuffles only), and after one block
+    // barrier thread d folds channel d of every row with those weights.
+    float* wbuf = scratch + NREP * n * kPartRow;  // [NREP][64] row weights
+    if (bar) {
+      // one bulk copy per head (its rows are contiguous), completing on `bar`
+      // (initialised by the kernel, used once per launch: phase 0)
+      if (tid == 0) {
+        asm volatile("fence.proxy.async.global;" ::: "memory");  // acquired partials -> async proxy
+        mbar_arrive_expect_tx(bar, NREP * n * kPartRow * 4);
+#pragma unroll
+        for (int r = 0; r < NREP; ++r)
+          bulk_g2s(scratch + r * n * kPartRow, src + static_cast<int64_t>(r) * n * kPartRow,
+                   n * kPartRow * 4, bar);
+      }
+      if (__syncthreads_or(!mbar_wait(bar, 0))) {
+        if (tid == 0) report_error(p.ws_status, HQ_ERR_DEVICE_TIMEOUT);
+        return;
+      }
+    } else {
+#pragma unroll
+      for (int r = 0; r < NREP; ++r) {
+        float* dst = scratch + r * n * kPartRow;
+        const float* from = src + static_cast<int64_t>(r) * n * kPartRow;
+        for (int i = tid; i < n * kRowVec; i += kThreads) cp_async16(dst + 4 * i, from + 4 * i);
+      }
+      cp_async_commit();
+      cp_async_wait<0>();
+      __syncthreads();
+    }
+    if (warp < NREP) {
+      const float* rows = scratch + warp * n * kPartRow;
+      const bool h0 = lane < n, h1 = lane + 32 < n;
+      const float m0 = h0 ? rows[lane * kPartRow] : -INFINITY;
+      const float m1 = h1 ? rows[(lane + 32) * kPartRow] : -INFINITY;
+      const float mx = warp_max(fmaxf(m0, m1), 1);
+      const float w0 = m0 == -INFINITY ? 0.0f : exp2f(m0 - mx);
+      const float w1 = m1 == -INFINITY ? 0.0f : exp2f(m1 - mx);
+      float l = (h0 ? w0 * rows[lane * kPartRow + 1] : 0.0f) +
+                (h1 ? w1 * rows[(lane + 32) * kPartRow + 1] : 0.0f);
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+      wbuf[warp * 64 + lane] = w0;
+      wbuf[warp * 64 + lane + 32] = w1;
+      if (lane == 0) {
+        s_red[0][warp] = mx;
+        s_l[0][warp] = l;
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < NREP; ++r) {
+      const float* rows = scratch + r * n * kPartRow + 4 + tid;
+      const float* w = wbuf + r * 64;
+      float o0 = 0.0f, o1 = 0.0f;
+      int s = 0;
+      for (; s + 1 < n; s += 2) {
+        o0 += w[s] * rows[s * kPartRow];
+        o1 += w[s + 1] * rows[(s + 1) * kPartRow];
+      }
+      if (s < n) o0 += w[s] * rows[s * kPartRow];
+      M[r] = s_red[0][r];
+      L[r] = s_l[0][r];
+      O[r] = o0 + o1;
+    }
+    if (tid == 0) p.ws_count[b * p.Hkv + kvh] = 0;  // ready for the next launch
+    finish_heads<NREP, QDT>(p, b, kvh, tid, M, L, O, gen0);
+    return;
+  }
 #pragma unroll
   for (int r = 0; r < NREP; ++r) {
     M[r] = -INFINITY;
@@ -813,7 +903,8 @@ __device__ __forceinline__ void grid_arrive(const Params& p, int S) {
 // takes the split ticket like every other split (and merges if it is last).
 template <int NREP, int SDT, int QDT>
 __device__ void append_split(const Params& p, int b, int kvh, int S, unsigned char* ring,
-                             int scratch_floats, float (&red)[kWarps][NREP], int& s_last) {
+                             int scratch_floats, float (&red)[kWarps][NREP], int& s_last,
+                             uint64_t* merge_bar) {
   using QE = Elem<QDT>;
   using SE = Elem<SDT>;
   const int d = threadIdx.x, lane = d & 31, warp = d >> 5;
@@ -895,15 +986,11 @@ __device__ void append_split(const Params& p, int b, int kvh, int S, unsigned ch
 #pragma unroll
   for (int r = 0; r < NREP; ++r) publish_split(p, b, kvh * NREP + r, split, d, Ms[r], Ls[r], Os[r]);
   __syncthreads();
-  if (d == 0) {
-    __threadfence();
-    const int ticket = atomicAdd(p.ws_count + b * p.Hkv + kvh, 1);
-    s_last = ticket == p.n_split - 1;
-  }
+  if (d == 0) s_last = ticket_add(p.ws_count + b * p.Hkv + kvh) == p.n_split - 1;
   __syncthreads();
   if (!s_last) return;
-  __threadfence();
-  merge_splits<NREP, QDT>(p, b, kvh, reinterpret_cast<float*>(ring), scratch_floats, 0u);
+  merge_splits<NREP, QDT>(p, b, kvh, reinterpret_cast<float*>(ring), scratch_floats, 0u,
+                          merge_bar);
 }
 
 template <int NREP, int SDT, int QDT>
@@ -925,10 +1012,15 @@ __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(
   __shared__ float red[kWarps][NREP];
   __shared__ float qmax_s[NREP];
   __shared__ int s_last;
+  __shared__ __align__(8) uint64_t merge_bar;  // bulk loads of the split partials
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, t4 = lane & 3;
   const int kvh = blockIdx.x, split = blockIdx.y, b = blockIdx.z;
+  if (tid == 0) {
+    mbar_init(&merge_bar, 1);
+    fence_mbar_init();
+  }
   // an overlapped launch after this one may be scheduled now: its blocks take
   // the slots of this grid's blocks as they exit, and wait for this grid's
   // completion before reading q or writing anything
@@ -941,7 +1033,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(
     tps = max(1, ((S + kTileT - 1) / kTileT + n_main - 1) / n_main);
   }
   if (p.k_new && split == p.n_split - 1) {
-    append_split<NREP, SDT, QDT>(p, b, kvh, S, ring, C::RING / 4, red, s_last);
+    append_split<NREP, SDT, QDT>(p, b, kvh, S, ring, C::RING / 4, red, s_last, &merge_bar);
     return;
   }
   const int s_begin = split * tps * kTileT;
@@ -1336,15 +1428,11 @@ __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(
 #pragma unroll
   for (int r = 0; r < NREP; ++r) publish_split(p, b, kvh * NREP + r, split, d, Ms[r], Ls[r], Os[r]);
   __syncthreads();
-  if (tid == 0) {
-    __threadfence();
-    const int ticket = atomicAdd(p.ws_count + b * p.Hkv + kvh, 1);
-    s_last = ticket == p.n_split - 1;
-  }
+  if (tid == 0) s_last = ticket_add(p.ws_count + b * p.Hkv + kvh) == p.n_split - 1;
   __syncthreads();
   if (!s_last) return;
-  __threadfence();
-  merge_splits<NREP, QDT>(p, b, kvh, reinterpret_cast<float*>(ring), C::RING / 4, gen0);
+  merge_splits<NREP, QDT>(p, b, kvh, reinterpret_cast<float*>(ring), C::RING / 4, gen0,
+                          &merge_bar);
 }
 
 }  // namespace mmak
@@ -1415,12 +1503,16 @@ inline Plan make_plan(int units, int S, int slots, int sms, int tile = kTile,
 }
 
 inline size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
+// arrival tickets [B*Hkv], after the 256-byte header
+inline size_t tickets_bytes(int B, int Hkv) {
+  return align256(sizeof(int) * static_cast<size_t>(B) * Hkv);
+}
 
 inline size_t workspace_bytes(int B, int Hq, int Hkv, int S, int sms) {
   const int units = B * Hkv;
   const int tiles = (S + kTile - 1) / kTile;
   const int ms = max_splits(units > 0 ? units : 1, tiles, sms);
-  return 256 + align256(sizeof(int) * static_cast<size_t>(B) * Hkv) +
+  return 256 + tickets_bytes(B, Hkv) +
          sizeof(float) * static_cast<size_t>(B) * Hq * ms * kPartRow;
 }
 
@@ -1447,7 +1539,7 @@ int launch(Params p, int B, void* ws, size_t ws_bytes, cudaStream_t st) {
   char* w = static_cast<char*>(ws);
   p.ws_status = reinterpret_cast<int*>(w);
   p.ws_count = reinterpret_cast<int*>(w + 256);
-  p.ws_part = reinterpret_cast<float*>(w + 256 + align256(sizeof(int) * static_cast<size_t>(B) * p.Hkv));
+  p.ws_part = reinterpret_cast<float*>(w + 256 + tickets_bytes(B, p.Hkv));
   p.n_split = pl.n_split;
   p.tiles_per_split = pl.tiles_per_split;
   dim3 grid(pl.n_split, p.Hkv, B);
@@ -1516,7 +1608,7 @@ int launch_mma(Params p, int B, void* ws, size_t ws_bytes, cudaStream_t st) {
   if (ws_bytes < workspace_bytes(B, p.Hq, p.Hkv, S_plan, sms)) return HQ_ERR_WORKSPACE;
   // fused append: one more partial row per head (the appended token's split)
   const int n_rows = pl.n_split + (p.k_new ? 1 : 0);
-  if (p.k_new && ws_bytes < 256 + align256(sizeof(int) * static_cast<size_t>(B) * p.Hkv) +
+  if (p.k_new && ws_bytes < 256 + tickets_bytes(B, p.Hkv) +
                                 sizeof(float) * static_cast<size_t>(B) * p.Hq * n_rows * kPartRow)
     return HQ_ERR_WORKSPACE;
   CUtensorMap tmk, tmv;
@@ -1526,9 +1618,14 @@ int launch_mma(Params p, int B, void* ws, size_t ws_bytes, cudaStream_t st) {
   char* w = static_cast<char*>(ws);
   p.ws_status = reinterpret_cast<int*>(w);
   p.ws_count = reinterpret_cast<int*>(w + 256);
-  p.ws_part = reinterpret_cast<float*>(w + 256 + align256(sizeof(int) * static_cast<size_t>(B) * p.Hkv));
+  p.ws_part = reinterpret_cast<float*>(w + 256 + tickets_bytes(B, p.Hkv));
   p.n_split = n_rows;
   p.tiles_per_split = pl.tiles_per_split;
+  if (p.clear_header) {
+    const cudaError_t e =
+        cudaMemsetAsync(ws, 0, 256 + tickets_bytes(B, p.Hkv), st);
+    if (e != cudaSuccess) return static_cast<int>(e);
+  }
   // kv head fastest: the blocks dispatched last are the last splits, which hold
   // the remainder tiles (the shortest runs)
   dim3 grid(p.Hkv, n_rows, B);
@@ -1608,7 +1705,7 @@ static int decode_int8_impl(const void* q, int q_dtype, const int64_t q_strides[
                               const int* seq_len = nullptr, int S_plan = 0, int overlap = 0,
                               const void* k_new = nullptr, const void* v_new = nullptr,
                               const int64_t* kn_strides = nullptr,
-                              const int64_t* vn_strides = nullptr) {
+                              const int64_t* vn_strides = nullptr, int clear_header = 0) {
   int rc = check_common(q_strides, kv_strides, out_strides, partial_out, B, Hq, Hkv, S, D, workspace);
   if (rc != HQ_OK) return rc;
   // an empty cache (S == 0) may come with null K/V/v_scale pointers
@@ -1650,6 +1747,7 @@ static int decode_int8_impl(const void* q, int q_dtype, const int64_t q_strides[
   p.seq_len = seq_len;
   p.S_plan = S_plan < 0 ? 0 : (S_plan > S ? S : S_plan);
   p.overlap = overlap;
+  p.clear_header = clear_header;
   p.k_new = k_new;
   p.v_new = v_new;
   if (k_new) {
@@ -1687,6 +1785,25 @@ extern "C" int hq_decode_int8(const void* q, int q_dtype, const int64_t q_stride
                           ksc_strides, vsc_strides, B, Hq, Hkv, S, D, sm_scale, q_quant, out,
                           out_strides, partial_out, workspace, workspace_bytes, stream, nullptr, 0, 0);
 }
+
+namespace hq {
+// hq_decode_int8 whose workspace header (status word, arrival tickets) is
+// zeroed on the stream right before the launch, once every argument check has
+// passed: for a shared scratch that may still hold the state of a call that
+// gave up.  Library-internal (not exported).
+int decode_int8_clear_first(const void* q, int q_dtype, const int64_t q_strides[3],
+                            const int8_t* k, const int8_t* v, const int64_t kv_strides[3],
+                            const void* k_scale, const void* v_scale, int scale_dtype,
+                            const int64_t ksc_strides[3], const int64_t vsc_strides[3], int B,
+                            int Hq, int Hkv, int S, int D, float sm_scale, int q_quant, void* out,
+                            const int64_t out_strides[3], float* partial_out, void* workspace,
+                            size_t workspace_bytes, hq_stream_t stream) {
+  return decode_int8_impl(q, q_dtype, q_strides, k, v, kv_strides, k_scale, v_scale, scale_dtype,
+                          ksc_strides, vsc_strides, B, Hq, Hkv, S, D, sm_scale, q_quant, out,
+                          out_strides, partial_out, workspace, workspace_bytes, stream, nullptr, 0,
+                          0, nullptr, 0, 0, nullptr, nullptr, nullptr, nullptr, 1);
+}
+}  // namespace hq
 
 extern "C" int hq_decode_int8_ex(const void* q, int q_dtype, const int64_t q_strides[3],
                                  const int8_t* k, const int8_t* v, const int64_t kv_strides[3],

@@ -12,9 +12,12 @@
 // The array is kNoallocScratchBytes (8 MiB) on every GPU that loads the
 // library, held until the process exits.  All calls share it: calls that
 // overlap on the GPU (different streams, or different host threads without
-// ordering) race on it and must be serialised by the caller.  Each call clears
-// the tickets and the status word before its launch, so a call that follows
-// one that gave up still starts clean.
+// ordering) race on it and must be serialised by the caller.  Once a call's
+// arguments have passed every check, it clears the tickets and the status word
+// on its stream right before its launch, so a call that follows one that gave
+// up still starts clean; a call that is refused enqueues nothing.  The array's
+// device address is looked up once per device and kept: calls must not cross a
+// cudaDeviceReset of that device.
 #include <atomic>
 
 #include <cuda_runtime.h>
@@ -50,9 +53,17 @@ cudaError_t scratch_address(void** out) {
   return cudaSuccess;
 }
 
-size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
-
 }  // namespace
+
+namespace hq {
+int decode_int8_clear_first(const void* q, int q_dtype, const int64_t q_strides[3],
+                            const int8_t* k, const int8_t* v, const int64_t kv_strides[3],
+                            const void* k_scale, const void* v_scale, int scale_dtype,
+                            const int64_t ksc_strides[3], const int64_t vsc_strides[3], int B,
+                            int Hq, int Hkv, int S, int D, float sm_scale, int q_quant, void* out,
+                            const int64_t out_strides[3], float* partial_out, void* workspace,
+                            size_t workspace_bytes, hq_stream_t stream);
+}  // namespace hq
 
 extern "C" int hq_decode_int8_noalloc(const void* q, int q_dtype, const int64_t q_strides[3],
                                       const int8_t* k, const int8_t* v,
@@ -62,17 +73,17 @@ extern "C" int hq_decode_int8_noalloc(const void* q, int q_dtype, const int64_t 
                                       int B, int Hq, int Hkv, int S, int D, float sm_scale,
                                       int q_quant, void* out, const int64_t out_strides[3],
                                       float* partial_out, hq_stream_t stream) {
+  if (B < 0 || Hq <= 0 || Hkv <= 0 || S < 0) return HQ_ERR_INVALID_ARGUMENT;
   const size_t need = hq_decode_workspace_bytes(B, Hq, Hkv, S, D);
-  if (need == 0) return HQ_ERR_UNSUPPORTED;
+  if (need == 0) return HQ_ERR_UNSUPPORTED;                   // head_dim other than 128
   if (need > kNoallocScratchBytes) return HQ_ERR_WORKSPACE;  // beyond the static scratch
   void* ws = nullptr;
-  cudaError_t e = scratch_address(&ws);
+  const cudaError_t e = scratch_address(&ws);
   if (e != cudaSuccess) return static_cast<int>(e);
-  // status word and arrival tickets must start at zero
-  e = cudaMemsetAsync(ws, 0, 256 + align256(sizeof(int) * static_cast<size_t>(B) * Hkv),
-                      reinterpret_cast<cudaStream_t>(stream));
-  if (e != cudaSuccess) return static_cast<int>(e);
-  return hq_decode_int8(q, q_dtype, q_strides, k, v, kv_strides, k_scale, v_scale, scale_dtype,
-                        ksc_strides, vsc_strides, B, Hq, Hkv, S, D, sm_scale, q_quant, out,
-                        out_strides, partial_out, ws, kNoallocScratchBytes, stream);
+  // the status word and arrival tickets are zeroed on `stream` just before the
+  // launch, after the remaining argument checks
+  return hq::decode_int8_clear_first(q, q_dtype, q_strides, k, v, kv_strides, k_scale, v_scale,
+                                     scale_dtype, ksc_strides, vsc_strides, B, Hq, Hkv, S, D,
+                                     sm_scale, q_quant, out, out_strides, partial_out, ws,
+                                     kNoallocScratchBytes, stream);
 }

@@ -516,6 +516,16 @@ def _is_causal(mask, Sq: int, S: int) -> bool:
     return bool(ok.all())
 
 
+def _kernel_mask(mask, length: int) -> bool:
+    """True when the decode kernel applies ``mask`` exactly: none, one column
+    (what HF builds for this cache during decode: one value added to every
+    score, which the softmax cancels) or a one-token cache.  A mask with a
+    column per cached token may be nonzero anywhere (padding), so that step
+    takes the reference's math over the dequantized cache instead; deciding
+    this needs no look at the mask's values (no host synchronisation)."""
+    return mask is None or mask.shape[-1] == 1 or length <= 1
+
+
 def _blockwise_attention(module, query, st: _BlockStore, attention_mask, scaling, dropout):
     """Attention over a block-wise K layer: decode steps with ``kernels.kblock_decode``;
     multi-token steps on the dequantized cache with the reference's math."""
@@ -525,10 +535,8 @@ def _blockwise_attention(module, query, st: _BlockStore, attention_mask, scaling
     if Sq == 1 and not (module.training and dropout > 0.0):
         if attention_mask is not None and attention_mask.shape[-1] not in (1, L):
             raise ValueError("quantized_attention_forward: unexpected decode mask width")
-        if attention_mask is not None and attention_mask.shape[-1] == L and L > 1:
-            if bool((attention_mask != 0).any()):
-                raise NotImplementedError("padded decode masks are not supported by the int8 kernel")
-        return kernels.kblock_decode(q[:, :, 0, :], st.c, L, sm_scale=scaling).unsqueeze(1)
+        if _kernel_mask(attention_mask, L):
+            return kernels.kblock_decode(q[:, :, 0, :], st.c, L, sm_scale=scaling).unsqueeze(1)
     key = kernels.kblock_dequant(st.c, L, query.dtype)
     value = kernels.dequant(st.c["v"][:, :, :L], st.c["v_scale"][:, :, :L].unsqueeze(-1),
                             query.dtype, per_channel=False)
@@ -551,11 +559,10 @@ def quantized_attention_forward(module, query, key, value, attention_mask, scali
     if st is not None and Sq == 1 and not (module.training and dropout > 0.0):
         if attention_mask is not None and attention_mask.shape[-1] not in (1, st.length):
             raise ValueError("quantized_attention_forward: unexpected decode mask width")
+    if (st is not None and Sq == 1 and not (module.training and dropout > 0.0)
+            and _kernel_mask(attention_mask, st.length)):
         q_quant = Q_DIMS is not None and tuple(Q_DIMS) == (3,)
         q = query if (Q_DIMS is None or q_quant) else _fake_quant(query, Q_DIMS)
-        if attention_mask is not None and attention_mask.shape[-1] == st.length and st.length > 1:
-            if bool((attention_mask != 0).any()):
-                raise NotImplementedError("padded decode masks are not supported by the int8 kernel")
         out = _decode_direct(st, q, module.num_key_value_groups, scaling, q_quant)
         if out is None:
             st.flush()
@@ -573,7 +580,8 @@ def quantized_attention_forward(module, query, key, value, attention_mask, scali
         return out, None
     if st is not None:
         k, v, k_sc, v_sc = st.codes()
-        if (st.prefill and Q_DIMS in (None, (3,)) and query.dtype in (torch.bfloat16, torch.float16)
+        if (st.prefill and Sq > 1 and Q_DIMS in (None, (3,))
+                and query.dtype in (torch.bfloat16, torch.float16)
                 and D == 128 and not (module.training and dropout > 0.0)
                 and _is_causal(attention_mask, Sq, st.length)):
             out = kernels.int8_prefill_attn(query, k, k_sc, v, v_sc, module.num_key_value_groups,

@@ -15,16 +15,20 @@
  *   - Pointers are device pointers; sizes and strides are in ELEMENTS of the
  *     pointed-to type.  The innermost (head_dim) stride is always 1.
  *   - Tensors are 4-D [B, H, S, D] (batch, head, token, head_dim) unless noted.
- *   - Nothing allocates.  Kernels that need scratch take a caller-owned
- *     `workspace`; its size comes from the matching *_workspace_bytes query.
+ *   - Nothing allocates, except hq_peer_alloc (the receive buffer of the
+ *     sequence-sharded exchange, by design).  Kernels that need scratch take a
+ *     caller-owned `workspace`; its size comes from the matching
+ *     *_workspace_bytes query (hq_decode_int8_noalloc uses a static array of
+ *     the library instead).
  *   - Work is enqueued on `stream` (a cudaStream_t; NULL = legacy default)
  *     without any host synchronisation.
  *   - The return value is HQ_OK (0), a negative hq_status for argument errors
  *     (nothing is launched), or a positive cudaError_t from the launch.
  *   - No C++ exception crosses this boundary; entry points are reentrant and
  *     keep no global mutable state besides per-device caches of the SM count,
- *     kernel occupancy and kernel attributes (set once per device), and the
- *     static scratch of hq_decode_int8_noalloc.
+ *     kernel occupancy and kernel attributes (set once per device).  The one
+ *     exception is hq_decode_int8_noalloc: its calls share one static scratch
+ *     array per device, so calls that overlap on the GPU race (see its comment).
  */
 #ifndef HALFTONE_B200_H_
 #define HALFTONE_B200_H_
@@ -281,9 +285,12 @@ HQ_API int hq_decode_combine(const float* parts, int n_parts, int64_t part_strid
  * that loads it until the process exits.  Returns HQ_ERR_WORKSPACE without
  * launching when hq_decode_workspace_bytes(B, Hq, Hkv, S, D) exceeds 8 MiB.
  * It allocates nothing; its first call on a device looks up the array's
- * device address (make that first call before any stream capture).  All
- * calls share the array and each clears its tickets first: calls that
- * overlap on the GPU race and must be ordered by the caller.
+ * device address and keeps it (make that first call before any stream
+ * capture; calls must not cross a cudaDeviceReset of that device).  All calls
+ * share the array: calls that overlap on the GPU race and must be ordered by
+ * the caller.  A call whose arguments pass every check clears the array's
+ * tickets and status word on `stream` right before its launch; a refused call
+ * (invalid counts: HQ_ERR_INVALID_ARGUMENT) enqueues nothing.
  */
 HQ_API int hq_decode_int8_noalloc(const void* q, int q_dtype, const int64_t q_strides[3],
                                   const int8_t* k, const int8_t* v, const int64_t kv_strides[3],

@@ -109,6 +109,37 @@ def oracle_attention_forward(module, query, key, value, attention_mask, scaling=
     return torch.matmul(probs, value).transpose(1, 2).contiguous(), None
 
 
+def oracle_attention_f32(module, query, key, value, attention_mask, scaling=None, dropout=0.0,
+                         math_dtype=torch.float32, **kwargs):
+    """The reference's attention (tests/qwen_kvcache_full.py:95-113) evaluated in
+    float32 (or ``math_dtype``): q fake-quantized per token in the model dtype
+    exactly as the reference does (:103), then - with ``key`` / ``value`` the
+    float32 dequantized codes (``code * scale``, not rounded to the model
+    dtype) - ``q K^T * scaling`` plus the mask, softmax, ``@ V``, all in
+    ``math_dtype``, and the output cast to the model dtype.  In float32 this is
+    the arithmetic of the int8 decode kernel (exact code products, float32
+    softmax); in float64 it is the most exact evaluation of the reference's
+    math, the yardstick both are measured against."""
+    if scaling is None:
+        scaling = module.head_dim ** -0.5
+    n_rep = module.num_key_value_groups
+    q = fake_quant(query, Q_DIMS).to(math_dtype)
+    k, v = key.to(math_dtype), value.to(math_dtype)
+    if n_rep != 1:
+        k = k.repeat_interleave(n_rep, dim=1)
+        v = v.repeat_interleave(n_rep, dim=1)
+    scores = torch.matmul(q, k.transpose(2, 3)) * scaling
+    if attention_mask is not None:
+        scores = scores + attention_mask[:, :, :, : k.shape[-2]].to(math_dtype)
+    probs = F.softmax(scores, dim=-1, dtype=math_dtype)
+    return torch.matmul(probs, v).transpose(1, 2).contiguous().to(query.dtype), None
+
+
+def oracle_attention_f64(*args, **kwargs):
+    """``oracle_attention_f32`` with every product and the softmax in float64."""
+    return oracle_attention_f32(*args, math_dtype=torch.float64, **kwargs)
+
+
 def qwen3_config(num_layers=28, vocab=151936, hidden=1024, heads=16, kv_heads=8,
                  head_dim=128, intermediate=3072):
     """The Qwen3-0.6B architecture (random init; no weights are loaded)."""

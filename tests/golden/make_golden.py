@@ -3,7 +3,7 @@
 Run from the repository root in a container where the reference checkout is
 mounted (it is read, never modified):
 
-    python tests/golden/make_golden.py --reference /root/reference
+    python tests/golden/make_golden.py --reference <path of the reference checkout>
 
 It imports the reference's own torch functions on CPU:
 
@@ -88,7 +88,8 @@ def quant_cases():
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True,
+                    help="root of the reference checkout (the directory holding reference/ and tests/)")
     args = ap.parse_args()
     pai, par, qkf = load_reference(args.reference)
     torch.manual_seed(0)

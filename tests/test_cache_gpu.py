@@ -86,3 +86,39 @@ def test_hf_strided_inputs():
     ref.update(k2.transpose(0, 2, 1, 3), v2.transpose(0, 2, 1, 3), 0)
     for name in ("_k_i8", "_v_i8", "_k_sc", "_v_sc"):
         np.testing.assert_array_equal(getattr(ours, name)[0].cpu().numpy(), getattr(ref, name)[0])
+
+
+def test_decode_with_full_width_padding_mask():
+    """A decode mask with one column per cached token (padding: some columns at
+    the dtype's minimum) is applied as the reference adds it
+    (tests/qwen_kvcache_full.py:108-109): the step takes the reference's math
+    over the dequantized cache, so it equals the oracle restatement exactly; a
+    one-column mask (what HF builds for this cache) keeps the int8 kernel."""
+    from halftone_quantizedkvcache_b200.integration import quantized_attention_forward
+    from oracle.hf_reference import OracleQuantizedKVCache, oracle_attention_forward
+
+    class Attn:
+        num_key_value_groups, head_dim, training = 2, 128, False
+
+    torch.manual_seed(3)
+    B, Hq, Hkv, S, D = 2, 16, 8, 77, 128
+    k = (torch.randn(B, Hkv, S, D) * 2).bfloat16().cuda()
+    v = torch.randn(B, Hkv, S, D).bfloat16().cuda()
+    kn = torch.randn(B, Hkv, 1, D).bfloat16().cuda()
+    vn = torch.randn(B, Hkv, 1, D).bfloat16().cuda()
+    q = torch.randn(B, Hq, 1, D).bfloat16().cuda()
+    ours, ref = QuantizedKVCache(mode="fused"), OracleQuantizedKVCache()
+    ours.update(k, v, 0)
+    ref.update(k, v, 0)
+    ko, vo = ours.update(kn, vn, 0)
+    kr, vr = ref.update(kn, vn, 0)
+    mask = torch.zeros(B, 1, 1, S + 1, dtype=torch.bfloat16, device="cuda")
+    mask[0, :, :, :5] = torch.finfo(torch.bfloat16).min     # left padding of sequence 0
+    mask[1, :, :, 40:44] = torch.finfo(torch.bfloat16).min
+    a, _ = quantized_attention_forward(Attn(), q, ko, vo, mask, scaling=D ** -0.5)
+    b, _ = oracle_attention_forward(Attn(), q, kr, vr, mask, scaling=D ** -0.5)
+    assert torch.equal(a, b)
+    # one column: the kernel path, within the decode tolerance of the unmasked oracle
+    a1, _ = quantized_attention_forward(Attn(), q, ko, vo, mask[..., :1] * 0, scaling=D ** -0.5)
+    b1, _ = oracle_attention_forward(Attn(), q, kr, vr, None, scaling=D ** -0.5)
+    assert float((a1.float() - b1.float()).abs().max()) < 5e-2

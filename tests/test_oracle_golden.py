@@ -131,3 +131,27 @@ def test_hf_restatement_matches_reference_logits(golden):
             o = model(ids[:, t:t + 1], past_key_values=cache, use_cache=True)
             logits.append(o.logits[0, -1].float().numpy())
     np.testing.assert_array_equal(np.stack(logits), g["logits"])
+
+
+def test_f32_comparator_is_the_pinned_restatement_in_float32():
+    """``oracle_attention_f32`` (the whole-model comparator at the int8 kernel's
+    precision) is the pinned restatement evaluated in float32: on float32
+    inputs the two are the same operations, bit for bit (on a bf16 model it
+    differs only in keeping the scores, softmax and products in float32)."""
+    torch = pytest.importorskip("torch")
+    from oracle.hf_reference import oracle_attention_f32, oracle_attention_forward
+
+    class Attn:
+        num_key_value_groups, head_dim, training = 2, 128, False
+
+    g = torch.Generator().manual_seed(5)
+    q = torch.randn((2, 8, 3, 128), generator=g)
+    k = torch.randn((2, 4, 40, 128), generator=g) * 3
+    v = torch.randn((2, 4, 40, 128), generator=g)
+    mask = torch.zeros((2, 1, 3, 40))
+    mask[0, :, :, :4] = -1e30
+    a, _ = oracle_attention_f32(Attn(), q, k, v, mask)
+    b, _ = oracle_attention_forward(Attn(), q, k, v, mask)
+    assert torch.equal(a, b)
+    a, _ = oracle_attention_f32(Attn(), q.bfloat16(), k, v, None)
+    assert a.dtype == torch.bfloat16
