@@ -71,6 +71,7 @@ SIGNATURES = {
                               _I, _I, _F, _P, _A4, _P, _Z, _P]),
     "hq_kblock_dequant": (_I, [_P, _A4, _P, _A4, _I, _I, _I, _I, _I, _P, _I, _A4, _P]),
     "hq_read_status": (_I, [_P, _P]),
+    "hq_set_plan_sms": (_I, [_I, _I]),
 }
 
 _lib = None

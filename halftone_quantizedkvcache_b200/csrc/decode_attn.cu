@@ -1629,18 +1629,27 @@ int launch_mma(Params p, int B, void* ws, size_t ws_bytes, cudaStream_t st) {
   // kv head fastest: the blocks dispatched last are the last splits, which hold
   // the remainder tiles (the shortest runs)
   dim3 grid(p.Hkv, n_rows, B);
-  if (p.overlap) {
+  if (p.overlap || p.world > 0) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = C::SMEM;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    if (p.world > 0) {
+      // the sequence-sharded exchange waits inside the grid: a cooperative
+      // launch, refused (cudaErrorCooperativeLaunchTooLarge) when its blocks
+      // cannot all be resident at once
+      attr[0].id = cudaLaunchAttributeCooperative;
+      attr[0].val.cooperative = 1;
+    } else {
+      attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr[0].val.programmaticStreamSerializationAllowed = 1;
+    }
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tmk, tmv, p);
+    if (e != cudaSuccess) cudaGetLastError();  // leave no error behind for the caller's next call
     return e == cudaSuccess ? HQ_OK : static_cast<int>(e);
   }
   kern<<<grid, kThreads, C::SMEM, st>>>(tmk, tmv, p);

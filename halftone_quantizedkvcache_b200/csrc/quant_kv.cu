@@ -746,9 +746,14 @@ __global__ void __launch_bounds__(kThreads) dequant_kernel(
 }
 
 // ------------------------------------------------------------------ host helpers
+// Per-device number of SMs the grids are planned for (0: the device's own).
+static std::atomic<int> g_plan_sms[64];
+
 int sm_count(int dev) {
   static std::atomic<int> cache[64];
   if (dev < 0 || dev >= 64) return 148;
+  const int planned = g_plan_sms[dev].load(std::memory_order_relaxed);
+  if (planned > 0) return planned;
   int v = cache[dev].load(std::memory_order_relaxed);
   if (v > 0) return v;
   if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0)
@@ -845,10 +850,27 @@ static int launch_quant_k(const void* x, const int64_t* xs, int B, int H, int S,
                        sizeof(unsigned) * nbh * D;
   e = cudaMemsetAsync(wsp, 0, clear, st);
   if (e != cudaSuccess) return static_cast<int>(e);
-  kern<<<static_cast<unsigned>(grid), kThreads, smem, st>>>(
-      static_cast<const char*>(x), xs[0], xs[1], xs[2], H, S, pl, q, qs[0], qs[1], qs[2], s32,
-      reinterpret_cast<__half*>(s16), ws);
-  return finish_launch();
+  // Blocks wait for one another (pass B for pass A's counts): a cooperative
+  // launch, so a grid that cannot be resident all at once (SMs held by other
+  // work, or planned for more SMs than there are) is refused at launch with
+  // cudaErrorCooperativeLaunchTooLarge instead of running into its bounded waits.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kern, static_cast<const char*>(x), xs[0], xs[1], xs[2], H, S, pl, q,
+                         qs[0], qs[1], qs[2], s32, reinterpret_cast<__half*>(s16), ws);
+  if (e != cudaSuccess) {
+    cudaGetLastError();  // a refused launch leaves no error behind for the caller's next call
+    return static_cast<int>(e);
+  }
+  return HQ_OK;
 }
 
 template <int DT, int D>
@@ -1087,6 +1109,12 @@ extern "C" int hq_dequant(const int8_t* q, const int64_t q_strides[4], int B, in
     }
   }
 #undef HQ_DQ
+}
+
+extern "C" int hq_set_plan_sms(int device, int sms) {
+  if (device < 0 || device >= 64 || sms < 0) return HQ_ERR_INVALID_ARGUMENT;
+  hq::g_plan_sms[device].store(sms, std::memory_order_relaxed);
+  return HQ_OK;
 }
 
 extern "C" int hq_read_status(const void* workspace, hq_stream_t stream) {

@@ -42,10 +42,52 @@ def _round_up(n: int, m: int) -> int:
     return (n + m - 1) // m * m
 
 
+class _DeviceStatus:
+    """The device status words a cache's kernels report into: the K quantizer's
+    (folded into one int32 per device after each call, on the stream), the
+    sticky status words of the decode workspaces its attention used, and the
+    status word of each device-length layer (``lens[2]``).  ``eager`` checks
+    after every call (synchronises)."""
+
+    def __init__(self, eager: bool = False):
+        self.eager = eager
+        self.quant: dict = {}       # device index -> int32 [1]
+        self.decode: dict = {}      # data_ptr -> decode workspace (uint8)
+
+    def quant_word(self, device) -> torch.Tensor:
+        t = self.quant.get(device.index)
+        if t is None:
+            t = self.quant[device.index] = torch.zeros(1, dtype=torch.int32, device=device)
+        return t
+
+    def note_decode(self, ws: torch.Tensor) -> None:
+        if ws.data_ptr() not in self.decode:
+            self.decode[ws.data_ptr()] = ws
+
+    def words(self, stores):
+        """(what, status) of every word; synchronises."""
+        out = [(f"quantize-K on cuda:{d}", int(t.item())) for d, t in self.quant.items()]
+        out += [("decode workspace", int(ws[:4].view(torch.int32).item()))
+                for ws in self.decode.values()]
+        out += [(f"layer {i} device length", int(st.lens[2].item()))
+                for i, st in stores.items() if st.lens is not None]
+        return out
+
+    def reset(self, stores) -> None:
+        for t in self.quant.values():
+            t.zero_()
+        for ws in self.decode.values():
+            ws[:4].zero_()
+        for st in stores.values():
+            if st.lens is not None:
+                st.lens[2].zero_()
+
+
 class _LayerStore:
     """Capacity buffers of one layer: codes ``[B,H,cap,D]``, fp16 scales."""
 
-    __slots__ = ("k", "v", "k_sc", "v_sc", "length", "st", "lens", "prefill", "pending")
+    __slots__ = ("k", "v", "k_sc", "v_sc", "length", "st", "lens", "prefill", "pending",
+                 "status")
 
     def __init__(self, B, H, D, cap, device, device_length=False):
         self.k = torch.empty((B, H, cap, D), dtype=torch.int8, device=device)
@@ -57,6 +99,7 @@ class _LayerStore:
         self.lens = torch.zeros(4, dtype=torch.int32, device=device) if device_length else None
         self.prefill = False  # fused int8 prefill attention over this store
         self.pending = None   # a one-token append left to the next decode (fused_append)
+        self.status = None    # the owning cache's _DeviceStatus
         self._strides()
 
     def _strides(self) -> None:
@@ -221,6 +264,7 @@ def _decode_direct(st: _LayerStore, query: torch.Tensor, n_rep: int, scaling: fl
                 out.data_ptr(), _lib.strides((Hq * D, D, 1), 3), wsa.data_ptr(), wsa.numel(),
                 kernels._stream(query.device))
             _lib.check(rc, "hq_decode_append_int8_len")
+            _note_decode(st, wsa)
             return out
         st.flush()
     if st.lens is not None:
@@ -232,6 +276,7 @@ def _decode_direct(st: _LayerStore, query: torch.Tensor, n_rep: int, scaling: fl
             out.data_ptr(), _lib.strides((Hq * D, D, 1), 3), ws.data_ptr(), ws.numel(),
             kernels._stream(query.device))
         _lib.check(rc, "hq_decode_int8_len")
+        _note_decode(st, ws)
         return out
     rc = _lib.lib().hq_decode_int8(
         query.data_ptr(), dt, _lib.strides((qs[0], qs[1], 1), 3), k.data_ptr(), v.data_ptr(),
@@ -240,7 +285,24 @@ def _decode_direct(st: _LayerStore, query: torch.Tensor, n_rep: int, scaling: fl
         _lib.strides((Hq * D, D, 1), 3), None, ws.data_ptr(), ws.numel(),
         kernels._stream(query.device))
     _lib.check(rc, "hq_decode_int8")
+    _note_decode(st, ws)
     return out
+
+
+def _note_decode(st: _LayerStore, ws: torch.Tensor) -> None:
+    """Records the decode workspace whose status word this layer's decode reports into."""
+    status = st.status
+    if status is not None:
+        status.note_decode(ws)
+        if status.eager:
+            _raise_on_status(status.words({}))
+
+
+def _raise_on_status(words) -> None:
+    bad = [(what, v) for what, v in words if v != 0]
+    if bad:
+        raise RuntimeError("QuantizedKVCache: device status: " + "; ".join(
+            f"{what}: {_lib.status_string(v)} ({v})" for what, v in bad))
 
 
 class QuantizedKVCache(DynamicCache):
@@ -275,13 +337,23 @@ class QuantizedKVCache(DynamicCache):
     launch (``hq_decode_append_int8_len``) - one kernel per layer and step instead
     of two.  Anything that reads the cache first (another ``update``, the code
     views, ``sync_lengths``) writes the pending token with the append kernel.
+
+    Device status: kernels whose blocks wait for one another give up after a
+    bounded wait and report ``HQ_ERR_DEVICE_TIMEOUT`` in a status word instead of
+    hanging; a device-length append into a full layer reports there too.
+    ``check()`` reads every status word this cache's kernels report into and
+    raises ``RuntimeError`` if any is set (it synchronises); ``reset_status()``
+    clears them.  ``check_status=True`` runs ``check()`` after every ``update``
+    and every decode step of this cache (a host synchronisation per call: for
+    debugging, or where a silent failure must never pass).
     """
 
     def __init__(self, mode: str = "auto", capacity: int | None = None,
                  device_lengths: bool = False, fused_prefill: bool = False,
                  static_k_scale=None, fused_append: bool = False,
-                 k_block_tokens: int | None = None):
+                 k_block_tokens: int | None = None, check_status: bool = False):
         super().__init__()
+        self._status = _DeviceStatus(eager=check_status)
         if k_block_tokens is not None:
             if k_block_tokens not in kernels.KBLOCK_TOKENS:
                 raise ValueError(f"k_block_tokens must be one of {kernels.KBLOCK_TOKENS}")
@@ -325,6 +397,18 @@ class QuantizedKVCache(DynamicCache):
         for st in self._store.values():
             st.flush()
 
+    def check(self) -> None:
+        """Raises ``RuntimeError`` if a status word of this cache's kernels is set:
+        a bounded device-side wait that gave up (``HQ_ERR_DEVICE_TIMEOUT``) in the
+        K quantizer or the decode, or a device-length append past the capacity.
+        Synchronises."""
+        self._flush()
+        _raise_on_status(self._status.words(self._store))
+
+    def reset_status(self) -> None:
+        """Clears the status words ``check`` reads (on the current stream)."""
+        self._status.reset(self._store)
+
     # -- reference-compatible views (tests/qwen_kvcache_full.py:34-36)
     @property
     def _k_i8(self):
@@ -364,12 +448,14 @@ class QuantizedKVCache(DynamicCache):
             cap = _round_up(max(S_new + _ALIGN, self.capacity or 0), _ALIGN)
             st = _LayerStore(B, H, D, cap, key_states.device, self.device_lengths)
             st.prefill = self.fused_prefill
+            st.status = self._status
             ks = self._static_scale(layer_idx)
             if ks is not None:
                 kernels.quant_k_static(key_states, ks, out=st.k[:, :, :S_new])
                 st.k_sc.copy_(ks.reshape(-1, H, 1, D).expand(B, H, 1, D))
             else:
-                kernels.quant_k_perchannel(key_states, out=st.k[:, :, :S_new], scale_out=st.k_sc)
+                kernels.quant_k_perchannel(key_states, out=st.k[:, :, :S_new], scale_out=st.k_sc,
+                                           status_into=self._status.quant_word(key_states.device))
             kernels.quant_v_pertoken(value_states, out=st.v[:, :, :S_new],
                                      scale_out=st.v_sc[:, :, :S_new])
             st.length = S_new
@@ -407,12 +493,16 @@ class QuantizedKVCache(DynamicCache):
                     kernels.append_kv(key_states, value_states, kdst, vdst, v_scale_dst=vsc)
                 else:
                     # codes with the new tokens' own per-channel scale; that scale is not kept
-                    kernels.quant_k_perchannel(key_states, out=kdst, scale_dtype=None)
+                    kernels.quant_k_perchannel(
+                        key_states, out=kdst, scale_dtype=None,
+                        status_into=self._status.quant_word(key_states.device))
                     kernels.quant_v_pertoken(value_states, out=vdst, scale_out=vsc)
                 if st.lens is not None:  # eager multi-token append: host length is current
                     st.lens[0].fill_(L + S_new)
             st.length = L + S_new
         L = st.length
+        if self._status.eager:  # (no flush: a pending fused append stays pending)
+            _raise_on_status(self._status.words(self._store))
         k, v = st.k[:, :, :L], st.v[:, :, :L]
         if self._fused():
             return _tag(k, st), _tag(v, st)

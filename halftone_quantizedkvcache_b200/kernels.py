@@ -82,7 +82,10 @@ class _Workspaces:
                     raise RuntimeError(
                         f"{kind} workspace of {nbytes} bytes needed during CUDA graph capture: "
                         "run the same call once on this stream before capturing it")
+                old = buf
                 buf = torch.zeros(max(nbytes, 4096), dtype=torch.uint8, device=dev)
+                if old is not None:
+                    buf[:4].copy_(old[:4])  # the status word (first error) outlives the growth
                 self._bufs[key] = buf
             return buf
 
@@ -102,7 +105,8 @@ def _check_bhsd(x: torch.Tensor, what: str) -> None:
 def quant_k_perchannel(x: torch.Tensor, *, out: torch.Tensor | None = None,
                        scale_dtype: torch.dtype | None = torch.float16,
                        scale_out: torch.Tensor | None = None,
-                       scale_f32_out: torch.Tensor | None = None):
+                       scale_f32_out: torch.Tensor | None = None,
+                       status_into: torch.Tensor | None = None):
     """K per channel: absmax over S of ``x [B,H,S,D]`` -> (int8 codes, scale ``[B,H,1,D]``).
 
     Same contract as ``quant_k_perchannel_triton`` (src/kernels/quant_kv_triton.py:90-102):
@@ -110,6 +114,9 @@ def quant_k_perchannel(x: torch.Tensor, *, out: torch.Tensor | None = None,
     the float32 scale of ``quantize_int8`` (reference/page_attention_int8_pytorch.py:23-30);
     ``scale_dtype=None`` writes no scale.  ``out`` / ``scale_out`` /
     ``scale_f32_out`` write into caller buffers (``out`` may be a strided view).
+    ``status_into`` (int32 CUDA tensor, first element): the call's device status
+    word (0, or ``HQ_ERR_DEVICE_TIMEOUT`` if a bounded wait gave up) is folded
+    into it on the stream (the minimum keeps the first error), without a sync.
     """
     _check_bhsd(x, "quant_k_perchannel")
     B, H, S, D = x.shape
@@ -134,6 +141,8 @@ def quant_k_perchannel(x: torch.Tensor, *, out: torch.Tensor | None = None,
         s16.data_ptr() if s16 is not None else None, ws.data_ptr(), ws.numel(),
         _stream(x.device))
     check(rc, "hq_quant_k_perchannel")
+    if status_into is not None:
+        torch.minimum(status_into[:1], ws[:4].view(torch.int32), out=status_into[:1])
     if scale_dtype == torch.float32:
         return q, s32
     return q, s16
@@ -642,6 +651,15 @@ def read_status(kind: str = "decode", device=None) -> int:
     dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
     ws = WORKSPACES.get(dev, kind, 4096)
     return _lib.lib().hq_read_status(ws.data_ptr(), _stream(dev))
+
+
+def set_plan_sms(sms: int, device=None) -> None:
+    """Plan this device's grids for ``sms`` SMs (0: the device's own count) -
+    ``hq_set_plan_sms``.  Cached decode workspace sizes are dropped, since they
+    depend on the planned count."""
+    dev = torch.cuda.current_device() if device is None else torch.device(device).index
+    check(_lib.lib().hq_set_plan_sms(int(dev), int(sms)), "hq_set_plan_sms")
+    _decode_ws_bytes.clear()
 
 
 # ---------------------------------------------------------------- block-wise per-channel K

@@ -87,7 +87,10 @@ HQ_API const char* hq_version(void);
  *          grid working through an ordered queue of chunks; blocks exchange
  *          per-channel maxima and per-group counts through the workspace; a
  *          bounded wait reports HQ_ERR_DEVICE_TIMEOUT in the workspace status
- *          word (hq_read_status) instead of hanging.
+ *          word (hq_read_status) instead of hanging.  The grid is a
+ *          cooperative launch: if its blocks cannot all be resident at once
+ *          the call returns cudaErrorCooperativeLaunchTooLarge and writes
+ *          nothing (see hq_set_plan_sms).
  */
 HQ_API size_t hq_quant_k_workspace_bytes(int B, int H, int D);
 HQ_API int hq_quant_k_perchannel(const void* x, int x_dtype, const int64_t x_strides[4], int B, int H,
@@ -393,7 +396,9 @@ HQ_API int hq_decode_int8_len(const void* q, int q_dtype, const int64_t q_stride
  * hq_decode_int8_peer: arguments as hq_decode_int8 (S = this rank's tokens,
  * may be 0; no partial output), plus the buffers, world (1..8) and rank.
  * Requires B * Hkv <= resident decode blocks of the GPU (HQ_ERR_UNSUPPORTED
- * otherwise): all blocks run at once.  A rank whose peers do not arrive
+ * otherwise): all blocks run at once, as a cooperative launch (a grid that
+ * cannot be resident at once is refused with cudaErrorCooperativeLaunchTooLarge
+ * and writes nothing).  A rank whose peers do not arrive
  * within 2 s stops waiting, writes no output and sets HQ_ERR_DEVICE_TIMEOUT in
  * the workspace status word (hq_read_status); the buffers of all ranks must
  * then be freed and allocated again.
@@ -474,6 +479,22 @@ HQ_API int hq_kblock_dequant(const int8_t* k_cache, const int64_t kq_strides[3],
  * bounded device wait gave up during an earlier call on that workspace.
  */
 HQ_API int hq_read_status(const void* workspace, hq_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Grid planning for a shared GPU (no counterpart in the reference).
+ * Every grid of this library is planned for the SMs of the current device;
+ * hq_set_plan_sms makes the calls on `device` plan for `sms` SMs instead (0
+ * restores the device's own count), for a caller that leaves part of the GPU
+ * to other work (another stream's kernels, an MPS partition).  The kernels
+ * whose blocks wait for one another - the K quantizer (hq_quant_k_perchannel)
+ * and the sequence-sharded decode (hq_decode_int8_peer) - are cooperative
+ * launches: a grid that cannot be resident all at once, for whatever reason,
+ * is refused at launch with cudaErrorCooperativeLaunchTooLarge (720) and
+ * writes nothing, instead of reaching its bounded waits.  Workspace sizes
+ * depend on the planned count: query them after changing it.  Not thread-safe
+ * against concurrent calls on the same device.
+ */
+HQ_API int hq_set_plan_sms(int device, int sms);
 
 #ifdef __cplusplus
 }
