@@ -10,9 +10,12 @@ quantize-on-write kernels from K ~ N(0,1) with 4 outlier channels per head x20
 and V ~ N(0,1) (synthetic, seeded).  A step decodes one token through 28
 layers, each with its own cache (28 x 68 MB = 1.9 GB > L2, read round-robin,
 so no layer's cache is still in L2 when it is read again); the 28 launches are
-one CUDA graph.  At N > 1 GPUs each rank holds a 32768-token chunk of every
-layer of an N x 32768-token sequence (weak scaling): per layer it computes its
-softmax partials, all-gathers them (NCCL) and combines on the device.
+one CUDA graph.  At N > 1 GPUs the headline is batch-sharded (weak scaling):
+every rank decodes its own sequence's 28 layers with no collective on the data
+path.  The ``seq_sharded`` extra at N > 1 is the case with a real exchange: one
+sequence of N x 32768 tokens split across the ranks, the softmax partials
+exchanged inside the decode kernel over peer memory (and, for comparison, with
+an NCCL all_gather plus a combine kernel).
 
 metric / value: algorithmic HBM GB/s of the decode kernel (K+V codes, scales,
 q and output bytes) over the whole job; ``us_per_layer`` and the fraction of
@@ -22,8 +25,12 @@ with each step's q / new K / new V copied from pinned host memory and the
 outputs read back.  The extra keys report the int8 / bf16-twin speedup, the S
 sweep and the bulk quantize-on-write GB/s (B=8, Hkv=8, S=32768, bf16).
 
-``--impl reference`` times the reference's CPU path (the numpy restatement in
-``oracle/``) on the host cores instead.
+``cpu_baseline`` (N = 1) and ``--impl reference`` time the reference's CPU
+PyTorch path on the host cores, all threads: its decode ops
+(``dequantize_int8`` + ``page_attention_reference``, restated in
+``oracle/torch_cpu.py``) on the same workload and config as the GPU arm, its
+``QuantizedKVCache.update`` for bulk writes and appends (config 4, batch
+scaled down), and its whole Qwen3 path (config 1) per token.
 """
 from __future__ import annotations
 
@@ -211,69 +218,154 @@ def time_graph(torch, fn, steps, warmup, stream, clocks_index=None, label=None, 
 
 
 # ---------------------------------------------------------------- CPU baseline
-def cpu_decode_gbs(seconds=10.0, max_layers=None):
-    """The oracle (numpy restatement of the reference CPU path) on all host
-    cores: decode attention of S=32768 layers, one (layer, kv head) per task."""
-    from concurrent.futures import ThreadPoolExecutor
-
-    import numpy as np
-
-    from oracle import attention as oa
-    from oracle import inputs as oin
+def _cpu_threads():
+    import torch
     cores = len(os.sched_getaffinity(0))
+    torch.set_num_threads(cores)
+    return cores
+
+
+def cpu_decode(seconds=10.0, max_layers=None):
+    """The reference's CPU PyTorch decode path (``oracle/torch_cpu.py``:
+    ``dequantize_int8`` of K and V, then ``page_attention_reference``) on all
+    host cores, over S=32768 layers of the headline workload (B=1, Hq=16,
+    Hkv=8, D=128, int8 K/V + fp32 scales, float32 q as in the reference's CPU
+    chain), one layer after another until ``seconds`` pass.  Returns (GB/s of
+    the algorithmic decode bytes, cores, layers, seconds)."""
+    import torch
+
+    from oracle import inputs as oin
+    from oracle import torch_cpu
+    cores = _cpu_threads()
     c = oin.decode_case(0, 1, HQ, HKV, S_HEAD, D, kv_dtype="bf16", q_dtype="bf16")
-    n_rep = HQ // HKV
+    t = {k: torch.from_numpy(c[k][0].copy()) for k in ("k_i8", "k_sc", "v_i8", "v_sc")}
+    q = torch.from_numpy(c["q"][0].copy())[:, None, :].float()
+    torch_cpu.decode_layer(q, t["k_i8"], t["k_sc"], t["v_i8"], t["v_sc"])  # warm-up
+    layers, t0 = 0, time.perf_counter()
+    while True:
+        torch_cpu.decode_layer(q, t["k_i8"], t["k_sc"], t["v_i8"], t["v_sc"])
+        layers += 1
+        el = time.perf_counter() - t0
+        if el >= seconds or (max_layers and layers >= max_layers):
+            break
+    return layers * decode_bytes(B, HQ, HKV, S_HEAD, D) / el / 1e9, cores, layers, el
 
-    def one_head(h):
-        sl = slice(h, h + 1)
-        qs = slice(h * n_rep, (h + 1) * n_rep)
-        return oa.decode_int8(c["q"][:, qs], c["k_i8"][:, sl], c["k_sc"][:, sl], c["v_i8"][:, sl],
-                              c["v_sc"][:, sl], n_rep)
 
-    per_round = max(1, cores // HKV)          # layers decoded concurrently
-    if max_layers:
-        per_round = min(per_round, max_layers)
-    tasks = list(range(HKV)) * per_round
-    layers = 0
+def cpu_quant_write(n_appends=8):
+    """Config 4 through the reference's ``QuantizedKVCache.update`` on the host
+    (``oracle.hf_reference.OracleQuantizedKVCache``, its torch restatement):
+    one bulk write of fresh bf16 K/V [1, 8, 32768, 128] (batch 1 of the
+    config's 8; K with 4 outlier channels per head x20) and ``n_appends``
+    single-token appends (of the config's 1024).  Each call also returns the
+    whole cache dequantized, as the reference does."""
+    import torch
+
+    from oracle.hf_reference import OracleQuantizedKVCache
+    cores = _cpu_threads()
+    g = torch.Generator().manual_seed(0)
+    Bc, H, Sq = 1, 8, 32768
+    gain = torch.ones((H, D))
+    for h in range(H):
+        gain[h, torch.randperm(D, generator=g)[:4]] = 20.0
+    k = (torch.randn((Bc, H, Sq, D), generator=g) * gain[None, :, None, :]).bfloat16()
+    v = torch.randn((Bc, H, Sq, D), generator=g).bfloat16()
+    cache = OracleQuantizedKVCache()
     t0 = time.perf_counter()
-    with ThreadPoolExecutor(max_workers=cores) as ex:
-        while True:
-            list(ex.map(one_head, tasks))
-            layers += per_round
-            el = time.perf_counter() - t0
-            if el >= seconds or (max_layers and layers >= max_layers):
+    cache.update(k, v, 0)
+    t_bulk = time.perf_counter() - t0
+    kn, vn = k[:, :, :1].clone(), v[:, :, :1].clone()
+    t0 = time.perf_counter()
+    for _ in range(n_appends):
+        cache.update(kn, vn, 0)
+    t_app = (time.perf_counter() - t0) / n_appends
+    n = Bc * H * Sq * D
+    nbytes = (3 * n + Bc * H * D * 4) + (3 * n + Bc * H * Sq * 4)   # K and V, as the GPU line
+    return {"bulk_gbs": round(nbytes / t_bulk / 1e9, 3), "bulk_s": round(t_bulk, 3),
+            "append_us": round(t_app * 1e6, 1), "cores": cores, "kind": "port",
+            "sample": f"QuantizedKVCache.update restated in torch on {cores} threads: bulk write of "
+                      f"K and V [{Bc},{H},{Sq},{D}] bf16 (batch {Bc} of 8), then {n_appends} "
+                      f"single-token appends (of 1024) at S~{Sq}"}
+
+
+def cpu_model_step(n0=512, budget_s=10.0):
+    """Config 1 on the host: the Qwen3-0.6B architecture (random init, bf16) through
+    HF transformers with the reference's cache and patched attention (their torch
+    restatements in ``oracle.hf_reference``): prefill ``n0`` tokens, then decode
+    steps until ``budget_s`` pass (at least one).  Per-token time."""
+    import torch
+    from transformers import Qwen3ForCausalLM
+
+    from oracle.hf_reference import (OracleQuantizedKVCache, oracle_attention_forward,
+                                     patched_attention, qwen3_config)
+    cores = _cpu_threads()
+    cfg = qwen3_config(num_layers=LAYERS)
+    cfg._attn_implementation = "eager"
+    torch.manual_seed(0)
+    model = Qwen3ForCausalLM(cfg).to(torch.bfloat16).eval()
+    ids = torch.randint(0, cfg.vocab_size, (1, n0 + 64), generator=torch.Generator().manual_seed(1))
+    with torch.no_grad(), patched_attention(oracle_attention_forward):
+        cache = OracleQuantizedKVCache()
+        t0 = time.perf_counter()
+        model(ids[:, :n0], past_key_values=cache, use_cache=True)
+        t_pre = time.perf_counter() - t0
+        steps, t0 = 0, time.perf_counter()
+        while steps < 64:
+            model(ids[:, n0 + steps:n0 + steps + 1], past_key_values=cache, use_cache=True)
+            steps += 1
+            if time.perf_counter() - t0 >= budget_s:
                 break
-    gbs = layers * decode_bytes(B, HQ, HKV, S_HEAD, D) / el / 1e9
-    return gbs, cores, layers, el
+        t_dec = (time.perf_counter() - t0) / steps
+    del model
+    return {"prefill_s": round(t_pre, 3), "ms_per_token": round(t_dec * 1e3, 2), "cores": cores,
+            "kind": "port",
+            "sample": f"Qwen3-0.6B architecture (random init, bf16, {LAYERS} layers) through HF "
+                      f"transformers with the reference's QuantizedKVCache and patched attention "
+                      f"(torch restatements) on {cores} threads: prefill {n0} tokens, then "
+                      f"{steps} decode step(s)"}
+
+
+def arm_config(nl, world, per_layer):
+    """The workload both arms report on (the reference arm samples it on the CPU)."""
+    return {"workload": f"decode attention over {nl} layer caches, S={S_HEAD} per "
+                        f"rank, B={B}, Hq={HQ}, Hkv={HKV}, D={D}, bf16 q, int8 K/V, "
+                        "fp32 scales",
+            "l2": f"inputs larger than L2: {nl} caches x {per_layer / 1e6:.1f} MB read round-robin",
+            "parallelism": (f"batch-sharded x{world}: one sequence per GPU, no collective"
+                            if world > 1 else "single GPU"),
+            "graph": f"{nl} launches per step in one CUDA graph"}
 
 
 # ---------------------------------------------------------------- reference arm
 def reference_arm(args):
+    """The reference's CPU PyTorch decode path on the host cores (rank 0 only),
+    on the GPU arm's workload: each step decodes one layer (a bounded sample of
+    the 28-layer step; the metric is per-layer bandwidth, so the sample does not
+    change it), whole run capped at ~150 s."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
     per = []
+    cores = layers = 0
     for i in range(args.warmup + args.steps):
-        # one step = one round of (layer, kv head) tasks filling every host core
-        gbs, cores, layers, el = cpu_decode_gbs(seconds=0.0)
+        gbs, cores, layers, el = cpu_decode(seconds=0.0, max_layers=1)
         if i >= args.warmup:
             per.append(el)
         if sum(per) > 150:   # keep the whole run within a few minutes
             break
     t = sum(per) / len(per)
-    per_step_bytes = layers * decode_bytes(B, HQ, HKV, S_HEAD, D)
-    value = per_step_bytes / t / 1e9
+    per_layer = decode_bytes(B, HQ, HKV, S_HEAD, D)
+    value = per_layer / t / 1e9
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s",
         "n_gpus": args.gpus, "steps": len(per), "warmup": args.warmup,
         "ms_per_step": round(t * 1e3, 3), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"decode attention, S={S_HEAD}, B={B}, Hq={HQ}, Hkv={HKV}, D={D}, "
-                               f"int8 K/V + fp32 scales; {layers} layer(s) per step on CPU",
-                   "l2": "n/a (CPU)"},
+        "config": arm_config(args.layers, args.gpus, per_layer),
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": cores, "kind": "port",
-                         "sample": f"{layers} layer(s) of S={S_HEAD} per step, numpy oracle, "
-                                   f"(layer, kv head) tasks on {cores} threads"},
+                         "sample": f"one layer of S={S_HEAD} per step (of the {args.layers}-layer "
+                                   "GPU step): the reference's dequantize_int8 + "
+                                   "page_attention_reference torch ops (oracle/torch_cpu.py) on "
+                                   f"{cores} threads"},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -406,14 +498,7 @@ def main():
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
             "data": "synthetic",
-            "config": {"workload": f"decode attention over {nl} layer caches, S={S_HEAD} per "
-                                   f"rank, B={B}, Hq={HQ}, Hkv={HKV}, D={D}, bf16 q, int8 K/V, "
-                                   "fp32 scales",
-                       "l2": f"inputs larger than L2: {nl} caches x "
-                             f"{per_layer / 1e6:.1f} MB read round-robin",
-                       "parallelism": (f"batch-sharded x{world}: one sequence per GPU, no "
-                                       "collective" if world > 1 else "single GPU"),
-                       "graph": f"{nl} launches per step in one CUDA graph"},
+            "config": arm_config(nl, world, per_layer),
             "us_per_layer": round(us_layer, 3),
             "frac_of_peak": round(achieved / peak, 4),
             "frac_of_8tbs": round(achieved / 8000.0, 4),
@@ -432,11 +517,15 @@ def main():
             line["seq_sharded"] = seq_sharded
         line.update(extras)
         if world == 1 and not args.no_cpu:
-            gbs, cores, layers, el = cpu_decode_gbs(seconds=10.0)
+            gbs, cores, layers, el = cpu_decode(seconds=10.0)
             line["cpu_baseline"] = {
                 "value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": "port",
-                "sample": f"{layers} layers of S={S_HEAD} decode in {el:.1f} s, numpy oracle, "
-                          f"(layer, kv head) tasks on {cores} threads"}
+                "sample": f"{layers} layers of S={S_HEAD} decode in {el:.1f} s: the reference's "
+                          "dequantize_int8 + page_attention_reference torch ops "
+                          f"(oracle/torch_cpu.py) on {cores} threads"}
+            if not args.no_extras:
+                line["cpu_baseline"]["quant_write"] = cpu_quant_write()
+                line["cpu_baseline"]["model_decode_step"] = cpu_model_step()
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

@@ -155,3 +155,17 @@ def test_f32_comparator_is_the_pinned_restatement_in_float32():
     assert torch.equal(a, b)
     a, _ = oracle_attention_f32(Attn(), q.bfloat16(), k, v, None)
     assert a.dtype == torch.bfloat16
+
+
+def test_torch_cpu_decode_path_equals_numpy_oracle():
+    """The timed CPU baseline (the reference's torch ops, oracle/torch_cpu.py) computes
+    the numpy oracle's int8 decode, to float32 round-off."""
+    torch = pytest.importorskip("torch")
+    from oracle import torch_cpu
+    c = oin.decode_case(3, 1, 16, 8, 700, 128)
+    ref = oa.decode_int8(c["q"], c["k_i8"], c["k_sc"], c["v_i8"], c["v_sc"], 2, acc="f64")
+    t = {k: torch.from_numpy(np.ascontiguousarray(c[k][0])) for k in
+         ("k_i8", "k_sc", "v_i8", "v_sc")}
+    q = torch.from_numpy(np.ascontiguousarray(c["q"][0]))[:, None, :].float()
+    got = torch_cpu.decode_layer(q, t["k_i8"], t["k_sc"], t["v_i8"], t["v_sc"])[:, 0].numpy()
+    np.testing.assert_allclose(got, ref[0], rtol=1e-5, atol=1e-5)
