@@ -689,14 +689,24 @@ def run_extras(torch, kernels, device, gen, stream, us_int8, peak):
     q = torch.randn((LAYERS, B, HQ, D), generator=gen, device=device).to(torch.bfloat16)
     o = torch.empty_like(q)
 
-    def tstep():
-        for l, (k, v) in enumerate(twin):
-            kernels.fp16_decode_attn(q[l], k, v, HQ // HKV, sm_scale=sm_scale, out=o[l])
+    def tstep(cuda_cores):
+        def run():
+            for l, (k, v) in enumerate(twin):
+                kernels.fp16_decode_attn(q[l], k, v, HQ // HKV, sm_scale=sm_scale, out=o[l],
+                                         cuda_cores=cuda_cores)
+        return run
     with torch.cuda.stream(stream):
-        ms, _ = time_graph(torch, tstep, 200, 10, stream)
-    us_bf16 = ms * 1e3 / LAYERS
+        ms, _ = time_graph(torch, tstep(False), 200, 10, stream)
+        ms_fma, _ = time_graph(torch, tstep(True), 200, 10, stream)
+    us_bf16, us_fma = ms * 1e3 / LAYERS, ms_fma * 1e3 / LAYERS
+    # the same-design twin (128-token TMA tiles, same ring / split plan / merge, bf16 tensor cores)
     res["bf16_twin_us_per_layer"] = round(us_bf16, 3)
     res["int8_vs_bf16_speedup"] = round(us_bf16 / us_int8, 3)
+    res["bf16_twin_frac_of_peak"] = round(decode_bytes(B, HQ, HKV, S_HEAD, D, kv_bytes=2) /
+                                          (us_bf16 * 1e-6) / 1e9 / peak, 4)
+    # second comparison point: the CUDA-core float32 twin over 64-token bulk-copied tiles
+    res["bf16_fma_twin_us_per_layer"] = round(us_fma, 3)
+    res["int8_vs_bf16_fma_speedup"] = round(us_fma / us_int8, 3)
     del twin
     torch.cuda.empty_cache()
     # -- sweep

@@ -46,6 +46,8 @@ SIGNATURES = {
                              _F, _I, _P, _A4, _P]),
     "hq_decode_dense": (_I, [_P, _A4, _P, _P, _I, _A4, _I, _I, _I, _I, _I, _F, _I, _P, _A4, _P, _P,
                              _Z, _P]),
+    "hq_decode_dense_fma": (_I, [_P, _A4, _P, _P, _I, _A4, _I, _I, _I, _I, _I, _F, _I, _P, _A4, _P,
+                                 _P, _Z, _P]),
     "hq_decode_combine": (_I, [_P, _I, ctypes.c_int64, _I, _I, _I, _P, _I, _A4, _P]),
     "hq_decode_int8_noalloc": (_I, [_P, _I, _A4, _P, _P, _A4, _P, _P, _I, _A4, _A4, _I, _I, _I, _I,
                                     _I, _F, _I, _P, _A4, _P, _P]),

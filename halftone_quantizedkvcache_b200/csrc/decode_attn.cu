@@ -1437,6 +1437,347 @@ __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(
 
 }  // namespace mmak
 
+// ------------------------------------------------------------------ dense tensor-core twin
+// The bf16 / f16 twin of decode_mma_kernel with the same design: 128-token K/V
+// tiles by tensor-map TMA into a 3-stage mbarrier ring (each 256-byte token row
+// arrives as two 128-byte-swizzled halves of 64 channels), the same grid, split
+// plan, split ticket and merge, 4 warps with 32 tokens each per tile and their
+// own online softmax.  Only the element type changes: the two products run on
+// the 16-bit tensor cores (mma.sync m16n8k16, float32 accumulation) instead of
+// the int8 ones, with no scales:
+//
+//   scores  S[t, c] = sum_d K[t, d] * Q[d, c]   q in the K/V dtype, exact; column c
+//                                               holds q head c % NREP, so every lane
+//                                               owns scores of real heads
+//   output  O[d, c] = sum_t V[t, d] * P[t, c]   A = V^T by ldmatrix.trans; column
+//                                               2h + i holds the high (i = 0) or low
+//                                               (i = 1) 16-bit part of head h's
+//                                               probabilities (about 16 bits)
+//
+// Per K/V byte it moves twice what the int8 kernel moves, so with the same
+// bytes in flight per SM it runs one block per SM (192 KB of ring).
+namespace mmab {
+
+constexpr int kTileT = 128;
+constexpr int kHalfB = kTileT * 128;  // 16 KB: 128 tokens x 64 channels x 2 bytes
+constexpr int kTileB = 2 * kHalfB;    // 32 KB per K or V tile
+constexpr int kStagesB = 3;
+constexpr int kPCol = 40;             // P staging column stride (16-bit words): conflict-free reads
+
+template <int NREP>
+struct BCfg {
+  static constexpr int RING = kStagesB * 2 * kTileB;   // 192 KB
+  static constexpr int PST = kWarps * 8 * kPCol * 2;   // per warp [8 columns][kPCol] 16-bit
+  static constexpr int QSM = NREP * kD * 2;            // q in the K/V dtype
+  static constexpr int SMEM = 1024 + RING + PST + QSM + 2 * kStagesB * 8;
+  static_assert(kWarps * NREP * kD * 4 + kWarps * NREP * 8 <= RING, "epilogue scratch");
+};
+
+template <int KVDT>
+__device__ __forceinline__ void mma_16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                       uint32_t b1) {
+  if constexpr (KVDT == HQ_DTYPE_BF16) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+        "{%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  } else {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+        "{%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+}
+
+template <int KVDT>
+__device__ __forceinline__ uint16_t bits16(float x) {
+  using E = Elem<KVDT>;
+  const typename E::T v = E::from_f32(x);
+  return *reinterpret_cast<const uint16_t*>(&v);
+}
+
+template <int NREP, int KVDT>
+__global__ void __launch_bounds__(kThreads, 1) decode_dense_mma_kernel(
+    const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
+    const Params p) {
+  using C = BCfg<NREP>;
+  using E = Elem<KVDT>;  // q has the K/V dtype
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* ring = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint16_t* pst = reinterpret_cast<uint16_t*>(ring + C::RING);
+  uint16_t* qsm = pst + kWarps * 8 * kPCol;
+  uint64_t* full = reinterpret_cast<uint64_t*>(qsm + NREP * kD);
+  uint64_t* empty = full + kStagesB;
+  __shared__ float red[kWarps][NREP];
+  __shared__ int s_last;
+  __shared__ __align__(8) uint64_t merge_bar;
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, t4 = lane & 3;
+  const int kvh = blockIdx.x, split = blockIdx.y, b = blockIdx.z;
+  const int d = tid;
+  const int S = p.S, tps = p.tiles_per_split;
+  const int s_begin = split * tps * kTileT;
+  const int ntok = max(0, min(S, s_begin + tps * kTileT) - s_begin);
+  const int ntiles = (ntok + kTileT - 1) / kTileT;
+
+  const uint64_t pol_stream = mmak::l2_evict_first();
+  int issued = 0;
+  auto issue = [&](int t) {
+    const int st = t % kStagesB;
+    unsigned char* dst = ring + st * 2 * kTileB;
+    const int y = s_begin + t * kTileT;
+    mbar_arrive_expect_tx(&full[st], 2 * kTileB);
+    mmak::tma_load_4d(dst, &tmk, 0, y, kvh, b, &full[st], pol_stream);
+    mmak::tma_load_4d(dst + kHalfB, &tmk, 64, y, kvh, b, &full[st], pol_stream);
+    mmak::tma_load_4d(dst + kTileB, &tmv, 0, y, kvh, b, &full[st], pol_stream);
+    mmak::tma_load_4d(dst + kTileB + kHalfB, &tmv, 64, y, kvh, b, &full[st], pol_stream);
+    issued = t + 1;
+  };
+  const auto* qp = reinterpret_cast<const typename E::T*>(p.q);
+  float qv[NREP];
+#pragma unroll
+  for (int r = 0; r < NREP; ++r) qv[r] = E::to_f32(qp[b * p.qsb + (kvh * NREP + r) * p.qsh + d]);
+  if (tid == 0) {
+    for (int s = 0; s < kStagesB; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kWarps);
+    }
+    mbar_init(&merge_bar, 1);
+    fence_mbar_init();
+  }
+  for (int i = tid; i < kWarps * 8 * kPCol; i += kThreads) pst[i] = 0;  // padding columns stay 0
+  __syncthreads();
+  if (tid == 0)
+    for (int t = 0; t < min(kStagesB, ntiles); ++t) issue(t);
+
+  // ---- q prologue: the reference's per-token fake quantization (q_quant), q kept
+  // in the K/V dtype (exact), staged for the B fragments
+  if (p.q_quant) {
+#pragma unroll
+    for (int r = 0; r < NREP; ++r) {
+      const float m = warp_max(fabsf(qv[r]), 1);
+      if (lane == 0) red[warp][r] = m;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < NREP; ++r) {
+      float m = red[0][r];
+#pragma unroll
+      for (int w = 1; w < kWarps; ++w) m = fmaxf(m, red[w][r]);
+      const Quantizer qz = Quantizer::from_amax(m);
+      qv[r] = static_cast<float>(qz.code(qv[r])) * qz.scale;
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < NREP; ++r) qsm[r * kD + d] = bits16<KVDT>(qv[r]);
+  __syncthreads();
+  // B fragments of q: column g holds head g % NREP; k-step j covers channels 16 j .. 16 j + 15
+  uint32_t bq[8][2];
+  {
+    const uint32_t* qw = reinterpret_cast<const uint32_t*>(qsm + (g % NREP) * kD);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      bq[j][0] = qw[8 * j + t4];
+      bq[j][1] = qw[8 * j + 4 + t4];
+    }
+  }
+
+  float m_run[NREP], l_run[NREP], o_acc[8][4];
+#pragma unroll
+  for (int h = 0; h < NREP; ++h) {
+    m_run[h] = -INFINITY;
+    l_run[h] = 0.0f;
+  }
+#pragma unroll
+  for (int m = 0; m < 8; ++m)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) o_acc[m][e] = 0.0f;
+  uint16_t* my_p = pst + warp * 8 * kPCol;
+
+  bool ok = true;
+  int consumed = 0;
+  for (int t = 0; t < ntiles; ++t) {
+    const int st = t % kStagesB;
+    const uint32_t par = (t / kStagesB) & 1;
+    if (!mbar_wait(&full[st], par)) {
+      ok = false;
+      break;
+    }
+    consumed = t + 1;
+    const uint32_t kt = smem_u32(ring + st * 2 * kTileB);
+    const uint32_t vt = kt + kTileB;
+    const int base_tok = t * kTileT + warp * 32;  // within the split
+
+    // ---- scores: 2 row blocks of 16 tokens x 8 k-steps of 16 channels
+    float sc[2][4];  // [rb]: (token g, column 2 t4), (g, 2 t4 + 1), (g + 8, 2 t4), (g + 8, 2 t4 + 1)
+#pragma unroll
+    for (int rb = 0; rb < 2; ++rb) {
+      float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int mat = lane >> 3;
+        const int row = warp * 32 + rb * 16 + (mat & 1) * 8 + (lane & 7);
+        uint32_t a[4];
+        mmak::ldsm_x4(kt + (j >> 2) * kHalfB + mmak::swz(row, (j & 3) * 2 + (mat >> 1)), a);
+        mma_16<KVDT>(acc, a, bq[j][0], bq[j][1]);
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int tok = base_tok + rb * 16 + g + 8 * (e >> 1);
+        sc[rb][e] = tok < ntok ? acc[e] * p.qk_scale : -INFINITY;
+      }
+    }
+    // ---- online softmax per head (every lane keeps every head's state)
+    float alpha[NREP], m_new[NREP];
+#pragma unroll
+    for (int h = 0; h < NREP; ++h) {
+      float mt = -INFINITY;
+#pragma unroll
+      for (int rb = 0; rb < 2; ++rb)
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if ((2 * t4 + (e & 1)) % NREP == h) mt = fmaxf(mt, sc[rb][e]);
+      mt = warp_max(mt, 1);
+      m_new[h] = fmaxf(m_run[h], mt);
+      alpha[h] = m_new[h] == -INFINITY ? 1.0f : exp2f(m_run[h] - m_new[h]);
+      m_run[h] = m_new[h];
+      l_run[h] *= alpha[h];
+    }
+    // probabilities of the first replica of each head (column < NREP) into the staging
+    __syncwarp();  // the previous tile's P reads are done
+#pragma unroll
+    for (int rb = 0; rb < 2; ++rb)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int col = 2 * t4 + (e & 1);
+        if (col < NREP) {
+          float mh = m_new[0];
+#pragma unroll
+          for (int h = 1; h < NREP; ++h)
+            if (col == h) mh = m_new[h];
+          const float pr = sc[rb][e] == -INFINITY ? 0.0f : exp2f(sc[rb][e] - mh);
+#pragma unroll
+          for (int h = 0; h < NREP; ++h)
+            if (col == h) l_run[h] += pr;
+          const uint16_t hi = bits16<KVDT>(pr);
+          typename E::T hv = *reinterpret_cast<const typename E::T*>(&hi);
+          const uint16_t lo = bits16<KVDT>(pr - E::to_f32(hv));
+          const int tk = rb * 16 + g + 8 * (e >> 1);
+          my_p[(2 * col) * kPCol + tk] = hi;
+          my_p[(2 * col + 1) * kPCol + tk] = lo;
+        }
+      }
+    // rescale this lane's output columns (head t4, its high and low parts)
+    if (t4 < NREP) {
+      float a = alpha[0];
+#pragma unroll
+      for (int h = 1; h < NREP; ++h)
+        if (t4 == h) a = alpha[h];
+      if (a != 1.0f) {
+#pragma unroll
+        for (int m = 0; m < 8; ++m)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) o_acc[m][e] *= a;
+      }
+    }
+    __syncwarp();
+    // ---- PV: A = V^T (ldmatrix.trans), B = P parts; 8 channel tiles x 2 token steps
+    uint32_t bp[2][2];
+#pragma unroll
+    for (int kk = 0; kk < 2; ++kk) {
+      const uint32_t* pw = reinterpret_cast<const uint32_t*>(my_p + g * kPCol + 16 * kk);
+      bp[kk][0] = pw[t4];
+      bp[kk][1] = pw[4 + t4];
+    }
+#pragma unroll
+    for (int m = 0; m < 8; ++m) {
+#pragma unroll
+      for (int kk = 0; kk < 2; ++kk) {
+        const int mat = lane >> 3;
+        const int row = warp * 32 + kk * 16 + (mat >> 1) * 8 + (lane & 7);
+        uint32_t a[4];
+        mmak::ldsm_x4_t(vt + (m >> 2) * kHalfB + mmak::swz(row, (m & 3) * 2 + (mat & 1)), a);
+        mma_16<KVDT>(o_acc[m], a, bp[kk][0], bp[kk][1]);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[st]);
+    if (tid == 0 && t + kStagesB < ntiles) {
+      if (!mbar_wait(&empty[st], par)) {
+        ok = false;
+        break;
+      }
+      issue(t + kStagesB);
+    }
+  }
+  if (!ok) {
+    report_error(p.ws_status, HQ_ERR_DEVICE_TIMEOUT);
+    if (tid == 0)
+      for (int t = consumed; t < issued; ++t) mbar_wait(&full[t % kStagesB], (t / kStagesB) & 1);
+  }
+  __syncthreads();
+  if (__syncthreads_or(!ok)) return;
+
+  // ---- block epilogue: the 4 warps' states into shared memory, merged per channel
+  float* wo = reinterpret_cast<float*>(ring);  // [kWarps][NREP][kD]
+  float* wl = wo + kWarps * NREP * kD;         // [kWarps][NREP]
+  float* wm = wl + kWarps * NREP;              // [kWarps][NREP]
+#pragma unroll
+  for (int h = 0; h < NREP; ++h) {
+    float l = l_run[h];
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+    if (lane == 0) {
+      wl[warp * NREP + h] = l;
+      wm[warp * NREP + h] = m_run[h];
+    }
+  }
+  if (t4 < NREP) {
+    float* dst = wo + (warp * NREP + t4) * kD;
+#pragma unroll
+    for (int m = 0; m < 8; ++m) {
+      dst[16 * m + g] = o_acc[m][0] + o_acc[m][1];
+      dst[16 * m + g + 8] = o_acc[m][2] + o_acc[m][3];
+    }
+  }
+  __syncthreads();
+  float Ms[NREP], Ls[NREP], Os[NREP];
+#pragma unroll
+  for (int r = 0; r < NREP; ++r) {
+    float M = wm[r];
+#pragma unroll
+    for (int w = 1; w < kWarps; ++w) M = fmaxf(M, wm[w * NREP + r]);
+    float L = 0.0f, O = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      const float mw = wm[w * NREP + r];
+      const float f = mw == -INFINITY ? 0.0f : exp2f(mw - M);
+      L += wl[w * NREP + r] * f;
+      O += wo[(w * NREP + r) * kD + d] * f;
+    }
+    Ms[r] = M;
+    Ls[r] = L;
+    Os[r] = O;
+  }
+  if (p.n_split == 1) {
+    finish_heads<NREP, KVDT>(p, b, kvh, d, Ms, Ls, Os, 0u);
+    return;
+  }
+#pragma unroll
+  for (int r = 0; r < NREP; ++r) publish_split(p, b, kvh * NREP + r, split, d, Ms[r], Ls[r], Os[r]);
+  __syncthreads();
+  if (tid == 0) s_last = ticket_add(p.ws_count + b * p.Hkv + kvh) == p.n_split - 1;
+  __syncthreads();
+  if (!s_last) return;
+  merge_splits<NREP, KVDT>(p, b, kvh, reinterpret_cast<float*>(ring), C::RING / 4, 0u, &merge_bar);
+}
+
+}  // namespace mmab
+
 // ------------------------------------------------------------------ cross-part combine
 template <int ODT>
 __global__ void __launch_bounds__(kThreads) combine_kernel(const float* __restrict__ parts,
@@ -1655,6 +1996,70 @@ int launch_mma(Params p, int B, void* ws, size_t ws_bytes, cudaStream_t st) {
   kern<<<grid, kThreads, C::SMEM, st>>>(tmk, tmv, p);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? HQ_OK : static_cast<int>(e);
+}
+
+// 16-bit [B, Hkv, S, 128] with element strides (sb, sh, 128): boxes of 128 tokens x 64
+// channels (128 bytes), 128-byte swizzle, zero fill past S; two boxes per token row.
+inline int encode_kv_map16(CUtensorMap* m, const void* base, int64_t sb, int64_t sh, int S,
+                           int Hkv, int B) {
+  auto enc = encode_fn();
+  if (!enc) return HQ_ERR_UNSUPPORTED;
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(kD), static_cast<cuuint64_t>(S > 0 ? S : 1),
+                        static_cast<cuuint64_t>(Hkv), static_cast<cuuint64_t>(B)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(kD * 2), static_cast<cuuint64_t>(sh * 2),
+                           static_cast<cuuint64_t>(sb * 2)};
+  cuuint32_t box[4] = {64, static_cast<cuuint32_t>(mmab::kTileT), 1, 1};
+  cuuint32_t es[4] = {1, 1, 1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 4, const_cast<void*>(base), dims, strides,
+                   box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? HQ_OK : HQ_ERR_INVALID_ARGUMENT;
+}
+
+template <int NREP, int KVDT>
+int launch_dense_mma(Params p, int B, void* ws, size_t ws_bytes, cudaStream_t st) {
+  using C = mmab::BCfg<NREP>;
+  auto kern = mmab::decode_dense_mma_kernel<NREP, KVDT>;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static std::atomic<int> occ[64];
+  int per_sm = (dev >= 0 && dev < 64) ? occ[dev].load(std::memory_order_relaxed) : 0;
+  if (per_sm <= 0) {
+    cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(kern),
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, C::SMEM);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    if (per_sm <= 0) return HQ_ERR_UNSUPPORTED;
+    if (dev >= 0 && dev < 64) occ[dev].store(per_sm, std::memory_order_relaxed);
+  }
+  const int sms = sm_count(dev);
+  const Plan pl = make_plan(B * p.Hkv, p.S, per_sm * sms, sms, mmab::kTileT);
+  if (ws_bytes < workspace_bytes(B, p.Hq, p.Hkv, p.S, sms)) return HQ_ERR_WORKSPACE;
+  CUtensorMap tmk, tmv;
+  int rc = encode_kv_map16(&tmk, p.k, p.kvsb, p.kvsh, p.S, p.Hkv, B);
+  if (rc == HQ_OK) rc = encode_kv_map16(&tmv, p.v, p.kvsb, p.kvsh, p.S, p.Hkv, B);
+  if (rc != HQ_OK) return rc;
+  char* w = static_cast<char*>(ws);
+  p.ws_status = reinterpret_cast<int*>(w);
+  p.ws_count = reinterpret_cast<int*>(w + 256);
+  p.ws_part = reinterpret_cast<float*>(w + 256 + tickets_bytes(B, p.Hkv));
+  p.n_split = pl.n_split;
+  p.tiles_per_split = pl.tiles_per_split;
+  dim3 grid(p.Hkv, pl.n_split, B);
+  kern<<<grid, kThreads, C::SMEM, st>>>(tmk, tmv, p);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? HQ_OK : static_cast<int>(e);
+}
+
+template <int KVDT>
+int dispatch_dense_mma(int nrep, const Params& p, int B, void* ws, size_t wsb, cudaStream_t st) {
+  switch (nrep) {
+    case 1: return launch_dense_mma<1, KVDT>(p, B, ws, wsb, st);
+    case 2: return launch_dense_mma<2, KVDT>(p, B, ws, wsb, st);
+    case 4: return launch_dense_mma<4, KVDT>(p, B, ws, wsb, st);
+    default: return HQ_ERR_UNSUPPORTED;
+  }
 }
 
 template <int SDT, int QDT>
@@ -1921,11 +2326,12 @@ extern "C" int hq_decode_int8_peer(const void* q, int q_dtype, const int64_t q_s
                           world, rank);
 }
 
-extern "C" int hq_decode_dense(const void* q, const int64_t q_strides[3], const void* k,
-                               const void* v, int kv_dtype, const int64_t kv_strides[3], int B,
-                               int Hq, int Hkv, int S, int D, float sm_scale, int q_quant,
-                               void* out, const int64_t out_strides[3], float* partial_out,
-                               void* workspace, size_t workspace_bytes, hq_stream_t stream) {
+static int decode_dense_impl(const void* q, const int64_t q_strides[3], const void* k,
+                             const void* v, int kv_dtype, const int64_t kv_strides[3], int B,
+                             int Hq, int Hkv, int S, int D, float sm_scale, int q_quant,
+                             void* out, const int64_t out_strides[3], float* partial_out,
+                             void* workspace, size_t workspace_bytes, hq_stream_t stream,
+                             bool tensor_cores) {
   int rc = check_common(q_strides, kv_strides, out_strides, partial_out, B, Hq, Hkv, S, D, workspace);
   if (rc != HQ_OK) return rc;
   if (!q || (!out && !partial_out) || (S > 0 && (!k || !v))) return HQ_ERR_INVALID_ARGUMENT;
@@ -1951,6 +2357,13 @@ extern "C" int hq_decode_dense(const void* q, const int64_t q_strides[3], const 
   p.partial_out = partial_out;
   const int nrep = Hq / Hkv;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (tensor_cores) {
+    switch (kv_dtype) {
+      case HQ_DTYPE_BF16: return dispatch_dense_mma<HQ_DTYPE_BF16>(nrep, p, B, workspace, workspace_bytes, st);
+      case HQ_DTYPE_F16: return dispatch_dense_mma<HQ_DTYPE_F16>(nrep, p, B, workspace, workspace_bytes, st);
+      default: return HQ_ERR_UNSUPPORTED;
+    }
+  }
   switch (kv_dtype) {
     case HQ_DTYPE_BF16:
       return dispatch_nrep<HQ_DTYPE_BF16, HQ_DTYPE_F32, HQ_DTYPE_BF16>(nrep, p, B, workspace, workspace_bytes, st);
@@ -1959,6 +2372,26 @@ extern "C" int hq_decode_dense(const void* q, const int64_t q_strides[3], const 
     default:
       return HQ_ERR_UNSUPPORTED;
   }
+}
+
+extern "C" int hq_decode_dense(const void* q, const int64_t q_strides[3], const void* k,
+                               const void* v, int kv_dtype, const int64_t kv_strides[3], int B,
+                               int Hq, int Hkv, int S, int D, float sm_scale, int q_quant,
+                               void* out, const int64_t out_strides[3], float* partial_out,
+                               void* workspace, size_t workspace_bytes, hq_stream_t stream) {
+  return decode_dense_impl(q, q_strides, k, v, kv_dtype, kv_strides, B, Hq, Hkv, S, D, sm_scale,
+                           q_quant, out, out_strides, partial_out, workspace, workspace_bytes,
+                           stream, true);
+}
+
+extern "C" int hq_decode_dense_fma(const void* q, const int64_t q_strides[3], const void* k,
+                                   const void* v, int kv_dtype, const int64_t kv_strides[3], int B,
+                                   int Hq, int Hkv, int S, int D, float sm_scale, int q_quant,
+                                   void* out, const int64_t out_strides[3], float* partial_out,
+                                   void* workspace, size_t workspace_bytes, hq_stream_t stream) {
+  return decode_dense_impl(q, q_strides, k, v, kv_dtype, kv_strides, B, Hq, Hkv, S, D, sm_scale,
+                           q_quant, out, out_strides, partial_out, workspace, workspace_bytes,
+                           stream, false);
 }
 
 extern "C" int hq_decode_combine(const float* parts, int n_parts, int64_t part_stride, int B,

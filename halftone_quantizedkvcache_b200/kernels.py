@@ -588,9 +588,11 @@ def int8_prefill_attn(q, k_i8, k_sc, v_i8, v_sc, n_rep=None, *, sm_scale=None, q
 
 
 def fp16_decode_attn(q, k, v, n_rep=None, *, sm_scale=None, q_quant=False, out=None,
-                     partial_out=None):
-    """Dense twin with the same tiling (src/kernels/int8_decode_attn_triton.py:116-127);
-    K/V float16 or bfloat16 (q must match)."""
+                     partial_out=None, cuda_cores=False):
+    """Dense twin with the int8 kernel's design (src/kernels/int8_decode_attn_triton.py:116-127):
+    128-token TMA tiles, the same ring, split plan and merge, 16-bit tensor-core
+    products (``hq_decode_dense``); K/V float16 or bfloat16 (q must match).
+    ``cuda_cores=True``: the CUDA-core float32 version (``hq_decode_dense_fma``)."""
     for t, n in ((q, "q"), (k, "k"), (v, "v")):
         _cuda(t, f"fp16_decode_attn {n}")
     qb, restore = _as_bhd(q)
@@ -613,7 +615,8 @@ def fp16_decode_attn(q, k, v, n_rep=None, *, sm_scale=None, q_quant=False, out=N
         res = out if out is not None else torch.empty((B, Hq, D), dtype=qb.dtype, device=qb.device)
     ws = _decode_ws(qb.device, B, Hq, Hkv, S, D)
     ost = _lib.strides(res.stride(), 3) if res is not None else None
-    rc = _lib.lib().hq_decode_dense(
+    fn = _lib.lib().hq_decode_dense_fma if cuda_cores else _lib.lib().hq_decode_dense
+    rc = fn(
         qb.data_ptr(), _lib.strides(qb.stride(), 3), k4.data_ptr(), v4.data_ptr(),
         _dtype_code(k4, "fp16_decode_attn kv"), _kv_strides(k4, v4), B, Hq, Hkv, S, D,
         float(sm_scale), int(bool(q_quant)), res.data_ptr() if res is not None else None, ost,

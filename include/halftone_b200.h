@@ -255,11 +255,21 @@ HQ_API int hq_prefill_int8(const void* q, int q_dtype, const int64_t q_strides[4
                            void* out, const int64_t out_strides[4], hq_stream_t stream);
 
 /* ------------------------------------------------------------------------
- * Same-design dense twin: identical tiling over bf16/f16 K/V (kv_dtype), no
- * scales.  Replaces fp16_decode_attn (src/kernels/int8_decode_attn_triton.py:116-127,
- * kernel :67-97).  Arguments as hq_decode_int8; q_dtype must equal kv_dtype.
+ * Same-design dense twin: the int8 kernel's design (128-token tensor-map tiles,
+ * 3-stage ring, split plan, split ticket and merge) over bf16/f16 K/V
+ * (kv_dtype), no scales, both products on the 16-bit tensor cores with float32
+ * accumulation.  Replaces fp16_decode_attn (src/kernels/int8_decode_attn_triton.py:116-127,
+ * kernel :67-97).  Arguments as hq_decode_int8; q_dtype must equal kv_dtype;
+ * K/V rows 16-byte aligned, strides multiples of 8 elements.
+ * hq_decode_dense_fma: the same attention on CUDA-core float32 FMAs over
+ * 64-token tiles (1-D bulk copies), kept as a second comparison point.
  */
 HQ_API int hq_decode_dense(const void* q, const int64_t q_strides[3], const void* k, const void* v,
+                    int kv_dtype, const int64_t kv_strides[3], int B, int Hq, int Hkv, int S,
+                    int D, float sm_scale, int q_quant, void* out, const int64_t out_strides[3],
+                    float* partial_out, void* workspace, size_t workspace_bytes,
+                    hq_stream_t stream);
+HQ_API int hq_decode_dense_fma(const void* q, const int64_t q_strides[3], const void* k, const void* v,
                     int kv_dtype, const int64_t kv_strides[3], int B, int Hq, int Hkv, int S,
                     int D, float sm_scale, int q_quant, void* out, const int64_t out_strides[3],
                     float* partial_out, void* workspace, size_t workspace_bytes,

@@ -121,19 +121,40 @@ def test_q_fake_quant_prologue():
     close(f32, oracle_int8(c, q_in=q_in))
 
 
+@pytest.mark.parametrize("cuda_cores", [False, True], ids=["tensor_cores", "cuda_cores"])
 @pytest.mark.parametrize("dt", ["bf16", "f16"])
 @pytest.mark.parametrize("S", [5, 4096, 32768])
-def test_dense_twin(dt, S):
+def test_dense_twin(dt, S, cuda_cores):
     c = oin.decode_case(77 + S, 2, 16, 8, S, 128, kv_dtype=dt, q_dtype=dt)
     q, k, v = dev(c["q"], dt), dev(c["k"], dt), dev(c["v"], dt)
     B, Hq, D = q.shape
     part = torch.empty((B, Hq, D + 2), dtype=torch.float32, device="cuda")
-    kernels.fp16_decode_attn(q, k, v, 2, partial_out=part)
-    out = kernels.fp16_decode_attn(q, k, v, 2)
+    kernels.fp16_decode_attn(q, k, v, 2, partial_out=part, cuda_cores=cuda_cores)
+    out = kernels.fp16_decode_attn(q, k, v, 2, cuda_cores=cuda_cores)
     p = part.cpu().numpy()
     ref = oa.decode_dense(c["q"], c["k"], c["v"], 2, 1 / math.sqrt(128), acc="f64")
     close(p[..., 2:] / p[..., 1:2], ref)
     close(out.float().cpu().numpy(), ref, atol=ATOL, rtol=2.0 ** -7)
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,S", [(1, 8, 8, 1), (3, 16, 4, 777), (1, 32, 8, 131072),
+                                        (2, 4, 4, 129), (1, 16, 8, 0)])
+@pytest.mark.parametrize("q_quant", [False, True])
+def test_dense_twin_shapes(B, Hq, Hkv, S, q_quant):
+    """The tensor-core twin over every group size it serves (n_rep 1, 2, 4), ragged
+    lengths, a single token, an empty cache and the per-token q fake quantization."""
+    c = oin.decode_case(5 + S + B, B, Hq, Hkv, max(S, 1), 128, kv_dtype="bf16", q_dtype="bf16")
+    k, v = c["k"][:, :, :S], c["v"][:, :, :S]
+    q, kt, vt = dev(c["q"], "bf16"), dev(np.ascontiguousarray(k), "bf16"), dev(np.ascontiguousarray(v), "bf16")
+    part = torch.empty((B, Hq, 130), dtype=torch.float32, device="cuda")
+    kernels.fp16_decode_attn(q, kt, vt, Hq // Hkv, partial_out=part, q_quant=q_quant)
+    p = part.cpu().numpy()
+    if S == 0:
+        assert np.all(p[..., 1] == 0) and np.all(p[..., 2:] == 0)
+        return
+    qin = oa.quant_dequant(c["q"], (2,), "bf16") if q_quant else c["q"]
+    ref = oa.decode_dense(qin, k, v, Hq // Hkv, 1 / math.sqrt(128), acc="f64")
+    close(p[..., 2:] / p[..., 1:2], ref)
 
 
 def test_reference_layout_and_partial_combine():
