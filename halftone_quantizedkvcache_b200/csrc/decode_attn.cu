@@ -89,6 +89,8 @@ struct Params {
   float* partial_out;  // [B*Hq][kD+2] or null
   float* ws_part;      // [B*Hq][n_split][kD+2]
   int* ws_count;       // [B*Hkv] arrival tickets
+  int* ws_next;        // [B*Hkv] tile claims of the dynamic schedule
+  int dynamic;         // host: use the dynamic tile schedule when the V-scale layout allows
   int* ws_status;
   int n_split;
   int tiles_per_split;
@@ -812,6 +814,7 @@ namespace mmak {
 constexpr int kTileT = 128;                // tokens per tile
 constexpr int kTileB = kTileT * kD;        // 16 KB per K or V tile
 constexpr int kStagesM = 3;
+constexpr int kStatic = kStagesM + 1;      // dynamic schedule: fixed tiles per block before claims
 constexpr float kLimbMax = 8355711.0f;     // 127 * (65536 + 256 + 1): largest |x| of 3 int8 digits
 
 template <int NREP>
@@ -820,7 +823,10 @@ struct MCfg {
   static constexpr int RING = kStagesM * 2 * kTileB;      // 96 KB
   static constexpr int LIMB = kWarps * NT * 8 * 32;       // p' limb staging
   static constexpr int QTAB = NT * 256 * 4;                // q' limb B-fragment words
-  static constexpr int SMEM = 1024 + RING + NREP * kD * 4 + LIMB + 2 * kStagesM * 8 + QTAB;
+  static constexpr int VSM = kStagesM * kTileT * 4;        // dynamic schedule: V scales per stage
+  static_assert(RING % 1024 == 0 && (kTileT * 2) % 128 == 0, "V scale slots on 128-byte boundaries");
+  static constexpr int SMEM =
+      1024 + RING + NREP * kD * 4 + LIMB + 2 * kStagesM * 8 + QTAB + VSM + 16;
   static_assert(kWarps * NREP * kD * 4 + kWarps * NREP * 8 <= RING, "epilogue scratch");
 };
 
@@ -850,6 +856,14 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, i
       " [%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_u32(bar)),
       "l"(pol)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y,
+                                            int z, uint64_t* bar, uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar)), "l"(pol)
       : "memory");
 }
 __device__ __forceinline__ uint64_t l2_evict_first() {
@@ -989,14 +1003,24 @@ __device__ void append_split(const Params& p, int b, int kvh, int S, unsigned ch
   if (d == 0) s_last = ticket_add(p.ws_count + b * p.Hkv + kvh) == p.n_split - 1;
   __syncthreads();
   if (!s_last) return;
+  if (d == 0) p.ws_next[b * p.Hkv + kvh] = 0;  // (dynamic schedule) every split has stopped claiming
   merge_splits<NREP, QDT>(p, b, kvh, reinterpret_cast<float*>(ring), scratch_floats, 0u,
                           merge_bar);
 }
 
-template <int NREP, int SDT, int QDT>
+// DYN: the dynamic tile schedule.  The ntiles tiles of (b, kvh) are shared out
+// among its n_main splits as they go: split j first streams tiles
+// j + k * n_main for k < kStatic (no atomics), then claims tile
+// kStatic * n_main + c with c = atomicAdd(next, 1) until none are left, so a
+// block whose copies were served late simply takes fewer.  Each stage carries
+// its tile index (-1: the block's run has ended) and the tile's V scales, copied
+// by a third tensor map with the tile.  The split partials then cover timing-
+// dependent tile sets: the result is the same attention with float32 sums
+// grouped differently from call to call (not bit-reproducible).
+template <int NREP, int SDT, int QDT, bool DYN>
 __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(
     const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
-    const Params p) {
+    const __grid_constant__ CUtensorMap tmvs, const Params p) {
   using C = MCfg<NREP>;
   using QE = Elem<QDT>;
   using SE = Elem<SDT>;
@@ -1004,11 +1028,15 @@ __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(
   extern __shared__ unsigned char smem_raw[];
   unsigned char* ring = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  float* qs = reinterpret_cast<float*>(ring + C::RING);
+  // V scale slots of the stages (DYN) right after the ring: a tensor copy's
+  // destination must start on a 128-byte boundary (each slot is 512 or 256 bytes)
+  auto* vsm = reinterpret_cast<typename SE::T*>(ring + C::RING);  // [kStagesM][kTileT]
+  float* qs = reinterpret_cast<float*>(ring + C::RING + C::VSM);
   unsigned char* plimb = reinterpret_cast<unsigned char*>(qs + NREP * kD);
   uint64_t* full = reinterpret_cast<uint64_t*>(plimb + C::LIMB);
   uint64_t* empty = full + kStagesM;
   uint32_t* qtab = reinterpret_cast<uint32_t*>(empty + kStagesM);
+  int* stile = reinterpret_cast<int*>(qtab + NT * 256);
   __shared__ float red[kWarps][NREP];
   __shared__ float qmax_s[NREP];
   __shared__ int s_last;
@@ -1043,12 +1071,35 @@ __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(
 
   int issued = 0;
   const uint64_t pol_stream = l2_evict_first();
-  auto issue = [&](int t) {
+  // dynamic schedule (tid 0): fixed part, claims, and the tile of iteration k
+  const int n_main = p.k_new ? p.n_split - 1 : p.n_split;
+  const int ntiles_all = (S + kTileT - 1) / kTileT;
+  int* next_ctr = p.ws_next + b * p.Hkv + kvh;
+  int claim = -1;  // tid 0 (DYN): the claim made one refill ahead (-1: none)
+  auto fixed_tile = [&](int k) {
+    const int t = split + k * n_main;
+    return t < ntiles_all ? t : -1;
+  };
+  // requests iteration t's tile into its stage: static - tile t of this split's run;
+  // DYN - absolute tile `tabs` (-1: no tile, the stage only carries the end mark)
+  auto issue = [&](int t, int tabs = 0) {
     const int st = t % kStagesM;
     unsigned char* dst = ring + st * 2 * kTileB;
-    mbar_arrive_expect_tx(&full[st], 2 * kTileB);
-    tma_load_4d(dst, &tmk, 0, s_begin + t * kTileT, kvh, b, &full[st], pol_stream);
-    tma_load_4d(dst + kTileB, &tmv, 0, s_begin + t * kTileT, kvh, b, &full[st], pol_stream);
+    if constexpr (DYN) {
+      stile[st] = tabs;
+      if (tabs < 0) {
+        mbar_arrive(&full[st]);
+        return;
+      }
+      mbar_arrive_expect_tx(&full[st], 2 * kTileB + kTileT * SE::kBytes);
+      tma_load_4d(dst, &tmk, 0, tabs * kTileT, kvh, b, &full[st], pol_stream);
+      tma_load_4d(dst + kTileB, &tmv, 0, tabs * kTileT, kvh, b, &full[st], pol_stream);
+      tma_load_3d(vsm + st * kTileT, &tmvs, tabs * kTileT, kvh, b, &full[st], pol_stream);
+    } else {
+      mbar_arrive_expect_tx(&full[st], 2 * kTileB);
+      tma_load_4d(dst, &tmk, 0, s_begin + t * kTileT, kvh, b, &full[st], pol_stream);
+      tma_load_4d(dst + kTileB, &tmv, 0, s_begin + t * kTileT, kvh, b, &full[st], pol_stream);
+    }
     issued = t + 1;
   };
   // V scales of this lane's own tokens (row g for even t4, g + 8 for odd t4, of
@@ -1078,9 +1129,11 @@ __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(
     for (int r = 0; r < NREP; ++r) q_raw[r] = qp[b * p.qsb + (kvh * NREP + r) * p.qsh + d];
   };
   if (!p.overlap) load_q();
-  float vs_a[2], vs_b[2];
-  load_vs(0, vs_a);
-  load_vs(1, vs_b);
+  float vs_a[2] = {0.0f, 0.0f}, vs_b[2] = {0.0f, 0.0f};
+  if constexpr (!DYN) {
+    load_vs(0, vs_a);
+    load_vs(1, vs_b);
+  }
   if (tid == 0) {
     for (int s = 0; s < kStagesM; ++s) {
       mbar_init(&full[s], 1);
@@ -1091,8 +1144,13 @@ __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(
   // zero the p' staging (columns 3 and 7 stay zero)
   for (int i = tid; i < C::LIMB / 4; i += kThreads) reinterpret_cast<uint32_t*>(plimb)[i] = 0;
   __syncthreads();
-  if (tid == 0)
-    for (int t = 0; t < min(p.overlap ? kStagesM : 1, ntiles); ++t) issue(t);
+  if (tid == 0) {
+    if constexpr (DYN) {
+      for (int t = 0; t < (p.overlap ? kStagesM : 1); ++t) issue(t, fixed_tile(t));
+    } else {
+      for (int t = 0; t < min(p.overlap ? kStagesM : 1, ntiles); ++t) issue(t);
+    }
+  }
   if (p.k_new && tid == 32) grid_arrive(p, S);  // every thread has read the length
   if (p.overlap) {
     asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -1138,8 +1196,16 @@ __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(
     }
     __syncthreads();
   }
-  if (tid == 0 && !p.overlap)
-    for (int t = 1; t < min(kStagesM, ntiles); ++t) issue(t);
+  if (tid == 0) {
+    if constexpr (DYN) {
+      if (!p.overlap)
+        for (int t = 1; t < kStagesM; ++t) issue(t, fixed_tile(t));
+      // the first claim, after any wait for the previous grid (whose merging blocks reset the counters)
+      if (fixed_tile(kStatic - 1) >= 0) claim = atomicAdd(next_ctr, 1);
+    } else if (!p.overlap) {
+      for (int t = 1; t < min(kStagesM, ntiles); ++t) issue(t);
+    }
+  }
 
   // q' limb B-fragments, built by the whole block into qtab: word
   // (nt, j, hh, lane g * 4 + t4) packs limb g % 4 of head 2 nt + g / 4 at the four
@@ -1220,22 +1286,41 @@ __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(
   unsigned char* my_limb = plimb + warp * NT * 256;
   bool ok = true;
   int consumed = 0;
-  for (int t = 0; t < ntiles; ++t) {
+  // tokens: static - relative to the split's first token; DYN - absolute
+  const int tok_limit = DYN ? S : ntok;
+  for (int t = 0; DYN || t < ntiles; ++t) {
     const int st = t % kStagesM;
     const uint32_t par = (t / kStagesM) & 1;
-    const int base_tok = t * kTileT + warp * 32;  // first token of this warp (within split)
     float vsf[2];
     bool own_ok[2];
+    int base_tok;
+    if constexpr (DYN) {
+      if (!mbar_wait(&full[st], par)) {
+        ok = false;
+        break;
+      }
+      const int tabs = stile[st];
+      if (tabs < 0) break;  // the block's run has ended (the same stage for every warp)
+      base_tok = tabs * kTileT + warp * 32;
 #pragma unroll
-    for (int rb = 0; rb < 2; ++rb) {
-      own_ok[rb] = base_tok + rb * 16 + g + 8 * (t4 & 1) < ntok;
-      vsf[rb] = vs_a[rb];
-      vs_a[rb] = vs_b[rb];
-    }
-    load_vs(t + 2, vs_b);
-    if (!mbar_wait(&full[st], par)) {
-      ok = false;
-      break;
+      for (int rb = 0; rb < 2; ++rb) {
+        const int i = warp * 32 + rb * 16 + g + 8 * (t4 & 1);  // this lane's own token
+        own_ok[rb] = tabs * kTileT + i < S;
+        vsf[rb] = SE::to_f32(vsm[st * kTileT + i]);
+      }
+    } else {
+      base_tok = t * kTileT + warp * 32;  // first token of this warp (within split)
+#pragma unroll
+      for (int rb = 0; rb < 2; ++rb) {
+        own_ok[rb] = base_tok + rb * 16 + g + 8 * (t4 & 1) < ntok;
+        vsf[rb] = vs_a[rb];
+        vs_a[rb] = vs_b[rb];
+      }
+      load_vs(t + 2, vs_b);
+      if (!mbar_wait(&full[st], par)) {
+        ok = false;
+        break;
+      }
     }
     consumed = t + 1;
     const uint32_t kt = smem_u32(ring + st * 2 * kTileB);
@@ -1266,8 +1351,8 @@ __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(
         lo += __shfl_xor_sync(0xffffffffu, lo, 1);
         hi += __shfl_xor_sync(0xffffffffu, hi, 1);
         const int tok = base_tok + rb * 16 + g;
-        sc[nt][rb][0] = tok < ntok ? lo : -INFINITY;
-        sc[nt][rb][1] = tok + 8 < ntok ? hi : -INFINITY;
+        sc[nt][rb][0] = tok < tok_limit ? lo : -INFINITY;
+        sc[nt][rb][1] = tok + 8 < tok_limit ? hi : -INFINITY;
       }
     }
     // ---- online softmax per head; p' limbs of this lane's own two tokens
@@ -1356,7 +1441,25 @@ __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[st]);
-    if (tid == 0 && t + kStagesM < ntiles) {
+    if constexpr (DYN) {
+      if (tid == 0) {
+        if (!mbar_wait(&empty[st], par)) {
+          ok = false;
+          break;
+        }
+        // iteration t + kStagesM: its fixed tile, or the claim made one refill ago (then
+        // the claim for the next refill goes out, its latency hidden by a tile's time)
+        const int k = t + kStagesM;
+        int tabs;
+        if (k < kStatic) {
+          tabs = fixed_tile(k);
+        } else {
+          tabs = claim >= 0 && kStatic * n_main + claim < ntiles_all ? kStatic * n_main + claim : -1;
+        }
+        issue(k, tabs);
+        if (k >= kStatic) claim = tabs >= 0 ? atomicAdd(next_ctr, 1) : -1;
+      }
+    } else if (tid == 0 && t + kStagesM < ntiles) {
       if (!mbar_wait(&empty[st], par)) {
         ok = false;
         break;
@@ -1422,6 +1525,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(
     Os[r] = O;
   }
   if (p.n_split == 1) {
+    if (DYN && tid == 0) *next_ctr = 0;  // ready for the next launch
     finish_heads<NREP, QDT>(p, b, kvh, d, Ms, Ls, Os, gen0);
     return;
   }
@@ -1431,6 +1535,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_mma_kernel(
   if (tid == 0) s_last = ticket_add(p.ws_count + b * p.Hkv + kvh) == p.n_split - 1;
   __syncthreads();
   if (!s_last) return;
+  if (DYN && tid == 0) *next_ctr = 0;  // every split has stopped claiming
   merge_splits<NREP, QDT>(p, b, kvh, reinterpret_cast<float*>(ring), C::RING / 4, gen0,
                           &merge_bar);
 }
@@ -1844,9 +1949,10 @@ inline Plan make_plan(int units, int S, int slots, int sms, int tile = kTile,
 }
 
 inline size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
-// arrival tickets [B*Hkv], after the 256-byte header
+// arrival tickets [B*Hkv] then the dynamic schedule's tile claims [B*Hkv],
+// after the 256-byte header
 inline size_t tickets_bytes(int B, int Hkv) {
-  return align256(sizeof(int) * static_cast<size_t>(B) * Hkv);
+  return align256(2 * sizeof(int) * static_cast<size_t>(B) * Hkv);
 }
 
 inline size_t workspace_bytes(int B, int Hq, int Hkv, int S, int sms) {
@@ -1880,6 +1986,7 @@ int launch(Params p, int B, void* ws, size_t ws_bytes, cudaStream_t st) {
   char* w = static_cast<char*>(ws);
   p.ws_status = reinterpret_cast<int*>(w);
   p.ws_count = reinterpret_cast<int*>(w + 256);
+  p.ws_next = p.ws_count + static_cast<size_t>(B) * p.Hkv;
   p.ws_part = reinterpret_cast<float*>(w + 256 + tickets_bytes(B, p.Hkv));
   p.n_split = pl.n_split;
   p.tiles_per_split = pl.tiles_per_split;
@@ -1922,19 +2029,48 @@ inline int encode_kv_map(CUtensorMap* m, const void* base, int64_t sb, int64_t s
   return r == CUDA_SUCCESS ? HQ_OK : HQ_ERR_INVALID_ARGUMENT;
 }
 
+// V scales [B, Hkv, S] with element strides (sb, sh, 1) for the dynamic schedule's
+// third tensor map: boxes of 128 tokens, zero fill past S.  Needs a token stride
+// of 1, a 16-byte aligned base and head / batch strides of multiples of 16 bytes.
+inline bool vs_map_ok(const void* base, int esz, int64_t sb, int64_t sh, int64_t ss) {
+  return base && ss == 1 && reinterpret_cast<uintptr_t>(base) % 16 == 0 && (sh * esz) % 16 == 0 &&
+         (sb * esz) % 16 == 0;
+}
+inline int encode_vs_map(CUtensorMap* m, const void* base, int esz, int64_t sb, int64_t sh, int S,
+                         int Hkv, int B) {
+  auto enc = encode_fn();
+  if (!enc) return HQ_ERR_UNSUPPORTED;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(S > 0 ? S : 1), static_cast<cuuint64_t>(Hkv),
+                        static_cast<cuuint64_t>(B)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(sh * esz), static_cast<cuuint64_t>(sb * esz)};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(mmak::kTileT), 1, 1};
+  cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = enc(m, esz == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT16,
+                   3, const_cast<void*>(base), dims, strides, box, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? HQ_OK : HQ_ERR_INVALID_ARGUMENT;
+}
+
 template <int NREP, int SDT, int QDT>
 int launch_mma(Params p, int B, void* ws, size_t ws_bytes, cudaStream_t st) {
   using C = mmak::MCfg<NREP>;
-  auto kern = mmak::decode_mma_kernel<NREP, SDT, QDT>;
+  const bool dyn = p.dynamic && vs_map_ok(p.vsc, Elem<SDT>::kBytes, p.vscb, p.vsch, p.vscs);
+  auto kern = dyn ? mmak::decode_mma_kernel<NREP, SDT, QDT, true>
+                  : mmak::decode_mma_kernel<NREP, SDT, QDT, false>;
   int dev = 0;
   cudaGetDevice(&dev);
   static std::atomic<int> occ[64];
   int per_sm = (dev >= 0 && dev < 64) ? occ[dev].load(std::memory_order_relaxed) : 0;
   if (per_sm <= 0) {
-    cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(kern),
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
-    if (e != cudaSuccess) return static_cast<int>(e);
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, C::SMEM);
+    // both schedules: the same shared memory, so the same occupancy
+    for (auto k : {mmak::decode_mma_kernel<NREP, SDT, QDT, true>,
+                   mmak::decode_mma_kernel<NREP, SDT, QDT, false>}) {
+      cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(k),
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+      if (e != cudaSuccess) return static_cast<int>(e);
+    }
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, C::SMEM);
     if (e != cudaSuccess) return static_cast<int>(e);
     if (per_sm <= 0) return HQ_ERR_UNSUPPORTED;
     if (dev >= 0 && dev < 64) occ[dev].store(per_sm, std::memory_order_relaxed);
@@ -1952,13 +2088,17 @@ int launch_mma(Params p, int B, void* ws, size_t ws_bytes, cudaStream_t st) {
   if (p.k_new && ws_bytes < 256 + tickets_bytes(B, p.Hkv) +
                                 sizeof(float) * static_cast<size_t>(B) * p.Hq * n_rows * kPartRow)
     return HQ_ERR_WORKSPACE;
-  CUtensorMap tmk, tmv;
+  CUtensorMap tmk, tmv, tmvs;
   int rc = encode_kv_map(&tmk, p.k, p.kvsb, p.kvsh, p.S, p.Hkv, B);
   if (rc == HQ_OK) rc = encode_kv_map(&tmv, p.v, p.kvsb, p.kvsh, p.S, p.Hkv, B);
+  if (rc == HQ_OK && dyn)
+    rc = encode_vs_map(&tmvs, p.vsc, Elem<SDT>::kBytes, p.vscb, p.vsch, p.S, p.Hkv, B);
   if (rc != HQ_OK) return rc;
+  if (!dyn) tmvs = tmv;  // unused by the static schedule
   char* w = static_cast<char*>(ws);
   p.ws_status = reinterpret_cast<int*>(w);
   p.ws_count = reinterpret_cast<int*>(w + 256);
+  p.ws_next = p.ws_count + static_cast<size_t>(B) * p.Hkv;
   p.ws_part = reinterpret_cast<float*>(w + 256 + tickets_bytes(B, p.Hkv));
   p.n_split = n_rows;
   p.tiles_per_split = pl.tiles_per_split;
@@ -1989,11 +2129,11 @@ int launch_mma(Params p, int B, void* ws, size_t ws_bytes, cudaStream_t st) {
     }
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tmk, tmv, p);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tmk, tmv, tmvs, p);
     if (e != cudaSuccess) cudaGetLastError();  // leave no error behind for the caller's next call
     return e == cudaSuccess ? HQ_OK : static_cast<int>(e);
   }
-  kern<<<grid, kThreads, C::SMEM, st>>>(tmk, tmv, p);
+  kern<<<grid, kThreads, C::SMEM, st>>>(tmk, tmv, tmvs, p);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? HQ_OK : static_cast<int>(e);
 }
@@ -2043,6 +2183,7 @@ int launch_dense_mma(Params p, int B, void* ws, size_t ws_bytes, cudaStream_t st
   char* w = static_cast<char*>(ws);
   p.ws_status = reinterpret_cast<int*>(w);
   p.ws_count = reinterpret_cast<int*>(w + 256);
+  p.ws_next = p.ws_count + static_cast<size_t>(B) * p.Hkv;
   p.ws_part = reinterpret_cast<float*>(w + 256 + tickets_bytes(B, p.Hkv));
   p.n_split = pl.n_split;
   p.tiles_per_split = pl.tiles_per_split;
@@ -2119,7 +2260,8 @@ static int decode_int8_impl(const void* q, int q_dtype, const int64_t q_strides[
                               const int* seq_len = nullptr, int S_plan = 0, int overlap = 0,
                               const void* k_new = nullptr, const void* v_new = nullptr,
                               const int64_t* kn_strides = nullptr,
-                              const int64_t* vn_strides = nullptr, int clear_header = 0) {
+                              const int64_t* vn_strides = nullptr, int clear_header = 0,
+                              int dynamic = 0) {
   int rc = check_common(q_strides, kv_strides, out_strides, partial_out, B, Hq, Hkv, S, D, workspace);
   if (rc != HQ_OK) return rc;
   // an empty cache (S == 0) may come with null K/V/v_scale pointers
@@ -2162,6 +2304,7 @@ static int decode_int8_impl(const void* q, int q_dtype, const int64_t q_strides[
   p.S_plan = S_plan < 0 ? 0 : (S_plan > S ? S : S_plan);
   p.overlap = overlap;
   p.clear_header = clear_header;
+  p.dynamic = dynamic;
   p.k_new = k_new;
   p.v_new = v_new;
   if (k_new) {
@@ -2227,11 +2370,13 @@ extern "C" int hq_decode_int8_ex(const void* q, int q_dtype, const int64_t q_str
                                  void* out, const int64_t out_strides[3], float* partial_out,
                                  void* workspace, size_t workspace_bytes, unsigned flags,
                                  hq_stream_t stream) {
-  if (flags & ~static_cast<unsigned>(HQ_DECODE_OVERLAP_PREVIOUS)) return HQ_ERR_INVALID_ARGUMENT;
+  if (flags & ~static_cast<unsigned>(HQ_DECODE_OVERLAP_PREVIOUS | HQ_DECODE_DYNAMIC_TILES))
+    return HQ_ERR_INVALID_ARGUMENT;
   return decode_int8_impl(q, q_dtype, q_strides, k, v, kv_strides, k_scale, v_scale, scale_dtype,
                           ksc_strides, vsc_strides, B, Hq, Hkv, S, D, sm_scale, q_quant, out,
                           out_strides, partial_out, workspace, workspace_bytes, stream, nullptr, 0,
-                          0, nullptr, 0, (flags & HQ_DECODE_OVERLAP_PREVIOUS) ? 1 : 0);
+                          0, nullptr, 0, (flags & HQ_DECODE_OVERLAP_PREVIOUS) ? 1 : 0, nullptr,
+                          nullptr, nullptr, nullptr, 0, (flags & HQ_DECODE_DYNAMIC_TILES) ? 1 : 0);
 }
 
 // ---------------------------------------------------------------- device-resident length

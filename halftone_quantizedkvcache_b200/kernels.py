@@ -421,7 +421,7 @@ def _check_cache_shapes(what: str, B: int, D: int, k4, v4, ks4=None, vs4=None) -
 
 def int8_decode_attn(q, k_i8, k_sc, v_i8, v_sc, n_rep=None, *, sm_scale=None, q_quant=False,
                      out=None, partial_out=None, peers=None, seq_len=None, s_plan=None,
-                     overlap_prev=False, append=None):
+                     overlap_prev=False, append=None, dynamic_tiles=False):
     """Int8 decode attention (split-KV), the contract of ``int8_decode_attn``
     (src/kernels/int8_decode_attn_triton.py:101-113), batched.
 
@@ -447,6 +447,12 @@ def int8_decode_attn(q, k_i8, k_sc, v_i8, v_sc, n_rep=None, *, sm_scale=None, q_
     ``overlap_prev``: the cache is not written by the kernel launched just
     before this call on the stream; the launch overlaps that kernel's tail
     (programmatic dependent launch, ``hq_decode_int8_ex``).
+    ``dynamic_tiles``: the splits of a (sequence, kv head) claim their 128-token
+    tiles as they go instead of streaming fixed runs (``HQ_DECODE_DYNAMIC_TILES``;
+    needs token-contiguous V scales with 16-byte aligned rows, else the fixed
+    runs are used): faster when the blocks are served unevenly, but the float32
+    sums are grouped by timing, so results may differ in their last bits from
+    call to call.
     """
     for t, n in ((q, "q"), (k_i8, "k_i8"), (k_sc, "k_sc"), (v_i8, "v_i8"), (v_sc, "v_sc")):
         _cuda(t, f"int8_decode_attn {n}")
@@ -454,8 +460,8 @@ def int8_decode_attn(q, k_i8, k_sc, v_i8, v_sc, n_rep=None, *, sm_scale=None, q_
         raise ValueError("int8_decode_attn: peers and partial_out are exclusive")
     if seq_len is not None and (peers is not None or partial_out is not None):
         raise ValueError("int8_decode_attn: seq_len excludes peers and partial_out")
-    if overlap_prev and (peers is not None or seq_len is not None):
-        raise ValueError("int8_decode_attn: overlap_prev excludes peers and seq_len")
+    if (overlap_prev or dynamic_tiles) and (peers is not None or seq_len is not None):
+        raise ValueError("int8_decode_attn: overlap_prev and dynamic_tiles exclude peers and seq_len")
     qb, restore = _as_bhd(q)
     k4, v4, ks4, vs4 = _as_bhsd(k_i8), _as_bhsd(v_i8), _as_bhsd(k_sc), _as_bhsd(v_sc)
     B, Hq, D = qb.shape
@@ -525,10 +531,11 @@ def int8_decode_attn(q, k_i8, k_sc, v_i8, v_sc, n_rep=None, *, sm_scale=None, q_
                                             _stream(qb.device))
         check(rc, "hq_decode_int8_peer")
         return restore(res) if out is None else res
-    if overlap_prev:
+    if overlap_prev or dynamic_tiles:
+        flags = (1 if overlap_prev else 0) | (2 if dynamic_tiles else 0)
         rc = _lib.lib().hq_decode_int8_ex(
             *args, partial_out.data_ptr() if partial_out is not None else None, ws.data_ptr(),
-            ws.numel(), 1, _stream(qb.device))
+            ws.numel(), flags, _stream(qb.device))
         check(rc, "hq_decode_int8_ex")
     else:
         rc = _lib.lib().hq_decode_int8(

@@ -218,7 +218,7 @@ HQ_API int hq_decode_int8(const void* q, int q_dtype, const int64_t q_strides[3]
  *   consecutive layers, or a decode whose cache was appended to earlier.
  *   With flags == 0 this is hq_decode_int8.
  */
-enum { HQ_DECODE_OVERLAP_PREVIOUS = 1 };
+enum { HQ_DECODE_OVERLAP_PREVIOUS = 1, HQ_DECODE_DYNAMIC_TILES = 2 };
 HQ_API int hq_decode_int8_ex(const void* q, int q_dtype, const int64_t q_strides[3],
                              const int8_t* k, const int8_t* v, const int64_t kv_strides[3],
                              const void* k_scale, const void* v_scale, int scale_dtype,

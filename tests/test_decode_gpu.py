@@ -253,3 +253,24 @@ def test_wrappers_reject_shapes_that_disagree():
     with pytest.raises(ValueError):
         kernels.int8_prefill_attn(qp, k, ks, k, vs, 2)            # head dim 64 against 128
     assert kernels.int8_decode_attn(q[:1], k, ks, k, vs, 2).shape == (1, 16, 128)
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,S", [(1, 16, 8, 32768), (2, 32, 8, 5000), (3, 16, 4, 777),
+                                        (1, 8, 8, 1), (1, 4, 1, 131072), (2, 16, 8, 100)])
+def test_dynamic_tile_schedule(B, Hq, Hkv, S):
+    """HQ_DECODE_DYNAMIC_TILES: splits claim tiles as they go (V scales by tensor map).
+    Within 1e-3 of the oracle, repeated calls included (the claim counters reset);
+    fp16 V scales (the cache's layout) and fp32 ones."""
+    c = oin.decode_case(31 + S + B, B, Hq, Hkv, S, 128)
+    q = dev(c["q"], "bf16")
+    k8, v8 = dev(c["k_i8"]), dev(c["v_i8"])
+    for sdt, name in ((torch.float32, "f32"), (torch.float16, "f16")):
+        ks, vs = dev(c["k_sc"]).to(sdt), dev(c["v_sc"]).to(sdt)
+        ref = oracle_int8(c, scale_dt=name)
+        part = torch.empty((B, Hq, 130), dtype=torch.float32, device="cuda")
+        for _ in range(3):
+            part.fill_(float("nan"))
+            kernels.int8_decode_attn(q, k8, ks, v8, vs, Hq // Hkv, partial_out=part,
+                                     dynamic_tiles=True)
+            p = part.cpu().numpy()
+            close(p[..., 2:] / p[..., 1:2], ref)

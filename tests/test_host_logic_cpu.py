@@ -20,7 +20,7 @@ def test_new_entry_points_reject_bad_arguments():
     # hq_decode_int8_ex: unknown flag bits
     args = [16, 1, st3, 16, 16, kv, 16, 16, 0, st3, st3, 1, 16, 8, 64, 128, 0.1, 0, 16, st3, None,
             256, 1 << 20]
-    assert L.hq_decode_int8_ex(*args, 2, None) == -1
+    assert L.hq_decode_int8_ex(*args, 4, None) == -1
     # hq_decode_int8_len: no length pointer
     largs = [16, 1, st3, 16, 16, kv, 16, 16, 0, st3, st3, 1, 16, 8, 64, None, 64, 128, 0.1, 0, 16,
              st3, 256, 1 << 20, None]
