@@ -2174,7 +2174,10 @@ int launch_dense_mma(Params p, int B, void* ws, size_t ws_bytes, cudaStream_t st
     if (dev >= 0 && dev < 64) occ[dev].store(per_sm, std::memory_order_relaxed);
   }
   const int sms = sm_count(dev);
-  const Plan pl = make_plan(B * p.Hkv, p.S, per_sm * sms, sms, mmab::kTileT);
+  // one block per SM: a second wave would leave the SMs of finished blocks idle while
+  // it starts, so plans fit in one wave when the work allows
+  const Plan pl = make_plan(B * p.Hkv, p.S, per_sm * sms, sms, mmab::kTileT,
+                            per_sm == 1 && B * p.Hkv <= sms);
   if (ws_bytes < workspace_bytes(B, p.Hq, p.Hkv, p.S, sms)) return HQ_ERR_WORKSPACE;
   CUtensorMap tmk, tmv;
   int rc = encode_kv_map16(&tmk, p.k, p.kvsb, p.kvsh, p.S, p.Hkv, B);
