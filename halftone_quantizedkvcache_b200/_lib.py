@@ -71,6 +71,10 @@ SIGNATURES = {
     "hq_kblock_decode_workspace_bytes": (_Z, [_I, _I, _I, _I, _I]),
     "hq_kblock_decode": (_I, [_P, _I, _A4, _P, _A4, _P, _A4, _P, _A4, _P, _I, _A4, _I, _I, _I, _I,
                               _I, _I, _F, _P, _A4, _P, _Z, _P]),
+    "hq_kblock_write_at": (_I, [_P, _P, _I, _A4, _A4, _I, _I, _I, _I, _P, _A4, _P, _A4, _P, _A4,
+                                _P, _A4, _P, _P, _A4, _I, _P, _P]),
+    "hq_kblock_decode_len": (_I, [_P, _I, _A4, _P, _A4, _P, _A4, _P, _A4, _P, _I, _A4, _I, _I, _I,
+                                  _I, _P, _I, _I, _I, _F, _P, _A4, _P, _Z, _P]),
     "hq_kblock_dequant": (_I, [_P, _A4, _P, _A4, _I, _I, _I, _I, _I, _P, _I, _A4, _P]),
     "hq_read_status": (_I, [_P, _P]),
     "hq_set_plan_sms": (_I, [_I, _I]),

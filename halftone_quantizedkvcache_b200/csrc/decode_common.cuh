@@ -87,6 +87,9 @@ struct Params {
   // host only: zero the workspace's status word and arrival tickets on the
   // stream just before the launch (after every argument check has passed)
   int clear_header;
+  // block-wise K layout (decode_kblock.cu): tokens per K-scale block; ksc then points
+  // at float32 scales [B, Hkv, n_blocks, kD] with strides (kscb, ksch, kscd = per block)
+  int kblock_tokens;
   // fused append (with seq_len): the token at row *seq_len is written by this
   // launch from k_new / v_new [B, Hkv, 1, D] (q's dtype), by one extra block per
   // (b, kv head) - split n_split - 1 - which also contributes the token's

@@ -36,6 +36,15 @@
 namespace hq {
 
 int current_sm_count();
+int kblock_decode_mma(const void* q, int q_dtype, const int64_t q_strides[3],
+                      const int8_t* k_cache, const int64_t kq_strides[3], const float* k_scale,
+                      const int64_t ks_strides[3], const int8_t* v_cache,
+                      const int64_t vq_strides[3], const void* v_scale, int scale_dtype,
+                      const int64_t vs_strides[3], int B, int Hq, int Hkv, int S, int D,
+                      int block_tokens, float sm_scale, void* out, const int64_t out_strides[3],
+                      void* workspace, size_t workspace_bytes, hq_stream_t stream,
+                      const int* seq_len = nullptr, int S_plan = 0);
+size_t kblock_decode_mma_workspace_bytes(int B, int Hq, int Hkv, int S, int D);
 
 namespace kb {
 
@@ -62,6 +71,11 @@ struct WriteParams {
   int64_t vssb, vssh, vsss;
   int D, BT, pos, S_new, blk0;
   int tail_mode;                   // 0: write the tail here, 1: leave it, 2: only write it
+  // device-resident length {length, ticket, status, -} (one-token writes): the token
+  // goes to row lens[0], the grid's last block advances it; a full cache (capacity
+  // cap) writes nothing and reports HQ_ERR_INVALID_ARGUMENT in lens[2]
+  int* lens;
+  int cap;
 };
 
 template <int DT>
@@ -89,14 +103,25 @@ __global__ void __launch_bounds__(kWriteThreads) kblock_write_kernel(WriteParams
   using E = Elem<DT>;
   using T = typename E::T;
   __shared__ float smax[2 * kWriteThreads];
+  __shared__ int s_pos;
   const int tid = threadIdx.x;
   constexpr int P = D / 2, G = kWriteThreads / P;
   const int j = tid % P, g = tid / P;
   const int c0 = 2 * j;
-  const int blk = p.blk0 + blockIdx.x;
+  int pos = p.pos, blk = p.blk0 + blockIdx.x;
+  if (p.lens) {
+    if (tid == 0) s_pos = __ldcg(p.lens);
+    __syncthreads();
+    pos = s_pos;
+    if (pos < 0 || pos + p.S_new > p.cap) {  // full cache: nothing is written
+      if (tid == 0) report_error(p.lens + 2, HQ_ERR_INVALID_ARGUMENT);
+      return;
+    }
+    blk = pos / p.BT + blockIdx.x;
+  }
   const int64_t b = blockIdx.z, h = blockIdx.y;
   const int r0 = blk * p.BT;
-  const int lo = max(r0, p.pos), hi = min(r0 + p.BT, p.pos + p.S_new);  // new rows here
+  const int lo = max(r0, pos), hi = min(r0 + p.BT, pos + p.S_new);  // new rows here
   const int n_old = lo - r0;                                             // rows already held
   const bool keep_tail = hi < r0 + p.BT;   // the block stays open: its originals are kept
   const T* kin = reinterpret_cast<const T*>(p.k) + b * p.ksb + h * p.ksh;
@@ -105,7 +130,7 @@ __global__ void __launch_bounds__(kWriteThreads) kblock_write_kernel(WriteParams
   if (p.tail_mode == 2) {
     if (keep_tail)
       for (int r = lo + g; r < hi; r += G) {
-        const T* x = kin + static_cast<int64_t>(r - p.pos) * p.kss + c0;
+        const T* x = kin + static_cast<int64_t>(r - pos) * p.kss + c0;
         T* t = tail + static_cast<int64_t>(r - r0) * p.kts + c0;
         t[0] = x[0];
         t[1] = x[1];
@@ -118,7 +143,7 @@ __global__ void __launch_bounds__(kWriteThreads) kblock_write_kernel(WriteParams
 #pragma unroll 8
   for (int r = lo + g; r < hi; r += G) {
     float x0, x1;
-    load_pair<DT>(kin + static_cast<int64_t>(r - p.pos) * p.kss + c0, x0, x1);
+    load_pair<DT>(kin + static_cast<int64_t>(r - pos) * p.kss + c0, x0, x1);
     a0 = fmaxf(a0, fabsf(x0));
     a1 = fmaxf(a1, fabsf(x1));
   }
@@ -151,7 +176,7 @@ __global__ void __launch_bounds__(kWriteThreads) kblock_write_kernel(WriteParams
   // pass 2: codes of the new rows (and their originals while the block is open)
 #pragma unroll 4
   for (int r = lo + g; r < hi; r += G) {
-    const T* xp = kin + static_cast<int64_t>(r - p.pos) * p.kss + c0;
+    const T* xp = kin + static_cast<int64_t>(r - pos) * p.kss + c0;
     float x0, x1;
     load_pair<DT>(xp, x0, x1);
     store_pair(kq + static_cast<int64_t>(r) * p.kqs, q0.code(x0), q1.code(x1));
@@ -190,7 +215,7 @@ __global__ void __launch_bounds__(kWriteThreads) kblock_write_kernel(WriteParams
         m[u] = 0.0f;
 #pragma unroll
         for (int i = 0; i < kN; ++i) {
-          x[u][i] = r < hi ? E::to_f32(vin[static_cast<int64_t>(r - p.pos) * p.vss + lane + 32 * i]) : 0.0f;
+          x[u][i] = r < hi ? E::to_f32(vin[static_cast<int64_t>(r - pos) * p.vss + lane + 32 * i]) : 0.0f;
           m[u] = fmaxf(m[u], fabsf(x[u][i]));
         }
       }
@@ -211,6 +236,18 @@ __global__ void __launch_bounds__(kWriteThreads) kblock_write_kernel(WriteParams
           if (p.vs32) p.vs32[so] = qv.scale;
           if (p.vs16) p.vs16[so] = __float2half_rn(qv.scale);
         }
+      }
+    }
+  }
+  if (p.lens) {
+    // every block has read lens[0]; the last one to arrive advances it
+    __syncthreads();
+    if (tid == 0) {
+      __threadfence();
+      const int total = static_cast<int>(gridDim.x * gridDim.y * gridDim.z);
+      if (atomicAdd(p.lens + 1, 1) == total - 1) {
+        p.lens[1] = 0;
+        p.lens[0] = pos + p.S_new;
       }
     }
   }
@@ -616,11 +653,17 @@ static Plan plan(int B, int Hkv, int S, int sms, int per_sm) {
 
 static size_t al256(size_t n) { return (n + 255) & ~size_t(255); }
 
+// Workspace layout, shared with the tensor-core kernel (decode_common.cuh) so that
+// either kernel finds the other's arrival tickets zero: a 256-byte header (status
+// word), the ticket region [B*Hkv] x 2 ints from byte 256, then the split partials.
+static size_t tickets_region(int B, int Hkv) {
+  return al256(2 * sizeof(int) * static_cast<size_t>(B) * Hkv);
+}
 static size_t ws_bytes(int B, int Hq, int Hkv, int S, int D, int sms, int per_sm) {
   const Plan pl = plan(B, Hkv, S, sms, per_sm);
   if (pl.n_split <= 1) return 256;
   const size_t rows = static_cast<size_t>(B) * Hq * pl.n_split;
-  return al256(sizeof(int) * static_cast<size_t>(B) * Hkv) + al256(rows * 2 * sizeof(float)) +
+  return 256 + tickets_region(B, Hkv) + al256(rows * 2 * sizeof(float)) +
          al256(rows * D * sizeof(float));
 }
 
@@ -704,19 +747,20 @@ static int launch_decode(const DecParams& p, int B, cudaStream_t st) {
 using namespace hq;
 using namespace hq::kb;
 
-extern "C" int hq_kblock_write(const void* k_new, const void* v_new, int x_dtype,
-                               const int64_t k_strides[4], const int64_t v_strides[4], int B,
-                               int H, int pos, int S_new, int D, int block_tokens,
-                               int8_t* k_cache, const int64_t kq_strides[4], float* k_scale,
-                               const int64_t ks_strides[3], void* k_tail,
-                               const int64_t kt_strides[4], int8_t* v_cache,
-                               const int64_t vq_strides[4], float* v_scale_f32,
-                               uint16_t* v_scale_f16, const int64_t vs_strides[3], int capacity,
-                               hq_stream_t stream) {
+static int kblock_write_impl(const void* k_new, const void* v_new, int x_dtype,
+                             const int64_t k_strides[4], const int64_t v_strides[4], int B,
+                             int H, int pos, int S_new, int D, int block_tokens,
+                             int8_t* k_cache, const int64_t kq_strides[4], float* k_scale,
+                             const int64_t ks_strides[3], void* k_tail,
+                             const int64_t kt_strides[4], int8_t* v_cache,
+                             const int64_t vq_strides[4], float* v_scale_f32,
+                             uint16_t* v_scale_f16, const int64_t vs_strides[3], int capacity,
+                             int* lens, hq_stream_t stream) {
   if (!k_new || !k_strides || !k_cache || !kq_strides || !k_scale || !ks_strides || !k_tail ||
       !kt_strides || B < 0 || H < 0 || pos < 0 || S_new < 1 || capacity < 1 ||
       static_cast<int64_t>(pos) + S_new > capacity)
     return HQ_ERR_INVALID_ARGUMENT;
+  if (lens && (S_new != 1 || !al(lens, 4))) return HQ_ERR_INVALID_ARGUMENT;
   if (v_new && (!v_strides || !v_cache || !vq_strides || (!v_scale_f32 && !v_scale_f16) ||
                 !vs_strides || (v_scale_f32 && v_scale_f16)))
     return HQ_ERR_INVALID_ARGUMENT;
@@ -753,6 +797,13 @@ extern "C" int hq_kblock_write(const void* k_new, const void* v_new, int x_dtype
   p.BT = block_tokens;
   p.pos = pos;
   p.S_new = S_new;
+  p.lens = lens;
+  p.cap = capacity;
+  if (lens) {  // one token: one block, whose index the kernel takes from lens[0]
+    p.blk0 = 0;
+    p.tail_mode = 0;
+    return launch_write(p, x_dtype, dim3(1, H, B), reinterpret_cast<cudaStream_t>(stream));
+  }
   const int blk0 = pos / block_tokens, blk1 = (pos + S_new - 1) / block_tokens;
   p.blk0 = blk0;
   // the first block reads the tail (its earlier rows) while the last one would write
@@ -770,13 +821,46 @@ extern "C" int hq_kblock_write(const void* k_new, const void* v_new, int x_dtype
   return launch_write(p, x_dtype, dim3(1, H, B), st);
 }
 
+extern "C" int hq_kblock_write(const void* k_new, const void* v_new, int x_dtype,
+                               const int64_t k_strides[4], const int64_t v_strides[4], int B,
+                               int H, int pos, int S_new, int D, int block_tokens,
+                               int8_t* k_cache, const int64_t kq_strides[4], float* k_scale,
+                               const int64_t ks_strides[3], void* k_tail,
+                               const int64_t kt_strides[4], int8_t* v_cache,
+                               const int64_t vq_strides[4], float* v_scale_f32,
+                               uint16_t* v_scale_f16, const int64_t vs_strides[3], int capacity,
+                               hq_stream_t stream) {
+  return kblock_write_impl(k_new, v_new, x_dtype, k_strides, v_strides, B, H, pos, S_new, D,
+                           block_tokens, k_cache, kq_strides, k_scale, ks_strides, k_tail,
+                           kt_strides, v_cache, vq_strides, v_scale_f32, v_scale_f16, vs_strides,
+                           capacity, nullptr, stream);
+}
+
+extern "C" int hq_kblock_write_at(const void* k_new, const void* v_new, int x_dtype,
+                                  const int64_t k_strides[4], const int64_t v_strides[4], int B,
+                                  int H, int D, int block_tokens, int8_t* k_cache,
+                                  const int64_t kq_strides[4], float* k_scale,
+                                  const int64_t ks_strides[3], void* k_tail,
+                                  const int64_t kt_strides[4], int8_t* v_cache,
+                                  const int64_t vq_strides[4], float* v_scale_f32,
+                                  uint16_t* v_scale_f16, const int64_t vs_strides[3],
+                                  int capacity, int* lens, hq_stream_t stream) {
+  if (!lens) return HQ_ERR_INVALID_ARGUMENT;
+  return kblock_write_impl(k_new, v_new, x_dtype, k_strides, v_strides, B, H, 0, 1, D,
+                           block_tokens, k_cache, kq_strides, k_scale, ks_strides, k_tail,
+                           kt_strides, v_cache, vq_strides, v_scale_f32, v_scale_f16, vs_strides,
+                           capacity, lens, stream);
+}
+
 extern "C" size_t hq_kblock_decode_workspace_bytes(int B, int Hq, int Hkv, int S, int D) {
   if (B < 1 || Hkv < 1 || Hq < Hkv || Hq % Hkv || S < 1 || (D != 64 && D != 128)) return 0;
   const int NR = Hq / Hkv;
   if (NR != 1 && NR != 2 && NR != 4 && NR != 8) return 0;
   const int per_sm = per_sm_for(NR, D);
   if (per_sm < 1) return 0;
-  return ws_bytes(B, Hq, Hkv, S, D, current_sm_count(), per_sm);
+  // either kernel may serve the call: room for the larger of their layouts
+  return std::max(ws_bytes(B, Hq, Hkv, S, D, current_sm_count(), per_sm),
+                  kblock_decode_mma_workspace_bytes(B, Hq, Hkv, S, D));
 }
 
 extern "C" int hq_kblock_decode(const void* q, int q_dtype, const int64_t q_strides[3],
@@ -805,6 +889,15 @@ extern "C" int hq_kblock_decode(const void* q, int q_dtype, const int64_t q_stri
       kq_strides[1] % 16 || kq_strides[2] % 16 || !al(v_cache, 16) || vq_strides[0] % 16 ||
       vq_strides[1] % 16 || vq_strides[2] % 16)
     return HQ_ERR_INVALID_ARGUMENT;
+  // the tensor-core kernel (decode_kblock.cu) for head_dim 128 and up to 4 q heads per
+  // kv head; the CUDA-core kernel below for the rest
+  if (B <= 65535) {
+    const int rc = kblock_decode_mma(q, q_dtype, q_strides, k_cache, kq_strides, k_scale,
+                                     ks_strides, v_cache, vq_strides, v_scale, scale_dtype,
+                                     vs_strides, B, Hq, Hkv, S, D, block_tokens, sm_scale, out,
+                                     out_strides, workspace, workspace_bytes, stream);
+    if (rc != HQ_ERR_UNSUPPORTED) return rc;
+  }
   const int sms = current_sm_count();
   const int per_sm = per_sm_for(NR, D);
   if (per_sm < 1) return HQ_ERR_UNSUPPORTED;
@@ -835,8 +928,8 @@ extern "C" int hq_kblock_decode(const void* q, int q_dtype, const int64_t q_stri
     if (!workspace || workspace_bytes < need || !al(workspace, 256)) return HQ_ERR_WORKSPACE;
     char* w = static_cast<char*>(workspace);
     const size_t rows = static_cast<size_t>(B) * Hq * pl.n_split;
-    p.ws_cnt = reinterpret_cast<int*>(w);
-    w += al256(sizeof(int) * static_cast<size_t>(B) * Hkv);
+    p.ws_cnt = reinterpret_cast<int*>(w + 256);
+    w += 256 + tickets_region(B, Hkv);
     p.ws_ml = reinterpret_cast<float*>(w);
     w += al256(rows * 2 * sizeof(float));
     p.ws_o = reinterpret_cast<float*>(w);
@@ -855,6 +948,38 @@ extern "C" int hq_kblock_decode(const void* q, int q_dtype, const int64_t q_stri
     HQ_KB_NR(64)
   }
 #undef HQ_KB_NR
+}
+
+extern "C" int hq_kblock_decode_len(const void* q, int q_dtype, const int64_t q_strides[3],
+                                    const int8_t* k_cache, const int64_t kq_strides[3],
+                                    const float* k_scale, const int64_t ks_strides[3],
+                                    const int8_t* v_cache, const int64_t vq_strides[3],
+                                    const void* v_scale, int scale_dtype,
+                                    const int64_t vs_strides[3], int B, int Hq, int Hkv,
+                                    int capacity, const int* seq_len, int S_plan, int D,
+                                    int block_tokens, float sm_scale, void* out,
+                                    const int64_t out_strides[3], void* workspace,
+                                    size_t workspace_bytes, hq_stream_t stream) {
+  if (!q || !q_strides || !k_cache || !kq_strides || !k_scale || !ks_strides || !v_cache ||
+      !vq_strides || !v_scale || !vs_strides || !out || !out_strides || !seq_len ||
+      !al(seq_len, 4) || B < 0 || Hkv < 1 || Hq < Hkv || Hq % Hkv || capacity < 1)
+    return HQ_ERR_INVALID_ARGUMENT;
+  if (q_dtype != HQ_DTYPE_BF16 && q_dtype != HQ_DTYPE_F16 && q_dtype != HQ_DTYPE_F32)
+    return HQ_ERR_UNSUPPORTED;
+  if ((scale_dtype != HQ_DTYPE_F32 && scale_dtype != HQ_DTYPE_F16) || !valid_bt(block_tokens))
+    return HQ_ERR_UNSUPPORTED;
+  if (B == 0) return HQ_OK;
+  if (B > 65535) return HQ_ERR_UNSUPPORTED;
+  if (q_strides[2] != 1 || out_strides[2] != 1 || !al(k_cache, 16) || kq_strides[0] % 16 ||
+      kq_strides[1] % 16 || kq_strides[2] % 16 || !al(v_cache, 16) || vq_strides[0] % 16 ||
+      vq_strides[1] % 16 || vq_strides[2] % 16)
+    return HQ_ERR_INVALID_ARGUMENT;
+  if (!workspace || !al(workspace, 256)) return HQ_ERR_WORKSPACE;
+  // the tensor-core kernel only (head_dim 128, up to 4 q heads per kv head)
+  return kblock_decode_mma(q, q_dtype, q_strides, k_cache, kq_strides, k_scale, ks_strides,
+                           v_cache, vq_strides, v_scale, scale_dtype, vs_strides, B, Hq, Hkv,
+                           capacity, D, block_tokens, sm_scale, out, out_strides, workspace,
+                           workspace_bytes, stream, seq_len, S_plan);
 }
 
 extern "C" int hq_kblock_dequant(const int8_t* k_cache, const int64_t kq_strides[3],

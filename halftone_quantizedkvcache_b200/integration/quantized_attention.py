@@ -156,17 +156,24 @@ class _BlockStore:
     """One layer in the block-wise per-channel K layout (``kernels.kblock_alloc``
     buffers): K per (block of ``block_tokens`` tokens, channel), V per token."""
 
-    __slots__ = ("c", "length")
+    __slots__ = ("c", "length", "lens")
 
-    def __init__(self, B, H, D, cap, block, dtype, device):
+    def __init__(self, B, H, D, cap, block, dtype, device, device_length=False):
         self.c = kernels.kblock_alloc(B, H, cap, D, block_tokens=block, dtype=dtype,
                                       device=device)
         self.length = 0
+        # {length, ticket, status, -} on the device (graph-replayable decode steps)
+        self.lens = torch.zeros(4, dtype=torch.int32, device=device) if device_length else None
 
     def reserve(self, n: int) -> None:
         cap = self.c["k"].shape[2]
         if n <= cap:
             return
+        if self.lens is not None:
+            # captured graphs hold the buffer addresses: no reallocation in this mode
+            raise RuntimeError(
+                f"QuantizedKVCache: capacity {cap} exhausted ({n} tokens) with "
+                "device_lengths=True; construct the cache with a larger capacity")
         B, H, _, D = self.c["k"].shape
         L, bt = self.length, self.c["block_tokens"]
         new = kernels.kblock_alloc(B, H, _round_up(max(n, 2 * cap), _ALIGN), D, block_tokens=bt,
@@ -357,8 +364,8 @@ class QuantizedKVCache(DynamicCache):
         if k_block_tokens is not None:
             if k_block_tokens not in kernels.KBLOCK_TOKENS:
                 raise ValueError(f"k_block_tokens must be one of {kernels.KBLOCK_TOKENS}")
-            if mode != "fused" or device_lengths or static_k_scale is not None or fused_prefill:
-                raise ValueError("k_block_tokens needs mode='fused' and excludes device_lengths, "
+            if mode != "fused" or fused_append or static_k_scale is not None or fused_prefill:
+                raise ValueError("k_block_tokens needs mode='fused' and excludes fused_append, "
                                  "fused_prefill and static_k_scale")
         self.k_block_tokens = k_block_tokens
         self._kblock: dict[int, _BlockStore] = {}
@@ -384,12 +391,14 @@ class QuantizedKVCache(DynamicCache):
         """Read the device lengths back into the host view (synchronises);
         raises if a device-side append found its layer full."""
         self._flush()
-        for i, st in self._store.items():
+        stores = list(self._store.items()) + list(self._kblock.items())
+        for i, st in stores:
             if st.lens is not None:
                 length, _, status, _ = (int(x) for x in st.lens.tolist())
                 if status != 0:
                     raise RuntimeError(f"QuantizedKVCache: layer {i}: append past the capacity "
-                                       f"{st.capacity} (status {status})")
+                                       f"{st.c['k'].shape[2] if hasattr(st, 'c') else st.capacity}"
+                                       f" (status {status})")
                 st.length = length
         return self._lens
 
@@ -403,11 +412,11 @@ class QuantizedKVCache(DynamicCache):
         K quantizer or the decode, or a device-length append past the capacity.
         Synchronises."""
         self._flush()
-        _raise_on_status(self._status.words(self._store))
+        _raise_on_status(self._status.words({**self._store, **self._kblock}))
 
     def reset_status(self) -> None:
         """Clears the status words ``check`` reads (on the current stream)."""
-        self._status.reset(self._store)
+        self._status.reset({**self._store, **self._kblock})
 
     # -- reference-compatible views (tests/qwen_kvcache_full.py:34-36)
     @property
@@ -431,7 +440,9 @@ class QuantizedKVCache(DynamicCache):
 
     @property
     def _lens(self):
-        return {i: s.length for i, s in self._store.items()}
+        lens = {i: s.length for i, s in self._store.items()}
+        lens.update({i: s.length for i, s in self._kblock.items()})
+        return lens
 
     def _fused(self) -> bool:
         return self.mode == "fused" or (self.mode == "auto" and is_installed())
@@ -519,12 +530,17 @@ class QuantizedKVCache(DynamicCache):
         if st is None:
             cap = _round_up(max(S_new + _ALIGN, self.capacity or 0), _ALIGN)
             st = _BlockStore(B, H, D, cap, self.k_block_tokens, key_states.dtype,
-                             key_states.device)
+                             key_states.device, self.device_lengths)
             self._kblock[layer_idx] = st
         elif tuple(st.c["k"].shape[:2]) != (B, H) or st.c["k"].shape[3] != D:
             raise ValueError("QuantizedKVCache.update: batch/head shape changed for this layer")
         st.reserve(st.length + S_new)
-        kernels.kblock_write(key_states, value_states, st.length, st.c)
+        if st.lens is not None and S_new == 1:
+            kernels.kblock_write(key_states, value_states, None, st.c, lens=st.lens)  # at lens[0]
+        else:
+            kernels.kblock_write(key_states, value_states, st.length, st.c)
+            if st.lens is not None:  # eager multi-token write: the host length is current
+                st.lens[0].fill_(st.length + S_new)
         st.length += S_new
         k, v = st.codes()
         k._hq_kblock = st
@@ -626,6 +642,9 @@ def _blockwise_attention(module, query, st: _BlockStore, attention_mask, scaling
         if attention_mask is not None and attention_mask.shape[-1] not in (1, L):
             raise ValueError("quantized_attention_forward: unexpected decode mask width")
         if _kernel_mask(attention_mask, L):
+            if st.lens is not None:  # length on the device: replayable in a CUDA graph
+                return kernels.kblock_decode(q[:, :, 0, :], st.c, L, sm_scale=scaling,
+                                             seq_len=st.lens, s_plan=L).unsqueeze(1)
             return kernels.kblock_decode(q[:, :, 0, :], st.c, L, sm_scale=scaling).unsqueeze(1)
     key = kernels.kblock_dequant(st.c, L, query.dtype)
     value = kernels.dequant(st.c["v"][:, :, :L], st.c["v_scale"][:, :, :L].unsqueeze(-1),

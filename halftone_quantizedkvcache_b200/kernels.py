@@ -66,6 +66,9 @@ class _Workspaces:
 
     Decode workspaces must be zero when first used (arrival tickets); the
     kernel leaves them zero again, so they are zero-filled only when allocated.
+    The ticket region's size follows B * Hkv, so a call of another shape could
+    find the split partials of an earlier call where its tickets live: decode
+    kinds carry B * Hkv (``"decode/8"``), one buffer per shape class.
     """
 
     def __init__(self):
@@ -88,6 +91,13 @@ class _Workspaces:
                     buf[:4].copy_(old[:4])  # the status word (first error) outlives the growth
                 self._bufs[key] = buf
             return buf
+
+    def matching(self, dev: torch.device, prefix: str) -> list:
+        """This stream's buffers whose kind starts with ``prefix``."""
+        st = _stream(dev)
+        with self._lock:
+            return [b for (d, s, k), b in self._bufs.items()
+                    if d == dev.index and s == st and k.split("/")[0] == prefix]
 
 
 WORKSPACES = _Workspaces()
@@ -391,7 +401,7 @@ def decode_workspace(dev, B, Hq, Hkv, S, D) -> torch.Tensor:
         if nb == 0:
             raise ValueError(f"decode: unsupported shape B={B} Hq={Hq} Hkv={Hkv} S={S} D={D}")
         _decode_ws_bytes[key] = nb
-    return WORKSPACES.get(dev, "decode", nb)
+    return WORKSPACES.get(dev, f"decode/{B * Hkv}", nb)
 
 
 _decode_ws = decode_workspace
@@ -657,10 +667,15 @@ def decode_combine(parts: torch.Tensor, out_dtype: torch.dtype = torch.bfloat16,
 
 
 def read_status(kind: str = "decode", device=None) -> int:
-    """Device status word of this stream's ``kind`` workspace (0 = ok)."""
+    """Device status word of this stream's ``kind`` workspaces (0 = ok; else the first
+    error found among them)."""
     dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
-    ws = WORKSPACES.get(dev, kind, 4096)
-    return _lib.lib().hq_read_status(ws.data_ptr(), _stream(dev))
+    bufs = WORKSPACES.matching(dev, kind) or [WORKSPACES.get(dev, kind, 4096)]
+    for ws in bufs:
+        st = _lib.lib().hq_read_status(ws.data_ptr(), _stream(dev))
+        if st != 0:
+            return st
+    return 0
 
 
 def set_plan_sms(sms: int, device=None) -> None:
@@ -711,10 +726,14 @@ def _kblock_check(cache: dict, device, B: int, H: int, D: int, what: str) -> Non
                              f"expected {shape} on {device}")
 
 
-def kblock_write(k_new: torch.Tensor, v_new: torch.Tensor | None, pos: int, cache: dict) -> None:
+def kblock_write(k_new: torch.Tensor, v_new: torch.Tensor | None, pos: int | None, cache: dict,
+                 lens: torch.Tensor | None = None) -> None:
     """Quantize tokens ``pos .. pos+S_new-1`` (``[B,H,S_new,D]``) into a block-wise K
     cache from ``kblock_alloc`` (``hq_kblock_write``): K per (block, channel), V per
-    token, the open block re-coded when a scale grows.  Writes must come in order."""
+    token, the open block re-coded when a scale grows.  Writes must come in order.
+    ``lens`` (int32 CUDA tensor ``{length, ticket, status, -}``): one token written at
+    row ``lens[0]``, which the launch advances (``hq_kblock_write_at``; ``pos`` is
+    ignored) - the same call for every token, so it replays in a CUDA graph."""
     _check_bhsd(k_new, "kblock_write k")
     k_new = k_new if k_new.stride(3) == 1 else k_new.contiguous()
     B, H, S_new, D = k_new.shape
@@ -722,7 +741,10 @@ def kblock_write(k_new: torch.Tensor, v_new: torch.Tensor | None, pos: int, cach
     if kt.dtype != k_new.dtype:
         raise TypeError("kblock_write: k_new must have the tail's dtype")
     _kblock_check(cache, k_new.device, B, H, D, "kblock_write")
-    if int(pos) < 0 or int(pos) + S_new > kc.shape[2]:
+    if lens is not None:
+        if S_new != 1 or lens.dtype != torch.int32 or not lens.is_cuda or lens.numel() < 4:
+            raise ValueError("kblock_write: lens (int32 CUDA [4]) writes one token per call")
+    elif int(pos) < 0 or int(pos) + S_new > kc.shape[2]:
         raise ValueError(f"kblock_write: tokens {int(pos)}..{int(pos) + S_new - 1} are outside "
                          f"the capacity {kc.shape[2]}")
     vc = vs = None
@@ -734,6 +756,21 @@ def kblock_write(k_new: torch.Tensor, v_new: torch.Tensor | None, pos: int, cach
         vc, vs = cache["v"], cache["v_scale"]
     vs32 = vs if vs is not None and vs.dtype == torch.float32 else None
     vs16 = vs if vs is not None and vs.dtype == torch.float16 else None
+    if lens is not None:
+        rc = _lib.lib().hq_kblock_write_at(
+            k_new.data_ptr(), v_new.data_ptr() if v_new is not None else None,
+            _dtype_code(k_new, "kblock_write"), _lib.strides(k_new.stride(), 4),
+            _lib.strides(v_new.stride(), 4) if v_new is not None else None, B, H, D,
+            int(cache["block_tokens"]), kc.data_ptr(), _lib.strides(kc.stride(), 4),
+            ks.data_ptr(), _lib.strides(ks.stride()[:3], 3), kt.data_ptr(),
+            _lib.strides(kt.stride(), 4), vc.data_ptr() if vc is not None else None,
+            _lib.strides(vc.stride(), 4) if vc is not None else None,
+            vs32.data_ptr() if vs32 is not None else None,
+            vs16.data_ptr() if vs16 is not None else None,
+            _lib.strides(vs.stride()[:3], 3) if vs is not None else None, kc.shape[2],
+            lens.data_ptr(), _stream(k_new.device))
+        check(rc, "hq_kblock_write_at")
+        return
     rc = _lib.lib().hq_kblock_write(
         k_new.data_ptr(), v_new.data_ptr() if v_new is not None else None,
         _dtype_code(k_new, "kblock_write"), _lib.strides(k_new.stride(), 4),
@@ -750,9 +787,13 @@ def kblock_write(k_new: torch.Tensor, v_new: torch.Tensor | None, pos: int, cach
 
 
 def kblock_decode(q: torch.Tensor, cache: dict, S: int, *, sm_scale: float | None = None,
-                  out: torch.Tensor | None = None) -> torch.Tensor:
+                  out: torch.Tensor | None = None, seq_len: torch.Tensor | None = None,
+                  s_plan: int | None = None) -> torch.Tensor:
     """Decode attention of ``q`` (``[B,Hq,D]`` or ``[B,Hq,1,D]``) over the first ``S``
-    tokens of a block-wise K cache (``hq_kblock_decode``); output in q's layout and dtype."""
+    tokens of a block-wise K cache (``hq_kblock_decode``); output in q's layout and dtype.
+    ``seq_len`` (int32 CUDA tensor, first element): the length lives on the device
+    (``hq_kblock_decode_len``; ``S`` is ignored, the split count planned for ``s_plan``
+    tokens) - replayable in a CUDA graph while the length grows."""
     _cuda(q, "kblock_decode q")
     qb, restore = _as_bhd(q)
     if qb.stride(2) != 1:
@@ -763,15 +804,35 @@ def kblock_decode(q: torch.Tensor, cache: dict, S: int, *, sm_scale: float | Non
     _kblock_check(cache, qb.device, B, Hkv, D, "kblock_decode")
     if Hq % Hkv:
         raise ValueError(f"kblock_decode: {Hq} query heads over {Hkv} kv heads")
-    if not 1 <= int(S) <= kc.shape[2]:
+    if seq_len is None and not 1 <= int(S) <= kc.shape[2]:
         raise ValueError(f"kblock_decode: S={int(S)} outside 1..{kc.shape[2]} (the capacity)")
     if sm_scale is None:
         sm_scale = 1.0 / math.sqrt(D)
     res = out if out is not None else torch.empty((B, Hq, D), dtype=qb.dtype, device=qb.device)
+    if seq_len is not None:
+        if seq_len.dtype != torch.int32 or not seq_len.is_cuda or seq_len.numel() < 1:
+            raise ValueError("kblock_decode: seq_len must be an int32 CUDA tensor")
+        cap = kc.shape[2]
+        plan = cap if s_plan is None else max(1, min(int(s_plan), cap))
+        # sized for the capacity: a captured step never has to grow it
+        nb = _lib.lib().hq_kblock_decode_workspace_bytes(B, Hq, Hkv, cap, D)
+        if nb == 0:
+            raise ValueError(f"kblock_decode: unsupported shape B={B} Hq={Hq} Hkv={Hkv} D={D}")
+        ws = WORKSPACES.get(qb.device, f"kblock/{B * Hkv}", nb)
+        rc = _lib.lib().hq_kblock_decode_len(
+            qb.data_ptr(), _dtype_code(qb, "kblock_decode q"), _lib.strides(qb.stride(), 3),
+            kc.data_ptr(), _lib.strides(kc.stride()[:3], 3), ks.data_ptr(),
+            _lib.strides(ks.stride()[:3], 3), vc.data_ptr(), _lib.strides(vc.stride()[:3], 3),
+            vs.data_ptr(), _dtype_code(vs, "kblock_decode v_scale"),
+            _lib.strides(vs.stride()[:3], 3), B, Hq, Hkv, cap, seq_len.data_ptr(), plan, D,
+            int(cache["block_tokens"]), float(sm_scale), res.data_ptr(),
+            _lib.strides(res.stride(), 3), ws.data_ptr(), ws.numel(), _stream(qb.device))
+        check(rc, "hq_kblock_decode_len")
+        return restore(res)
     nb = _lib.lib().hq_kblock_decode_workspace_bytes(B, Hq, Hkv, max(int(S), 1), D)
     if nb == 0:
         raise ValueError(f"kblock_decode: unsupported shape B={B} Hq={Hq} Hkv={Hkv} D={D}")
-    ws = WORKSPACES.get(qb.device, "kblock", nb)
+    ws = WORKSPACES.get(qb.device, f"kblock/{B * Hkv}", nb)
     rc = _lib.lib().hq_kblock_decode(
         qb.data_ptr(), _dtype_code(qb, "kblock_decode q"), _lib.strides(qb.stride(), 3),
         kc.data_ptr(), _lib.strides(kc.stride()[:3], 3), ks.data_ptr(),

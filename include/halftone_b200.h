@@ -195,8 +195,13 @@ HQ_API int hq_dequant(const int8_t* q, const int64_t q_strides[4], int B, int H,
  *          of s * sm_scale * log2(e), l = sum 2^(s-m), o = sum 2^(s-m) v.
  * Requires D == 128, Hq / Hkv in {1, 2, 4}, S >= 0 (S == 0 gives zeros).
  * workspace: >= hq_decode_workspace_bytes(B, Hq, Hkv, S, D) bytes, 256-byte
- *          aligned, zero-filled once when allocated; the kernel leaves it
- *          zero-filled again (its arrival counters reset themselves).
+ *          aligned, zero-filled once when allocated; the kernel leaves its
+ *          arrival counters (bytes 256 .. 256 + 8 * B * Hkv, rounded up to 256)
+ *          zero again.  The split partials follow them, so a workspace serves
+ *          calls of one B * Hkv: a call of a larger B * Hkv could find an earlier
+ *          call's partials where its counters live - zero the workspace (or use
+ *          another) when the shape changes.  The decode kernels of this library
+ *          (int8, dense twins, block-wise) share this layout.
  */
 HQ_API size_t hq_decode_workspace_bytes(int B, int Hq, int Hkv, int S, int D);
 HQ_API int hq_decode_int8(const void* q, int q_dtype, const int64_t q_strides[3], const int8_t* k,
@@ -456,7 +461,18 @@ HQ_API int hq_decode_int8_peer(const void* q, int q_dtype, const int64_t q_strid
  *   ks_strides the (b, h, block) strides of k_scale, vs_strides the (b, h, s)
  *   strides of v_scale (scale_dtype F32 or F16).  out [B, Hq, D] of q_dtype.
  *   workspace: hq_kblock_decode_workspace_bytes(B, Hq, Hkv, S, D) bytes, zero
- *   when first used (the launch leaves it zero), 256-byte aligned.
+ *   when first used (the launch leaves it zero), 256-byte aligned.  D = 128
+ *   with up to 4 q heads per kv head runs on the int8 tensor cores (the
+ *   default layout's kernel with q' rebuilt per block), when K and V share
+ *   strides and k_scale rows are 16-byte aligned; the rest on CUDA cores.
+ * hq_kblock_write_at / hq_kblock_decode_len (no counterpart in the reference):
+ *   the same with the cache length on the device, lens = int32[4] {length,
+ *   ticket, status, -} (as hq_append_kv_at), so a decode step replays as a CUDA
+ *   graph.  hq_kblock_write_at writes ONE token at row lens[0] (the grid's last
+ *   block advances it; a full cache writes nothing and sets lens[2]);
+ *   hq_kblock_decode_len attends over the first lens[0] tokens of buffers of
+ *   `capacity` tokens with a split count planned for S_plan (tensor-core path
+ *   only: D = 128, Hq / Hkv in {1, 2, 4}; otherwise HQ_ERR_UNSUPPORTED).
  * hq_kblock_dequant: out[b, h, s, d] = code * k_scale[b, h, s / BT, d] for
  *   s < S (the read path of a block-wise K cache).
  */
@@ -478,6 +494,25 @@ HQ_API int hq_kblock_decode(const void* q, int q_dtype, const int64_t q_strides[
                             int B, int Hq, int Hkv, int S, int D, int block_tokens,
                             float sm_scale, void* out, const int64_t out_strides[3],
                             void* workspace, size_t workspace_bytes, hq_stream_t stream);
+HQ_API int hq_kblock_write_at(const void* k_new, const void* v_new, int x_dtype,
+                              const int64_t k_strides[4], const int64_t v_strides[4], int B,
+                              int H, int D, int block_tokens, int8_t* k_cache,
+                              const int64_t kq_strides[4], float* k_scale,
+                              const int64_t ks_strides[3], void* k_tail,
+                              const int64_t kt_strides[4], int8_t* v_cache,
+                              const int64_t vq_strides[4], float* v_scale_f32,
+                              uint16_t* v_scale_f16, const int64_t vs_strides[3], int capacity,
+                              int* lens, hq_stream_t stream);
+HQ_API int hq_kblock_decode_len(const void* q, int q_dtype, const int64_t q_strides[3],
+                                const int8_t* k_cache, const int64_t kq_strides[3],
+                                const float* k_scale, const int64_t ks_strides[3],
+                                const int8_t* v_cache, const int64_t vq_strides[3],
+                                const void* v_scale, int scale_dtype,
+                                const int64_t vs_strides[3], int B, int Hq, int Hkv,
+                                int capacity, const int* seq_len, int S_plan, int D,
+                                int block_tokens, float sm_scale, void* out,
+                                const int64_t out_strides[3], void* workspace,
+                                size_t workspace_bytes, hq_stream_t stream);
 HQ_API int hq_kblock_dequant(const int8_t* k_cache, const int64_t kq_strides[3],
                              const float* k_scale, const int64_t ks_strides[3], int B, int H,
                              int S, int D, int block_tokens, void* out, int out_dtype,

@@ -121,6 +121,19 @@ def test_blockwise_entry_points_reject_bad_arguments():
     assert decode(B=70000) == -2
     assert decode(B=0) == 0
     assert L.hq_kblock_decode_workspace_bytes(1, 24, 8, 64, 128) == 0
+    # device-length variants: no length buffer; the decode serves head_dim 128 and up to
+    # 4 q heads per kv head only
+    wa = [16, 16, 1, st4, st4, 1, 8, 128, 128, 16, st4, 16, st3, 16, st4, 16, st4, None, 16, st3,
+          256, None, None]
+    assert L.hq_kblock_write_at(*wa) == -1
+    unit = _lib.strides((0, 0, 1), 3)
+    da = dict(q=16, qdt=1, qs=unit, kc=16, kqs=st3, ksc=16, kscs=st3, vc=16, vqs=st3, vsc=16,
+              sdt=2, vss=st3, B=1, Hq=16, Hkv=8, cap=256, lens=None, plan=64, D=128, bt=128,
+              sm=0.1, out=16, os=unit, ws=256, wsb=1 << 20)
+    assert L.hq_kblock_decode_len(*da.values(), None) == -1
+    da["lens"] = 16
+    assert L.hq_kblock_decode_len(*dict(da, D=64).values(), None) == -2
+    assert L.hq_kblock_decode_len(*dict(da, Hq=64).values(), None) == -2
     assert L.hq_kblock_dequant(16, st3, 16, st3, 1, 8, 64, 128, 96, 16, 1, st4, None) == -1
     assert L.hq_kblock_dequant(16, st3, 16, st3, 1, 8, 0, 128, 128, 16, 1, st4, None) == 0
 
@@ -130,7 +143,8 @@ def test_blockwise_cache_option_combinations():
         QuantizedKVCache(mode="fused", k_block_tokens=96)
     with pytest.raises(ValueError):
         QuantizedKVCache(mode="auto", k_block_tokens=128)
-    with pytest.raises(ValueError):
-        QuantizedKVCache(mode="fused", k_block_tokens=128, device_lengths=True)
+    with pytest.raises(ValueError):   # the appended token's re-coding is a launch of its own
+        QuantizedKVCache(mode="fused", k_block_tokens=128, device_lengths=True, fused_append=True)
+    QuantizedKVCache(mode="fused", k_block_tokens=128, device_lengths=True)
     c = QuantizedKVCache(mode="fused", k_block_tokens=64)
     assert c.get_seq_length(0) == 0 and len(c) == 0 and c.storage_bytes() == 0

@@ -251,3 +251,89 @@ def test_wrappers_check_shapes_against_the_cache():
     with pytest.raises(ValueError):
         kernels.kblock_dequant(c, 300)
     assert kernels.kblock_decode(q[:1], c, 4).shape == (1, 16, 128)
+
+
+@pytest.mark.parametrize("block", [64, 128, 256])
+def test_device_length_steps_equal_host_length_steps(block):
+    """hq_kblock_write_at + hq_kblock_decode_len (length on the device) against the
+    host-length calls, one token per step from a 300-token prefill: the cache is
+    bit-exact with the oracle's bulk block-wise quantization after every step and the
+    outputs are identical (same split plan, same kernel)."""
+    B, Hq, Hkv, D, S0, n = 2, 16, 8, 128, 300, 70
+    k, v = make(B, Hkv, S0 + n, D, "bf16", seed=block)
+    cap = 512
+    host = kernels.kblock_alloc(B, Hkv, cap, D, block_tokens=block, device="cuda")
+    devc = kernels.kblock_alloc(B, Hkv, cap, D, block_tokens=block, device="cuda")
+    kt, vt = dev(k, "bf16"), dev(v, "bf16")
+    kernels.kblock_write(kt[:, :, :S0], vt[:, :, :S0], 0, host)
+    kernels.kblock_write(kt[:, :, :S0], vt[:, :, :S0], 0, devc)
+    lens = torch.tensor([S0, 0, 0, 0], dtype=torch.int32, device="cuda")
+    rng = np.random.default_rng(7)
+    for i in range(n):
+        L = S0 + i
+        kernels.kblock_write(kt[:, :, L:L + 1], vt[:, :, L:L + 1], L, host)
+        kernels.kblock_write(kt[:, :, L:L + 1], vt[:, :, L:L + 1], None, devc, lens=lens)
+        q = dev(oin.normal(rng, (B, Hq, D)), "bf16")
+        a = kernels.kblock_decode(q, host, L + 1)
+        b = kernels.kblock_decode(q, devc, L + 1, seq_len=lens, s_plan=L + 1)
+        assert torch.equal(a, b), i
+    assert lens.tolist()[:3] == [S0 + n, 0, 0]
+    for name in ("k", "k_scale", "v", "v_scale"):
+        assert torch.equal(host[name], devc[name]), name
+    check_cache(devc, k, v, S0 + n, block, torch.float16)
+
+
+def test_device_length_step_replays_in_a_cuda_graph():
+    """One decode step (one-token write at lens[0] + decode over lens[0] tokens) captured
+    once and replayed for 100 tokens: the cache stays bit-exact with the oracle's bulk
+    block-wise quantization, a full cache writes nothing and sets the status word, and
+    every replayed output is within the decode tolerance of the float64 oracle."""
+    B, Hq, Hkv, D, S0, n, block = 1, 16, 8, 128, 1000, 100, 128
+    cap = S0 + n
+    k, v = make(B, Hkv, cap + 1, D, "bf16", seed=3)
+    c = kernels.kblock_alloc(B, Hkv, cap, D, block_tokens=block, device="cuda")
+    kt, vt = dev(k, "bf16"), dev(v, "bf16")
+    kernels.kblock_write(kt[:, :, :S0], vt[:, :, :S0], 0, c)
+    lens = torch.tensor([S0, 0, 0, 0], dtype=torch.int32, device="cuda")
+    knew = torch.empty((B, Hkv, 1, D), dtype=torch.bfloat16, device="cuda")
+    vnew = torch.empty_like(knew)
+    q = torch.empty((B, Hq, D), dtype=torch.bfloat16, device="cuda")
+    out = torch.empty_like(q)
+    qs = dev(oin.normal(np.random.default_rng(11), (n + 1, B, Hq, D)), "bf16")
+
+    def step():
+        kernels.kblock_write(knew, vnew, None, c, lens=lens)
+        kernels.kblock_decode(q, c, cap, seq_len=lens, s_plan=S0, out=out)
+
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        knew.copy_(kt[:, :, S0:S0 + 1])
+        vnew.copy_(vt[:, :, S0:S0 + 1])
+        q.copy_(qs[0])
+        step()                                   # eager: workspaces exist
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            step()
+        for i in range(1, n):
+            knew.copy_(kt[:, :, S0 + i:S0 + i + 1])
+            vnew.copy_(vt[:, :, S0 + i:S0 + i + 1])
+            q.copy_(qs[i])
+            g.replay()
+            if i % 33 == 0 or i == n - 1:
+                torch.cuda.synchronize()
+                L = S0 + i + 1
+                codes, scales = ob.quant_k_blockwise(k[:, :, :L], block)
+                vc, vs = oq.quant_v_pertoken(v[:, :, :L])
+                ref = ob.decode_blockwise(qs[i].float().cpu().numpy(), codes, scales, vc,
+                                          oq.to_f16(vs[..., 0]).astype(np.float32), block)
+                np.testing.assert_allclose(out.float().cpu().numpy(), ref, atol=1e-2, rtol=2.0 ** -7)
+        torch.cuda.synchronize()
+        assert lens.tolist()[:3] == [cap, 0, 0]
+        check_cache(c, k, v, cap, block, torch.float16)
+        knew.copy_(kt[:, :, cap:cap + 1])        # one past the capacity: refused on the device
+        g.replay()
+        torch.cuda.synchronize()
+        assert lens.tolist()[0] == cap and lens.tolist()[2] != 0
+        del g
+    check_cache(c, k, v, cap, block, torch.float16)
