@@ -337,3 +337,62 @@ def test_device_length_step_replays_in_a_cuda_graph():
         assert lens.tolist()[0] == cap and lens.tolist()[2] != 0
         del g
     check_cache(c, k, v, cap, block, torch.float16)
+
+
+def test_whole_model_step_as_one_cuda_graph_with_blockwise_layout():
+    """QuantizedKVCache(k_block_tokens=128, device_lengths=True) through HF transformers:
+    the full decode step of a random-init 2-layer Qwen3-shaped model captured once as a
+    CUDA graph and replayed per token (token id and position in static tensors), against
+    the same cache run eagerly with host lengths: the prefill's codes and scales are
+    bit-identical, the first logits identical, and the replayed logits stay within a
+    small distance of the eager ones (the replayed split plan is the one planned at
+    capture, so the float32 sums are grouped differently)."""
+    from halftone_quantizedkvcache_b200.integration import QuantizedKVCache, installed
+    from test_e2e_qwen3_gpu import build as build_model, tokens
+    layers, n0, nd = 2, 200, 40
+    model = build_model(layers)
+    ids = tokens(model, 1, n0 + nd)
+    with torch.no_grad(), installed():
+        ref = QuantizedKVCache(mode="fused", k_block_tokens=128)
+        want = [model(ids[:, :n0], past_key_values=ref, use_cache=True).logits[:, -1].float()]
+        for t in range(n0, n0 + nd):
+            want.append(model(ids[:, t:t + 1], past_key_values=ref, use_cache=True).logits[:, -1].float())
+        cache = QuantizedKVCache(mode="fused", k_block_tokens=128, device_lengths=True,
+                                 capacity=n0 + nd + 128)
+        got = [model(ids[:, :n0], past_key_values=cache, use_cache=True).logits[:, -1].float()]
+        tok = torch.empty((1, 1), dtype=torch.long, device="cuda")
+        pos = torch.empty((1, 1), dtype=torch.long, device="cuda")
+        masks = {"full_attention": None}
+
+        def step():
+            return model(input_ids=tok, position_ids=pos, attention_mask=masks,
+                         past_key_values=cache, use_cache=True).logits[:, -1]
+
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            tok.copy_(ids[:, n0:n0 + 1])
+            pos.fill_(n0)
+            got.append(step().float())             # eager step: workspaces exist
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                out = step()
+            for t in range(n0 + 1, n0 + nd):
+                tok.copy_(ids[:, t:t + 1])
+                pos.fill_(t)
+                g.replay()
+                got.append(out.float().clone())
+            torch.cuda.synchronize()
+        lens = cache.sync_lengths()
+        del g
+    assert all(v == n0 + nd for v in lens.values())
+    for layer in range(layers):
+        a, b = ref._kblock[layer].c, cache._kblock[layer].c
+        assert torch.equal(a["k"][:, :, :n0], b["k"][:, :, :n0])
+        assert torch.equal(a["v"][:, :, :n0], b["v"][:, :, :n0])
+        assert torch.equal(a["v_scale"][:, :, :n0], b["v_scale"][:, :, :n0])
+        assert torch.equal(a["k_scale"][:, :, :n0 // 128], b["k_scale"][:, :, :n0 // 128])
+    err = (torch.stack(got, 1) - torch.stack(want, 1)).abs()
+    assert torch.equal(got[0], want[0])
+    print(f"block-wise graph-vs-eager logits: max {float(err.max()):.4f} mean {float(err.mean()):.5f}")
+    assert float(err.mean()) < 5e-3 and float(err.max()) < 0.25
