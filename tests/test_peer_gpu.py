@@ -183,7 +183,9 @@ def test_absent_rank_times_out_and_context_survives():
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_two_ranks_over_nvlink():
+def test_every_gpu_a_rank_over_nvlink():
+    """One rank per visible GPU (up to 8), each decoding its share of one sequence and
+    exchanging (m, l, o) inside the decode kernel over NVLink."""
     world = min(torch.cuda.device_count(), 8)
     env = dict(os.environ, NCCL_NVLS_ENABLE="0", PYTHONPATH=ROOT)
     cmd = ["timeout", "-k", "60", "600", sys.executable, "-m", "torch.distributed.run",
