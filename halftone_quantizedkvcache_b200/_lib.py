@@ -43,7 +43,7 @@ SIGNATURES = {
     "hq_decode_int8_ex": (_I, [_P, _I, _A4, _P, _P, _A4, _P, _P, _I, _A4, _A4, _I, _I, _I, _I, _I,
                                _F, _I, _P, _A4, _P, _P, _Z, ctypes.c_uint, _P]),
     "hq_prefill_int8": (_I, [_P, _I, _A4, _P, _P, _A4, _P, _P, _I, _A4, _A4, _I, _I, _I, _I, _I, _I,
-                             _F, _I, _P, _A4, _P]),
+                             _F, _I, _P, _A4, _P, _P]),
     "hq_decode_dense": (_I, [_P, _A4, _P, _P, _I, _A4, _I, _I, _I, _I, _I, _F, _I, _P, _A4, _P, _P,
                              _Z, _P]),
     "hq_decode_dense_fma": (_I, [_P, _A4, _P, _P, _I, _A4, _I, _I, _I, _I, _I, _F, _I, _P, _A4, _P,

@@ -9,18 +9,27 @@
 // 0 .. S - Sq + i (the newest Sq of S cached tokens are the queries).
 //
 // The reference materialises the dequantized cache and runs it through ~15
-// torch kernels; here one launch reads the int8 codes once per q tile:
+// torch kernels; here one launch reads the int8 codes:
 //
-//   * grid = (q tiles of 64 rows, q head, batch), the longest (last) q tiles
-//     first; 8 warps: warps w and w + 4 share q rows 16 w .. 16 w + 15 and take
-//     alternate key tiles (two tiles per step), then merge their softmax states
-//     in shared memory - the causal rows of the last q tile cost half the steps;
+//   * a block takes 64 query rows of G query heads that share one kv head
+//     (G = 2 when the group size is even, else 1): 4 G warps, warp w holds 16
+//     rows of head w / 4, and the dequantized K / V tiles serve all G heads;
+//   * the 64-token key tiles that a q tile's causal rows reach are dealt round
+//     robin to the C blocks of a thread-block cluster (C = 1, 2, 4 or 8, chosen
+//     on the host so that the grid fills the resident block slots of the GPU;
+//     the longest q tiles are scheduled first).  Each block runs an online
+//     softmax over its tiles; the cluster then merges the C partial states
+//     through distributed shared memory: every block leaves its unnormalised
+//     output rows and (max, sum) in its own shared memory, and after a cluster
+//     barrier block c merges rows c R / C .. (c + 1) R / C of all C blocks and
+//     stores them (R = 64 G rows).  No workspace, no second launch;
+//   * code tiles (64 tokens x 128 bytes of K and of V) arrive by TMA
+//     (cp.async.bulk.tensor) into a two-stage ring with mbarrier completion and
+//     bounded waits; all threads dequantize a stage exactly as the reference's
+//     update() does (float product rounded to the model dtype) into 16-bit
+//     tiles with a 16-byte XOR swizzle (conflict-free ldmatrix);
 //   * q rows are fake-quantized in the prologue and kept in shared memory as
 //     bf16/f16 (A-fragments by ldmatrix in every key tile);
-//   * 64-token K/V tiles: int8 codes are loaded into registers one tile ahead,
-//     dequantized exactly as the reference's update() does (float product,
-//     rounded to the model dtype) and stored to shared memory with a 16-byte
-//     XOR swizzle (conflict-free ldmatrix);
 //   * S = q K^T and O += P V on the tensor cores (mma.sync m16n8k16, float32
 //     accumulation) with an online float32 softmax; P is split into a high
 //     and a low 16-bit part (two MMAs), so the probabilities keep ~16 bits
@@ -33,33 +42,57 @@
 
 #include <atomic>
 
+#include "decode_common.cuh"
 #include "hq_common.cuh"
 
 namespace hq {
 namespace pre {
 
 constexpr int kD = 128;
-constexpr int kThreads = 256;
-constexpr int kRows = 64;    // q rows per block (16 per warp)
+constexpr int kRows = 64;    // q rows per head per block (16 per warp)
 constexpr int kKeys = 64;    // keys per tile
 constexpr int kRowB = kD * 2;  // bytes of one 16-bit row
+constexpr int kMaxCluster = 8;
 constexpr float kLog2e = 1.4426950408889634f;
-constexpr int kSmem = (kRows + 4 * kKeys) * kRowB + kD * 4;  // q, 2 K tiles, 2 V tiles, K scales
 
 struct Params {
   const void* q;
   int64_t qsb, qsh, qsi;       // q [B, Hq, Sq, D] element strides
-  const int8_t* k;
-  const int8_t* v;
-  int64_t kvsb, kvsh, kvss;    // codes [B, Hkv, S, D]
   const void* ksc;
   const void* vsc;
   int64_t kscb, ksch, kscd, vscb, vsch, vscs;
   void* out;
   int64_t osb, osh, osi;       // out [B, Sq, Hq, D] addressed as (b, h, i)
   int Hq, Hkv, Sq, S;
+  int n_qt;                    // q tiles
+  int n_chunks;                // blocks per cluster: key tiles dealt round robin
   float qk_scale;              // sm_scale * log2(e)
   int q_quant;
+  int* status;                 // optional: HQ_ERR_DEVICE_TIMEOUT when a bounded wait gave up
+};
+
+// Shared memory of a block (bytes): G q tiles, the dequantized K and V tiles,
+// the two-stage ring of code tiles, the K scales, two mbarriers.  After the
+// key loop the front is reused for the partial state the cluster merges.
+template <int G>
+struct Cfg {
+  static constexpr int kWarps = 4 * G;
+  static constexpr int kThreads = 32 * kWarps;
+  static constexpr int kR = G * kRows;                      // q rows of the block
+  static constexpr int kCode = kKeys * kD;                  // one int8 code tile
+  static constexpr int kOffK = kR * kRowB;
+  static constexpr int kOffV = kOffK + kKeys * kRowB;
+  static constexpr int kOffRing = kOffV + kKeys * kRowB;    // stage s: K codes, V codes
+  static constexpr int kOffKsc = kOffRing + 2 * 2 * kCode;  // K scales; merge weights later
+  static constexpr int kOffBar = kOffKsc + kD * 4;
+  static constexpr int kSmem = kOffBar + 2 * 8;
+  static constexpr int kPieces = kKeys * (kD / 16) / kThreads;  // 16-code pieces per thread
+  // partial state: rows of kPartStride floats (conflict-free float2 stores), then (m, l)
+  static constexpr int kPartStride = kD + 8;
+  static constexpr int kOffML = kR * kPartStride * 4;
+  static_assert(kOffML + kR * 8 <= kOffKsc, "the partial state overlaps the K scales");
+  static_assert(kOffRing % 128 == 0 && kCode % 128 == 0, "TMA destinations");
+  static_assert(kR <= kD, "the merge weights (rows x blocks = kR) fit the K-scale slot");
 };
 
 template <int DT> struct T16;
@@ -133,59 +166,190 @@ __device__ __forceinline__ void dq_store(unsigned char* tile, int r, int p, cons
   *reinterpret_cast<uint4*>(tile + sw(r, 2 * p + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
 }
 
-template <int DT, int SDT>
-__global__ void __launch_bounds__(kThreads) prefill_kernel(const Params p) {
+// Dequantizes 16 codes (one 16-byte piece: channels 16 p .. 16 p + 15 of row r) with
+// the scales sc (per channel: 8 pairs; per row: one pair repeated) into two swizzled
+// chunks of a 16-bit tile: the float product code * scale (exact codes from a byte
+// permute, packed f32x2 multiplies) rounded to the model dtype, as the reference's
+// update() computes it.
+template <int DT, bool PER_CHANNEL>
+__device__ __forceinline__ void dq_piece(unsigned char* tile, int r, int p, const uint4& codes,
+                                         const F2* sc) {
+  const uint32_t w[4] = {codes.x, codes.y, codes.z, codes.w};
+  uint32_t o[8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    F2 lo, hi;
+    s8x4_to_f2x2(w[i], lo, hi);
+    lo = f2_mul(lo, sc[PER_CHANNEL ? 2 * i : 0]);
+    hi = f2_mul(hi, sc[PER_CHANNEL ? 2 * i + 1 : 0]);
+    float a, b;
+    f2_split(lo, a, b);
+    o[2 * i] = T16<DT>::pack(a, b);
+    f2_split(hi, a, b);
+    o[2 * i + 1] = T16<DT>::pack(a, b);
+  }
+  *reinterpret_cast<uint4*>(tile + sw(r, 2 * p)) = make_uint4(o[0], o[1], o[2], o[3]);
+  *reinterpret_cast<uint4*>(tile + sw(r, 2 * p + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
+}
+
+__device__ __forceinline__ float ex2_ftz(float x) {  // 2^x; -inf -> +0
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// P = hi + lo with hi = RN16(P), lo = RN16(P - hi), for two probabilities: the two
+// 16-bit pair words of the A-fragments.
+template <int DT>
+__device__ __forceinline__ void split_hilo(float a, float b, uint32_t& hw, uint32_t& lw);
+template <>
+__device__ __forceinline__ void split_hilo<HQ_DTYPE_BF16>(float a, float b, uint32_t& hw,
+                                                          uint32_t& lw) {
+  hw = T16<HQ_DTYPE_BF16>::pack(a, b);
+  const F2 h = bf16x2_to_f2(hw);
+  float da, db;
+  f2_split(f2_sub(f2_make(a, b), h), da, db);
+  lw = T16<HQ_DTYPE_BF16>::pack(da, db);
+}
+template <>
+__device__ __forceinline__ void split_hilo<HQ_DTYPE_F16>(float a, float b, uint32_t& hw,
+                                                         uint32_t& lw) {
+  hw = T16<HQ_DTYPE_F16>::pack(a, b);
+  const F2 h = f16x2_to_f2(hw);
+  float da, db;
+  f2_split(f2_sub(f2_make(a, b), h), da, db);
+  lw = T16<HQ_DTYPE_F16>::pack(da, db);
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" :::
+                   "memory");
+}
+// address of the same shared-memory location in block `rank` of the cluster
+__device__ __forceinline__ uint32_t dsmem_addr(const void* p, int rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float4 dsmem_ld4(uint32_t a) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(a)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ float2 dsmem_ld2(uint32_t a) {
+  float2 v;
+  asm volatile("ld.shared::cluster.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(a) : "memory");
+  return v;
+}
+// code tiles are read by every block of the q tiles and head groups of a kv head
+__device__ __forceinline__ uint64_t l2_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+template <int DT, int SDT, int G>
+__global__ void __launch_bounds__(Cfg<G>::kThreads, 2)
+    prefill_kernel(const __grid_constant__ CUtensorMap mk, const __grid_constant__ CUtensorMap mv,
+                   const Params p) {
+  using C = Cfg<G>;
   using E = T16<DT>;
   using SE = Elem<SDT>;
   using QT = typename E::T;
+  constexpr int T = C::kThreads;
+  constexpr int NP = C::kPieces;
   extern __shared__ __align__(128) unsigned char smem_raw[];
-  unsigned char* qs = smem_raw;                    // 16 KB: the q tile
-  unsigned char* ks = qs + kRows * kRowB;          // 2 x 16 KB: dequantized K tiles
-  unsigned char* vs = ks + 2 * kKeys * kRowB;      // 2 x 16 KB: dequantized V tiles
-  float* ksc = reinterpret_cast<float*>(vs + 2 * kKeys * kRowB);  // K scales of the kv head
+  unsigned char* qs = smem_raw;
+  unsigned char* kts = smem_raw + C::kOffK;
+  unsigned char* vts = smem_raw + C::kOffV;
+  unsigned char* ring = smem_raw + C::kOffRing;
+  float* ksc = reinterpret_cast<float*>(smem_raw + C::kOffKsc);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw + C::kOffBar);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int rw = warp & 3, kp = warp >> 2;  // q rows 16 rw .., key tiles of parity kp
+  const int hl = warp >> 2, rw = warp & 3;  // head within the block, 16-row group
   const int g = lane >> 2, t = lane & 3;
-  const int n_qt = (p.Sq + kRows - 1) / kRows;
-  const int qt = n_qt - 1 - static_cast<int>(blockIdx.x);  // longest rows first
-  const int hq = blockIdx.y, b = blockIdx.z;
-  const int nrep = p.Hq / p.Hkv, hk = hq / nrep;
+  const int nc = p.n_chunks;
+  const int chunk = static_cast<int>(blockIdx.x) % nc;  // rank in the cluster
+  const int qt = p.n_qt - 1 - static_cast<int>(blockIdx.x) / nc;  // longest rows first
+  const int nrep = p.Hq / p.Hkv, groups = nrep / G;
+  const int hk = blockIdx.y / groups;
+  const int hq0 = hk * nrep + (blockIdx.y % groups) * G;
+  const int b = blockIdx.z;
   const int i0 = qt * kRows;
   const int off = p.S - p.Sq;  // key index of query 0
+  const int last_key = min(p.S - 1, off + min(i0 + kRows, p.Sq) - 1);
+  const int n_kt = last_key / kKeys + 1;
+  const int n_my = n_kt > chunk ? (n_kt - 1 - chunk) / nc + 1 : 0;  // this block's key tiles
+  const uint64_t pol = l2_evict_last();
 
-  // ---- q tile: 4 threads per row, 32 elements each; per-row fake quantization
+  auto issue = [&](int j) {  // thread 0: this block's tile j into stage j & 1
+    const int st = j & 1, kt = chunk + j * nc;
+    unsigned char* dst = ring + st * 2 * C::kCode;
+    mbar_arrive_expect_tx(&full[st], 2 * C::kCode);
+    dec::mmak::tma_load_4d(dst, &mk, 0, kt * kKeys, hk, b, &full[st], pol);
+    dec::mmak::tma_load_4d(dst + C::kCode, &mv, 0, kt * kKeys, hk, b, &full[st], pol);
+  };
+  if (tid == 0) {
+    mbar_init(&full[0], 1);
+    mbar_init(&full[1], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (tid == 0)
+    for (int j = 0; j < min(2, n_my); ++j) issue(j);
+
+  // V scales of this thread's code rows, one tile ahead
+  const auto* vsp = reinterpret_cast<const typename SE::T*>(p.vsc) + b * p.vscb + hk * p.vsch;
+  float vsr[NP];
+  auto load_vs = [&](int j) {
+    const int s0 = (chunk + j * nc) * kKeys;
+#pragma unroll
+    for (int i = 0; i < NP; ++i) {
+      const int s = s0 + ((tid + i * T) >> 3);
+      vsr[i] = s < p.S ? SE::to_f32(vsp[s * p.vscs]) : 0.0f;
+    }
+  };
+  if (n_my > 0) load_vs(0);
+
+  // ---- q tiles: 4 threads per row, 32 elements each; per-row fake quantization
   {
-    const int r = tid >> 2, quarter = tid & 3;
-    const int i = i0 + r;
-    const QT* src = reinterpret_cast<const QT*>(p.q) + b * p.qsb + hq * p.qsh +
-                    static_cast<int64_t>(i < p.Sq ? i : 0) * p.qsi + quarter * 32;
-    float x[32];
+    const int quarter = tid & 3;
+#pragma unroll 1
+    for (int rr = tid >> 2; rr < C::kR; rr += T / 4) {
+      const int h = rr / kRows, i = i0 + rr % kRows;
+      const QT* src = reinterpret_cast<const QT*>(p.q) + b * p.qsb + (hq0 + h) * p.qsh +
+                      static_cast<int64_t>(i < p.Sq ? i : 0) * p.qsi + quarter * 32;
+      float x[32];
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      const uint4 w = i < p.Sq ? *reinterpret_cast<const uint4*>(src + 8 * c) : make_uint4(0, 0, 0, 0);
-      float f[8];
-      Vec16<DT>::unpack(w, f);
+      for (int c = 0; c < 4; ++c) {
+        const uint4 w = i < p.Sq ? *reinterpret_cast<const uint4*>(src + 8 * c) : make_uint4(0, 0, 0, 0);
+        float f[8];
+        Vec16<DT>::unpack(w, f);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) x[8 * c + e] = f[e];
-    }
-    if (p.q_quant) {
-      float m = 0.0f;
+        for (int e = 0; e < 8; ++e) x[8 * c + e] = f[e];
+      }
+      if (p.q_quant) {
+        float m = 0.0f;
 #pragma unroll
-      for (int e = 0; e < 32; ++e) m = fmaxf(m, fabsf(x[e]));
-      m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
-      m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
-      const Quantizer qz = Quantizer::from_amax(m);
+        for (int e = 0; e < 32; ++e) m = fmaxf(m, fabsf(x[e]));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+        const Quantizer qz = Quantizer::from_amax(m);
 #pragma unroll
-      for (int e = 0; e < 32; ++e) x[e] = E::round(static_cast<float>(qz.code(x[e])) * qz.scale);
-    }
+        for (int e = 0; e < 32; ++e) x[e] = E::round(static_cast<float>(qz.code(x[e])) * qz.scale);
+      }
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      uint4 w;
-      w.x = E::pack(x[8 * c], x[8 * c + 1]);
-      w.y = E::pack(x[8 * c + 2], x[8 * c + 3]);
-      w.z = E::pack(x[8 * c + 4], x[8 * c + 5]);
-      w.w = E::pack(x[8 * c + 6], x[8 * c + 7]);
-      *reinterpret_cast<uint4*>(qs + sw(r, quarter * 4 + c)) = w;
+      for (int c = 0; c < 4; ++c) {
+        uint4 w;
+        w.x = E::pack(x[8 * c], x[8 * c + 1]);
+        w.y = E::pack(x[8 * c + 2], x[8 * c + 3]);
+        w.z = E::pack(x[8 * c + 4], x[8 * c + 5]);
+        w.w = E::pack(x[8 * c + 6], x[8 * c + 7]);
+        *reinterpret_cast<uint4*>(qs + sw(rr, quarter * 4 + c)) = w;
+      }
     }
   }
   // ---- K scales of the kv head, one per channel
@@ -193,30 +357,7 @@ __global__ void __launch_bounds__(kThreads) prefill_kernel(const Params p) {
     const auto* kp = reinterpret_cast<const typename SE::T*>(p.ksc) + b * p.kscb + hk * p.ksch;
     if (tid < kD) ksc[tid] = SE::to_f32(kp[tid * p.kscd]);
   }
-  // dequantization: threads 0-127 fill the even tile of a step, 128-255 the odd one
-  const int half = tid >> 7;
-  const int pc = tid & 7;         // 16-byte piece of a code row (channels 16 pc .. 16 pc + 15)
-  const int rr = (tid & 127) >> 3;  // rows rr, rr + 16, rr + 32, rr + 48 of the tile
-  const int last_key = min(p.S - 1, off + min(i0 + kRows, p.Sq) - 1);
-  const int n_kt = last_key >= 0 ? last_key / kKeys + 1 : 0;
-  const int8_t* kbase = p.k + b * p.kvsb + hk * p.kvsh;
-  const int8_t* vbase = p.v + b * p.kvsb + hk * p.kvsh;
-  const auto* vsp = reinterpret_cast<const typename SE::T*>(p.vsc) + b * p.vscb + hk * p.vsch;
-  uint4 kc[4], vc[4];
-  float vsc[4];
-  auto load_tile = [&](int kt) {  // this thread's rows of tile kt
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int s = kt * kKeys + rr + 16 * j;
-      const bool in = s < p.S;
-      kc[j] = in ? *reinterpret_cast<const uint4*>(kbase + s * p.kvss + 16 * pc) : make_uint4(0, 0, 0, 0);
-      vc[j] = in ? *reinterpret_cast<const uint4*>(vbase + s * p.kvss + 16 * pc) : make_uint4(0, 0, 0, 0);
-      vsc[j] = in ? SE::to_f32(vsp[s * p.vscs]) : 0.0f;
-    }
-  };
-  const int n_steps = (n_kt + 1) / 2;  // two key tiles per step
-  if (n_steps > 0) load_tile(half);
-  __syncthreads();  // q tile and K scales complete
+  __syncthreads();  // q tiles and K scales complete
 
   float o[16][4];
 #pragma unroll
@@ -225,24 +366,35 @@ __global__ void __launch_bounds__(kThreads) prefill_kernel(const Params p) {
   const int row_lo = i0 + rw * 16 + g, row_hi = row_lo + 8;  // query indices
   const int lim_lo = row_lo < p.Sq ? off + row_lo : -1;        // last key of each row
   const int lim_hi = row_hi < p.Sq ? off + row_hi : -1;
+  const uint32_t qaddr = smem_u32(qs + hl * kRows * kRowB);
+  const float qk = p.qk_scale;
+  // the smallest key limit of the warp's rows (-1 when a row lies past Sq)
+  const int wlim = i0 + rw * 16 + 15 < p.Sq ? off + i0 + rw * 16 : -1;
 
-  unsigned char* kst = ks + kp * kKeys * kRowB;  // this warp's K / V tile of each step
-  unsigned char* vst = vs + kp * kKeys * kRowB;
-  for (int step = 0; step < n_steps; ++step) {
-    // dequantize the two tiles held in registers into shared memory
-    __syncthreads();  // the previous step's reads are done
+  int j = 0;
+  bool failed = false;
+  for (; j < n_my; ++j) {
+    // ---- dequantize stage j & 1 into the 16-bit tiles
+    const bool ok = mbar_wait(&full[j & 1], (j >> 1) & 1);
+    if (ok) {
+      const unsigned char* kc = ring + (j & 1) * 2 * C::kCode;
+      const unsigned char* vc = kc + C::kCode;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int r = rr + 16 * j;
-      dq_store<DT>(ks + half * kKeys * kRowB, r, pc, kc[j], ksc + 16 * pc);
-      float vv[16];
-#pragma unroll
-      for (int e = 0; e < 16; ++e) vv[e] = vsc[j];
-      dq_store<DT>(vs + half * kKeys * kRowB, r, pc, vc[j], vv);
+      for (int i = 0; i < NP; ++i) {
+        const int pi = tid + i * T, r = pi >> 3, pc = pi & 7;
+        dq_piece<DT, true>(kts, r, pc, *reinterpret_cast<const uint4*>(kc + r * kD + pc * 16),
+                           reinterpret_cast<const F2*>(ksc + 16 * pc));
+        const F2 vs2 = f2_make(vsr[i], vsr[i]);
+        dq_piece<DT, false>(vts, r, pc, *reinterpret_cast<const uint4*>(vc + r * kD + pc * 16), &vs2);
+      }
     }
-    __syncthreads();
-    if (step + 1 < n_steps) load_tile(2 * (step + 1) + half);  // in flight during the math
-    const int kt = 2 * step + kp;
+    if (__syncthreads_or(!ok)) {  // tiles ready; stage j & 1 consumed
+      failed = true;
+      break;
+    }
+    if (tid == 0 && j + 2 < n_my) issue(j + 2);
+    if (j + 1 < n_my) load_vs(j + 1);
+    const int kt = chunk + j * nc;
 
     // ---- S = q K^T for 64 keys: 8 n-tiles of 8 keys
     float sacc[8][4];
@@ -250,158 +402,273 @@ __global__ void __launch_bounds__(kThreads) prefill_kernel(const Params p) {
     for (int n = 0; n < 8; ++n) sacc[n][0] = sacc[n][1] = sacc[n][2] = sacc[n][3] = 0.0f;
 #pragma unroll
     for (int kk = 0; kk < 8; ++kk) {
-      // q A-fragment of this warp's 16 rows, channels 16 kk .. 16 kk + 15
       uint32_t qa[4];
-      ldsm4(smem_u32(qs) + sw(rw * 16 + (lane & 15), 2 * kk + (lane >> 4)), qa);
+      ldsm4(qaddr + sw(rw * 16 + (lane & 15), 2 * kk + (lane >> 4)), qa);
 #pragma unroll
       for (int np = 0; np < 4; ++np) {  // pairs of n-tiles
         uint32_t bfr[4];
         const int key = np * 16 + ((lane >> 4) << 3) + (lane & 7);
-        ldsm4(smem_u32(kst) + sw(key, 2 * kk + ((lane >> 3) & 1)), bfr);
+        ldsm4(smem_u32(kts) + sw(key, 2 * kk + ((lane >> 3) & 1)), bfr);
         mma16816<DT>(sacc[2 * np], qa, bfr[0], bfr[1]);
         mma16816<DT>(sacc[2 * np + 1], qa, bfr[2], bfr[3]);
       }
     }
-    // ---- online softmax (base 2), causal and ragged masks
+    // ---- online softmax (base 2): raw scores, the scale folded into the exponent;
+    // masks only where a key of the tile lies past the warp's first row limit
     const int key0 = kt * kKeys;
-    float mx_lo = -INFINITY, mx_hi = -INFINITY;
+    if (key0 + kKeys - 1 > wlim) {
+#pragma unroll
+      for (int n = 0; n < 8; ++n) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int key = key0 + 8 * n + 2 * t + e;
+          if (key > lim_lo) sacc[n][e] = -INFINITY;
+          if (key > lim_hi) sacc[n][2 + e] = -INFINITY;
+        }
+      }
+    }
+    float mx_lo = m_lo, mx_hi = m_hi;
 #pragma unroll
     for (int n = 0; n < 8; ++n) {
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int key = key0 + 8 * n + 2 * t + e;
-        sacc[n][e] = key <= lim_lo ? sacc[n][e] * p.qk_scale : -INFINITY;
-        sacc[n][2 + e] = key <= lim_hi ? sacc[n][2 + e] * p.qk_scale : -INFINITY;
-        mx_lo = fmaxf(mx_lo, sacc[n][e]);
-        mx_hi = fmaxf(mx_hi, sacc[n][2 + e]);
-      }
+      mx_lo = fmaxf(mx_lo, fmaxf(sacc[n][0], sacc[n][1]));
+      mx_hi = fmaxf(mx_hi, fmaxf(sacc[n][2], sacc[n][3]));
     }
     mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, 1));
     mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, 2));
     mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, 1));
     mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, 2));
-    const float mn_lo = fmaxf(m_lo, mx_lo), mn_hi = fmaxf(m_hi, mx_hi);
-    const float a_lo = mn_lo == -INFINITY ? 1.0f : exp2f(m_lo - mn_lo);
-    const float a_hi = mn_hi == -INFINITY ? 1.0f : exp2f(m_hi - mn_hi);
-    m_lo = mn_lo;
-    m_hi = mn_hi;
-    l_lo *= a_lo;
-    l_hi *= a_hi;
+    // new running maxima (raw units); a row with no key so far keeps its state
+    const float a_lo = mx_lo == -INFINITY ? 1.0f : ex2_ftz((m_lo - mx_lo) * qk);
+    const float a_hi = mx_hi == -INFINITY ? 1.0f : ex2_ftz((m_hi - mx_hi) * qk);
+    const float nb_lo = mx_lo == -INFINITY ? 0.0f : -mx_lo * qk;
+    const float nb_hi = mx_hi == -INFINITY ? 0.0f : -mx_hi * qk;
+    m_lo = mx_lo;
+    m_hi = mx_hi;
+    {
+      const F2 alo = f2_make(a_lo, a_lo), ahi = f2_make(a_hi, a_hi);
 #pragma unroll
-    for (int n = 0; n < 16; ++n) {
-      o[n][0] *= a_lo;
-      o[n][1] *= a_lo;
-      o[n][2] *= a_hi;
-      o[n][3] *= a_hi;
-    }
-#pragma unroll
-    for (int n = 0; n < 8; ++n) {
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const float plo = sacc[n][e] == -INFINITY ? 0.0f : exp2f(sacc[n][e] - mn_lo);
-        const float phi = sacc[n][2 + e] == -INFINITY ? 0.0f : exp2f(sacc[n][2 + e] - mn_hi);
-        sacc[n][e] = plo;
-        sacc[n][2 + e] = phi;
-        l_lo += plo;
-        l_hi += phi;
+      for (int n = 0; n < 16; ++n) {
+        float x0, x1;
+        f2_split(f2_mul(f2_make(o[n][0], o[n][1]), alo), x0, x1);
+        o[n][0] = x0;
+        o[n][1] = x1;
+        f2_split(f2_mul(f2_make(o[n][2], o[n][3]), ahi), x0, x1);
+        o[n][2] = x0;
+        o[n][3] = x1;
       }
     }
+    F2 ls_lo = f2_make(l_lo * a_lo, 0.0f), ls_hi = f2_make(l_hi * a_hi, 0.0f);
     // ---- O += P V: P as high + low 16-bit parts (A-fragments from the S accumulators)
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk) {  // 16 keys per k-step
-      uint32_t ph[4], pl[4];
+      uint32_t ah[4], al[4];
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        const float* c = sacc[2 * kk + h];
-        const float h0 = E::round(c[0]), h1 = E::round(c[1]);
-        const float h2 = E::round(c[2]), h3 = E::round(c[3]);
-        ph[2 * h] = E::pack(h0, h1);          // row g, keys 2t, 2t+1 (+8 for h = 1)
-        ph[2 * h + 1] = E::pack(h2, h3);      // row g + 8
-        pl[2 * h] = E::pack(c[0] - h0, c[1] - h1);
-        pl[2 * h + 1] = E::pack(c[2] - h2, c[3] - h3);
+        float* c = sacc[2 * kk + h];
+        const float p0 = ex2_ftz(__fmaf_rn(c[0], qk, nb_lo)), p1 = ex2_ftz(__fmaf_rn(c[1], qk, nb_lo));
+        const float p2 = ex2_ftz(__fmaf_rn(c[2], qk, nb_hi)), p3 = ex2_ftz(__fmaf_rn(c[3], qk, nb_hi));
+        ls_lo = f2_add(ls_lo, f2_make(p0, p1));
+        ls_hi = f2_add(ls_hi, f2_make(p2, p3));
+        // fragment order a0..a3 = (g, k lo), (g+8, k lo), (g, k hi), (g+8, k hi)
+        split_hilo<DT>(p0, p1, ah[2 * h], al[2 * h]);
+        split_hilo<DT>(p2, p3, ah[2 * h + 1], al[2 * h + 1]);
       }
-      // fragment order a0..a3 = (g, k lo), (g+8, k lo), (g, k hi), (g+8, k hi)
-      const uint32_t ah[4] = {ph[0], ph[1], ph[2], ph[3]};
-      const uint32_t al[4] = {pl[0], pl[1], pl[2], pl[3]};
 #pragma unroll
       for (int np = 0; np < 8; ++np) {  // pairs of 8-channel n-tiles
         uint32_t bfr[4];
         const int key = 16 * kk + (((lane >> 3) & 1) << 3) + (lane & 7);
-        ldsm4t(smem_u32(vst) + sw(key, 2 * np + (lane >> 4)), bfr);
+        ldsm4t(smem_u32(vts) + sw(key, 2 * np + (lane >> 4)), bfr);
         mma16816<DT>(o[2 * np], ah, bfr[0], bfr[1]);
-        mma16816<DT>(o[2 * np], al, bfr[0], bfr[1]);
         mma16816<DT>(o[2 * np + 1], ah, bfr[2], bfr[3]);
+        mma16816<DT>(o[2 * np], al, bfr[0], bfr[1]);
         mma16816<DT>(o[2 * np + 1], al, bfr[2], bfr[3]);
       }
     }
-  }
-  // ---- merge the odd-tile warps' state into the even-tile warps (same rows)
-  __syncthreads();  // every warp is done with the tiles: reuse K / V as scratch
-  float* mo = reinterpret_cast<float*>(ks);            // [4 warps][16][4][32 lanes]
-  float* ml = reinterpret_cast<float*>(vs);            // [4 warps][4][32 lanes]
-  if (kp == 1) {
-#pragma unroll
-    for (int n = 0; n < 16; ++n)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) mo[((rw * 16 + n) * 4 + e) * 32 + lane] = o[n][e];
-    ml[(rw * 4 + 0) * 32 + lane] = m_lo;
-    ml[(rw * 4 + 1) * 32 + lane] = m_hi;
-    ml[(rw * 4 + 2) * 32 + lane] = l_lo;
-    ml[(rw * 4 + 3) * 32 + lane] = l_hi;
-  }
-  __syncthreads();
-  if (kp == 1) return;
-  {
-    const float m2_lo = ml[(rw * 4 + 0) * 32 + lane], m2_hi = ml[(rw * 4 + 1) * 32 + lane];
-    const float mn_lo = fmaxf(m_lo, m2_lo), mn_hi = fmaxf(m_hi, m2_hi);
-    const float a_lo = m_lo == -INFINITY ? 0.0f : exp2f(m_lo - mn_lo);
-    const float a_hi = m_hi == -INFINITY ? 0.0f : exp2f(m_hi - mn_hi);
-    const float b_lo = m2_lo == -INFINITY ? 0.0f : exp2f(m2_lo - mn_lo);
-    const float b_hi = m2_hi == -INFINITY ? 0.0f : exp2f(m2_hi - mn_hi);
-    l_lo = l_lo * a_lo + ml[(rw * 4 + 2) * 32 + lane] * b_lo;
-    l_hi = l_hi * a_hi + ml[(rw * 4 + 3) * 32 + lane] * b_hi;
-#pragma unroll
-    for (int n = 0; n < 16; ++n) {
-      o[n][0] = o[n][0] * a_lo + mo[((rw * 16 + n) * 4 + 0) * 32 + lane] * b_lo;
-      o[n][1] = o[n][1] * a_lo + mo[((rw * 16 + n) * 4 + 1) * 32 + lane] * b_lo;
-      o[n][2] = o[n][2] * a_hi + mo[((rw * 16 + n) * 4 + 2) * 32 + lane] * b_hi;
-      o[n][3] = o[n][3] * a_hi + mo[((rw * 16 + n) * 4 + 3) * 32 + lane] * b_hi;
+    {
+      float x0, x1;
+      f2_split(ls_lo, x0, x1);
+      l_lo = x0 + x1;
+      f2_split(ls_hi, x0, x1);
+      l_hi = x0 + x1;
     }
+    __syncthreads();  // the tiles are read before the next dequantization
   }
-  // ---- normalise and store [b, i, hq, :]
+  if (failed) {
+    if (tid == 0) report_error(p.status, HQ_ERR_DEVICE_TIMEOUT);
+    // the copies still in flight land before the block moves on (bounded again);
+    // the block then contributes an empty state
+    for (int jj = j; jj < min(n_my, j + 2); ++jj) mbar_wait(&full[jj & 1], (jj >> 1) & 1);
+    m_lo = m_hi = -INFINITY;
+    l_lo = l_hi = 0.0f;
+#pragma unroll
+    for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
+  }
   l_lo += __shfl_xor_sync(0xffffffffu, l_lo, 1);
   l_lo += __shfl_xor_sync(0xffffffffu, l_lo, 2);
   l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 1);
   l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 2);
-  const float inv_lo = l_lo > 0.0f ? 1.0f / l_lo : 0.0f;
-  const float inv_hi = l_hi > 0.0f ? 1.0f / l_hi : 0.0f;
-  QT* out = reinterpret_cast<QT*>(p.out) + b * p.osb + hq * p.osh;
+
+  if (nc == 1) {
+    // ---- the block holds every key tile of its rows: normalise and store [b, i, hq, :]
+    const float inv_lo = l_lo > 0.0f ? 1.0f / l_lo : 0.0f;
+    const float inv_hi = l_hi > 0.0f ? 1.0f / l_hi : 0.0f;
+    QT* out = reinterpret_cast<QT*>(p.out) + b * p.osb + (hq0 + hl) * p.osh;
 #pragma unroll
-  for (int n = 0; n < 16; ++n) {
-    const int d = 8 * n + 2 * t;
-    if (row_lo < p.Sq)
-      *reinterpret_cast<uint32_t*>(out + row_lo * p.osi + d) = E::pack(o[n][0] * inv_lo, o[n][1] * inv_lo);
-    if (row_hi < p.Sq)
-      *reinterpret_cast<uint32_t*>(out + row_hi * p.osi + d) = E::pack(o[n][2] * inv_hi, o[n][3] * inv_hi);
+    for (int n = 0; n < 16; ++n) {
+      const int d = 8 * n + 2 * t;
+      if (row_lo < p.Sq)
+        *reinterpret_cast<uint32_t*>(out + row_lo * p.osi + d) = E::pack(o[n][0] * inv_lo, o[n][1] * inv_lo);
+      if (row_hi < p.Sq)
+        *reinterpret_cast<uint32_t*>(out + row_hi * p.osi + d) = E::pack(o[n][2] * inv_hi, o[n][3] * inv_hi);
+    }
+    return;
   }
+
+  // ---- cluster merge: the partial state of every block in its own shared memory
+  __syncthreads();  // every warp is done with the q / K / V tiles
+  float* part = reinterpret_cast<float*>(smem_raw);
+  float2* ml = reinterpret_cast<float2*>(smem_raw + C::kOffML);
+  {
+    const int pr_lo = hl * kRows + rw * 16 + g, pr_hi = pr_lo + 8;
+#pragma unroll
+    for (int n = 0; n < 16; ++n) {
+      *reinterpret_cast<float2*>(part + pr_lo * C::kPartStride + 8 * n + 2 * t) = make_float2(o[n][0], o[n][1]);
+      *reinterpret_cast<float2*>(part + pr_hi * C::kPartStride + 8 * n + 2 * t) = make_float2(o[n][2], o[n][3]);
+    }
+    if (t == 0) {
+      ml[pr_lo] = make_float2(m_lo * qk, l_lo);  // maxima in base-2 exponent units
+      ml[pr_hi] = make_float2(m_hi * qk, l_hi);
+    }
+  }
+  cluster_sync_all();  // every block's partial state is visible to the cluster
+  const int rows = C::kR / nc, r0 = chunk * rows;
+  float* wt = ksc;  // [rows][nc] merge weights, 1 / sum folded in
+  if (tid < rows) {
+    float mj[kMaxCluster], lj[kMaxCluster];
+    float M = -INFINITY;
+#pragma unroll
+    for (int c = 0; c < kMaxCluster; ++c) {
+      if (c < nc) {
+        const float2 v = dsmem_ld2(dsmem_addr(ml + r0 + tid, c));
+        mj[c] = v.x;
+        lj[c] = v.y;
+        M = fmaxf(M, v.x);
+      }
+    }
+    float L = 0.0f;
+#pragma unroll
+    for (int c = 0; c < kMaxCluster; ++c) {
+      if (c < nc) {
+        mj[c] = (M == -INFINITY || mj[c] == -INFINITY) ? 0.0f : exp2f(mj[c] - M);
+        L += mj[c] * lj[c];
+      }
+    }
+    const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+#pragma unroll
+    for (int c = 0; c < kMaxCluster; ++c)
+      if (c < nc) wt[tid * nc + c] = mj[c] * inv;
+  }
+  __syncthreads();
+  QT* out = reinterpret_cast<QT*>(p.out) + b * p.osb;
+#pragma unroll 1
+  for (int it = tid; it < rows * (kD / 4); it += T) {
+    const int r = it / (kD / 4), d4 = it % (kD / 4);
+    const int pr = r0 + r;
+    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+    for (int c = 0; c < kMaxCluster; ++c) {
+      if (c < nc) {
+        const float w = wt[r * nc + c];
+        const float4 v = dsmem_ld4(dsmem_addr(part + pr * C::kPartStride + 4 * d4, c));
+        acc.x += w * v.x;
+        acc.y += w * v.y;
+        acc.z += w * v.z;
+        acc.w += w * v.w;
+      }
+    }
+    const int i = i0 + pr % kRows;
+    if (i < p.Sq) {
+      QT* dst = out + (hq0 + pr / kRows) * p.osh + i * p.osi + 4 * d4;
+      reinterpret_cast<uint32_t*>(dst)[0] = E::pack(acc.x, acc.y);
+      reinterpret_cast<uint32_t*>(dst)[1] = E::pack(acc.z, acc.w);
+    }
+  }
+  cluster_sync_all();  // no block leaves while the others may still read its shared memory
 }
 
-// Sets the kernel's dynamic shared-memory limit once per device, then launches.
-template <int DT, int SDT>
-int launch(const Params& p, dim3 grid, cudaStream_t st) {
+// int8 codes [B, Hkv, S, 128] with byte strides (sb, sh, ss): boxes of 64 tokens x
+// 128 bytes, zero fill past S.
+inline int encode_code_map(CUtensorMap* m, const void* base, int64_t sb, int64_t sh, int64_t ss,
+                           int S, int Hkv, int B) {
+  auto enc = dec::encode_fn();
+  if (!enc) return HQ_ERR_UNSUPPORTED;
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(kD), static_cast<cuuint64_t>(S),
+                        static_cast<cuuint64_t>(Hkv), static_cast<cuuint64_t>(B)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(ss), static_cast<cuuint64_t>(sh),
+                           static_cast<cuuint64_t>(sb)};
+  cuuint32_t box[4] = {static_cast<cuuint32_t>(kD), static_cast<cuuint32_t>(kKeys), 1, 1};
+  cuuint32_t es[4] = {1, 1, 1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void*>(base), dims, strides,
+                   box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? HQ_OK : HQ_ERR_INVALID_ARGUMENT;
+}
+
+// Sets the kernel's dynamic shared-memory limit once per device, then launches the
+// grid with clusters of `nc` blocks along x.
+template <int DT, int SDT, int G>
+int launch(const CUtensorMap& mk, const CUtensorMap& mv, const Params& p, dim3 grid,
+           cudaStream_t st) {
+  using C = Cfg<G>;
+  auto kern = prefill_kernel<DT, SDT, G>;
   static std::atomic<uint64_t> ready{0};  // bit d: the attribute is set on device d
   int dev = 0;
   cudaGetDevice(&dev);
   const uint64_t bit = (dev >= 0 && dev < 64) ? (uint64_t(1) << dev) : 0;
   if (!bit || !(ready.load(std::memory_order_acquire) & bit)) {
-    cudaError_t e = cudaFuncSetAttribute(prefill_kernel<DT, SDT>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
     if (e != cudaSuccess) return static_cast<int>(e);
     ready.fetch_or(bit, std::memory_order_acq_rel);
   }
-  prefill_kernel<DT, SDT><<<grid, kThreads, kSmem, st>>>(p);
-  cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? HQ_OK : static_cast<int>(e);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(C::kThreads);
+  cfg.dynamicSmemBytes = C::kSmem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(p.n_chunks);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, mk, mv, p);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return static_cast<int>(e);
+  }
+  return HQ_OK;
+}
+
+// Blocks per cluster: double while every q tile still has tiles for each block and
+// the grid fits the resident slots (2 blocks per SM).
+inline int plan_chunks(int n_qt, int S, int head_groups, int B) {
+  const int max_kt = (S - 1) / kKeys + 1;
+  const int64_t units = static_cast<int64_t>(n_qt) * head_groups * B;
+  const int64_t slots = 2 * static_cast<int64_t>(current_sm_count());
+  int nc = 1;
+  while (nc < kMaxCluster && 2 * nc <= max_kt && units * 2 * nc <= slots) nc *= 2;
+  return nc;
+}
+
+template <int DT, int SDT>
+int dispatch(const CUtensorMap& mk, const CUtensorMap& mv, Params& p, int B, cudaStream_t st) {
+  const int nrep = p.Hq / p.Hkv;
+  const int G = nrep % 2 == 0 ? 2 : 1;
+  p.n_qt = (p.Sq + kRows - 1) / kRows;
+  p.n_chunks = plan_chunks(p.n_qt, p.S, p.Hq / G, B);
+  dim3 grid(p.n_qt * p.n_chunks, p.Hq / G, B);
+  return G == 2 ? launch<DT, SDT, 2>(mk, mv, p, grid, st) : launch<DT, SDT, 1>(mk, mv, p, grid, st);
 }
 
 }  // namespace pre
@@ -414,7 +681,8 @@ extern "C" int hq_prefill_int8(const void* q, int q_dtype, const int64_t q_strid
                                const void* k_scale, const void* v_scale, int scale_dtype,
                                const int64_t ksc_strides[3], const int64_t vsc_strides[3], int B,
                                int Hq, int Hkv, int Sq, int S, int D, float sm_scale, int q_quant,
-                               void* out, const int64_t out_strides[4], hq_stream_t stream) {
+                               void* out, const int64_t out_strides[4], int* status,
+                               hq_stream_t stream) {
   if (!q || !k || !v || !k_scale || !v_scale || !out || !q_strides || !kv_strides ||
       !ksc_strides || !vsc_strides || !out_strides || B < 0 || Hq <= 0 || Hkv <= 0 || Sq < 0 ||
       S < Sq)
@@ -423,24 +691,25 @@ extern "C" int hq_prefill_int8(const void* q, int q_dtype, const int64_t q_strid
       (q_dtype != HQ_DTYPE_BF16 && q_dtype != HQ_DTYPE_F16) ||
       (scale_dtype != HQ_DTYPE_F32 && scale_dtype != HQ_DTYPE_F16))
     return HQ_ERR_UNSUPPORTED;
-  // 16-byte rows: q rows and code rows are read as 16-byte vectors
+  // 16-byte rows: q rows are read as 16-byte vectors, code tiles by TMA (16-byte
+  // aligned base and strides)
   auto al = [](const void* x, uintptr_t a) { return reinterpret_cast<uintptr_t>(x) % a == 0; };
   if (q_strides[3] != 1 || out_strides[3] != 1 || kv_strides[2] % 16 || kv_strides[0] % 16 ||
-      kv_strides[1] % 16 || !al(k, 16) || !al(v, 16) || !al(q, 16) || q_strides[0] % 8 ||
-      q_strides[1] % 8 || q_strides[2] % 8 || !al(out, 4) || out_strides[0] % 2 ||
-      out_strides[1] % 2 || out_strides[2] % 2)
+      kv_strides[1] % 16 || kv_strides[2] < pre::kD || !al(k, 16) || !al(v, 16) || !al(q, 16) ||
+      q_strides[0] % 8 || q_strides[1] % 8 || q_strides[2] % 8 || !al(out, 4) ||
+      out_strides[0] % 2 || out_strides[1] % 2 || out_strides[2] % 2)
     return HQ_ERR_INVALID_ARGUMENT;
   if (B == 0 || Sq == 0) return HQ_OK;
+  CUtensorMap mk, mv;
+  int rc = pre::encode_code_map(&mk, k, kv_strides[0], kv_strides[1], kv_strides[2], S, Hkv, B);
+  if (rc == HQ_OK)
+    rc = pre::encode_code_map(&mv, v, kv_strides[0], kv_strides[1], kv_strides[2], S, Hkv, B);
+  if (rc != HQ_OK) return rc;
   pre::Params p{};
   p.q = q;
   p.qsb = q_strides[0];
   p.qsh = q_strides[1];
   p.qsi = q_strides[2];
-  p.k = k;
-  p.v = v;
-  p.kvsb = kv_strides[0];
-  p.kvsh = kv_strides[1];
-  p.kvss = kv_strides[2];
   p.ksc = k_scale;
   p.vsc = v_scale;
   p.kscb = ksc_strides[0];
@@ -459,11 +728,11 @@ extern "C" int hq_prefill_int8(const void* q, int q_dtype, const int64_t q_strid
   p.S = S;
   p.qk_scale = sm_scale * pre::kLog2e;
   p.q_quant = q_quant;
-  dim3 grid((Sq + pre::kRows - 1) / pre::kRows, Hq, B);
+  p.status = status;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (q_dtype == HQ_DTYPE_BF16)
-    return scale_dtype == HQ_DTYPE_F16 ? pre::launch<HQ_DTYPE_BF16, HQ_DTYPE_F16>(p, grid, st)
-                                       : pre::launch<HQ_DTYPE_BF16, HQ_DTYPE_F32>(p, grid, st);
-  return scale_dtype == HQ_DTYPE_F16 ? pre::launch<HQ_DTYPE_F16, HQ_DTYPE_F16>(p, grid, st)
-                                     : pre::launch<HQ_DTYPE_F16, HQ_DTYPE_F32>(p, grid, st);
+    return scale_dtype == HQ_DTYPE_F16 ? pre::dispatch<HQ_DTYPE_BF16, HQ_DTYPE_F16>(mk, mv, p, B, st)
+                                       : pre::dispatch<HQ_DTYPE_BF16, HQ_DTYPE_F32>(mk, mv, p, B, st);
+  return scale_dtype == HQ_DTYPE_F16 ? pre::dispatch<HQ_DTYPE_F16, HQ_DTYPE_F16>(mk, mv, p, B, st)
+                                     : pre::dispatch<HQ_DTYPE_F16, HQ_DTYPE_F32>(mk, mv, p, B, st);
 }

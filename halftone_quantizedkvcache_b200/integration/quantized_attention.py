@@ -44,7 +44,8 @@ def _round_up(n: int, m: int) -> int:
 
 class _DeviceStatus:
     """The device status words a cache's kernels report into: the K quantizer's
-    (folded into one int32 per device after each call, on the stream), the
+    and the fused prefill's (one int32 per device: the quantizer's folded in after
+    each call, on the stream; the prefill writes it directly), the
     sticky status words of the decode workspaces its attention used, and the
     status word of each device-length layer (``lens[2]``).  ``eager`` checks
     after every call (synchronises)."""
@@ -66,7 +67,7 @@ class _DeviceStatus:
 
     def words(self, stores):
         """(what, status) of every word; synchronises."""
-        out = [(f"quantize-K on cuda:{d}", int(t.item())) for d, t in self.quant.items()]
+        out = [(f"quantize-K / prefill on cuda:{d}", int(t.item())) for d, t in self.quant.items()]
         out += [("decode workspace", int(ws[:4].view(torch.int32).item()))
                 for ws in self.decode.values()]
         out += [(f"layer {i} device length", int(st.lens[2].item()))
@@ -693,8 +694,10 @@ def quantized_attention_forward(module, query, key, value, attention_mask, scali
                 and query.dtype in (torch.bfloat16, torch.float16)
                 and D == 128 and not (module.training and dropout > 0.0)
                 and _is_causal(attention_mask, Sq, st.length)):
-            out = kernels.int8_prefill_attn(query, k, k_sc, v, v_sc, module.num_key_value_groups,
-                                            sm_scale=scaling, q_quant=Q_DIMS is not None)
+            out = kernels.int8_prefill_attn(
+                query, k, k_sc, v, v_sc, module.num_key_value_groups, sm_scale=scaling,
+                q_quant=Q_DIMS is not None,
+                status_into=st.status.quant_word(query.device) if st.status is not None else None)
             return out, None
         key = kernels.dequant(k, k_sc, query.dtype, per_channel=True)
         value = kernels.dequant(v, v_sc, query.dtype, per_channel=False)

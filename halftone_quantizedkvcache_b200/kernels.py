@@ -49,6 +49,15 @@ def _stream(dev: torch.device) -> int:
     return torch.cuda.current_stream(dev).cuda_stream
 
 
+def _status_ptr(word: torch.Tensor | None, dev: torch.device) -> int | None:
+    """Device address of an int32 status word on ``dev`` (None: no word)."""
+    if word is None:
+        return None
+    if word.dtype != torch.int32 or word.device != dev or word.numel() < 1:
+        raise ValueError("status word: an int32 tensor on the call's device expected")
+    return word.data_ptr()
+
+
 def _rows_ok(t: torch.Tensor) -> bool:
     """[..., D] with unit inner stride and 16-byte aligned rows."""
     es = t.element_size()
@@ -558,7 +567,7 @@ def int8_decode_attn(q, k_i8, k_sc, v_i8, v_sc, n_rep=None, *, sm_scale=None, q_
 
 
 def int8_prefill_attn(q, k_i8, k_sc, v_i8, v_sc, n_rep=None, *, sm_scale=None, q_quant=False,
-                      out=None):
+                      out=None, status_into=None):
     """Causal prefill attention over an int8 cache (``hq_prefill_int8``).
 
     The prefill branch of the reference's patched attention
@@ -567,7 +576,8 @@ def int8_prefill_attn(q, k_i8, k_sc, v_i8, v_sc, n_rep=None, *, sm_scale=None, q
     ``[B,Hkv,S,D]`` with ``S >= Sq`` (the last Sq tokens are the queries'),
     k_sc ``[B,Hkv,1,D]``, v_sc ``[B,Hkv,S,1]`` (f16/f32).  Query i attends keys
     ``0 .. S - Sq + i``.  Returns ``[B,Sq,Hq,D]`` in q's dtype (or writes ``out``,
-    a tensor of that shape).
+    a tensor of that shape).  ``status_into``: an int32 CUDA word that receives
+    ``HQ_ERR_DEVICE_TIMEOUT`` if a bounded device wait gave up (first error sticks).
     """
     for t, n in ((q, "q"), (k_i8, "k_i8"), (k_sc, "k_sc"), (v_i8, "v_i8"), (v_sc, "v_sc")):
         _cuda(t, f"int8_prefill_attn {n}")
@@ -599,7 +609,8 @@ def int8_prefill_attn(q, k_i8, k_sc, v_i8, v_sc, n_rep=None, *, sm_scale=None, q
         _lib.strides((k_sc.stride(0), k_sc.stride(1), k_sc.stride(3)), 3),
         _lib.strides((v_sc.stride(0), v_sc.stride(1), v_sc.stride(2)), 3), B, Hq, Hkv, Sq, S, D,
         float(sm_scale), int(bool(q_quant)), out.data_ptr(),
-        _lib.strides((os_[0], os_[2], os_[1], os_[3]), 4), _stream(q.device))
+        _lib.strides((os_[0], os_[2], os_[1], os_[3]), 4), _status_ptr(status_into, q.device),
+        _stream(q.device))
     check(rc, "hq_prefill_int8")
     return out
 

@@ -249,15 +249,22 @@ HQ_API int hq_decode_int8_ex(const void* q, int q_dtype, const int64_t q_strides
  * out      logical [B, Hq, Sq, D] of q_dtype addressed by out_strides[4]
  *          (the reference's [B, Sq, Hq, D] output is strides
  *          (Sq*Hq*D, D, Hq*D, 1)).
- * Requires D == 128, Hq % Hkv == 0, S >= Sq, 16-byte aligned q and code rows.
- * No workspace.
+ * status   optional int32 device word: a block whose bounded wait for a code
+ *          tile gave up sets HQ_ERR_DEVICE_TIMEOUT there (first error sticks;
+ *          the rows it served are then incomplete).  May be NULL.
+ * Requires D == 128, Hq % Hkv == 0, S >= Sq, 16-byte aligned q rows, code
+ * rows of at least 128 bytes with a 16-byte aligned base and strides (the code
+ * tiles are read by TMA).  No workspace: the key tiles of a q tile are split
+ * over the blocks of a thread-block cluster, which merge their softmax states
+ * through distributed shared memory.
  */
 HQ_API int hq_prefill_int8(const void* q, int q_dtype, const int64_t q_strides[4],
                            const int8_t* k, const int8_t* v, const int64_t kv_strides[3],
                            const void* k_scale, const void* v_scale, int scale_dtype,
                            const int64_t ksc_strides[3], const int64_t vsc_strides[3], int B,
                            int Hq, int Hkv, int Sq, int S, int D, float sm_scale, int q_quant,
-                           void* out, const int64_t out_strides[4], hq_stream_t stream);
+                           void* out, const int64_t out_strides[4], int* status,
+                           hq_stream_t stream);
 
 /* ------------------------------------------------------------------------
  * Same-design dense twin: the int8 kernel's design (128-token tensor-map tiles,

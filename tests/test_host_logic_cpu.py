@@ -32,7 +32,7 @@ def test_new_entry_points_reject_bad_arguments():
     assert L.hq_append_kv_at(*aargs) == -1
     # hq_prefill_int8: null q; head_dim other than 128; f32 q; S < Sq
     pargs = [16, 1, st4, 16, 16, kv, 16, 16, 0, st3, st3, 1, 16, 8, 64, 64, 128, 0.1, 1, 16, st4,
-             None]
+             None, None]
     pargs[0] = None
     assert L.hq_prefill_int8(*pargs) == -1
     pargs[0], pargs[16] = 16, 64

@@ -43,6 +43,8 @@ def check(got, ref, what=""):
     (1, 8, 8, 65, 65, "f16", "f16", True),         # no GQA, ragged q and key tiles
     (1, 32, 8, 130, 300, "bf16", "f16", False),    # n_rep = 4, q used as given
     (2, 4, 2, 3, 3, "bf16", "f32", True),          # tiny
+    (4, 16, 8, 640, 640, "bf16", "f16", True),     # grid beyond the resident slots: no cluster split
+    (1, 6, 2, 200, 260, "f16", "f32", False),      # n_rep = 3: one head per block
 ])
 def test_prefill_vs_oracle(B, Hq, Hkv, Sq, S, dt, sdt, qq):
     rng = np.random.default_rng(S * 7 + Sq)
@@ -60,6 +62,25 @@ def test_prefill_vs_oracle(B, Hq, Hkv, Sq, S, dt, sdt, qq):
     ref = oa.prefill_int8(q, k8, ks.astype(np.float32), v8, vs.astype(np.float32), Hq // Hkv,
                           dtype=dt, q_quant=qq)
     check(out, ref, f"B={B} Hq={Hq} Sq={Sq} S={S}")
+
+
+def test_prefill_status_word_and_repeat():
+    """A status word stays 0 on a normal launch; repeated launches give identical rows
+    (the cluster merge has a fixed order)."""
+    rng = np.random.default_rng(11)
+    B, Hq, Hkv, S = 1, 16, 8, 512
+    k8, ks = oq.quant_k_perchannel(oin.outlier_k(rng, B, Hkv, S, 128))
+    v8, vs = oq.quant_v_pertoken(oin.normal(rng, (B, Hkv, S, 128)))
+    q = dev(oin.normal(rng, (B, Hq, S, 128)), "bf16")
+    word = torch.zeros(1, dtype=torch.int32, device="cuda")
+    args = (q, dev(k8), dev(oq.to_f16(ks)), dev(v8), dev(oq.to_f16(vs)), 2)
+    a = kernels.int8_prefill_attn(*args, q_quant=True, status_into=word)
+    b = kernels.int8_prefill_attn(*args, q_quant=True, status_into=word)
+    torch.cuda.synchronize()
+    assert int(word.item()) == 0
+    assert torch.equal(a, b)
+    with pytest.raises(ValueError):
+        kernels.int8_prefill_attn(*args, q_quant=True, status_into=word.to(torch.int64))
 
 
 def test_prefill_strided_q_and_output():
