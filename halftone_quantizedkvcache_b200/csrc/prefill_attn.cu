@@ -596,6 +596,563 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 2)
   cluster_sync_all();  // no block leaves while the others may still read its shared memory
 }
 
+// ================================================================ tcgen05 version
+// Used when the group size is even (two q heads of one kv head per block).
+// 128 q rows (row r = 64 h + i: head h of the pair, query i of the q tile) sit
+// on the 128 lanes of tensor memory; 4 warps, thread r owns row r.  Per key
+// tile: S = Q K^T (128 x 64 float32) and O += P V (128 x 128 float32) are
+// tcgen05.mma products issued by one thread into tensor memory (S: columns
+// 0..63, O: columns 128..255); Q, the dequantized K and V tiles and P (high
+// and low 16-bit parts) sit in shared memory in the 128-byte-swizzled layouts
+// the MMA reads (K-major for Q, K and P; MN-major for V, whose rows are
+// tokens).  Completion of the copies and of the MMAs is tracked by mbarriers
+// with bounded waits.  Each thread runs the online softmax of its own row from
+// a tcgen05.ld of S; O is rescaled in tensor memory when a row maximum grows.
+namespace um {
+
+constexpr int kThreads = 128;
+constexpr int kR = 128;                  // q rows of a block
+constexpr int kPieces = kKeys * (kD / 16) / kThreads;  // 16-code pieces per thread and tile
+static_assert((kThreads / 8) * kPieces == kKeys, "rows (tid >> 3) + 16 i cover the tile once");
+constexpr int kOffQ = 0;                 // 2 column blocks x 128 rows x 128 B
+constexpr int kOffK = 32768;             // 2 column blocks x 64 rows x 128 B; P high part later
+constexpr int kOffV = kOffK + 16384;     // 2 column blocks x 64 rows x 128 B
+constexpr int kOffPl = kOffV + 16384;    // 128 rows x 128 B
+constexpr int kOffCk = kOffPl + 16384;   // K codes of a tile (64 x 128 B)
+constexpr int kOffCv = kOffCk + 8192;    // V codes
+constexpr int kOffBar = kOffCv + 8192;   // fullK, fullV, s_done, pv_done
+constexpr int kOffTmem = kOffBar + 32;   // tensor-memory base written by tcgen05.alloc
+constexpr int kSmem = 1024 + kOffTmem + 16;  // 1024: alignment of the swizzled tiles
+constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kColS = 0, kColO = 128;
+constexpr int kPartStride = kD + 8;      // cluster merge: partial rows (floats)
+constexpr int kOffML = kR * kPartStride * 4;
+static_assert(kOffML + kR * 8 <= kOffCk, "the partial state overlaps the code staging");
+static_assert(kSmem + 1024 <= 233472 / 2, "two blocks per SM");
+
+// 128-byte-swizzled tile of 128-byte rows: byte offset of 16-byte chunk c of row r
+__device__ __forceinline__ uint32_t sw128(int r, int c) {
+  return static_cast<uint32_t>(r * 128 + ((c ^ (r & 7)) << 4));
+}
+
+// shared-memory matrix descriptor: 128-byte swizzle, version 1
+__device__ __forceinline__ uint64_t sdesc(uint32_t addr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  return static_cast<uint64_t>((addr >> 4) & 0x3FFFu) |
+         (static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16) |
+         (static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32) | (uint64_t(1) << 46) |
+         (uint64_t(2) << 61);
+}
+// instruction descriptor, kind::f16: float32 accumulator, A and B of the model dtype
+template <int DT>
+__host__ __device__ constexpr uint32_t idesc(int M, int N, bool b_mn_major) {
+  return (1u << 4) | (uint32_t(DT == HQ_DTYPE_BF16 ? 1 : 0) << 7) |
+         (uint32_t(DT == HQ_DTYPE_BF16 ? 1 : 0) << 10) | (uint32_t(b_mn_major ? 1 : 0) << 16) |
+         (uint32_t(N >> 3) << 17) | (uint32_t(M >> 4) << 24);
+}
+__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t id,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+      "l"(da), "l"(db), "r"(id), "r"(accumulate));
+}
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void fence_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+// 32 consecutive float32 columns of this thread's lane, the load awaited in the same
+// statement (the registers are not read before they are valid)
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
+      "%28, %29, %30, %31}, [%32];\n\ttcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
+      "%28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+      "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+      "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+      "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+      "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+      "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+      "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+      "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+      "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+      "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// 16 codes of one piece dequantized into two 16-byte chunks cc, cc + 1 of row r of a
+// 128-byte-swizzled column block (the float product code * scale rounded to the model
+// dtype, as the reference's update() computes it)
+template <int DT, bool PER_CHANNEL>
+__device__ __forceinline__ void dq_piece_sw(unsigned char* blk, int r, int cc, const uint4& codes,
+                                            const F2* sc) {
+  const uint32_t w[4] = {codes.x, codes.y, codes.z, codes.w};
+  uint32_t o[8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    F2 lo, hi;
+    s8x4_to_f2x2(w[i], lo, hi);
+    lo = f2_mul(lo, sc[PER_CHANNEL ? 2 * i : 0]);
+    hi = f2_mul(hi, sc[PER_CHANNEL ? 2 * i + 1 : 0]);
+    float a, b;
+    f2_split(lo, a, b);
+    o[2 * i] = T16<DT>::pack(a, b);
+    f2_split(hi, a, b);
+    o[2 * i + 1] = T16<DT>::pack(a, b);
+  }
+  *reinterpret_cast<uint4*>(blk + sw128(r, cc)) = make_uint4(o[0], o[1], o[2], o[3]);
+  *reinterpret_cast<uint4*>(blk + sw128(r, cc + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
+}
+
+template <int DT, int SDT>
+__global__ void __launch_bounds__(kThreads, 2)
+    prefill_umma_kernel(const __grid_constant__ CUtensorMap mk,
+                        const __grid_constant__ CUtensorMap mv, const Params p) {
+  using E = T16<DT>;
+  using SE = Elem<SDT>;
+  using QT = typename E::T;
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* qs = smem + kOffQ;
+  unsigned char* kts = smem + kOffK;
+  unsigned char* ph = smem + kOffK;  // P high part: the K tile is free once S is read
+  unsigned char* vts = smem + kOffV;
+  unsigned char* pl = smem + kOffPl;
+  unsigned char* ck = smem + kOffCk;
+  unsigned char* cv = smem + kOffCv;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
+  uint64_t* full_k = bars;
+  uint64_t* full_v = bars + 1;
+  uint64_t* s_done = bars + 2;
+  uint64_t* pv_done = bars + 3;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffTmem);
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int nc = p.n_chunks;
+  const int chunk = static_cast<int>(blockIdx.x) % nc;
+  const int qt = p.n_qt - 1 - static_cast<int>(blockIdx.x) / nc;  // longest rows first
+  const int nrep = p.Hq / p.Hkv, groups = nrep / 2;
+  const int hk = blockIdx.y / groups;
+  const int hq0 = hk * nrep + (blockIdx.y % groups) * 2;
+  const int b = blockIdx.z;
+  const int i0 = qt * kRows;
+  const int off = p.S - p.Sq;
+  const int last_key = min(p.S - 1, off + min(i0 + kRows, p.Sq) - 1);
+  const int n_kt = last_key / kKeys + 1;
+  const int n_my = n_kt > chunk ? (n_kt - 1 - chunk) / nc + 1 : 0;
+  const uint64_t pol = l2_evict_last();
+
+  auto issue_k = [&](int j) {
+    mbar_arrive_expect_tx(full_k, kKeys * kD);
+    dec::mmak::tma_load_4d(ck, &mk, 0, (chunk + j * nc) * kKeys, hk, b, full_k, pol);
+  };
+  auto issue_v = [&](int j) {
+    mbar_arrive_expect_tx(full_v, kKeys * kD);
+    dec::mmak::tma_load_4d(cv, &mv, 0, (chunk + j * nc) * kKeys, hk, b, full_v, pol);
+  };
+  if (tid == 0) {
+    for (int i = 0; i < 4; ++i) mbar_init(&bars[i], 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) {  // tensor memory: S and O
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+  if (tid == 0 && n_my > 0) {
+    issue_k(0);
+    issue_v(0);
+  }
+
+  // this thread's dequantization pieces: rows (tid >> 3) + 16 i (i < kPieces), channels
+  // 16 pc .. 16 pc + 15
+  const int pc = tid & 7, prow = tid >> 3;
+  F2 ksc2[8];
+  {
+    const auto* kp = reinterpret_cast<const typename SE::T*>(p.ksc) + b * p.kscb + hk * p.ksch;
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      ksc2[e] = f2_make(SE::to_f32(kp[(16 * pc + 2 * e) * p.kscd]),
+                        SE::to_f32(kp[(16 * pc + 2 * e + 1) * p.kscd]));
+  }
+  const auto* vsp = reinterpret_cast<const typename SE::T*>(p.vsc) + b * p.vscb + hk * p.vsch;
+  float vsr[kPieces];
+  auto load_vs = [&](int j) {
+    const int s0 = (chunk + j * nc) * kKeys + prow;
+#pragma unroll
+    for (int i = 0; i < kPieces; ++i) {
+      const int s = s0 + 16 * i;
+      vsr[i] = s < p.S ? SE::to_f32(vsp[s * p.vscs]) : 0.0f;
+    }
+  };
+  if (n_my > 0) load_vs(0);
+
+  // ---- this thread's q row: per-row fake quantization, 16-bit, swizzled K-major
+  const int r = tid, h = r >> 6, i_row = i0 + (r & 63);
+  {
+    const QT* src = reinterpret_cast<const QT*>(p.q) + b * p.qsb + (hq0 + h) * p.qsh +
+                    static_cast<int64_t>(i_row < p.Sq ? i_row : 0) * p.qsi;
+    uint4 w[16];
+#pragma unroll
+    for (int c = 0; c < 16; ++c)
+      w[c] = i_row < p.Sq ? *reinterpret_cast<const uint4*>(src + 8 * c) : make_uint4(0, 0, 0, 0);
+    Quantizer qz{};
+    if (p.q_quant) {
+      float m = 0.0f;
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        float f[8];
+        Vec16<DT>::unpack(w[c], f);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) m = fmaxf(m, fabsf(f[e]));
+      }
+      qz = Quantizer::from_amax(m);
+    }
+#pragma unroll
+    for (int c = 0; c < 16; ++c) {
+      uint4 o = w[c];
+      if (p.q_quant) {
+        float f[8];
+        Vec16<DT>::unpack(w[c], f);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) f[e] = static_cast<float>(qz.code(f[e])) * qz.scale;
+        o.x = E::pack(f[0], f[1]);
+        o.y = E::pack(f[2], f[3]);
+        o.z = E::pack(f[4], f[5]);
+        o.w = E::pack(f[6], f[7]);
+      }
+      *reinterpret_cast<uint4*>(qs + (c >> 3) * (kR * 128) + sw128(r, c & 7)) = o;
+    }
+  }
+  fence_async_smem();  // Q is read by the tensor cores
+
+  // descriptors: K-major tiles advance 32 bytes per 16-element k-step inside a
+  // 128-byte column block, then by the block; V (MN-major) by 16 token rows
+  const uint32_t qa = smem_u32(qs), ka = smem_u32(kts), va = smem_u32(vts);
+  const uint32_t pha = smem_u32(ph), pla = smem_u32(pl);
+  constexpr uint32_t id_s = idesc<DT>(128, 64, false);
+  constexpr uint32_t id_o = idesc<DT>(128, 128, true);
+  const float qk = p.qk_scale;
+  const int lim = i_row < p.Sq ? off + i_row : -1;  // last key of the row
+  float m_run = -INFINITY, l_run = 0.0f;
+  // issued copies / products (uniform over the block) and completions this thread saw
+  int k_iss = n_my > 0 ? 1 : 0, v_iss = k_iss, s_iss = 0, pv_iss = 0;
+  int k_wt = 0, v_wt = 0, s_wt = 0, pv_wt = 0;
+  bool ok = true;
+  int j = 0;
+  for (; j < n_my; ++j) {
+    const int kt = chunk + j * nc;
+    // the previous P V has finished reading V and P (P's high part lies in the K tile)
+    if (ok && pv_wt < pv_iss) {
+      ok = mbar_wait(pv_done, pv_wt & 1);
+      pv_wt += ok;
+    }
+    if (ok) {
+      ok = mbar_wait(full_k, k_wt & 1);
+      k_wt += ok;
+    }
+    if (ok) {
+#pragma unroll
+      for (int i = 0; i < kPieces; ++i) {
+        const int rr = prow + 16 * i;
+        const uint4 c = *reinterpret_cast<const uint4*>(ck + rr * kD + pc * 16);
+        dq_piece_sw<DT, true>(kts + (pc >> 2) * (kKeys * 128), rr, (2 * pc) & 7, c, ksc2);
+      }
+    }
+    fence_async_smem();
+    tc_fence_before();
+    if (__syncthreads_or(!ok)) break;
+    if (j + 1 < n_my) {
+      if (tid == 0) issue_k(j + 1);
+      ++k_iss;
+    }
+    if (tid == 0) {
+      tc_fence_after();
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk)
+        mma_f16(tmem + kColS, sdesc(qa + (kk >> 2) * (kR * 128) + (kk & 3) * 32, 16, 1024),
+                sdesc(ka + (kk >> 2) * (kKeys * 128) + (kk & 3) * 32, 16, 1024), id_s, kk > 0);
+      mma_commit(s_done);
+    }
+    ++s_iss;
+    // ---- V tile while S is computed
+    if (ok) {
+      ok = mbar_wait(full_v, v_wt & 1);
+      v_wt += ok;
+    }
+    if (ok) {
+#pragma unroll
+      for (int i = 0; i < kPieces; ++i) {
+        const int rr = prow + 16 * i;
+        const uint4 c = *reinterpret_cast<const uint4*>(cv + rr * kD + pc * 16);
+        const F2 s2 = f2_make(vsr[i], vsr[i]);
+        dq_piece_sw<DT, false>(vts + (pc >> 2) * (kKeys * 128), rr, (2 * pc) & 7, c, &s2);
+      }
+    }
+    if (j + 1 < n_my) load_vs(j + 1);
+    // ---- softmax of this row
+    if (ok) {
+      ok = mbar_wait(s_done, s_wt & 1);
+      s_wt += ok;
+    }
+    tc_fence_after();
+    float s[64];
+    {
+      float t0[32], t1[32];
+      tmem_ld32(tmem + lane_base + kColS, t0);
+      tmem_ld32(tmem + lane_base + kColS + 32, t1);
+#pragma unroll
+      for (int e = 0; e < 32; ++e) {
+        s[e] = t0[e];
+        s[32 + e] = t1[e];
+      }
+    }
+    const int key0 = kt * kKeys;
+    if (key0 + kKeys - 1 > lim) {
+#pragma unroll
+      for (int e = 0; e < 64; ++e)
+        if (key0 + e > lim) s[e] = -INFINITY;
+    }
+    float mx = m_run;
+#pragma unroll
+    for (int e = 0; e < 64; ++e) mx = fmaxf(mx, s[e]);
+    const float a = mx == -INFINITY ? 1.0f : ex2_ftz((m_run - mx) * qk);
+    const float nb = mx == -INFINITY ? 0.0f : -mx * qk;
+    m_run = mx;
+    // O *= a in tensor memory (the previous P V has completed) when a row maximum grew
+    if (j > 0 && __any_sync(0xffffffffu, a != 1.0f)) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float o[32];
+        tmem_ld32(tmem + lane_base + kColO + 32 * c, o);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) o[e] *= a;
+        tmem_st32(tmem + lane_base + kColO + 32 * c, o);
+      }
+      tmem_wait_st();
+    }
+    // P = 2^(s qk - m qk): high and low 16-bit parts, K-major rows of 64 keys
+    F2 ls = f2_make(l_run * a, 0.0f);
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      uint32_t hw[4], lw[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float p0 = ex2_ftz(__fmaf_rn(s[8 * c + 2 * e], qk, nb));
+        const float p1 = ex2_ftz(__fmaf_rn(s[8 * c + 2 * e + 1], qk, nb));
+        ls = f2_add(ls, f2_make(p0, p1));
+        split_hilo<DT>(p0, p1, hw[e], lw[e]);
+      }
+      *reinterpret_cast<uint4*>(ph + sw128(r, c)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+      *reinterpret_cast<uint4*>(pl + sw128(r, c)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+    }
+    {
+      float x0, x1;
+      f2_split(ls, x0, x1);
+      l_run = x0 + x1;
+    }
+    fence_async_smem();
+    tc_fence_before();
+    if (__syncthreads_or(!ok)) break;
+    if (j + 1 < n_my) {
+      if (tid == 0) issue_v(j + 1);
+      ++v_iss;
+    }
+    if (tid == 0) {
+      tc_fence_after();
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        const uint64_t dv = sdesc(va + kk * 16 * 128, kKeys * 128, 1024);
+        mma_f16(tmem + kColO, sdesc(pha + kk * 32, 16, 1024), dv, id_o, (j > 0 || kk > 0) ? 1u : 0u);
+        mma_f16(tmem + kColO, sdesc(pla + kk * 32, 16, 1024), dv, id_o, 1u);
+      }
+      mma_commit(pv_done);
+    }
+    ++pv_iss;
+  }
+  // every copy and product in flight completes before the block moves on (each wait
+  // bounded): in the normal case this is the wait for the last P V
+  bool done = true;
+  for (; k_wt < k_iss; ++k_wt) done = mbar_wait(full_k, k_wt & 1) && done;
+  for (; v_wt < v_iss; ++v_wt) done = mbar_wait(full_v, v_wt & 1) && done;
+  for (; s_wt < s_iss; ++s_wt) done = mbar_wait(s_done, s_wt & 1) && done;
+  for (; pv_wt < pv_iss; ++pv_wt) done = mbar_wait(pv_done, pv_wt & 1) && done;
+  if (j < n_my || !done) {  // a bounded wait gave up: the rows contribute nothing
+    report_error(p.status, HQ_ERR_DEVICE_TIMEOUT);
+    m_run = -INFINITY;
+    l_run = 0.0f;
+  }
+  tc_fence_after();
+  const bool have = n_my > 0 && l_run > 0.0f;
+
+  if (nc == 1) {
+    // ---- normalise this row and store [b, i, hq, :]
+    const float inv = have ? 1.0f / l_run : 0.0f;
+    QT* out = reinterpret_cast<QT*>(p.out) + b * p.osb + (hq0 + h) * p.osh + i_row * p.osi;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      float o[32];
+      tmem_ld32(tmem + lane_base + kColO + 32 * c, o);
+      if (i_row < p.Sq) {
+#pragma unroll
+        for (int e = 0; e < 16; ++e)
+          reinterpret_cast<uint32_t*>(out + 32 * c)[e] = E::pack(o[2 * e] * inv, o[2 * e + 1] * inv);
+      }
+    }
+  } else {
+    // ---- cluster merge through distributed shared memory
+    float* part = reinterpret_cast<float*>(smem);
+    float2* ml = reinterpret_cast<float2*>(smem + kOffML);
+    __syncthreads();  // no thread still reads the tiles the partial state overwrites
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      float o[32];
+      tmem_ld32(tmem + lane_base + kColO + 32 * c, o);
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        *reinterpret_cast<float4*>(part + r * kPartStride + 32 * c + 4 * e) =
+            have ? make_float4(o[4 * e], o[4 * e + 1], o[4 * e + 2], o[4 * e + 3])
+                 : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    }
+    ml[r] = make_float2(have ? m_run * qk : -INFINITY, have ? l_run : 0.0f);
+    cluster_sync_all();
+    const int rows = kR / nc, r0 = chunk * rows;
+    float* wt = reinterpret_cast<float*>(smem + kOffCk);  // [rows][nc]; codes no longer needed
+    if (tid < rows) {
+      float mj[kMaxCluster], lj[kMaxCluster];
+      float M = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < kMaxCluster; ++c) {
+        if (c < nc) {
+          const float2 v = dsmem_ld2(dsmem_addr(ml + r0 + tid, c));
+          mj[c] = v.x;
+          lj[c] = v.y;
+          M = fmaxf(M, v.x);
+        }
+      }
+      float L = 0.0f;
+#pragma unroll
+      for (int c = 0; c < kMaxCluster; ++c) {
+        if (c < nc) {
+          mj[c] = (M == -INFINITY || mj[c] == -INFINITY) ? 0.0f : exp2f(mj[c] - M);
+          L += mj[c] * lj[c];
+        }
+      }
+      const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+#pragma unroll
+      for (int c = 0; c < kMaxCluster; ++c)
+        if (c < nc) wt[tid * nc + c] = mj[c] * inv;
+    }
+    __syncthreads();
+    QT* out = reinterpret_cast<QT*>(p.out) + b * p.osb;
+#pragma unroll 1
+    for (int it = tid; it < rows * (kD / 4); it += kThreads) {
+      const int rr = it / (kD / 4), d4 = it % (kD / 4);
+      const int pr = r0 + rr;
+      float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+      for (int c = 0; c < kMaxCluster; ++c) {
+        if (c < nc) {
+          const float w = wt[rr * nc + c];
+          const float4 v = dsmem_ld4(dsmem_addr(part + pr * kPartStride + 4 * d4, c));
+          acc.x += w * v.x;
+          acc.y += w * v.y;
+          acc.z += w * v.z;
+          acc.w += w * v.w;
+        }
+      }
+      const int i = i0 + (pr & 63);
+      if (i < p.Sq) {
+        QT* dst = out + (hq0 + (pr >> 6)) * p.osh + i * p.osi + 4 * d4;
+        reinterpret_cast<uint32_t*>(dst)[0] = E::pack(acc.x, acc.y);
+        reinterpret_cast<uint32_t*>(dst)[1] = E::pack(acc.z, acc.w);
+      }
+    }
+    cluster_sync_all();  // no block leaves while the others may still read its shared memory
+  }
+  // ---- release the tensor memory
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(kTmemCols)
+                 : "memory");
+  }
+}
+
+template <int DT, int SDT>
+int launch(const CUtensorMap& mk, const CUtensorMap& mv, const Params& p, dim3 grid,
+           cudaStream_t st) {
+  auto kern = prefill_umma_kernel<DT, SDT>;
+  static std::atomic<uint64_t> ready{0};  // bit d: the attribute is set on device d
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint64_t bit = (dev >= 0 && dev < 64) ? (uint64_t(1) << dev) : 0;
+  if (!bit || !(ready.load(std::memory_order_acquire) & bit)) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    ready.fetch_or(bit, std::memory_order_acq_rel);
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(p.n_chunks);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, mk, mv, p);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return static_cast<int>(e);
+  }
+  return HQ_OK;
+}
+
+}  // namespace um
+
 // int8 codes [B, Hkv, S, 128] with byte strides (sb, sh, ss): boxes of 64 tokens x
 // 128 bytes, zero fill past S.
 inline int encode_code_map(CUtensorMap* m, const void* base, int64_t sb, int64_t sh, int64_t ss,
@@ -668,7 +1225,7 @@ int dispatch(const CUtensorMap& mk, const CUtensorMap& mv, Params& p, int B, cud
   p.n_qt = (p.Sq + kRows - 1) / kRows;
   p.n_chunks = plan_chunks(p.n_qt, p.S, p.Hq / G, B);
   dim3 grid(p.n_qt * p.n_chunks, p.Hq / G, B);
-  return G == 2 ? launch<DT, SDT, 2>(mk, mv, p, grid, st) : launch<DT, SDT, 1>(mk, mv, p, grid, st);
+  return G == 2 ? um::launch<DT, SDT>(mk, mv, p, grid, st) : launch<DT, SDT, 1>(mk, mv, p, grid, st);
 }
 
 }  // namespace pre
