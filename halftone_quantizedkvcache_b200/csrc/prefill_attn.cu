@@ -58,6 +58,7 @@ constexpr float kLog2e = 1.4426950408889634f;
 struct Params {
   const void* q;
   int64_t qsb, qsh, qsi;       // q [B, Hq, Sq, D] element strides
+  int q_heads_inner;           // q tensor map dims (D, Hq, Sq, B) instead of (D, Sq, Hq, B)
   const void* ksc;
   const void* vsc;
   int64_t kscb, ksch, kscd, vscb, vsch, vscs;
@@ -251,6 +252,21 @@ __device__ __forceinline__ uint64_t l2_evict_last() {
   return p;
 }
 
+// Fake quantization of two 16-bit values (the reference's per-token rule on q, whose
+// row maximum is itself a 16-bit value): the quotient x / s by the reciprocal and one
+// FMA residual correction (rint of it equals rint(RN(x / s)) for every bf16 and fp16
+// |x| <= amax), rounded half to even by adding 1.5 * 2^23, then RN16(code * s).  No
+// branch and no divide.
+template <int DT>
+__device__ __forceinline__ uint32_t fq_pair(uint32_t w, F2 ns2, F2 r2, F2 s2) {
+  const F2 m2 = f2_make(12582912.0f, 12582912.0f);
+  const F2 x = DT == HQ_DTYPE_BF16 ? bf16x2_to_f2(w) : f16x2_to_f2(w);
+  const F2 k = f2_sub(round_magic(quot_pair(x, ns2, r2)), m2);
+  float a, c;
+  f2_split(f2_mul(k, s2), a, c);
+  return T16<DT>::pack(a, c);
+}
+
 template <int DT, int SDT, int G>
 __global__ void __launch_bounds__(Cfg<G>::kThreads, 2)
     prefill_kernel(const __grid_constant__ CUtensorMap mk, const __grid_constant__ CUtensorMap mv,
@@ -337,9 +353,14 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 2)
         for (int e = 0; e < 32; ++e) m = fmaxf(m, fabsf(x[e]));
         m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
         m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
-        const Quantizer qz = Quantizer::from_amax(m);
+        const Quantizer qz = Quantizer::from_amax16(m);
+        const float M = 12582912.0f;
 #pragma unroll
-        for (int e = 0; e < 32; ++e) x[e] = E::round(static_cast<float>(qz.code(x[e])) * qz.scale);
+        for (int e = 0; e < 32; ++e) {  // exact quotient (16-bit inputs), half-to-even code
+          const float q0 = x[e] * qz.rcp;
+          const float q1 = __fmaf_rn(__fmaf_rn(q0, -qz.scale, x[e]), qz.rcp, q0);
+          x[e] = ((q1 + M) - M) * qz.scale;
+        }
       }
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
@@ -607,7 +628,9 @@ __global__ void __launch_bounds__(Cfg<G>::kThreads, 2)
 // the MMA reads (K-major for Q, K and P; MN-major for V, whose rows are
 // tokens).  Completion of the copies and of the MMAs is tracked by mbarriers
 // with bounded waits.  Each thread runs the online softmax of its own row from
-// a tcgen05.ld of S; O is rescaled in tensor memory when a row maximum grows.
+// a tcgen05.ld of S; O is rescaled in tensor memory when a row maximum grows by
+// more than 2^8 in probability.  Q arrives by TMA in the layout the MMA reads and
+// is fake-quantized in place, one row per thread.
 namespace um {
 
 constexpr int kThreads = 128;
@@ -620,8 +643,8 @@ constexpr int kOffV = kOffK + 16384;     // 2 column blocks x 64 rows x 128 B
 constexpr int kOffPl = kOffV + 16384;    // 128 rows x 128 B
 constexpr int kOffCk = kOffPl + 16384;   // K codes of a tile (64 x 128 B)
 constexpr int kOffCv = kOffCk + 8192;    // V codes
-constexpr int kOffBar = kOffCv + 8192;   // fullK, fullV, s_done, pv_done
-constexpr int kOffTmem = kOffBar + 32;   // tensor-memory base written by tcgen05.alloc
+constexpr int kOffBar = kOffCv + 8192;   // fullK, fullV, s_done, pv_done, fullQ
+constexpr int kOffTmem = kOffBar + 40;   // tensor-memory base written by tcgen05.alloc
 constexpr int kSmem = 1024 + kOffTmem + 16;  // 1024: alignment of the swizzled tiles
 constexpr uint32_t kTmemCols = 256;
 constexpr uint32_t kColS = 0, kColO = 128;
@@ -737,7 +760,8 @@ __device__ __forceinline__ void dq_piece_sw(unsigned char* blk, int r, int cc, c
 template <int DT, int SDT>
 __global__ void __launch_bounds__(kThreads, 2)
     prefill_umma_kernel(const __grid_constant__ CUtensorMap mk,
-                        const __grid_constant__ CUtensorMap mv, const Params p) {
+                        const __grid_constant__ CUtensorMap mv,
+                        const __grid_constant__ CUtensorMap mq, const Params p) {
   using E = T16<DT>;
   using SE = Elem<SDT>;
   using QT = typename E::T;
@@ -756,6 +780,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint64_t* full_v = bars + 1;
   uint64_t* s_done = bars + 2;
   uint64_t* pv_done = bars + 3;
+  uint64_t* full_q = bars + 4;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffTmem);
   const int tid = threadIdx.x, warp = tid >> 5;
   const int nc = p.n_chunks;
@@ -781,8 +806,21 @@ __global__ void __launch_bounds__(kThreads, 2)
     dec::mmak::tma_load_4d(cv, &mv, 0, (chunk + j * nc) * kKeys, hk, b, full_v, pol);
   };
   if (tid == 0) {
-    for (int i = 0; i < 4; ++i) mbar_init(&bars[i], 1);
+    for (int i = 0; i < 5; ++i) mbar_init(&bars[i], 1);
     fence_mbar_init();
+    // the block's q rows by TMA, straight into the swizzled K-major Q tile: per head of
+    // the pair, two boxes of 64 rows x 64 channels (rows past Sq read as zeros)
+    mbar_arrive_expect_tx(full_q, kR * kD * 2);
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+      for (int cb = 0; cb < 2; ++cb) {
+        unsigned char* dst = smem + kOffQ + cb * (kR * 128) + hh * (kRows * 128);
+        if (p.q_heads_inner)
+          dec::mmak::tma_load_4d(dst, &mq, 64 * cb, hq0 + hh, i0, b, full_q, pol);
+        else
+          dec::mmak::tma_load_4d(dst, &mq, 64 * cb, i0, hq0 + hh, b, full_q, pol);
+      }
   }
   if (warp == 0) {  // tensor memory: S and O
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -824,44 +862,37 @@ __global__ void __launch_bounds__(kThreads, 2)
   };
   if (n_my > 0) load_vs(0);
 
-  // ---- this thread's q row: per-row fake quantization, 16-bit, swizzled K-major
-  const int r = tid, h = r >> 6, i_row = i0 + (r & 63);
+  // ---- q: this thread's row of the Q tile (16 chunks of 16 bytes, swizzled), fake
+  // quantized in place per row (the reference's per-token rule); compact loops
   {
-    const QT* src = reinterpret_cast<const QT*>(p.q) + b * p.qsb + (hq0 + h) * p.qsh +
-                    static_cast<int64_t>(i_row < p.Sq ? i_row : 0) * p.qsi;
-    uint4 w[16];
-#pragma unroll
-    for (int c = 0; c < 16; ++c)
-      w[c] = i_row < p.Sq ? *reinterpret_cast<const uint4*>(src + 8 * c) : make_uint4(0, 0, 0, 0);
-    Quantizer qz{};
-    if (p.q_quant) {
+    const int qr = tid;
+    const bool ok_q = mbar_wait(full_q, 0);
+    if (!ok_q) report_error(p.status, HQ_ERR_DEVICE_TIMEOUT);
+    if (p.q_quant && ok_q) {
       float m = 0.0f;
-#pragma unroll
+#pragma unroll 4
       for (int c = 0; c < 16; ++c) {
-        float f[8];
-        Vec16<DT>::unpack(w[c], f);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) m = fmaxf(m, fabsf(f[e]));
+        const uint4 w = *reinterpret_cast<const uint4*>(qs + (c >> 3) * (kR * 128) + sw128(qr, c & 7));
+        m = fmaxf(m, fmaxf(fmaxf(absmax_of_x2<DT>(w.x), absmax_of_x2<DT>(w.y)),
+                           fmaxf(absmax_of_x2<DT>(w.z), absmax_of_x2<DT>(w.w))));
       }
-      qz = Quantizer::from_amax(m);
-    }
-#pragma unroll
-    for (int c = 0; c < 16; ++c) {
-      uint4 o = w[c];
-      if (p.q_quant) {
-        float f[8];
-        Vec16<DT>::unpack(w[c], f);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) f[e] = static_cast<float>(qz.code(f[e])) * qz.scale;
-        o.x = E::pack(f[0], f[1]);
-        o.y = E::pack(f[2], f[3]);
-        o.z = E::pack(f[4], f[5]);
-        o.w = E::pack(f[6], f[7]);
+      const Quantizer qz = Quantizer::from_amax16(m);
+      const F2 r2 = f2_make(qz.rcp, qz.rcp), s2 = f2_make(qz.scale, qz.scale);
+      const F2 ns2 = f2_make(-qz.scale, -qz.scale);
+#pragma unroll 4
+      for (int c = 0; c < 16; ++c) {
+        uint4* at = reinterpret_cast<uint4*>(qs + (c >> 3) * (kR * 128) + sw128(qr, c & 7));
+        uint4 w = *at;
+        w.x = fq_pair<DT>(w.x, ns2, r2, s2);
+        w.y = fq_pair<DT>(w.y, ns2, r2, s2);
+        w.z = fq_pair<DT>(w.z, ns2, r2, s2);
+        w.w = fq_pair<DT>(w.w, ns2, r2, s2);
+        *at = w;
       }
-      *reinterpret_cast<uint4*>(qs + (c >> 3) * (kR * 128) + sw128(r, c & 7)) = o;
     }
   }
   fence_async_smem();  // Q is read by the tensor cores
+  const int r = tid, h = r >> 6, i_row = i0 + (r & 63);  // this thread's row
 
   // descriptors: K-major tiles advance 32 bytes per 16-element k-step inside a
   // 128-byte column block, then by the block; V (MN-major) by 16 token rows
@@ -950,15 +981,29 @@ __global__ void __launch_bounds__(kThreads, 2)
       for (int e = 0; e < 64; ++e)
         if (key0 + e > lim) s[e] = -INFINITY;
     }
-    float mx = m_run;
+    float mx;
+    {  // row maximum as a tree (short dependency chain)
+      float t[16];
 #pragma unroll
-    for (int e = 0; e < 64; ++e) mx = fmaxf(mx, s[e]);
-    const float a = mx == -INFINITY ? 1.0f : ex2_ftz((m_run - mx) * qk);
-    const float nb = mx == -INFINITY ? 0.0f : -mx * qk;
-    m_run = mx;
-    // O *= a in tensor memory (the previous P V has completed) when a row maximum grew
+      for (int e = 0; e < 16; ++e) t[e] = fmaxf(fmaxf(s[e], s[e + 16]), fmaxf(s[e + 32], s[e + 48]));
+#pragma unroll
+      for (int w = 8; w >= 1; w >>= 1)
+#pragma unroll
+        for (int e = 0; e < w; ++e) t[e] = fmaxf(t[e], t[e + w]);
+      mx = fmaxf(m_run, t[0]);
+    }
+    // the running maximum moves only when the row maximum grows by more than 2^8 in
+    // probability: P stays below 256 (exact in its high and low parts), O and l keep
+    // a common scale, and O in tensor memory is rarely rescaled
+    float a = 1.0f;
+    if (mx != -INFINITY && (m_run == -INFINITY || (mx - m_run) * qk > 8.0f)) {
+      a = ex2_ftz((m_run - mx) * qk);
+      m_run = mx;
+    }
+    const float nb = m_run == -INFINITY ? 0.0f : -m_run * qk;
+    // O *= a in tensor memory (the previous P V has completed) when the maximum moved
     if (j > 0 && __any_sync(0xffffffffu, a != 1.0f)) {
-#pragma unroll
+#pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         float o[32];
         tmem_ld32(tmem + lane_base + kColO + 32 * c, o);
@@ -969,7 +1014,9 @@ __global__ void __launch_bounds__(kThreads, 2)
       tmem_wait_st();
     }
     // P = 2^(s qk - m qk): high and low 16-bit parts, K-major rows of 64 keys
-    F2 ls = f2_make(l_run * a, 0.0f);
+    F2 ls[4];  // four partial sums of pairs (short dependency chains)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) ls[e] = f2_make(0.0f, 0.0f);
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
       uint32_t hw[4], lw[4];
@@ -977,7 +1024,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       for (int e = 0; e < 4; ++e) {
         const float p0 = ex2_ftz(__fmaf_rn(s[8 * c + 2 * e], qk, nb));
         const float p1 = ex2_ftz(__fmaf_rn(s[8 * c + 2 * e + 1], qk, nb));
-        ls = f2_add(ls, f2_make(p0, p1));
+        ls[e] = f2_add(ls[e], f2_make(p0, p1));
         split_hilo<DT>(p0, p1, hw[e], lw[e]);
       }
       *reinterpret_cast<uint4*>(ph + sw128(r, c)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
@@ -985,8 +1032,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     {
       float x0, x1;
-      f2_split(ls, x0, x1);
-      l_run = x0 + x1;
+      f2_split(f2_add(f2_add(ls[0], ls[1]), f2_add(ls[2], ls[3])), x0, x1);
+      l_run = l_run * a + (x0 + x1);
     }
     fence_async_smem();
     tc_fence_before();
@@ -1009,7 +1056,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
   // every copy and product in flight completes before the block moves on (each wait
   // bounded): in the normal case this is the wait for the last P V
-  bool done = true;
+  bool done = mbar_wait(full_q, 0);
   for (; k_wt < k_iss; ++k_wt) done = mbar_wait(full_k, k_wt & 1) && done;
   for (; v_wt < v_iss; ++v_wt) done = mbar_wait(full_v, v_wt & 1) && done;
   for (; s_wt < s_iss; ++s_wt) done = mbar_wait(s_done, s_wt & 1) && done;
@@ -1026,7 +1073,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     // ---- normalise this row and store [b, i, hq, :]
     const float inv = have ? 1.0f / l_run : 0.0f;
     QT* out = reinterpret_cast<QT*>(p.out) + b * p.osb + (hq0 + h) * p.osh + i_row * p.osi;
-#pragma unroll
+#pragma unroll 1
     for (int c = 0; c < 4; ++c) {
       float o[32];
       tmem_ld32(tmem + lane_base + kColO + 32 * c, o);
@@ -1041,7 +1088,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     float* part = reinterpret_cast<float*>(smem);
     float2* ml = reinterpret_cast<float2*>(smem + kOffML);
     __syncthreads();  // no thread still reads the tiles the partial state overwrites
-#pragma unroll
+#pragma unroll 1
     for (int c = 0; c < 4; ++c) {
       float o[32];
       tmem_ld32(tmem + lane_base + kColO + 32 * c, o);
@@ -1082,27 +1129,40 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     __syncthreads();
     QT* out = reinterpret_cast<QT*>(p.out) + b * p.osb;
+    const int n_items = rows * (kD / 4);  // (row, 4 channels) items: a multiple of 2 * kThreads
 #pragma unroll 1
-    for (int it = tid; it < rows * (kD / 4); it += kThreads) {
-      const int rr = it / (kD / 4), d4 = it % (kD / 4);
-      const int pr = r0 + rr;
-      float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    for (int it0 = tid; it0 < n_items; it0 += 2 * kThreads) {
+      float4 v[2][kMaxCluster];  // every remote load of the two items in flight together
 #pragma unroll
-      for (int c = 0; c < kMaxCluster; ++c) {
-        if (c < nc) {
-          const float w = wt[rr * nc + c];
-          const float4 v = dsmem_ld4(dsmem_addr(part + pr * kPartStride + 4 * d4, c));
-          acc.x += w * v.x;
-          acc.y += w * v.y;
-          acc.z += w * v.z;
-          acc.w += w * v.w;
-        }
+      for (int u = 0; u < 2; ++u) {
+        const int it = it0 + u * kThreads;
+        const int pr = r0 + it / (kD / 4), d4 = it % (kD / 4);
+#pragma unroll
+        for (int c = 0; c < kMaxCluster; ++c)
+          if (c < nc) v[u][c] = dsmem_ld4(dsmem_addr(part + pr * kPartStride + 4 * d4, c));
       }
-      const int i = i0 + (pr & 63);
-      if (i < p.Sq) {
-        QT* dst = out + (hq0 + (pr >> 6)) * p.osh + i * p.osi + 4 * d4;
-        reinterpret_cast<uint32_t*>(dst)[0] = E::pack(acc.x, acc.y);
-        reinterpret_cast<uint32_t*>(dst)[1] = E::pack(acc.z, acc.w);
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int it = it0 + u * kThreads;
+        const int rr = it / (kD / 4), d4 = it % (kD / 4);
+        const int pr = r0 + rr;
+        float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+        for (int c = 0; c < kMaxCluster; ++c) {
+          if (c < nc) {
+            const float w = wt[rr * nc + c];
+            acc.x += w * v[u][c].x;
+            acc.y += w * v[u][c].y;
+            acc.z += w * v[u][c].z;
+            acc.w += w * v[u][c].w;
+          }
+        }
+        const int i = i0 + (pr & 63);
+        if (i < p.Sq) {
+          QT* dst = out + (hq0 + (pr >> 6)) * p.osh + i * p.osi + 4 * d4;
+          reinterpret_cast<uint32_t*>(dst)[0] = E::pack(acc.x, acc.y);
+          reinterpret_cast<uint32_t*>(dst)[1] = E::pack(acc.z, acc.w);
+        }
       }
     }
     cluster_sync_all();  // no block leaves while the others may still read its shared memory
@@ -1119,8 +1179,8 @@ __global__ void __launch_bounds__(kThreads, 2)
 }
 
 template <int DT, int SDT>
-int launch(const CUtensorMap& mk, const CUtensorMap& mv, const Params& p, dim3 grid,
-           cudaStream_t st) {
+int launch(const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mq, const Params& p,
+           dim3 grid, cudaStream_t st) {
   auto kern = prefill_umma_kernel<DT, SDT>;
   static std::atomic<uint64_t> ready{0};  // bit d: the attribute is set on device d
   int dev = 0;
@@ -1143,7 +1203,7 @@ int launch(const CUtensorMap& mk, const CUtensorMap& mv, const Params& p, dim3 g
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, mk, mv, p);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, mk, mv, mq, p);
   if (e != cudaSuccess) {
     cudaGetLastError();
     return static_cast<int>(e);
@@ -1168,6 +1228,31 @@ inline int encode_code_map(CUtensorMap* m, const void* base, int64_t sb, int64_t
   CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void*>(base), dims, strides,
                    box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? HQ_OK : HQ_ERR_INVALID_ARGUMENT;
+}
+
+// q [B, Hq, Sq, 128] of a 16-bit dtype with element strides (sb, sh, si): boxes of 64
+// channels x 64 rows, 128-byte swizzle (the K-major layout tcgen05.mma reads), zero
+// fill past Sq.  The dims run in increasing stride: (D, Sq, Hq, B), or (D, Hq, Sq, B)
+// when heads are closer than rows (q viewed from [B, Sq, Hq, D]); both give the same
+// shared-memory image of a box.
+inline int encode_q_map(CUtensorMap* m, const void* base, int dt, int64_t sb, int64_t sh,
+                        int64_t si, int Sq, int Hq, int B, int* heads_inner) {
+  auto enc = dec::encode_fn();
+  if (!enc) return HQ_ERR_UNSUPPORTED;
+  const bool hi = sh < si;
+  *heads_inner = hi ? 1 : 0;
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(kD), static_cast<cuuint64_t>(hi ? Hq : Sq),
+                        static_cast<cuuint64_t>(hi ? Sq : Hq), static_cast<cuuint64_t>(B)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>((hi ? sh : si) * 2),
+                           static_cast<cuuint64_t>((hi ? si : sh) * 2),
+                           static_cast<cuuint64_t>(sb * 2)};
+  cuuint32_t box[4] = {64, hi ? 1u : 64u, hi ? 64u : 1u, 1};
+  cuuint32_t es[4] = {1, 1, 1, 1};
+  CUresult r = enc(m, dt == HQ_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                   4, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? HQ_OK : HQ_ERR_INVALID_ARGUMENT;
 }
 
@@ -1225,7 +1310,11 @@ int dispatch(const CUtensorMap& mk, const CUtensorMap& mv, Params& p, int B, cud
   p.n_qt = (p.Sq + kRows - 1) / kRows;
   p.n_chunks = plan_chunks(p.n_qt, p.S, p.Hq / G, B);
   dim3 grid(p.n_qt * p.n_chunks, p.Hq / G, B);
-  return G == 2 ? um::launch<DT, SDT>(mk, mv, p, grid, st) : launch<DT, SDT, 1>(mk, mv, p, grid, st);
+  if (G == 1) return launch<DT, SDT, 1>(mk, mv, p, grid, st);
+  CUtensorMap mq;
+  const int rc = encode_q_map(&mq, p.q, DT, p.qsb, p.qsh, p.qsi, p.Sq, p.Hq, B, &p.q_heads_inner);
+  if (rc != HQ_OK) return rc;
+  return um::launch<DT, SDT>(mk, mv, mq, p, grid, st);
 }
 
 }  // namespace pre
