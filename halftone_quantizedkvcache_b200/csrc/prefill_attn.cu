@@ -757,6 +757,64 @@ __device__ __forceinline__ void dq_piece_sw(unsigned char* blk, int r, int cc, c
   *reinterpret_cast<uint4*>(blk + sw128(r, cc + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
 }
 
+// Merge of rows chunk R / NC .. of the cluster's partial states, pulled from every
+// block's shared memory: (row, 4 channels) items, consecutive threads on consecutive
+// channels of a row (coalesced remote reads), every load of a thread's items issued at
+// once and in flight while the row weights are formed (threads < rows, into wt); then
+// the weighted sums, stored as [b, i, hq, :].
+template <int DT, int NC>
+__device__ __forceinline__ void merge_pull(const float* part, const float2* ml, float* wt,
+                                           int chunk, int tid, int i0, int hq0, int Sq,
+                                           typename T16<DT>::T* out_b, int64_t osh, int64_t osi) {
+  constexpr int rows = kR / NC, NQ = rows * (kD / 4) / kThreads;
+  const int r0 = chunk * rows;
+  float4 v[NQ][NC];
+#pragma unroll
+  for (int k = 0; k < NQ; ++k) {
+    const int it = tid + kThreads * k, pr = r0 + (it >> 5), d4 = it & 31;
+#pragma unroll
+    for (int c = 0; c < NC; ++c)
+      v[k][c] = dsmem_ld4(dsmem_addr(part + pr * kPartStride + 4 * d4, c));
+  }
+  if (tid < rows) {
+    float2 mv[NC];
+#pragma unroll
+    for (int c = 0; c < NC; ++c) mv[c] = dsmem_ld2(dsmem_addr(ml + r0 + tid, c));
+    float M = -INFINITY;
+#pragma unroll
+    for (int c = 0; c < NC; ++c) M = fmaxf(M, mv[c].x);
+    float w[NC], L = 0.0f;
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      w[c] = (M == -INFINITY || mv[c].x == -INFINITY) ? 0.0f : exp2f(mv[c].x - M);
+      L += w[c] * mv[c].y;
+    }
+    const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+#pragma unroll
+    for (int c = 0; c < NC; ++c) wt[tid * NC + c] = w[c] * inv;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int k = 0; k < NQ; ++k) {
+    const int it = tid + kThreads * k, rr = it >> 5, d4 = it & 31, pr = r0 + rr;
+    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      const float w = wt[rr * NC + c];
+      acc.x += w * v[k][c].x;
+      acc.y += w * v[k][c].y;
+      acc.z += w * v[k][c].z;
+      acc.w += w * v[k][c].w;
+    }
+    const int i = i0 + (pr & 63);
+    if (i < Sq) {
+      auto* dst = out_b + (hq0 + (pr >> 6)) * osh + i * osi + 4 * d4;
+      reinterpret_cast<uint32_t*>(dst)[0] = T16<DT>::pack(acc.x, acc.y);
+      reinterpret_cast<uint32_t*>(dst)[1] = T16<DT>::pack(acc.z, acc.w);
+    }
+  }
+}
+
 template <int DT, int SDT>
 __global__ void __launch_bounds__(kThreads, 2)
     prefill_umma_kernel(const __grid_constant__ CUtensorMap mk,
@@ -1070,17 +1128,35 @@ __global__ void __launch_bounds__(kThreads, 2)
   const bool have = n_my > 0 && l_run > 0.0f;
 
   if (nc == 1) {
-    // ---- normalise this row and store [b, i, hq, :]
+    // ---- normalise this row into the (free) Q tile, swizzled; then store [b, i, hq, :]
+    // with consecutive threads on consecutive words of a row (coalesced)
     const float inv = have ? 1.0f / l_run : 0.0f;
-    QT* out = reinterpret_cast<QT*>(p.out) + b * p.osb + (hq0 + h) * p.osh + i_row * p.osi;
+    __syncthreads();  // no thread still reads Q
 #pragma unroll 1
     for (int c = 0; c < 4; ++c) {
       float o[32];
       tmem_ld32(tmem + lane_base + kColO + 32 * c, o);
-      if (i_row < p.Sq) {
 #pragma unroll
-        for (int e = 0; e < 16; ++e)
-          reinterpret_cast<uint32_t*>(out + 32 * c)[e] = E::pack(o[2 * e] * inv, o[2 * e + 1] * inv);
+      for (int e = 0; e < 4; ++e) {  // 16-byte chunk 4 c + e of the row
+        const int ch = 4 * c + e;
+        *reinterpret_cast<uint4*>(qs + (ch >> 3) * (kR * 128) + sw128(r, ch & 7)) =
+            make_uint4(E::pack(o[8 * e] * inv, o[8 * e + 1] * inv),
+                       E::pack(o[8 * e + 2] * inv, o[8 * e + 3] * inv),
+                       E::pack(o[8 * e + 4] * inv, o[8 * e + 5] * inv),
+                       E::pack(o[8 * e + 6] * inv, o[8 * e + 7] * inv));
+      }
+    }
+    __syncthreads();
+    QT* out_b = reinterpret_cast<QT*>(p.out) + b * p.osb;
+#pragma unroll 4
+    for (int k = 0; k < kR * (kD / 2) / kThreads; ++k) {  // words (element pairs) of the tile
+      const int wi = tid + kThreads * k, rr = wi >> 6, pw = wi & 63;
+      const int i = i0 + (rr & 63);
+      if (i < p.Sq) {
+        const int ch = pw >> 2;
+        const uint32_t v = *reinterpret_cast<const uint32_t*>(
+            qs + (ch >> 3) * (kR * 128) + sw128(rr, ch & 7) + (pw & 3) * 4);
+        reinterpret_cast<uint32_t*>(out_b + (hq0 + (rr >> 6)) * p.osh + i * p.osi)[pw] = v;
       }
     }
   } else {
@@ -1100,71 +1176,14 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     ml[r] = make_float2(have ? m_run * qk : -INFINITY, have ? l_run : 0.0f);
     cluster_sync_all();
-    const int rows = kR / nc, r0 = chunk * rows;
+    QT* out_b = reinterpret_cast<QT*>(p.out) + b * p.osb;
     float* wt = reinterpret_cast<float*>(smem + kOffCk);  // [rows][nc]; codes no longer needed
-    if (tid < rows) {
-      float mj[kMaxCluster], lj[kMaxCluster];
-      float M = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < kMaxCluster; ++c) {
-        if (c < nc) {
-          const float2 v = dsmem_ld2(dsmem_addr(ml + r0 + tid, c));
-          mj[c] = v.x;
-          lj[c] = v.y;
-          M = fmaxf(M, v.x);
-        }
-      }
-      float L = 0.0f;
-#pragma unroll
-      for (int c = 0; c < kMaxCluster; ++c) {
-        if (c < nc) {
-          mj[c] = (M == -INFINITY || mj[c] == -INFINITY) ? 0.0f : exp2f(mj[c] - M);
-          L += mj[c] * lj[c];
-        }
-      }
-      const float inv = L > 0.0f ? 1.0f / L : 0.0f;
-#pragma unroll
-      for (int c = 0; c < kMaxCluster; ++c)
-        if (c < nc) wt[tid * nc + c] = mj[c] * inv;
-    }
-    __syncthreads();
-    QT* out = reinterpret_cast<QT*>(p.out) + b * p.osb;
-    const int n_items = rows * (kD / 4);  // (row, 4 channels) items: a multiple of 2 * kThreads
-#pragma unroll 1
-    for (int it0 = tid; it0 < n_items; it0 += 2 * kThreads) {
-      float4 v[2][kMaxCluster];  // every remote load of the two items in flight together
-#pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const int it = it0 + u * kThreads;
-        const int pr = r0 + it / (kD / 4), d4 = it % (kD / 4);
-#pragma unroll
-        for (int c = 0; c < kMaxCluster; ++c)
-          if (c < nc) v[u][c] = dsmem_ld4(dsmem_addr(part + pr * kPartStride + 4 * d4, c));
-      }
-#pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const int it = it0 + u * kThreads;
-        const int rr = it / (kD / 4), d4 = it % (kD / 4);
-        const int pr = r0 + rr;
-        float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-#pragma unroll
-        for (int c = 0; c < kMaxCluster; ++c) {
-          if (c < nc) {
-            const float w = wt[rr * nc + c];
-            acc.x += w * v[u][c].x;
-            acc.y += w * v[u][c].y;
-            acc.z += w * v[u][c].z;
-            acc.w += w * v[u][c].w;
-          }
-        }
-        const int i = i0 + (pr & 63);
-        if (i < p.Sq) {
-          QT* dst = out + (hq0 + (pr >> 6)) * p.osh + i * p.osi + 4 * d4;
-          reinterpret_cast<uint32_t*>(dst)[0] = E::pack(acc.x, acc.y);
-          reinterpret_cast<uint32_t*>(dst)[1] = E::pack(acc.z, acc.w);
-        }
-      }
-    }
+    if (nc == 2)
+      merge_pull<DT, 2>(part, ml, wt, chunk, tid, i0, hq0, p.Sq, out_b, p.osh, p.osi);
+    else if (nc == 4)
+      merge_pull<DT, 4>(part, ml, wt, chunk, tid, i0, hq0, p.Sq, out_b, p.osh, p.osi);
+    else
+      merge_pull<DT, 8>(part, ml, wt, chunk, tid, i0, hq0, p.Sq, out_b, p.osh, p.osi);
     cluster_sync_all();  // no block leaves while the others may still read its shared memory
   }
   // ---- release the tensor memory
