@@ -254,9 +254,10 @@ HQ_API int hq_decode_int8_ex(const void* q, int q_dtype, const int64_t q_strides
  *          the rows it served are then incomplete).  May be NULL.
  * Requires D == 128, Hq % Hkv == 0, S >= Sq, 16-byte aligned q rows, code
  * rows of at least 128 bytes with a 16-byte aligned base and strides (the code
- * tiles are read by TMA).  No workspace: the key tiles of a q tile are split
- * over the blocks of a thread-block cluster, which merge their softmax states
- * through distributed shared memory.
+ * tiles, and q for even group sizes, are read by TMA).  No workspace: the key
+ * tiles of a q tile are split over the blocks of a thread-block cluster, which
+ * merge their softmax states through distributed shared memory.  Even group
+ * sizes run on tcgen05 with S and O in tensor memory (256 columns per block).
  */
 HQ_API int hq_prefill_int8(const void* q, int q_dtype, const int64_t q_strides[4],
                            const int8_t* k, const int8_t* v, const int64_t kv_strides[3],
