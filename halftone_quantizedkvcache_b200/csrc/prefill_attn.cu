@@ -950,7 +950,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
   }
   fence_async_smem();  // Q is read by the tensor cores
-  const int r = tid, h = r >> 6, i_row = i0 + (r & 63);  // this thread's row
+  const int r = tid, i_row = i0 + (r & 63);  // this thread's row
 
   // descriptors: K-major tiles advance 32 bytes per 16-element k-step inside a
   // 128-byte column block, then by the block; V (MN-major) by 16 token rows
