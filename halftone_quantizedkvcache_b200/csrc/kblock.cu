@@ -89,6 +89,21 @@ __device__ __forceinline__ void store_pair(int8_t* dst, int c0, int c1) {
       static_cast<uint16_t>((static_cast<uint32_t>(c0) & 0xffu) | ((static_cast<uint32_t>(c1) & 0xffu) << 8));
 }
 
+// Code of a 16-bit input x for the scale s = RN(m / 127) of a 16-bit maximum m >= |x|
+// (r = RN(1 / s)): the quotient x * r with one FMA residual correction, rounded half to
+// even by adding 1.5 * 2^23 - equal to rint(RN(x / s)) for every bf16 and fp16 such x,
+// so no divide and no branch.  float32 inputs keep Quantizer::code.
+template <int DT>
+__device__ __forceinline__ int code_of(const Quantizer& q, float x) {
+  if constexpr (DT == HQ_DTYPE_F32) {
+    return q.code(x);
+  } else {
+    const float q0 = x * q.rcp;
+    const float q1 = __fmaf_rn(__fmaf_rn(q0, -q.scale, x), q.rcp, q0);
+    return __float_as_int(q1 + 12582912.0f) - 0x4B400000;
+  }
+}
+
 __device__ __forceinline__ Quantizer quantizer_of_scale(float s) {
   Quantizer q;
   q.scale = s;
@@ -179,7 +194,7 @@ __global__ void __launch_bounds__(kWriteThreads) kblock_write_kernel(WriteParams
     const T* xp = kin + static_cast<int64_t>(r - pos) * p.kss + c0;
     float x0, x1;
     load_pair<DT>(xp, x0, x1);
-    store_pair(kq + static_cast<int64_t>(r) * p.kqs, q0.code(x0), q1.code(x1));
+    store_pair(kq + static_cast<int64_t>(r) * p.kqs, code_of<DT>(q0, x0), code_of<DT>(q1, x1));
     if (keep_tail && p.tail_mode == 0) {
       T* t = tail + static_cast<int64_t>(r - r0) * p.kts + c0;
       t[0] = xp[0];
@@ -193,7 +208,7 @@ __global__ void __launch_bounds__(kWriteThreads) kblock_write_kernel(WriteParams
     for (int r = r0 + g; r < lo; r += G) {
       float x0, x1;
       load_pair<DT>(tail + static_cast<int64_t>(r - r0) * p.kts + c0, x0, x1);
-      store_pair(kq + static_cast<int64_t>(r) * p.kqs, q0.code(x0), q1.code(x1));
+      store_pair(kq + static_cast<int64_t>(r) * p.kqs, code_of<DT>(q0, x0), code_of<DT>(q1, x1));
     }
   }
   if (g == 0) {
@@ -227,10 +242,10 @@ __global__ void __launch_bounds__(kWriteThreads) kblock_write_kernel(WriteParams
       for (int u = 0; u < kR; ++u) {
         const int r = rb + u * kWarps;
         if (r >= hi) break;
-        const Quantizer qv = Quantizer::from_amax(m[u]);
+        const Quantizer qv = DT == HQ_DTYPE_F32 ? Quantizer::from_amax(m[u]) : Quantizer::from_amax16(m[u]);
         int8_t* dst = vq + static_cast<int64_t>(r) * p.vqs;
 #pragma unroll
-        for (int i = 0; i < kN; ++i) dst[lane + 32 * i] = static_cast<int8_t>(qv.code(x[u][i]));
+        for (int i = 0; i < kN; ++i) dst[lane + 32 * i] = static_cast<int8_t>(code_of<DT>(qv, x[u][i]));
         if (lane == 0) {
           const int64_t so = b * p.vssb + h * p.vssh + static_cast<int64_t>(r) * p.vsss;
           if (p.vs32) p.vs32[so] = qv.scale;
