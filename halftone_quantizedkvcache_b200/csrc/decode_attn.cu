@@ -1424,7 +1424,12 @@ int launch_mma(Params p, int B, void* ws, size_t ws_bytes, cudaStream_t st) {
   // slot of a block another rank is waiting for.
   if (p.world > 0 && B * p.Hkv > per_sm * sms) return HQ_ERR_UNSUPPORTED;
   const int S_plan = p.seq_len ? p.S_plan : p.S;
-  const Plan pl = make_plan(B * p.Hkv, S_plan, per_sm * sms, sms, mmak::kTileT, p.world > 0);
+  // fused append: the appended token's split is one more block per (b, kv head); the
+  // main splits are planned for the slots left, so that it runs in the same wave
+  // rather than waiting for a slot while every merge waits for it
+  const int slots = per_sm * sms;
+  const int plan_slots = (p.k_new && slots >= 2 * B * p.Hkv) ? slots - B * p.Hkv : slots;
+  const Plan pl = make_plan(B * p.Hkv, S_plan, plan_slots, sms, mmak::kTileT, p.world > 0);
   if (ws_bytes < workspace_bytes(B, p.Hq, p.Hkv, S_plan, sms)) return HQ_ERR_WORKSPACE;
   // fused append: one more partial row per head (the appended token's split)
   const int n_rows = pl.n_split + (p.k_new ? 1 : 0);
