@@ -9,11 +9,19 @@
 // 0 .. S - Sq + i (the newest Sq of S cached tokens are the queries).
 //
 // The reference materialises the dequantized cache and runs it through ~15
-// torch kernels; here one launch reads the int8 codes:
+// torch kernels; here one launch reads the int8 codes.  Two kernels share the
+// work decomposition:
 //
-//   * a block takes 64 query rows of G query heads that share one kv head
-//     (G = 2 when the group size is even, else 1): 4 G warps, warp w holds 16
-//     rows of head w / 4, and the dequantized K / V tiles serve all G heads;
+//   * even group sizes (every Qwen3 shape): prefill_umma_kernel (namespace um,
+//     below) - a block takes 64 query rows of the two q heads that share a kv
+//     head (128 rows = 128 tensor-memory lanes, one per thread), S = Q K^T and
+//     O += P V are tcgen05.mma products in tensor memory, Q arrives by TMA in
+//     the swizzled layout the MMA reads and is fake-quantized in place;
+//   * odd group sizes: prefill_kernel - a block takes 64 query rows of one q
+//     head, 8 warps (warps w and w + 4 share 16 rows and take alternate key
+//     tiles), S and P V on mma.sync m16n8k16 with ldmatrix A/B fragments.
+//
+// Shared by both:
 //   * the 64-token key tiles that a q tile's causal rows reach are dealt round
 //     robin to the C blocks of a thread-block cluster (C = 1, 2, 4 or 8, chosen
 //     on the host so that the grid fills the resident block slots of the GPU;
@@ -22,18 +30,16 @@
 //     through distributed shared memory: every block leaves its unnormalised
 //     output rows and (max, sum) in its own shared memory, and after a cluster
 //     barrier block c merges rows c R / C .. (c + 1) R / C of all C blocks and
-//     stores them (R = 64 G rows).  No workspace, no second launch;
+//     stores them.  No workspace, no second launch;
 //   * code tiles (64 tokens x 128 bytes of K and of V) arrive by TMA
-//     (cp.async.bulk.tensor) into a two-stage ring with mbarrier completion and
-//     bounded waits; all threads dequantize a stage exactly as the reference's
-//     update() does (float product rounded to the model dtype) into 16-bit
-//     tiles with a 16-byte XOR swizzle (conflict-free ldmatrix);
-//   * q rows are fake-quantized in the prologue and kept in shared memory as
-//     bf16/f16 (A-fragments by ldmatrix in every key tile);
-//   * S = q K^T and O += P V on the tensor cores (mma.sync m16n8k16, float32
-//     accumulation) with an online float32 softmax; P is split into a high
-//     and a low 16-bit part (two MMAs), so the probabilities keep ~16 bits
-//     instead of the 8 of a single bf16 rounding.
+//     (cp.async.bulk.tensor) with mbarrier completion and bounded waits; all
+//     threads dequantize them exactly as the reference's update() does (float
+//     product rounded to the model dtype) into swizzled 16-bit tiles;
+//   * q rows are fake-quantized per row (the reference's per-token rule) with a
+//     branch-free exact quotient;
+//   * the online softmax runs in float32 with the scale folded into the
+//     exponent; P is split into a high and a low 16-bit part (two MMAs), so the
+//     probabilities keep ~16 bits instead of the 8 of a single bf16 rounding.
 // The inputs of both products are exactly the reference's 16-bit values, so
 // the result differs from the float32 math of record only by accumulation
 // order and the 2^-16 relative rounding of P.
