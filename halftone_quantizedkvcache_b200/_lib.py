@@ -36,6 +36,8 @@ SIGNATURES = {
     "hq_quant_k_static": (_I, [_P, _I, _A4, _I, _I, _I, _I, _P, _I, _A4, _P, _A4, _P]),
     "hq_append_kv_static": (_I, [_P, _P, _I, _A4, _A4, _I, _I, _I, _I, _P, _I, _A4, _P, _A4, _P,
                                  _A4, _P, _P, _A4, _P]),
+    "hq_column_absmax": (_I, [_P, _I, _A4, _I, _I, _I, _I, _P, _P]),
+    "hq_k_scale_from_amax": (_I, [_P, _I, _P, _P, _P]),
     "hq_dequant": (_I, [_P, _A4, _I, _I, _I, _I, _P, _I, _A4, _I, _P, _I, _A4, _P]),
     "hq_decode_workspace_bytes": (_Z, [_I, _I, _I, _I, _I]),
     "hq_decode_int8": (_I, [_P, _I, _A4, _P, _P, _A4, _P, _P, _I, _A4, _A4, _I, _I, _I, _I, _I,

@@ -912,6 +912,70 @@ static int launch_quant_k_static(const void* x, const int64_t* xs, int B, int H,
   return finish_launch();
 }
 
+// ------------------------------------------------------------------ column maxima
+// max |x| over the tokens of x [B, H, S, D] per (b, h, d): the input of the K scale
+// of a bulk write sharded along the sequence (each rank reduces its own tokens and
+// the ranks combine their maxima with one all-reduce, after which the codes come from
+// the static-scale kernel with scale = RN(max(amax, 1e-8) / 127), the reference's
+// rule).  grid (row chunks of kAbsRows, H, B): a block folds its rows into
+// per-column maxima (16-byte vectors; a row slot per D / VE threads), reduces the
+// row slots in shared memory and publishes one atomicMax per column (float bits:
+// every value is >= 0).  amax is zero-filled by the entry point first.
+constexpr int kAbsRows = 512;
+
+template <int DT, int D>
+__global__ void __launch_bounds__(kThreads) column_absmax_kernel(
+    const char* __restrict__ x, int64_t xsb, int64_t xsh, int64_t xss, int S,
+    unsigned* __restrict__ amax) {
+  constexpr int EB = Elem<DT>::kBytes, VE = 16 / EB, VPR = D / VE, RS = kThreads / VPR;
+  __shared__ float red[RS][D];
+  const int tid = threadIdx.x, cg = tid % VPR, rs = tid / VPR;
+  const int64_t b = blockIdx.z, h = blockIdx.y;
+  const int r0 = static_cast<int>(blockIdx.x) * kAbsRows, r1 = min(S, r0 + kAbsRows);
+  const char* base = x + (b * xsb + h * xsh) * EB + cg * 16;
+  float m[VE];
+#pragma unroll
+  for (int e = 0; e < VE; ++e) m[e] = 0.0f;
+#pragma unroll 4
+  for (int r = r0 + rs; r < r1; r += RS) {
+    float f[VE];
+    Vec16<DT>::unpack(ldg_stream(base + static_cast<int64_t>(r) * xss * EB), f);
+#pragma unroll
+    for (int e = 0; e < VE; ++e) m[e] = fmaxf(m[e], fabsf(f[e]));
+  }
+#pragma unroll
+  for (int e = 0; e < VE; ++e) red[rs][cg * VE + e] = m[e];
+  __syncthreads();
+  if (tid < D) {
+    float a = red[0][tid];
+#pragma unroll
+    for (int w = 1; w < RS; ++w) a = fmaxf(a, red[w][tid]);
+    atomicMax(amax + (b * gridDim.y + h) * D + tid, __float_as_uint(a));
+  }
+}
+
+// the reference's scale of a column maximum: RN(max(amax, 1e-8) / 127)
+__global__ void k_scale_from_amax_kernel(const float* __restrict__ amax, int n,
+                                         float* __restrict__ s32, __half* __restrict__ s16) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const float s = Quantizer::from_amax(amax[i]).scale;
+  if (s32) s32[i] = s;
+  if (s16) s16[i] = __float2half_rn(s);
+}
+
+template <int DT, int D>
+static int launch_column_absmax(const void* x, const int64_t* xs, int B, int H, int S,
+                                float* amax, cudaStream_t st) {
+  cudaError_t e = cudaMemsetAsync(amax, 0, sizeof(float) * static_cast<size_t>(B) * H * D, st);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  if (S == 0) return HQ_OK;
+  dim3 grid((S + kAbsRows - 1) / kAbsRows, H, B);
+  column_absmax_kernel<DT, D><<<grid, kThreads, 0, st>>>(static_cast<const char*>(x), xs[0], xs[1],
+                                                         xs[2], S, reinterpret_cast<unsigned*>(amax));
+  return finish_launch();
+}
+
 static bool valid_dtype_x(int dt) {
   return dt == HQ_DTYPE_F32 || dt == HQ_DTYPE_BF16 || dt == HQ_DTYPE_F16;
 }
@@ -1125,4 +1189,27 @@ extern "C" int hq_read_status(const void* workspace, hq_stream_t stream) {
   if (e == cudaSuccess) e = cudaStreamSynchronize(st);
   if (e != cudaSuccess) return static_cast<int>(e);
   return v;
+}
+
+extern "C" int hq_column_absmax(const void* x, int x_dtype, const int64_t x_strides[4], int B,
+                                int H, int S, int D, float* amax, hq_stream_t stream) {
+  if (!x || !x_strides || !amax || B < 0 || H < 0 || S < 0) return HQ_ERR_INVALID_ARGUMENT;
+  if (!valid_dtype_x(x_dtype)) return HQ_ERR_UNSUPPORTED;
+  if (B > 65535 || H > 65535) return HQ_ERR_UNSUPPORTED;  // grid z / y limits
+  if (B == 0 || H == 0) return HQ_OK;
+  if (!aligned(amax, 4) || (S > 0 && !rows16(x, x_strides, x_dtype))) return HQ_ERR_INVALID_ARGUMENT;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  HQ_DISPATCH_X(x_dtype, HQ_DISPATCH_D(D, return launch_column_absmax<kDT, kD>(
+                                              x, x_strides, B, H, S, amax, st);))
+}
+
+extern "C" int hq_k_scale_from_amax(const float* amax, int n, float* scale_f32,
+                                    uint16_t* scale_f16, hq_stream_t stream) {
+  if (!amax || n < 0 || (!scale_f32 && !scale_f16)) return HQ_ERR_INVALID_ARGUMENT;
+  if (n == 0) return HQ_OK;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  k_scale_from_amax_kernel<<<(n + 255) / 256, 256, 0, st>>>(amax, n, scale_f32,
+                                                            reinterpret_cast<__half*>(scale_f16));
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? HQ_OK : static_cast<int>(e);
 }

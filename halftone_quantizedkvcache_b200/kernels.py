@@ -212,6 +212,47 @@ def quant_k_static(x: torch.Tensor, scale: torch.Tensor, *,
     return q
 
 
+def column_absmax(x: torch.Tensor, *, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Per-channel ``max(|x|)`` over the tokens of ``x [B,H,S,D]`` (``hq_column_absmax``):
+    float32 ``[B,H,1,D]`` (or writes ``out``, a contiguous float32 tensor of that
+    shape).  An empty ``x`` (S = 0) gives zeros.  The K scale's input for a bulk
+    write whose tokens are split over ranks (``sharding.sequence_sharded_quant_k``)."""
+    _cuda(x, "column_absmax")
+    if x.dim() != 4:
+        raise ValueError(f"column_absmax: expected [B, H, S, D], got {tuple(x.shape)}")
+    B, H, S, D = x.shape
+    x = _rowmajor(x) if S > 0 else x
+    if out is None:
+        out = torch.empty((B, H, 1, D), dtype=torch.float32, device=x.device)
+    elif out.shape != (B, H, 1, D) or out.dtype != torch.float32 or not out.is_contiguous():
+        raise ValueError("column_absmax: out must be a contiguous float32 [B,H,1,D] tensor")
+    rc = _lib.lib().hq_column_absmax(
+        x.data_ptr() if S > 0 else out.data_ptr(), _dtype_code(x, "column_absmax"),
+        _lib.strides(x.stride(), 4), B, H, S, D, out.data_ptr(), _stream(x.device))
+    check(rc, "hq_column_absmax")
+    return out
+
+
+def k_scale_from_amax(amax: torch.Tensor, *, scale_dtype: torch.dtype | None = torch.float16):
+    """The reference's per-channel scale ``RN(max(amax, 1e-8) / 127)`` of float32 column
+    maxima (``hq_k_scale_from_amax``): returns ``(scale_f32, scale_in_scale_dtype)``
+    (the second is None when ``scale_dtype`` is None), both of ``amax``'s shape."""
+    _cuda(amax, "k_scale_from_amax amax")
+    if amax.dtype != torch.float32 or not amax.is_contiguous():
+        raise ValueError("k_scale_from_amax: amax must be contiguous float32")
+    s32 = torch.empty_like(amax)
+    s16 = None
+    if scale_dtype is not None:
+        if scale_dtype not in (torch.float16, torch.float32):
+            raise TypeError("k_scale_from_amax: scale_dtype must be float16, float32 or None")
+        s16 = torch.empty_like(amax, dtype=torch.float16) if scale_dtype == torch.float16 else None
+    rc = _lib.lib().hq_k_scale_from_amax(amax.data_ptr(), amax.numel(), s32.data_ptr(),
+                                         s16.data_ptr() if s16 is not None else None,
+                                         _stream(amax.device))
+    check(rc, "hq_k_scale_from_amax")
+    return s32, (s16 if scale_dtype == torch.float16 else (s32 if scale_dtype is not None else None))
+
+
 def calibrate_k_scale(samples, dtype: torch.dtype = torch.float32) -> torch.Tensor:
     """Static per-channel K scales ``[1, H, 1, D]`` from calibration samples
     (K tensors ``[B, H, S, D]``): ``max(|x|) / 127`` over every sample, batch and

@@ -5,6 +5,8 @@ Two partitions, as the workloads define them:
 * **batch / kv-head sharding** (batched serving decode, bulk quantize-on-write):
   sequences are independent, so each rank owns a contiguous batch range and
   runs the single-GPU kernels on it; there is no collective on the data path.
+  A bulk write split along the sequence instead (``sequence_sharded_quant_k``)
+  has one exchange: an ``all_reduce(MAX)`` of the K column maxima.
 * **sequence sharding** (one very long sequence): each rank owns a contiguous
   token range of the int8 cache (a multiple of the 64-token kernel tile) plus
   the replicated per-channel K scales and computes the float32 (m, l, o)
@@ -45,6 +47,45 @@ def sequence_range(S: int, world: int, rank: int, align: int = TILE) -> tuple[in
     units = (S + align - 1) // align
     u0, u1 = batch_range(units, world, rank)
     return min(S, u0 * align), min(S, u1 * align)
+
+
+def sequence_sharded_quant_k(x_shard: torch.Tensor, *, group=None,
+                             scale_dtype: torch.dtype | None = torch.float16,
+                             out: torch.Tensor | None = None,
+                             column_absmax=None, scale_from_amax=None, quant_static=None):
+    """K per channel for a bulk write whose tokens are split over ranks (each rank
+    holds ``x_shard [B, H, S_rank, D]``, its ``sequence_range`` of every sequence).
+
+    The per-channel scale is that of the whole sequence, as an unsharded
+    ``quant_k_perchannel`` computes it (quantize_int8 with dims (2,),
+    reference/page_attention_int8_pytorch.py:23-30): each rank reduces its own
+    tokens to column maxima (``hq_column_absmax``), one ``all_reduce(MAX)`` of the
+    ``B * H * D`` float32 maxima combines them - the write's only exchange - and
+    every rank derives the scale ``RN(max(amax, 1e-8) / 127)``
+    (``hq_k_scale_from_amax``) and codes its tokens with the static-scale kernel
+    (``hq_quant_k_static``).  The codes and the scale are bit-identical to the
+    unsharded quantization's; an empty shard contributes zeros to the maximum.
+
+    Returns ``(codes [B, H, S_rank, D] int8, scale [B, H, 1, D])`` with the scale in
+    ``scale_dtype`` (float32 when None).  ``column_absmax`` / ``scale_from_amax`` /
+    ``quant_static`` replace the three steps (host-side tests pass CPU versions);
+    the defaults are this library's kernels.
+    """
+    from . import kernels
+    column_absmax = column_absmax or kernels.column_absmax
+    quant_static = quant_static or kernels.quant_k_static
+    if scale_from_amax is None:
+        def scale_from_amax(a):
+            return kernels.k_scale_from_amax(a, scale_dtype=scale_dtype)
+    amax = column_absmax(x_shard)
+    if dist.is_available() and dist.is_initialized() and dist.get_world_size(group) > 1:
+        dist.all_reduce(amax, op=dist.ReduceOp.MAX, group=group)
+    s32, s_out = scale_from_amax(amax)
+    if x_shard.shape[2] == 0:
+        codes = torch.empty(x_shard.shape, dtype=torch.int8, device=x_shard.device)
+    else:
+        codes = quant_static(x_shard, s32, out=out)
+    return codes, (s_out if s_out is not None else s32)
 
 
 def gather_partials(local: torch.Tensor, group=None) -> torch.Tensor:

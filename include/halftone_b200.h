@@ -161,6 +161,30 @@ HQ_API int hq_append_kv_static(const void* k_new, const void* v_new, int x_dtype
                                hq_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * Bulk K write sharded along the sequence: each rank holds tokens s0 .. s1 of
+ * every sequence but the per-channel scale is that of the whole sequence,
+ * scale = RN(max(amax, 1e-8) / 127) with amax over every rank's tokens - the
+ * rule of quantize_int8 (reference/page_attention_int8_pytorch.py:23-30)
+ * applied per channel as quant_k_perchannel_triton does
+ * (src/kernels/quant_kv_triton.py:16-50, 90-103).  The reference runs on one
+ * device; its multi-GPU form is this library's.
+ *
+ * hq_column_absmax: amax[b, h, d] = max |x[b, h, s, d]| over the S tokens of x
+ *   [B, H, S, D] (x_dtype F32/BF16/F16, rows 16-byte aligned, D in {64, 128,
+ *   256}); amax float32 [B, H, D] contiguous, zero-filled by the call first, so
+ *   S = 0 (an empty shard) gives zeros.  Ranks combine the maxima with an
+ *   all-reduce (MAX) of the float words.
+ * hq_k_scale_from_amax: scale[i] = RN(max(amax[i], 1e-8) / 127) for n values,
+ *   into scale_f32 and / or scale_f16 (rounded to half).  hq_quant_k_static with
+ *   that scale then gives every rank the codes an unsharded
+ *   hq_quant_k_perchannel gives those tokens, bit for bit.
+ */
+HQ_API int hq_column_absmax(const void* x, int x_dtype, const int64_t x_strides[4], int B, int H,
+                            int S, int D, float* amax, hq_stream_t stream);
+HQ_API int hq_k_scale_from_amax(const float* amax, int n, float* scale_f32, uint16_t* scale_f16,
+                                hq_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * Dequantize an int8 cache tensor: out = dtype(float(code) * float(scale)).
  * Replaces the read path of QuantizedKVCache.update
  * (tests/qwen_kvcache_full.py:64-65) and dequantize_int8
