@@ -148,3 +148,18 @@ def test_blockwise_cache_option_combinations():
     QuantizedKVCache(mode="fused", k_block_tokens=128, device_lengths=True)
     c = QuantizedKVCache(mode="fused", k_block_tokens=64)
     assert c.get_seq_length(0) == 0 and len(c) == 0 and c.storage_bytes() == 0
+
+
+def test_sharded_write_entry_points_reject_bad_arguments():
+    """hq_column_absmax / hq_k_scale_from_amax: argument checks that return before any launch."""
+    L = _lib.lib()
+    st4 = _lib.strides((0, 0, 128, 1), 4)
+    assert L.hq_column_absmax(None, 1, st4, 1, 8, 64, 128, 16, None) == -1   # no input
+    assert L.hq_column_absmax(16, 1, st4, 1, 8, 64, 128, None, None) == -1   # no output
+    assert L.hq_column_absmax(16, 3, st4, 1, 8, 64, 128, 16, None) == -2     # int8 input
+    assert L.hq_column_absmax(16, 1, st4, 1, 8, 64, 96, 16, None) == -2      # head_dim
+    assert L.hq_column_absmax(16, 1, st4, 1, 8, -1, 128, 16, None) == -1     # negative S
+    assert L.hq_column_absmax(16, 1, st4, 0, 8, 64, 128, 16, None) == 0      # nothing to do
+    assert L.hq_k_scale_from_amax(None, 8, 16, None, None) == -1
+    assert L.hq_k_scale_from_amax(16, 8, None, None, None) == -1             # no output
+    assert L.hq_k_scale_from_amax(16, 0, 16, None, None) == 0
