@@ -402,9 +402,27 @@ __device__ void append_split(const Params& p, int b, int kvh, int S, unsigned ch
   float mv = vred[0];
 #pragma unroll
   for (int w = 1; w < kWarps; ++w) mv = fmaxf(mv, vred[w]);
-  const Quantizer qk = Quantizer::from_amax(fabsf(xk));
-  const Quantizer qvz = Quantizer::from_amax(mv);
-  const int ck = qk.code(xk), cv = qvz.code(xv);
+  // 16-bit inputs: the scale without a divide (exact for a 16-bit maximum) and the code
+  // as the rint of the quotient with one FMA residual correction (exact for |x| <= that
+  // maximum) - no divide and no branch on this block's path to the merge
+  Quantizer qk, qvz;
+  int ck, cv;
+  if constexpr (QDT == HQ_DTYPE_F32) {
+    qk = Quantizer::from_amax(fabsf(xk));
+    qvz = Quantizer::from_amax(mv);
+    ck = qk.code(xk);
+    cv = qvz.code(xv);
+  } else {
+    qk = Quantizer::from_amax16(fabsf(xk));
+    qvz = Quantizer::from_amax16(mv);
+    auto code16 = [](const Quantizer& q, float x) {
+      const float q0 = x * q.rcp;
+      const float q1 = __fmaf_rn(__fmaf_rn(q0, -q.scale, x), q.rcp, q0);
+      return __float_as_int(q1 + 12582912.0f) - 0x4B400000;
+    };
+    ck = code16(qk, xk);
+    cv = code16(qvz, xv);
+  }
   const typename SE::T vs_stored = SE::from_f32(qvz.scale);
   if (room) {
     int8_t* kc = const_cast<int8_t*>(reinterpret_cast<const int8_t*>(p.k)) + b * p.kvsb + kvh * p.kvsh +
